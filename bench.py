@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the hexir hot path on B200: f64 hexir.linear + fused relu.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hexir|reference]
+
+Workload (per GPU): hexir.linear a[8192 x 8192] . w[8192 x 8192] f64 with
+the relu fused in the epilogue, a and w uniform[-1, 1] from the writer's
+seeded stream (seed 1, a then w).  At N GPUs the job is the row-sharded
+linear a[8192N x 8192] . w: each GPU holds its 8192 rows of a, w is
+broadcast from GPU 0 over NVLink (NCCL) and the output rows are gathered back
+to GPU 0 every step (weak scaling; N = 4 is the 32768 x 8192 x 8192 shape).
+
+One JSON line on rank 0:
+  value      GFLOP/s of the whole job, inputs resident in HBM, device time
+             (CUDA events on the launching stream, max over ranks)
+  e2e        the same through the public API with host buffers: a .hxb module
+             run by hexir_execute_capture (constants copied host->device,
+             result copied back) at N = 1; host->device copies of each rank's
+             rows, the sharded linear and the gather, result copied to the
+             host, at N > 1
+  roofline   the GEMM kernel's FLOP rate against the FP64 tensor-core (DMMA)
+             peak measured on this GPU by a register-only DMMA probe
+  cpu_baseline  the reference's own CPU kernel (hexir_ref_matmul_f64, built
+             from the reference sources into oracle/_ref) on a bounded row
+             sample with all host threads
+--impl reference times that CPU implementation alone, as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = ("f64 hexir.linear GFLOP/s & % FP64 peak @8192³ (1/2/4/8 GPU); "
+          "relu HBM GB/s")
+M_PER_GPU = N_DIM = K_DIM = 8192
+SEED = 1
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "linear_f64_tma_8192.json")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["hexir", "reference"], default="hexir")
+    p.add_argument("--m", type=int, default=M_PER_GPU,
+                   help="rows of a per GPU (default 8192)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples every 200 ms during the timed
+    region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,"
+             "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not shutil.which("nvidia-smi"):
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.out = open(self.path, "w")
+        self.proc = subprocess.Popen(
+            ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=self.out, stderr=subprocess.DEVNULL)
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for name, flag in zip(names, parts[5:9]):
+                    if flag.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+
+def make_w(world: int, m_rows: int):
+    import hexir_b200 as hx
+    rng = hx.Rng(SEED)
+    rng.uniform((world * m_rows, K_DIM))
+    return rng.uniform((K_DIM, N_DIM))
+
+
+def dmma_peak_tflops(ordinal: int) -> float:
+    """FP64 DMMA throughput of this GPU: register-only probe, best of 5."""
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+    import ctypes as C
+    sms = hx.lib().hexir_cuda_sm_count(ordinal)
+    blocks = sms * 4
+    out = torch.empty(blocks * 256, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    flops = C.c_double()
+    best = 0.0
+    iters = 4096
+    for trial in range(6):
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record()
+        _ffi.check(hx.lib().hexir_cuda_dmma_probe(
+            ordinal, out.data_ptr(), blocks, iters, stream, C.byref(flops)),
+            "dmma probe")
+        stop.record()
+        torch.cuda.synchronize()
+        if trial:
+            best = max(best, flops.value / (start.elapsed_time(stop) * 1e-3) / 1e12)
+    return best
+
+
+def cublas_dgemm_tflops(a, w, steps: int = 3) -> float:
+    """Vendor line: torch.matmul in f64 (cuBLAS DGEMM), kernel only."""
+    import torch
+    c = torch.matmul(a, w)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        torch.matmul(a, w, out=c)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    return 2.0 * a.shape[0] * a.shape[1] * w.shape[1] / (ms * 1e-3) / 1e12
+
+
+def cpu_reference_rate(rows: int, steps: int = 1, warmup: int = 0):
+    """GFLOP/s of the reference CPU kernel on `rows` rows of the workload
+    (all host threads, each on its own row slice).  Returns (gflops, threads,
+    kind, sample description, step seconds list)."""
+    import numpy as np
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    kind = "reference" if oracle.have_reference() else "port"
+    rng = np.random.default_rng(SEED)
+    a = rng.uniform(-1, 1, (rows, K_DIM))
+    w = rng.uniform(-1, 1, (K_DIM, N_DIM))
+    c = np.empty((rows, N_DIM))
+
+    def one_step():
+        per = (rows + threads - 1) // threads
+        jobs = []
+        for t in range(threads):
+            r0, r1 = t * per, min(rows, (t + 1) * per)
+            if r0 >= r1:
+                break
+            if kind == "reference":
+                fn = lambda r0=r0, r1=r1: oracle.ref_matmul_rows_into(a, w, c, r0, r1)
+            else:
+                fn = lambda r0=r0, r1=r1: c.__setitem__(
+                    slice(r0, r1), oracle.matmul_rows(a, w, r0, r1))
+            jobs.append(threading.Thread(target=fn))
+        t0 = time.perf_counter()
+        for j in jobs:
+            j.start()
+        for j in jobs:
+            j.join()
+        return time.perf_counter() - t0
+
+    for _ in range(warmup):
+        one_step()
+    times = [one_step() for _ in range(steps)]
+    flops = 2.0 * rows * N_DIM * K_DIM
+    gflops = flops / statistics.median(times) / 1e9
+    used = min(threads, rows)
+    sample = (f"{rows} rows of the {M_PER_GPU}x{N_DIM}x{K_DIM} linear per step "
+              f"(cost is linear in rows), hexir_ref_matmul_f64 on row slices, "
+              f"{used} threads")
+    return gflops, used, kind, sample, times
+
+
+# ------------------------------------------------------------------ arms
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    rows = max(2 * threads, 16)
+    gflops, used, kind, sample, times = cpu_reference_rate(
+        rows, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gflops, 3),
+        "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(times) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64", "data": "synthetic uniform[-1,1]",
+        "config": {"workload": "hexir.linear f64 8192x8192x8192 (reference CPU "
+                               "kernel on a row sample)",
+                   "sample_rows": rows},
+        "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s",
+                         "cores": used, "kind": kind, "sample": sample},
+        "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_hexir(args):
+    import numpy as np
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+    from oracle import oracle
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    ordinal = local
+    m_rows = args.m
+    m_total = m_rows * world
+
+    pg = None
+    comm = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+        import ctypes as C
+        uid = C.create_string_buffer(128)
+        if rank == 0:
+            _ffi.check(hx.lib().hexir_comm_unique_id(uid, 128), "unique id")
+        obj = [uid.raw if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = C.create_string_buffer(obj[0], 128)
+        h = C.c_void_p()
+        _ffi.check(hx.lib().hexir_comm_init_rank(uid, 128, world, rank, ordinal,
+                                                 C.byref(h)), "comm init")
+        comm = h.value
+
+    # Inputs: this rank's rows of a; w on every rank (rank 0's is the source
+    # of the broadcast; the others' buffers are overwritten every step).
+    rng = hx.Rng(SEED)
+    if rank:
+        rng.uniform((rank * m_rows, K_DIM))
+    a_host = rng.uniform((m_rows, K_DIM))
+    w_host = make_w(world, m_rows)
+    a = torch.from_numpy(a_host).cuda()
+    w = torch.from_numpy(w_host).cuda()
+    c_rows = m_total if rank == 0 else m_rows
+    c = torch.empty((c_rows, N_DIM), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        if comm is None:
+            hx.cuda_matmul(ordinal, a.data_ptr(), w.data_ptr(), c.data_ptr(),
+                           m_rows, N_DIM, K_DIM, _ffi.MATMUL_RELU, stream)
+        else:
+            _ffi.check(hx.lib().hexir_sharded_linear_f64(
+                comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
+                K_DIM, _ffi.MATMUL_RELU, stream), "sharded linear")
+
+    for _ in range(args.warmup):
+        step()
+    hx.cuda_synchronize(ordinal, stream)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(ordinal)
+    clocks.start()
+    launches0 = hx.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    stop.record()
+    torch.cuda.synchronize()
+    launches = hx.launch_count() - launches0
+    clock_info = clocks.stop()
+    hx.cuda_synchronize(ordinal, stream)
+    ms = start.elapsed_time(stop) / args.steps
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        pg.barrier()
+
+    # The timed kernel computes the right thing: spread rows vs the oracle.
+    rows = np.linspace(0, m_rows - 1, 4).astype(int)
+    got = c[:m_rows].cpu().numpy()[rows]
+    want = oracle.relu(oracle.matmul(a_host[rows], w_host))
+    err = oracle.normwise_error(got, want)
+    if not err <= 1e-12:
+        raise SystemExit(f"bench output wrong: normwise error {err}")
+
+    flops_total = 2.0 * m_total * N_DIM * K_DIM
+    value = flops_total / (ms * 1e-3) / 1e9
+
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic: uniform[-1,1], SplitMix64 seed 1 (a then w)",
+            "config": {"workload": f"hexir.linear+relu f64 row-sharded "
+                                   f"a[{m_total}x{K_DIM}] . w[{K_DIM}x{N_DIM}] "
+                                   f"({m_rows} rows per GPU)",
+                       "m": m_total, "n": N_DIM, "k": K_DIM,
+                       "parallelism": f"rows x{world}" + (
+                           ", w broadcast + row gather over NVLink (NCCL)"
+                           if world > 1 else ""),
+                       "l2": "inputs larger than L2 (a+w = 1 GiB per GPU)"},
+            "gpu_launches": launches,
+            "clocks": clock_info}
+
+    if rank == 0:
+        # Roofline of the dominant kernel (hexir_linear_f64_tma): one launch
+        # per step at N = 1, so the step's device time is its duration.
+        peak = dmma_peak_tflops(ordinal)
+        gemm_ms = ms
+        if world > 1:
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for _ in range(3):
+                hx.cuda_matmul(ordinal, a.data_ptr(), w.data_ptr(), c.data_ptr(),
+                               m_rows, N_DIM, K_DIM, _ffi.MATMUL_RELU, stream)
+            s1.record()
+            torch.cuda.synchronize()
+            gemm_ms = s0.elapsed_time(s1) / 3
+        achieved = 2.0 * m_rows * N_DIM * K_DIM / (gemm_ms * 1e-3) / 1e12
+        traffic = None
+        if os.path.exists(PROFILE_SUMMARY):
+            with open(PROFILE_SUMMARY) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch")
+        line["roofline"] = {
+            "bound": "tensor", "achieved": round(achieved, 3),
+            "peak": round(peak, 3), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4) if peak else None,
+            "traffic": traffic,
+            "peak_source": "FP64 DMMA register-only probe on this GPU "
+                           "(hexir_dmma_peak_probe, best of 5)",
+            "kernel": "hexir_linear_f64_tma"}
+        line["vendor"] = {"cublas_dgemm_tflops": round(
+            cublas_dgemm_tflops(a, w), 3)}
+
+    if not args.no_e2e:
+        line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg)
+
+    if rank == 0 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rows = max(2 * threads, 16)
+        gflops, used, kind, sample, _ = cpu_reference_rate(rows, steps=1)
+        line["cpu_baseline"] = {"value": round(gflops, 3), "unit": "GFLOP/s",
+                                "cores": used, "kind": kind, "sample": sample}
+
+    if comm:
+        hx.lib().hexir_comm_release(comm)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg):
+    """Same metric through the public API with host buffers."""
+    import numpy as np
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+
+    m_rows = a_host.shape[0]
+    m_total = m_rows * world
+    steps = max(1, min(args.steps, 5))
+    warm = max(1, min(args.warmup, 2))
+    if world == 1:
+        # A .hxb module run by the VM: CONST uploads of a and w from the
+        # module's RODATA, the fused linear+relu, capture of the result into
+        # pinned host memory.
+        prog = hx.Program()
+        prog.relu(prog.linear(prog.constant(a_host), prog.constant(w_host)))
+        tmp = tempfile.mkdtemp()
+        path = os.path.join(tmp, "linear_relu_8192.hxb")
+        prog.emit_file(path, "hexir.linear=cuda,hexir.relu=cuda")
+        del prog
+        module = hx.Module(path)
+        dev = hx.Device(f"cuda:{ordinal}")
+        out = torch.empty((m_rows, N_DIM), dtype=torch.float64).pin_memory()
+        out_np = out.numpy()
+        import ctypes as C
+
+        def once():
+            _ffi.check(hx.lib().hexir_execute_capture(
+                module.handle, dev.handle, b"main", out_np.ctypes.data,
+                out_np.nbytes), "hexir_execute_capture")
+
+        for _ in range(warm):
+            once()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            once()
+        sec = (time.perf_counter() - t0) / steps
+        module.close()
+        dev.close()
+        shutil.rmtree(tmp, ignore_errors=True)
+        h2d = a_host.nbytes + w_host.nbytes
+        d2h = m_rows * N_DIM * 8
+    else:
+        a_pin = torch.from_numpy(a_host).pin_memory()
+        w_pin = torch.from_numpy(w_host).pin_memory()
+        a = torch.empty_like(a_pin, device="cuda")
+        w = torch.empty_like(w_pin, device="cuda")
+        c = torch.empty((m_total if rank == 0 else m_rows, N_DIM),
+                        dtype=torch.float64, device="cuda")
+        out = torch.empty((m_total, N_DIM), dtype=torch.float64).pin_memory() \
+            if rank == 0 else None
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def once():
+            a.copy_(a_pin, non_blocking=True)
+            if rank == 0:
+                w.copy_(w_pin, non_blocking=True)
+            _ffi.check(hx.lib().hexir_sharded_linear_f64(
+                comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
+                K_DIM, _ffi.MATMUL_RELU, stream), "sharded linear")
+            if rank == 0:
+                out.copy_(c, non_blocking=True)
+            torch.cuda.synchronize()
+
+        for _ in range(warm):
+            once()
+        pg.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            once()
+        sec = (time.perf_counter() - t0) / steps
+        t = torch.tensor([sec], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        sec = float(t.item())
+        h2d = a_host.nbytes * world + w_host.nbytes
+        d2h = m_total * N_DIM * 8
+    value = 2.0 * m_total * N_DIM * K_DIM / sec / 1e9
+    return {"value": round(value, 3), "unit": "GFLOP/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(sec * 1e3, 3),
+            "path": ("hexir_execute_capture of a .hxb (linear=cuda, relu=cuda)"
+                     if world == 1 else
+                     "pinned host rows -> hexir_sharded_linear_f64 -> pinned "
+                     "host result on rank 0"),
+            "timing": "host wall clock around synchronous calls, max over ranks"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_hexir(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,79 @@
+/*
+ * launch_abi.h -- by-value argument blocks of the sm_100a kernels.
+ *
+ * Shared by the device code (the .cu files under kernels/) and the host launcher
+ * (runtime/kernel_lib.cc), which passes each block by value through
+ * cuLaunchKernel.  Plain C, fixed-width fields, no pointers to host memory.
+ */
+#ifndef HEXIR_B200_LAUNCH_ABI_H
+#define HEXIR_B200_LAUNCH_ABI_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Tile shape of the TMA-fed DMMA GEMM (linear_f64.cu). */
+#define HEXIR_LINEAR_BM 128
+#define HEXIR_LINEAR_BN 128
+#define HEXIR_LINEAR_BK 32
+#define HEXIR_LINEAR_STAGES 3
+#define HEXIR_LINEAR_CONSUMER_WARPS 8
+#define HEXIR_LINEAR_THREADS (HEXIR_LINEAR_CONSUMER_WARPS * 32)
+/* A stage: BK/8 slabs of [BM][8] f64; B stage: BN/16 slabs of [BK][16] f64. */
+#define HEXIR_LINEAR_STAGE_BYTES \
+  ((HEXIR_LINEAR_BM * HEXIR_LINEAR_BK + HEXIR_LINEAR_BK * HEXIR_LINEAR_BN) * 8)
+/* + 1024 for aligning the ring to the 128-byte swizzle atom, + barriers. */
+#define HEXIR_LINEAR_SMEM_BYTES \
+  (HEXIR_LINEAR_STAGES * HEXIR_LINEAR_STAGE_BYTES + 1024 + 256)
+
+/* Tile shape of the guarded GEMM for shapes TMA cannot describe. */
+#define HEXIR_LINEAR_G_BM 64
+#define HEXIR_LINEAR_G_BN 64
+#define HEXIR_LINEAR_G_BK 16
+#define HEXIR_LINEAR_G_THREADS 128
+#define HEXIR_LINEAR_G_SMEM_BYTES \
+  (2 * (HEXIR_LINEAR_G_BM * HEXIR_LINEAR_G_BK + \
+        HEXIR_LINEAR_G_BK * HEXIR_LINEAR_G_BN) * 8 + 1024)
+
+#define HEXIR_EPILOGUE_RELU 0x1u
+
+/* Error bits a kernel ORs into the device error word. */
+#define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */
+#define HEXIR_KERR_BAD_ARGS 0x2u      /* launch arguments failed a check */
+
+typedef struct {
+  double *c;             /* destination (or split-K partials), row-major */
+  const double *a;       /* [m][k] row-major; read by the guarded kernel */
+  const double *b;       /* [k][n] row-major; read by the guarded kernel */
+  uint32_t m, n, k;
+  uint32_t epilogue;     /* HEXIR_EPILOGUE_* applied when split_k == 1 */
+  uint32_t tiles_m, tiles_n;
+  uint32_t group_m;      /* tile raster: group_m row-tiles per column sweep */
+  uint32_t k_tiles;      /* ceil(k / BK) */
+  uint32_t split_k;      /* K ranges; > 1 writes partials to c + s*m*n */
+  uint32_t k_tiles_per_split;
+  unsigned int *error;   /* device error word */
+  uint64_t timeout_ns;   /* bound on every pipeline wait */
+} hexir_linear_args_t;
+
+typedef struct {
+  const double *partials; /* [split][m*n] */
+  double *c;
+  uint64_t count;         /* m * n */
+  uint32_t split;
+  uint32_t epilogue;
+} hexir_reduce_args_t;
+
+typedef struct {
+  const double *x;
+  const double *y; /* second operand of add; unused by relu */
+  double *out;
+  uint64_t count;
+} hexir_elementwise_args_t;
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXIR_B200_LAUNCH_ABI_H */

@@ -1,0 +1,167 @@
+// comm.cc -- row-shard planning and the multi-process sharded linear
+// (include/hexir_b200/comm.h).
+
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "cuda_driver.h"
+#include "hexir_b200/comm.h"
+#include "hexir_b200/kernels.h"
+#include "kernel_lib.h"
+#include "nccl_shim.h"
+
+using namespace hexir;
+
+struct hexir_comm_t {
+  ncclComm_t comm = nullptr;
+  int nranks = 0;
+  int rank = 0;
+  int ordinal = 0;
+};
+
+extern "C" {
+
+hexir_status_t hexir_shard_rows(uint64_t rows, uint32_t shards, uint32_t index,
+                                uint64_t *begin, uint64_t *count) {
+  if (!begin || !count || shards == 0 || index >= shards)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  const uint64_t base = rows / shards, extra = rows % shards;
+  *begin = index * base + (index < extra ? index : extra);
+  *count = base + (index < extra ? 1 : 0);
+  return HEXIR_OK;
+}
+
+hexir_status_t hexir_comm_unique_id(void *id, size_t size) {
+  if (!id || size < sizeof(ncclUniqueId))
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  const Nccl &n = nccl();
+  if (!n.ok) {
+    set_last_error(n.error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ncclUniqueId uid;
+  ncclResult_t r = n.GetUniqueId(&uid);
+  if (r != ncclSuccess) {
+    set_last_error(nccl_message("ncclGetUniqueId", r));
+    return HEXIR_ERROR_DEVICE;
+  }
+  std::memcpy(id, &uid, sizeof(uid));
+  return HEXIR_OK;
+}
+
+hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
+                                    int rank, int ordinal, hexir_comm_t **out) {
+  if (!id || !out || size < sizeof(ncclUniqueId) || nranks < 1 || rank < 0 ||
+      rank >= nranks)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  *out = nullptr;
+  const Nccl &n = nccl();
+  if (!n.ok) {
+    set_last_error(n.error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  std::string error;
+  DeviceState *dev = device_state(ordinal, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  auto *comm = new (std::nothrow) hexir_comm_t;
+  if (!comm)
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  ContextGuard guard(dev->context);
+  ncclResult_t r = n.CommInitRank(&comm->comm, nranks, uid, rank);
+  if (r != ncclSuccess) {
+    set_last_error(nccl_message("ncclCommInitRank", r));
+    delete comm;
+    return HEXIR_ERROR_DEVICE;
+  }
+  comm->nranks = nranks;
+  comm->rank = rank;
+  comm->ordinal = ordinal;
+  *out = comm;
+  return HEXIR_OK;
+}
+
+void hexir_comm_release(hexir_comm_t *comm) {
+  if (!comm)
+    return;
+  if (comm->comm && nccl().ok)
+    nccl().CommDestroy(comm->comm);
+  delete comm;
+}
+
+int hexir_comm_rank(const hexir_comm_t *comm) { return comm ? comm->rank : -1; }
+int hexir_comm_size(const hexir_comm_t *comm) {
+  return comm ? comm->nranks : 0;
+}
+
+hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows,
+                                        double *w, double *c, uint32_t m,
+                                        uint32_t n, uint32_t k, uint32_t flags,
+                                        void *stream) {
+  if (!comm || !w || !c)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  const Nccl &nc = nccl();
+  std::string error;
+  DeviceState *dev = device_state(comm->ordinal, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  KernelLib *lib = embedded_library(dev, &error);
+  if (!lib) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ContextGuard guard(dev->context);
+  CUstream s = static_cast<CUstream>(stream);
+  const uint32_t ranks = static_cast<uint32_t>(comm->nranks);
+  uint64_t begin = 0, rows = 0;
+  hexir_shard_rows(m, ranks, static_cast<uint32_t>(comm->rank), &begin, &rows);
+
+  // 1. Weight from the root to everyone, over NVLink.
+  ncclResult_t r = nc.Broadcast(w, w, static_cast<size_t>(k) * n, ncclDouble, 0,
+                                comm->comm, reinterpret_cast<cudaStream_t>(s));
+  if (r != ncclSuccess) {
+    set_last_error(nccl_message("ncclBroadcast", r));
+    return HEXIR_ERROR_DEVICE;
+  }
+  // 2. This rank's rows; the root writes straight into its part of c.
+  if (rows) {
+    hexir_status_t st = launch_matmul(dev, lib, a_rows, w, c,
+                                      static_cast<uint32_t>(rows), n, k,
+                                      flags & HEXIR_MATMUL_RELU, s, &error);
+    if (st != HEXIR_OK) {
+      set_last_error(error);
+      return st;
+    }
+  }
+  // 3. Rows back to the root.
+  if (ranks > 1) {
+    nc.GroupStart();
+    if (comm->rank == 0) {
+      for (uint32_t peer = 1; peer < ranks; ++peer) {
+        uint64_t pb = 0, pr = 0;
+        hexir_shard_rows(m, ranks, peer, &pb, &pr);
+        if (pr)
+          nc.Recv(c + pb * n, pr * n, ncclDouble, static_cast<int>(peer),
+                  comm->comm, reinterpret_cast<cudaStream_t>(s));
+      }
+    } else if (rows) {
+      nc.Send(c, rows * n, ncclDouble, 0, comm->comm,
+              reinterpret_cast<cudaStream_t>(s));
+    }
+    r = nc.GroupEnd();
+    if (r != ncclSuccess) {
+      set_last_error(nccl_message("ncclGroupEnd (row gather)", r));
+      return HEXIR_ERROR_DEVICE;
+    }
+  }
+  return HEXIR_OK;
+}
+
+}  // extern "C"

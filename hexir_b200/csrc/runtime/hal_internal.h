@@ -1,0 +1,95 @@
+// hal_internal.h -- backend interface behind include/hexir_runtime/hal.h.
+//
+// The reference keeps a C vtable per backend (runtime/src/hal/hal_internal.h);
+// here each backend is a C++ class deriving from hexir_device_t.  The public
+// structs stay opaque to C callers.
+#pragma once
+
+#include <cuda.h>
+
+#include <cstddef>
+#include <string>
+
+#include "hexir_runtime/hal.h"
+
+namespace hexir {
+struct DeviceState;
+}
+
+struct hexir_device_t {
+  hexir_device_kind_t kind = HEXIR_DEVICE_CPU;
+  int ordinal = -1;
+  std::string name;
+
+  virtual ~hexir_device_t() = default;
+  virtual hexir_status_t buffer_allocate(size_t size, hexir_memory_kind_t memory,
+                                         hexir_buffer_t **out) = 0;
+  virtual void buffer_release(hexir_buffer_t *buffer) = 0;
+  virtual hexir_status_t buffer_write(hexir_buffer_t *dst, const void *src,
+                                      size_t size) = 0;
+  virtual hexir_status_t buffer_read(const hexir_buffer_t *src, void *dst,
+                                     size_t size) = 0;
+  virtual void *buffer_host_pointer(hexir_buffer_t *buffer) = 0;
+  virtual hexir_status_t launch(const void *image, size_t image_size,
+                                const char *entry, unsigned grid_x,
+                                unsigned grid_y, unsigned block_x,
+                                unsigned block_y, hexir_buffer_t **args,
+                                unsigned arg_count) {
+    (void)image; (void)image_size; (void)entry; (void)grid_x; (void)grid_y;
+    (void)block_x; (void)block_y; (void)args; (void)arg_count;
+    return HEXIR_ERROR_UNIMPLEMENTED;
+  }
+  virtual hexir_status_t wait() = 0;
+};
+
+struct hexir_buffer_t {
+  hexir_device_t *device = nullptr;
+  size_t size = 0;
+  hexir_memory_kind_t memory = HEXIR_MEMORY_HOST_LOCAL;
+  void *impl = nullptr;  // host pointer (CPU) or CUdeviceptr (CUDA)
+};
+
+namespace hexir {
+
+// The CUDA backend, visible to the VM for asynchronous copies and launches.
+struct CudaDevice : hexir_device_t {
+  DeviceState *state = nullptr;
+  CUstream stream = nullptr;
+
+  ~CudaDevice() override;
+  hexir_status_t buffer_allocate(size_t size, hexir_memory_kind_t memory,
+                                 hexir_buffer_t **out) override;
+  void buffer_release(hexir_buffer_t *buffer) override;
+  hexir_status_t buffer_write(hexir_buffer_t *dst, const void *src,
+                              size_t size) override;
+  hexir_status_t buffer_read(const hexir_buffer_t *src, void *dst,
+                             size_t size) override;
+  void *buffer_host_pointer(hexir_buffer_t *) override { return nullptr; }
+  hexir_status_t launch(const void *image, size_t image_size, const char *entry,
+                        unsigned grid_x, unsigned grid_y, unsigned block_x,
+                        unsigned block_y, hexir_buffer_t **args,
+                        unsigned arg_count) override;
+  hexir_status_t wait() override;
+
+  // Host to device copy on this device's stream; returns before the copy
+  // completes (pageable sources are staged by the driver first).
+  hexir_status_t write_async(CUdeviceptr dst, const void *src, size_t size);
+  // Allocate without zeroing (the VM zeroes lazily where it must).
+  hexir_status_t allocate_raw(size_t size, hexir_buffer_t **out);
+};
+
+CudaDevice *as_cuda(hexir_device_t *device);
+
+// Reports a backend failure the way the reference does: "hexir: <message>"
+// on stderr.
+void report(const std::string &message);
+
+}  // namespace hexir
+
+// CPU reference kernels used for cpu-placed dispatches (cpu_kernels.cc).
+namespace hexir {
+void cpu_matmul_f64(const double *a, const double *b, double *c, uint32_t m,
+                    uint32_t n, uint32_t k);
+void cpu_add_f64(const double *a, const double *b, double *c, size_t n);
+void cpu_relu_f64(const double *x, double *y, size_t n);
+}  // namespace hexir

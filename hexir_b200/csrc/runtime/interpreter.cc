@@ -1,0 +1,990 @@
+// interpreter.cc -- replay an entry point's command list (include/hexir_runtime/vm.h).
+//
+// Command semantics follow the reference interpreter
+// (runtime/src/vm/interpreter.c:200-340): ALLOC binds a zeroed destination,
+// CONST binds RODATA bytes, DISPATCH runs an executable with the destination
+// last, PRINT prints "%f " per element and a newline per row, END captures
+// the last dispatch destination and releases everything.  Every number read
+// from the module (slot, executable index, RODATA range, operand count) is
+// bounds checked before use, and so are buffer sizes against the kernel
+// extents (the reference trusts those).
+//
+// What is new is where values live.  A slot can have a host copy (RODATA or
+// a host buffer) and a copy on any open GPU; a dispatch makes its inputs
+// valid where it runs (host<->device copies, or NVLink peer copies) and its
+// destination valid only there.  That lets cpu- and cuda-placed kernels mix
+// in one program, and lets a linear be row-sharded over several GPUs:
+//
+//   weight  -> first GPU, then ncclBroadcast to the rest of the range
+//   a rows  -> each GPU gets its rows (hexir_shard_rows) straight from where
+//              a lives
+//   c rows  -> each GPU computes its rows with no collective; ncclSend/Recv
+//              gathers them into c on the first GPU
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "cuda_driver.h"
+#include "hal_internal.h"
+#include "hexir_b200/comm.h"
+#include "hexir_b200/kernels.h"
+#include "hexir_runtime/program.h"
+#include "hexir_runtime/vm.h"
+#include "kernel_lib.h"
+#include "nccl_shim.h"
+
+namespace hexir {
+
+namespace {
+
+constexpr int kMaxSlots = 256;  // as the reference (interpreter.c:20)
+constexpr int kHost = -1;
+
+thread_local double g_last_kernel_ms = 0.0;
+
+// NCCL communicators for in-process row sharding, one set per group of CUDA
+// ordinals; kept for the life of the process.
+std::mutex g_comms_mu;
+std::map<std::vector<int>, std::vector<ncclComm_t>> g_comms;
+
+hexir_status_t comms_for(const std::vector<int> &ordinals,
+                         std::vector<ncclComm_t> *out, std::string *error) {
+  std::lock_guard<std::mutex> lock(g_comms_mu);
+  auto it = g_comms.find(ordinals);
+  if (it != g_comms.end()) {
+    *out = it->second;
+    return HEXIR_OK;
+  }
+  const Nccl &n = nccl();
+  if (!n.ok) {
+    *error = n.error;
+    return HEXIR_ERROR_DEVICE;
+  }
+  std::vector<ncclComm_t> comms(ordinals.size());
+  ncclResult_t r = n.CommInitAll(comms.data(), static_cast<int>(ordinals.size()),
+                                 ordinals.data());
+  if (r != ncclSuccess) {
+    *error = nccl_message("ncclCommInitAll", r);
+    return HEXIR_ERROR_DEVICE;
+  }
+  g_comms[ordinals] = comms;
+  *out = comms;
+  return HEXIR_OK;
+}
+
+struct Slot {
+  bool defined = false;
+  uint64_t bytes = 0;
+  const uint8_t *rodata = nullptr;  // CONST: bytes in the module mapping
+  std::vector<double> host;         // host copy
+  bool host_valid = false;
+  bool zero = false;                // ALLOC'd and not written yet
+  std::map<int, hexir_buffer_t *> dev;  // program ordinal -> buffer
+  std::set<int> dev_valid;
+};
+
+struct Span {
+  CudaDevice *device = nullptr;
+  CUevent start = nullptr, stop = nullptr;
+};
+
+struct Vm {
+  const uint8_t *rodata = nullptr;
+  uint64_t rodata_size = 0;
+  const hexir_executable_entry_t *exes = nullptr;
+  uint32_t exe_count = 0;
+  const uint8_t *exe_base = nullptr;
+  uint64_t exe_size = 0;
+  const hexir_launch_entry_t *launches = nullptr;
+  uint32_t launch_count = 0;
+
+  hexir_device_t *primary = nullptr;  // device named in messages
+  std::vector<CudaDevice *> cuda;     // program ordinal -> device
+  std::map<std::pair<uint32_t, int>, KernelLib *> libs;
+  Slot slots[kMaxSlots];
+  std::vector<std::pair<CudaDevice *, hexir_buffer_t *>> temps;
+  std::vector<Span> spans;
+  bool trace = false;
+
+  ~Vm() { release(); }
+
+  void release() {
+    for (Slot &s : slots) {
+      for (auto &kv : s.dev)
+        hexir_buffer_release(kv.second);
+      s = Slot();
+    }
+    for (auto &t : temps)
+      hexir_buffer_release(t.second);
+    temps.clear();
+    for (Span &sp : spans) {
+      ContextGuard guard(sp.device->state->context);
+      driver().EventDestroy(sp.start);
+      driver().EventDestroy(sp.stop);
+    }
+    spans.clear();
+  }
+
+  Slot *slot(uint64_t index) {
+    return index < kMaxSlots && slots[index].defined ? &slots[index] : nullptr;
+  }
+
+  // ---- binding -----------------------------------------------------------
+
+  hexir_status_t bind(uint64_t index, uint64_t bytes) {
+    if (index >= kMaxSlots)
+      return HEXIR_ERROR_INVALID_MODULE;
+    Slot &s = slots[index];
+    for (auto &kv : s.dev)
+      hexir_buffer_release(kv.second);
+    s = Slot();
+    s.defined = true;
+    s.bytes = bytes;
+    return HEXIR_OK;
+  }
+
+  // ---- where values live -------------------------------------------------
+
+  // Order `to`'s stream after the work queued so far on `from`'s stream.
+  hexir_status_t order_after(CudaDevice *from, CudaDevice *to) {
+    if (from == to)
+      return HEXIR_OK;
+    const Driver &d = driver();
+    CUevent ev = nullptr;
+    ContextGuard g(from->state->context);
+    CUresult r = d.EventCreate(&ev, CU_EVENT_DISABLE_TIMING);
+    if (r == CUDA_SUCCESS)
+      r = d.EventRecord(ev, from->stream);
+    if (r == CUDA_SUCCESS) {
+      ContextGuard g2(to->state->context);
+      r = d.StreamWaitEvent(to->stream, ev, 0);
+    }
+    if (ev)
+      d.EventDestroy(ev);  // deferred by the driver until the event completes
+    if (r != CUDA_SUCCESS) {
+      report(cuda_message("cross-device ordering", r));
+      return HEXIR_ERROR_DEVICE;
+    }
+    return HEXIR_OK;
+  }
+
+  hexir_status_t buffer_on(Slot &s, int o, uint64_t bytes, CUdeviceptr *out) {
+    auto it = s.dev.find(o);
+    if (it == s.dev.end()) {
+      hexir_buffer_t *b = nullptr;
+      hexir_status_t st = cuda[o]->allocate_raw(bytes, &b);
+      if (st != HEXIR_OK)
+        return st;
+      it = s.dev.emplace(o, b).first;
+    }
+    *out = reinterpret_cast<CUdeviceptr>(it->second->impl);
+    return HEXIR_OK;
+  }
+
+  hexir_status_t temp_on(int o, uint64_t bytes, CUdeviceptr *out) {
+    hexir_buffer_t *b = nullptr;
+    hexir_status_t st = cuda[o]->allocate_raw(bytes, &b);
+    if (st != HEXIR_OK)
+      return st;
+    temps.emplace_back(cuda[o], b);
+    *out = reinterpret_cast<CUdeviceptr>(b->impl);
+    return HEXIR_OK;
+  }
+
+  // Copy bytes [offset, offset + bytes) of slot s to `dst` on GPU o, from
+  // wherever the slot is valid.  Asynchronous on o's stream.
+  hexir_status_t copy_range_to(Slot &s, uint64_t offset, uint64_t bytes, int o,
+                               CUdeviceptr dst) {
+    const Driver &d = driver();
+    CudaDevice *to = cuda[o];
+    if (bytes == 0)
+      return HEXIR_OK;
+    ContextGuard guard(to->state->context);
+    CUresult r = CUDA_SUCCESS;
+    if (s.zero) {
+      r = d.MemsetD8Async(dst, 0, bytes, to->stream);
+    } else if (s.rodata) {
+      return to->write_async(dst, s.rodata + offset, bytes);
+    } else if (s.host_valid) {
+      return to->write_async(
+          dst, reinterpret_cast<const uint8_t *>(s.host.data()) + offset, bytes);
+    } else if (s.dev_valid.count(o)) {
+      r = d.MemcpyDtoDAsync(
+          dst, reinterpret_cast<CUdeviceptr>(s.dev[o]->impl) + offset, bytes,
+          to->stream);
+    } else if (!s.dev_valid.empty()) {
+      const int p = *s.dev_valid.begin();
+      CudaDevice *from = cuda[p];
+      hexir_status_t st = order_after(from, to);
+      if (st != HEXIR_OK)
+        return st;
+      r = d.MemcpyPeerAsync(dst, to->state->context,
+                            reinterpret_cast<CUdeviceptr>(s.dev[p]->impl) +
+                                offset,
+                            from->state->context, bytes, to->stream);
+      // Later work on `from` must not overwrite the source under the copy.
+      if (r == CUDA_SUCCESS && (st = order_after(to, from)) != HEXIR_OK)
+        return st;
+    } else {
+      r = d.MemsetD8Async(dst, 0, bytes, to->stream);
+    }
+    if (r != CUDA_SUCCESS) {
+      report(cuda_message("device copy", r));
+      return HEXIR_ERROR_DEVICE;
+    }
+    return HEXIR_OK;
+  }
+
+  // Make slot s valid on GPU o and return its address there.
+  hexir_status_t on_device(Slot &s, int o, CUdeviceptr *out) {
+    hexir_status_t st = buffer_on(s, o, s.bytes, out);
+    if (st != HEXIR_OK || s.dev_valid.count(o))
+      return st;
+    st = copy_range_to(s, 0, s.bytes, o, *out);
+    if (st == HEXIR_OK)
+      s.dev_valid.insert(o);
+    return st;
+  }
+
+  // Make slot s valid on the host and return its bytes.
+  hexir_status_t on_host(Slot &s, const uint8_t **out) {
+    if (s.rodata) {
+      *out = s.rodata;
+      return HEXIR_OK;
+    }
+    if (!s.host_valid) {
+      s.host.assign((s.bytes + 7) / 8, 0.0);
+      if (!s.zero && !s.dev_valid.empty()) {
+        const int p = *s.dev_valid.begin();
+        hexir_status_t st = hexir_buffer_read(
+            s.dev[p], s.host.data(), static_cast<size_t>(s.bytes));
+        if (st != HEXIR_OK)
+          return st;
+      }
+      s.host_valid = true;
+    }
+    *out = reinterpret_cast<const uint8_t *>(s.host.data());
+    return HEXIR_OK;
+  }
+
+  // The destination of a dispatch becomes valid only where it is written.
+  void written_on_device(Slot &s, int o) {
+    s.zero = false;
+    s.rodata = nullptr;
+    s.host_valid = false;
+    s.dev_valid.clear();
+    s.dev_valid.insert(o);
+  }
+  double *written_on_host(Slot &s) {
+    s.host.resize((s.bytes + 7) / 8);
+    s.zero = false;
+    s.rodata = nullptr;
+    s.host_valid = true;
+    s.dev_valid.clear();
+    return s.host.data();
+  }
+
+  // ---- dispatch ----------------------------------------------------------
+
+  KernelLib *library(uint32_t index, int o) {
+    auto key = std::make_pair(index, o);
+    auto it = libs.find(key);
+    if (it != libs.end())
+      return it->second;
+    const hexir_executable_entry_t &exe = exes[index];
+    std::string error;
+    KernelLib *lib = library_for_image(cuda[o]->state,
+                                       exe_base + exe.image_offset,
+                                       exe.image_size, &error);
+    if (!lib)
+      report(std::string("kernel '") + exe.name + "': " + error);
+    libs[key] = lib;
+    return lib;
+  }
+
+  Span *begin_span(CudaDevice *dev) {
+    const Driver &d = driver();
+    ContextGuard g(dev->state->context);
+    Span sp;
+    sp.device = dev;
+    if (d.EventCreate(&sp.start, CU_EVENT_DEFAULT) != CUDA_SUCCESS ||
+        d.EventCreate(&sp.stop, CU_EVENT_DEFAULT) != CUDA_SUCCESS)
+      return nullptr;
+    d.EventRecord(sp.start, dev->stream);
+    spans.push_back(sp);
+    return &spans.back();
+  }
+  void end_span(Span *sp) {
+    if (!sp)
+      return;
+    ContextGuard g(sp->device->state->context);
+    driver().EventRecord(sp->stop, sp->device->stream);
+  }
+
+  static uint64_t elems(const hexir_executable_entry_t &e) {
+    return static_cast<uint64_t>(e.m) * e.n;
+  }
+
+  // Buffer sizes against the kernel's extents.
+  hexir_status_t check_sizes(const hexir_executable_entry_t &exe,
+                             Slot *const *args, uint64_t argc) {
+    if (exe.elem_size != sizeof(double))
+      return HEXIR_ERROR_UNIMPLEMENTED;
+    const uint64_t mn = elems(exe) * 8;
+    switch (exe.kind) {
+    case HEXIR_KERNEL_MATMUL:
+    case HEXIR_KERNEL_MATMUL_RELU:
+      if (argc != 3)
+        return HEXIR_ERROR_INVALID_MODULE;
+      if (args[0]->bytes < static_cast<uint64_t>(exe.m) * exe.k * 8 ||
+          args[1]->bytes < static_cast<uint64_t>(exe.k) * exe.n * 8 ||
+          args[2]->bytes < mn)
+        return HEXIR_ERROR_INVALID_MODULE;
+      return HEXIR_OK;
+    case HEXIR_KERNEL_ADD:
+      if (argc != 3)
+        return HEXIR_ERROR_INVALID_MODULE;
+      if (args[0]->bytes < mn || args[1]->bytes < mn || args[2]->bytes < mn)
+        return HEXIR_ERROR_INVALID_MODULE;
+      return HEXIR_OK;
+    case HEXIR_KERNEL_RELU:
+      if (argc != 2)
+        return HEXIR_ERROR_INVALID_MODULE;
+      if (args[0]->bytes < mn || args[1]->bytes < mn)
+        return HEXIR_ERROR_INVALID_MODULE;
+      return HEXIR_OK;
+    default:
+      return HEXIR_ERROR_UNIMPLEMENTED;
+    }
+  }
+
+  hexir_status_t run_host(const hexir_executable_entry_t &exe, Slot *const *args) {
+    const uint8_t *in0 = nullptr, *in1 = nullptr;
+    hexir_status_t st = on_host(*args[0], &in0);
+    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
+    if (st == HEXIR_OK && binary)
+      st = on_host(*args[1], &in1);
+    if (st != HEXIR_OK)
+      return st;
+    Slot &dst = *args[binary ? 2 : 1];
+    // Inputs may alias the destination slot only in a malformed module; copy
+    // them out first so writing cannot corrupt them.
+    std::vector<double> keep0, keep1;
+    if (args[0] == &dst) {
+      keep0.assign(reinterpret_cast<const double *>(in0),
+                   reinterpret_cast<const double *>(in0) + args[0]->bytes / 8);
+      in0 = reinterpret_cast<const uint8_t *>(keep0.data());
+    }
+    if (binary && args[1] == &dst) {
+      keep1.assign(reinterpret_cast<const double *>(in1),
+                   reinterpret_cast<const double *>(in1) + args[1]->bytes / 8);
+      in1 = reinterpret_cast<const uint8_t *>(keep1.data());
+    }
+    const double *a = reinterpret_cast<const double *>(in0);
+    const double *b = reinterpret_cast<const double *>(in1);
+    double *c = written_on_host(dst);
+    switch (exe.kind) {
+    case HEXIR_KERNEL_MATMUL:
+      cpu_matmul_f64(a, b, c, exe.m, exe.n, exe.k);
+      break;
+    case HEXIR_KERNEL_MATMUL_RELU:
+      cpu_matmul_f64(a, b, c, exe.m, exe.n, exe.k);
+      cpu_relu_f64(c, c, elems(exe));
+      break;
+    case HEXIR_KERNEL_ADD:
+      cpu_add_f64(a, b, c, elems(exe));
+      break;
+    case HEXIR_KERNEL_RELU:
+      cpu_relu_f64(a, c, elems(exe));
+      break;
+    }
+    return HEXIR_OK;
+  }
+
+  hexir_status_t run_device(uint32_t index, int o, Slot *const *args) {
+    const hexir_executable_entry_t &exe = exes[index];
+    KernelLib *lib = library(index, o);
+    if (!lib)
+      return HEXIR_ERROR_DEVICE;
+    CudaDevice *dev = cuda[o];
+    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
+    CUdeviceptr in0 = 0, in1 = 0, out = 0;
+    Slot &dst = *args[binary ? 2 : 1];
+    hexir_status_t st = on_device(*args[0], o, &in0);
+    if (st == HEXIR_OK && binary)
+      st = on_device(*args[1], o, &in1);
+    if (st != HEXIR_OK)
+      return st;
+    if (&dst == args[0] || (binary && &dst == args[1])) {
+      // Malformed aliasing: give the destination a fresh buffer.
+      CUdeviceptr tmp = 0;
+      if ((st = temp_on(o, dst.bytes, &tmp)) != HEXIR_OK)
+        return st;
+      out = tmp;
+    } else if ((st = buffer_on(dst, o, dst.bytes, &out)) != HEXIR_OK) {
+      return st;
+    }
+    std::string error;
+    ContextGuard guard(dev->state->context);
+    Span *span = begin_span(dev);
+    const double *a = reinterpret_cast<const double *>(in0);
+    const double *b = reinterpret_cast<const double *>(in1);
+    double *c = reinterpret_cast<double *>(out);
+    switch (exe.kind) {
+    case HEXIR_KERNEL_MATMUL:
+    case HEXIR_KERNEL_MATMUL_RELU:
+      st = launch_matmul(dev->state, lib, a, b, c, exe.m, exe.n, exe.k,
+                         exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
+                                                              : 0u,
+                         dev->stream, &error);
+      break;
+    case HEXIR_KERNEL_ADD:
+      st = launch_add(dev->state, lib, a, b, c, elems(exe), dev->stream, &error);
+      break;
+    case HEXIR_KERNEL_RELU:
+      st = launch_relu(dev->state, lib, a, c, elems(exe), dev->stream, &error);
+      break;
+    }
+    end_span(span);
+    if (st != HEXIR_OK) {
+      report(std::string("kernel '") + exe.name + "': " + error);
+      return st;
+    }
+    if (out != reinterpret_cast<CUdeviceptr>(dst.dev.count(o) ? dst.dev[o]->impl
+                                                              : nullptr)) {
+      CUdeviceptr home = 0;
+      if ((st = buffer_on(dst, o, dst.bytes, &home)) != HEXIR_OK)
+        return st;
+      driver().MemcpyDtoDAsync(home, out, dst.bytes, dev->stream);
+    }
+    written_on_device(dst, o);
+    return HEXIR_OK;
+  }
+
+  hexir_status_t run_sharded(uint32_t index, int first, int count,
+                             Slot *const *args) {
+    const hexir_executable_entry_t &exe = exes[index];
+    const Nccl &nc = nccl();
+    std::vector<int> ordinals;
+    for (int r = 0; r < count; ++r)
+      ordinals.push_back(cuda[first + r]->ordinal);
+    std::vector<ncclComm_t> comms;
+    std::string error;
+    hexir_status_t st = comms_for(ordinals, &comms, &error);
+    if (st != HEXIR_OK) {
+      report(std::string("kernel '") + exe.name + "': " + error);
+      return st;
+    }
+    const bool matmul = exe.kind == HEXIR_KERNEL_MATMUL ||
+                        exe.kind == HEXIR_KERNEL_MATMUL_RELU;
+    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
+    Slot &dst = *args[binary ? 2 : 1];
+    if (&dst == args[0] || (binary && &dst == args[1]))
+      return HEXIR_ERROR_INVALID_MODULE;
+    for (int r = 0; r < count; ++r)
+      if (!library(index, first + r))
+        return HEXIR_ERROR_DEVICE;
+    CudaDevice *root = cuda[first];
+    Span *span = begin_span(root);
+    // Every stream of the range starts after the work queued on the root.
+    for (int r = 1; r < count; ++r)
+      if ((st = order_after(root, cuda[first + r])) != HEXIR_OK)
+        return st;
+
+    // Weight of a matmul: valid on the root, then broadcast over NVLink.
+    std::vector<CUdeviceptr> w(count, 0);
+    if (matmul) {
+      Slot &ws = *args[1];
+      if ((st = on_device(ws, first, &w[0])) != HEXIR_OK)
+        return st;
+      bool everywhere = true;
+      for (int r = 1; r < count; ++r) {
+        if ((st = buffer_on(ws, first + r, ws.bytes, &w[r])) != HEXIR_OK)
+          return st;
+        everywhere &= ws.dev_valid.count(first + r) > 0;
+      }
+      if (!everywhere) {
+        const size_t elemsw = static_cast<size_t>(exe.k) * exe.n;
+        nc.GroupStart();
+        for (int r = 0; r < count; ++r)
+          nc.Broadcast(reinterpret_cast<void *>(w[r]), reinterpret_cast<void *>(w[r]),
+                       elemsw, ncclDouble, 0, comms[r],
+                       reinterpret_cast<cudaStream_t>(cuda[first + r]->stream));
+        ncclResult_t nr = nc.GroupEnd();
+        if (nr != ncclSuccess) {
+          report(nccl_message("ncclBroadcast (weight)", nr));
+          return HEXIR_ERROR_DEVICE;
+        }
+        for (int r = 1; r < count; ++r)
+          ws.dev_valid.insert(first + r);
+      }
+    }
+
+    CUdeviceptr c_root = 0;
+    if ((st = buffer_on(dst, first, dst.bytes, &c_root)) != HEXIR_OK)
+      return st;
+    const uint64_t row_in = matmul ? static_cast<uint64_t>(exe.k) * 8
+                                   : static_cast<uint64_t>(exe.n) * 8;
+    const uint64_t row_out = static_cast<uint64_t>(exe.n) * 8;
+    std::vector<CUdeviceptr> c_part(count, 0);
+    std::vector<uint64_t> begin(count), rows(count);
+    for (int r = 0; r < count; ++r) {
+      hexir_shard_rows(exe.m, static_cast<uint32_t>(count),
+                       static_cast<uint32_t>(r), &begin[r], &rows[r]);
+      if (!rows[r])
+        continue;
+      const int o = first + r;
+      CudaDevice *dev = cuda[o];
+      // This shard's rows of the row-split inputs.
+      CUdeviceptr x = 0, y = 0;
+      const int split_inputs = matmul ? 1 : (binary ? 2 : 1);
+      for (int i = 0; i < split_inputs; ++i) {
+        Slot &in = *args[i];
+        CUdeviceptr p = 0;
+        if (in.dev_valid.count(o)) {
+          p = reinterpret_cast<CUdeviceptr>(in.dev[o]->impl) + begin[r] * row_in;
+        } else {
+          if ((st = temp_on(o, rows[r] * row_in, &p)) != HEXIR_OK ||
+              (st = copy_range_to(in, begin[r] * row_in, rows[r] * row_in, o,
+                                  p)) != HEXIR_OK)
+            return st;
+        }
+        (i == 0 ? x : y) = p;
+      }
+      CUdeviceptr out = 0;
+      if (r == 0) {
+        out = c_root;
+      } else if ((st = temp_on(o, rows[r] * row_out, &out)) != HEXIR_OK) {
+        return st;
+      }
+      c_part[r] = out;
+      ContextGuard guard(dev->state->context);
+      KernelLib *lib = libs[std::make_pair(index, o)];
+      const uint32_t m = static_cast<uint32_t>(rows[r]);
+      const uint64_t count_elems = rows[r] * exe.n;
+      switch (exe.kind) {
+      case HEXIR_KERNEL_MATMUL:
+      case HEXIR_KERNEL_MATMUL_RELU:
+        st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(x),
+                           reinterpret_cast<const double *>(w[r]),
+                           reinterpret_cast<double *>(out), m, exe.n, exe.k,
+                           exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
+                                                                : 0u,
+                           dev->stream, &error);
+        break;
+      case HEXIR_KERNEL_ADD:
+        st = launch_add(dev->state, lib, reinterpret_cast<const double *>(x),
+                        reinterpret_cast<const double *>(y),
+                        reinterpret_cast<double *>(out), count_elems,
+                        dev->stream, &error);
+        break;
+      case HEXIR_KERNEL_RELU:
+        st = launch_relu(dev->state, lib, reinterpret_cast<const double *>(x),
+                         reinterpret_cast<double *>(out), count_elems,
+                         dev->stream, &error);
+        break;
+      }
+      if (st != HEXIR_OK) {
+        report(std::string("kernel '") + exe.name + "' shard " +
+               std::to_string(r) + ": " + error);
+        return st;
+      }
+    }
+    // Rows back to the root.
+    if (count > 1) {
+      nc.GroupStart();
+      for (int r = 1; r < count; ++r) {
+        if (!rows[r])
+          continue;
+        nc.Send(reinterpret_cast<void *>(c_part[r]), rows[r] * exe.n, ncclDouble,
+                0, comms[r],
+                reinterpret_cast<cudaStream_t>(cuda[first + r]->stream));
+        nc.Recv(reinterpret_cast<void *>(c_root + begin[r] * row_out),
+                rows[r] * exe.n, ncclDouble, r, comms[0],
+                reinterpret_cast<cudaStream_t>(root->stream));
+      }
+      ncclResult_t nr = nc.GroupEnd();
+      if (nr != ncclSuccess) {
+        report(nccl_message("row gather", nr));
+        return HEXIR_ERROR_DEVICE;
+      }
+    }
+    end_span(span);
+    written_on_device(dst, first);
+    return HEXIR_OK;
+  }
+
+  hexir_status_t dispatch(const uint64_t *ops, uint32_t count) {
+    if (count < 2)
+      return HEXIR_ERROR_INVALID_MODULE;
+    const uint64_t index = ops[0], argc = ops[1];
+    if (index >= exe_count || count != 2 + argc)
+      return HEXIR_ERROR_INVALID_MODULE;
+    const hexir_executable_entry_t &exe = exes[index];
+    if (argc > 4)
+      return HEXIR_ERROR_INVALID_MODULE;
+    Slot *args[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (uint64_t i = 0; i < argc; ++i)
+      if (!(args[i] = slot(ops[2 + i])))
+        return HEXIR_ERROR_INVALID_MODULE;
+
+    if (exe.device == HEXIR_DEVICE_CUDA) {
+      if (cuda.empty()) {
+        // The reference's refusal (interpreter.c:82-92), word for word.
+        std::fprintf(stderr,
+                     "hexir-run: kernel '%.32s' is placed on cuda but the "
+                     "active device is %s\n",
+                     exe.name, hexir_device_name(primary));
+        return HEXIR_ERROR_DEVICE;
+      }
+      if (!exe.image_size) {
+        std::fprintf(stderr,
+                     "hexir-run: kernel '%.32s' is placed on cuda, but the "
+                     "module carries a kernel descriptor rather than device "
+                     "code, and there is nothing to launch\n",
+                     exe.name);
+        return HEXIR_ERROR_UNIMPLEMENTED;
+      }
+      if (static_cast<uint64_t>(exe.image_offset) + exe.image_size > exe_size)
+        return HEXIR_ERROR_INVALID_MODULE;
+      const hexir_launch_entry_t *L =
+          (launches && index < launch_count) ? &launches[index] : nullptr;
+      if (L && L->abi == HEXIR_LAUNCH_ABI_V1 &&
+          (L->flags & HEXIR_LAUNCH_FLAG_LIBRARY)) {
+        hexir_status_t st = check_sizes(exe, args, argc);
+        if (st != HEXIR_OK)
+          return st;
+        const uint64_t first = L->device_first;
+        const uint64_t n_dev = L->device_count ? L->device_count : 1;
+        if (first + n_dev > cuda.size()) {
+          std::fprintf(stderr,
+                       "hexir-run: kernel '%.32s' is placed on cuda:%llu%s%s but "
+                       "only %zu CUDA device(s) are open\n",
+                       exe.name, static_cast<unsigned long long>(first),
+                       n_dev > 1 ? "-" : "",
+                       n_dev > 1 ? std::to_string(first + n_dev - 1).c_str() : "",
+                       cuda.size());
+          return HEXIR_ERROR_DEVICE;
+        }
+        if (trace)
+          std::fprintf(stderr, "hexir: dispatch %.32s %s %ux%ux%u on cuda:%llu%s\n",
+                       exe.name, hexir_kernel_kind_string(exe.kind), exe.m,
+                       exe.n, exe.k, static_cast<unsigned long long>(first),
+                       n_dev > 1 ? (" x" + std::to_string(n_dev)).c_str() : "");
+        if (n_dev == 1)
+          return run_device(static_cast<uint32_t>(index), static_cast<int>(first),
+                            args);
+        return run_sharded(static_cast<uint32_t>(index), static_cast<int>(first),
+                           static_cast<int>(n_dev), args);
+      }
+      // An image following the reference convention: launch by entry name
+      // with one device pointer per argument, on the first GPU.
+      hexir_buffer_t *buffers[4];
+      for (uint64_t i = 0; i < argc; ++i) {
+        CUdeviceptr p = 0;
+        hexir_status_t st;
+        if (i + 1 == argc) {
+          st = buffer_on(*args[i], 0, args[i]->bytes, &p);
+          if (st == HEXIR_OK && !args[i]->dev_valid.count(0))
+            st = copy_range_to(*args[i], 0, args[i]->bytes, 0, p);
+        } else {
+          st = on_device(*args[i], 0, &p);
+        }
+        if (st != HEXIR_OK)
+          return st;
+        buffers[i] = args[i]->dev[0];
+      }
+      Span *span = begin_span(cuda[0]);
+      hexir_status_t st = cuda[0]->launch(
+          exe_base + exe.image_offset, exe.image_size, exe.name, exe.grid_x,
+          exe.grid_y, exe.block_x, exe.block_y, buffers,
+          static_cast<unsigned>(argc));
+      end_span(span);
+      if (st == HEXIR_OK)
+        written_on_device(*args[argc - 1], 0);
+      return st;
+    }
+
+    // cpu placement.
+    if (exe.image_size)
+      return HEXIR_ERROR_UNIMPLEMENTED;  // no host images exist
+    hexir_status_t st = check_sizes(exe, args, argc);
+    if (st != HEXIR_OK)
+      return st;
+    if (trace)
+      std::fprintf(stderr, "hexir: dispatch %.32s %s %ux%ux%u on cpu\n", exe.name,
+                   hexir_kernel_kind_string(exe.kind), exe.m, exe.n, exe.k);
+    return run_host(exe, args);
+  }
+
+  hexir_status_t print(uint64_t index, uint64_t rows, uint64_t cols) {
+    Slot *s = slot(index);
+    if (!s)
+      return HEXIR_ERROR_INVALID_MODULE;
+    if (rows != 0 && cols > UINT64_MAX / 8 / rows)
+      return HEXIR_ERROR_INVALID_MODULE;
+    if (rows * cols * 8 > s->bytes)
+      return HEXIR_ERROR_INVALID_MODULE;
+    const uint8_t *data = nullptr;
+    hexir_status_t st = on_host(*s, &data);
+    if (st != HEXIR_OK)
+      return st;
+    const double *v = reinterpret_cast<const double *>(data);
+    for (uint64_t i = 0; i < rows; ++i) {
+      for (uint64_t j = 0; j < cols; ++j)
+        std::printf("%f ", v[i * cols + j]);
+      std::printf("\n");
+    }
+    return HEXIR_OK;
+  }
+
+  // Wait for every GPU, collect kernel error words and span timings.
+  hexir_status_t settle() {
+    hexir_status_t result = HEXIR_OK;
+    for (CudaDevice *dev : cuda) {
+      std::string error;
+      if (check_device(dev->state, dev->stream, &error) != HEXIR_OK) {
+        report(error);
+        result = HEXIR_ERROR_DEVICE;
+      }
+    }
+    double ms = 0.0;
+    for (Span &sp : spans) {
+      ContextGuard g(sp.device->state->context);
+      float t = 0.0f;
+      if (driver().EventElapsedTime(&t, sp.start, sp.stop) == CUDA_SUCCESS)
+        ms += t;
+    }
+    g_last_kernel_ms = ms;
+    return result;
+  }
+
+  hexir_status_t capture(uint64_t index, void *out, size_t size) {
+    Slot *s = slot(index);
+    if (!s || size > s->bytes)
+      return HEXIR_ERROR_INVALID_ARGUMENT;
+    if (!s->host_valid && !s->rodata && !s->zero && !s->dev_valid.empty()) {
+      const int p = *s->dev_valid.begin();
+      return hexir_buffer_read(s->dev[p], out, size);
+    }
+    const uint8_t *data = nullptr;
+    hexir_status_t st = on_host(*s, &data);
+    if (st == HEXIR_OK && size)
+      std::memcpy(out, data, size);
+    return st;
+  }
+};
+
+hexir_status_t execute(const hexir_module_t *module, hexir_device_t *primary,
+                       std::vector<CudaDevice *> cuda, const char *entry,
+                       void *out_result, size_t out_size) {
+  if (!module || !entry)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  g_last_kernel_ms = 0.0;
+  const void *symbols_data = nullptr, *program_data = nullptr;
+  uint64_t symbols_size = 0, program_size = 0;
+  if (hexir_module_section(module, HEXIR_SECTION_SYMBOLS, &symbols_data,
+                           &symbols_size) != HEXIR_OK ||
+      hexir_module_section(module, HEXIR_SECTION_PROGRAM, &program_data,
+                           &program_size) != HEXIR_OK)
+    return HEXIR_ERROR_INVALID_MODULE;
+
+  auto vm = std::make_unique<Vm>();
+  vm->primary = primary;
+  vm->cuda = std::move(cuda);
+  const char *trace = std::getenv("HEXIR_TRACE");
+  vm->trace = trace && trace[0] && trace[0] != '0';
+
+  const void *data = nullptr;
+  uint64_t size = 0;
+  if (hexir_module_section(module, HEXIR_SECTION_RODATA, &data, &size) ==
+      HEXIR_OK) {
+    vm->rodata = static_cast<const uint8_t *>(data);
+    vm->rodata_size = size;
+  }
+  if (hexir_module_section(module, HEXIR_SECTION_EXECUTABLES, &data, &size) ==
+          HEXIR_OK &&
+      size >= sizeof(hexir_executable_header_t)) {
+    hexir_executable_header_t header;
+    std::memcpy(&header, data, sizeof(header));
+    const uint64_t table = sizeof(header) + static_cast<uint64_t>(header.count) *
+                                                sizeof(hexir_executable_entry_t);
+    if (table > size)
+      return HEXIR_ERROR_INVALID_MODULE;
+    vm->exes = reinterpret_cast<const hexir_executable_entry_t *>(
+        static_cast<const uint8_t *>(data) + sizeof(header));
+    vm->exe_count = header.count;
+    vm->exe_base = static_cast<const uint8_t *>(data);
+    vm->exe_size = size;
+  }
+  if (hexir_module_section(module, HEXIR_SECTION_LAUNCH, &data, &size) ==
+          HEXIR_OK &&
+      size >= sizeof(hexir_launch_header_t)) {
+    hexir_launch_header_t header;
+    std::memcpy(&header, data, sizeof(header));
+    const uint64_t table = sizeof(header) + static_cast<uint64_t>(header.count) *
+                                                sizeof(hexir_launch_entry_t);
+    if (table > size)
+      return HEXIR_ERROR_INVALID_MODULE;
+    vm->launches = reinterpret_cast<const hexir_launch_entry_t *>(
+        static_cast<const uint8_t *>(data) + sizeof(header));
+    vm->launch_count = header.count;
+  }
+
+  const auto *symbols = static_cast<const hexir_symbol_entry_t *>(symbols_data);
+  const uint64_t symbol_count = symbols_size / sizeof(hexir_symbol_entry_t);
+  uint64_t pc = 0;
+  bool found = false;
+  for (uint64_t i = 0; i < symbol_count; ++i) {
+    if (std::strncmp(symbols[i].name, entry, HEXIR_NAME_SIZE) == 0) {
+      pc = symbols[i].program_offset;
+      found = true;
+      break;
+    }
+  }
+  if (!found)
+    return HEXIR_ERROR_NOT_FOUND;
+
+  const uint8_t *program = static_cast<const uint8_t *>(program_data);
+  hexir_status_t status = HEXIR_OK;
+  int64_t result_slot = -1;
+  while (status == HEXIR_OK) {
+    if (pc + sizeof(hexir_command_header_t) > program_size) {
+      status = HEXIR_ERROR_INVALID_MODULE;
+      break;
+    }
+    hexir_command_header_t header;
+    std::memcpy(&header, program + pc, sizeof(header));
+    pc += sizeof(header);
+    const uint64_t operand_bytes =
+        static_cast<uint64_t>(header.operand_count) * sizeof(uint64_t);
+    if (pc + operand_bytes > program_size) {
+      status = HEXIR_ERROR_INVALID_MODULE;
+      break;
+    }
+    std::vector<uint64_t> ops(header.operand_count);
+    if (operand_bytes)
+      std::memcpy(ops.data(), program + pc, operand_bytes);
+    pc += operand_bytes;
+
+    switch (header.kind) {
+    case HEXIR_CMD_END: {
+      hexir_status_t settled = vm->settle();
+      if (settled != HEXIR_OK)
+        return settled;
+      if (out_result && out_size && result_slot >= 0)
+        status = vm->capture(static_cast<uint64_t>(result_slot), out_result,
+                             out_size);
+      return status;
+    }
+    case HEXIR_CMD_ALLOC:
+      if (header.operand_count != 2) {
+        status = HEXIR_ERROR_INVALID_MODULE;
+        break;
+      }
+      status = vm->bind(ops[0], ops[1]);
+      if (status == HEXIR_OK)
+        vm->slots[ops[0]].zero = true;
+      break;
+    case HEXIR_CMD_CONST: {
+      if (header.operand_count != 3) {
+        status = HEXIR_ERROR_INVALID_MODULE;
+        break;
+      }
+      const uint64_t offset = ops[1], bytes = ops[2];
+      if (offset > vm->rodata_size || bytes > vm->rodata_size - offset) {
+        status = HEXIR_ERROR_INVALID_MODULE;
+        break;
+      }
+      status = vm->bind(ops[0], bytes);
+      if (status == HEXIR_OK)
+        vm->slots[ops[0]].rodata = vm->rodata + offset;
+      break;
+    }
+    case HEXIR_CMD_DISPATCH:
+      status = vm->dispatch(ops.data(), header.operand_count);
+      if (status == HEXIR_OK && header.operand_count >= 3)
+        result_slot = static_cast<int64_t>(ops[header.operand_count - 1]);
+      break;
+    case HEXIR_CMD_PRINT:
+      if (header.operand_count != 3)
+        status = HEXIR_ERROR_INVALID_MODULE;
+      else
+        status = vm->print(ops[0], ops[1], ops[2]);
+      break;
+    default:
+      status = HEXIR_ERROR_INVALID_MODULE;
+      break;
+    }
+  }
+  vm->settle();
+  return status;
+}
+
+}  // namespace
+
+}  // namespace hexir
+
+using namespace hexir;
+
+extern "C" {
+
+const char *hexir_kernel_kind_string(uint32_t kind) {
+  switch (kind) {
+  case HEXIR_KERNEL_MATMUL: return "matmul";
+  case HEXIR_KERNEL_ADD: return "add";
+  case HEXIR_KERNEL_RELU: return "relu";
+  case HEXIR_KERNEL_MATMUL_RELU: return "matmul_relu";
+  }
+  return "unknown";
+}
+
+hexir_status_t hexir_execute(const hexir_module_t *module,
+                             hexir_device_t *device, const char *entry) {
+  return hexir_execute_capture(module, device, entry, nullptr, 0);
+}
+
+hexir_status_t hexir_execute_capture(const hexir_module_t *module,
+                                     hexir_device_t *device, const char *entry,
+                                     void *out_result, size_t out_size) {
+  if (!module || !device || !entry)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  std::vector<CudaDevice *> cuda;
+  if (CudaDevice *c = as_cuda(device))
+    cuda.push_back(c);
+  return execute(module, device, std::move(cuda), entry, out_result, out_size);
+}
+
+hexir_status_t hexir_execute_devices(const hexir_module_t *module,
+                                     hexir_device_t *const *devices,
+                                     unsigned device_count, const char *entry,
+                                     void *out_result, size_t out_size) {
+  if (!module || !entry || (device_count && !devices))
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  std::vector<CudaDevice *> cuda;
+  for (unsigned i = 0; i < device_count; ++i) {
+    CudaDevice *c = as_cuda(devices[i]);
+    if (!c)
+      return HEXIR_ERROR_INVALID_ARGUMENT;
+    cuda.push_back(c);
+  }
+  hexir_device_t *primary = device_count ? devices[0] : nullptr;
+  static hexir_device_t *host_only = nullptr;
+  if (!primary) {
+    if (!host_only && hexir_device_create(HEXIR_DEVICE_CPU, &host_only) != HEXIR_OK)
+      return HEXIR_ERROR_OUT_OF_MEMORY;
+    primary = host_only;
+  }
+  return execute(module, primary, std::move(cuda), entry, out_result, out_size);
+}
+
+double hexir_last_execute_kernel_ms(void) { return g_last_kernel_ms; }
+
+}  // extern "C"

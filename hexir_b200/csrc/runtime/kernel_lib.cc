@@ -1,0 +1,577 @@
+// kernel_lib.cc -- per-GPU state, kernel module cache, launch planning and the
+// kernel-level C ABI (include/hexir_b200/kernels.h).
+
+#include "kernel_lib.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+
+#include "../kernels/launch_abi.h"
+#include "cuda_driver.h"
+#include "hexir_b200/kernels.h"
+
+extern "C" {
+extern const unsigned char hexir_embedded_cubin_begin[];
+extern const unsigned char hexir_embedded_cubin_end[];
+}
+
+namespace hexir {
+
+namespace {
+
+std::mutex g_devices_mu;
+std::map<int, std::unique_ptr<DeviceState>> g_devices;
+std::atomic<uint64_t> g_launches{0};
+thread_local std::string g_last_error;
+
+// Every pipeline wait in the kernels gives up after this much wall time.
+constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
+
+bool aligned16(const void *p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+uint32_t ceil_div(uint64_t a, uint64_t b) {
+  return static_cast<uint32_t>((a + b - 1) / b);
+}
+
+hexir_status_t fail(std::string *error, std::string message,
+                    hexir_status_t status = HEXIR_ERROR_DEVICE) {
+  if (error)
+    *error = std::move(message);
+  return status;
+}
+
+// Workspace for split-K partials: grown on demand, never shrunk.  Growing
+// frees the old block only after the context is idle.
+hexir_status_t ensure_workspace(DeviceState *dev, size_t bytes,
+                                std::string *error) {
+  const Driver &d = driver();
+  if (dev->workspace_bytes >= bytes)
+    return HEXIR_OK;
+  if (dev->workspace) {
+    d.CtxSynchronize();
+    d.MemFree(dev->workspace);
+    dev->workspace = 0;
+    dev->workspace_bytes = 0;
+  }
+  CUresult r = d.MemAlloc(&dev->workspace, bytes);
+  if (r != CUDA_SUCCESS)
+    return fail(error, cuda_message("cuMemAlloc(split-K workspace)", r),
+                HEXIR_ERROR_OUT_OF_MEMORY);
+  dev->workspace_bytes = bytes;
+  return HEXIR_OK;
+}
+
+hexir_status_t launch(CUfunction fn, unsigned gx, unsigned gy, unsigned bx,
+                      unsigned smem, CUstream stream, void **params,
+                      const char *what, std::string *error) {
+  CUresult r =
+      driver().LaunchKernel(fn, gx, gy, 1, bx, 1, 1, smem, stream, params, nullptr);
+  if (r != CUDA_SUCCESS)
+    return fail(error, cuda_message(what, r));
+  count_launch();
+  return HEXIR_OK;
+}
+
+unsigned stream_grid(const DeviceState *dev, uint64_t pairs) {
+  // Four 16-byte vectors per thread per pass, 256 threads per CTA; at most
+  // 8 CTAs per SM, the rest by grid stride.
+  const uint64_t want = (pairs + 1023) / 1024;
+  const uint64_t cap = static_cast<uint64_t>(std::max(dev->sm_count, 1)) * 8;
+  return static_cast<unsigned>(std::max<uint64_t>(1, std::min(want, cap)));
+}
+
+}  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_last_error(const std::string &message) { g_last_error = message; }
+
+uint64_t hash_bytes(const void *data, size_t size) {
+  const unsigned char *p = static_cast<const unsigned char *>(data);
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < size; ++i) {
+    h ^= p[i];
+    h *= 1099511628211ull;
+  }
+  return h ^ size;
+}
+
+const void *embedded_image_data() { return hexir_embedded_cubin_begin; }
+size_t embedded_image_size() {
+  return static_cast<size_t>(hexir_embedded_cubin_end - hexir_embedded_cubin_begin);
+}
+
+DeviceState *device_state(int ordinal, std::string *error) {
+  const Driver &d = driver();
+  if (!d.ok) {
+    if (error)
+      *error = d.error;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_devices_mu);
+  auto it = g_devices.find(ordinal);
+  if (it != g_devices.end())
+    return it->second.get();
+
+  int count = 0;
+  CUresult r = d.DeviceGetCount(&count);
+  if (r != CUDA_SUCCESS) {
+    fail(error, cuda_message("cuDeviceGetCount", r));
+    return nullptr;
+  }
+  if (ordinal < 0 || ordinal >= count) {
+    fail(error, "no CUDA device " + std::to_string(ordinal) + " (" +
+                    std::to_string(count) + " visible)");
+    return nullptr;
+  }
+  auto dev = std::make_unique<DeviceState>();
+  dev->ordinal = ordinal;
+  r = d.DeviceGet(&dev->device, ordinal);
+  if (r == CUDA_SUCCESS)
+    r = d.DevicePrimaryCtxRetain(&dev->context, dev->device);
+  if (r != CUDA_SUCCESS) {
+    fail(error, "cannot open CUDA device " + std::to_string(ordinal) + ": " +
+                    cuda_message("cuDevicePrimaryCtxRetain", r));
+    return nullptr;
+  }
+  d.DeviceGetAttribute(&dev->sm_count, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT,
+                       dev->device);
+  char name[128] = {0};
+  if (d.DeviceGetName(name, sizeof(name) - 1, dev->device) == CUDA_SUCCESS)
+    dev->name = name;
+  {
+    ContextGuard guard(dev->context);
+    d.EventCreate(&dev->ws_ready, CU_EVENT_DISABLE_TIMING);
+  }
+  DeviceState *raw = dev.get();
+  g_devices[ordinal] = std::move(dev);
+  return raw;
+}
+
+KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
+                             std::string *error) {
+  const Driver &d = driver();
+  const uint64_t key = hash_bytes(image, size);
+  std::lock_guard<std::mutex> lock(dev->mu);
+  auto it = dev->libs.find(key);
+  if (it != dev->libs.end())
+    return it->second.get();
+
+  ContextGuard guard(dev->context);
+  auto lib = std::make_unique<KernelLib>();
+  CUresult r = d.ModuleLoadData(&lib->module, image);
+  if (r != CUDA_SUCCESS) {
+    int major = 0, minor = 0;
+    d.DeviceGetAttribute(&major, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MAJOR,
+                         dev->device);
+    d.DeviceGetAttribute(&minor, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MINOR,
+                         dev->device);
+    fail(error, cuda_message("cuModuleLoadData", r) +
+                    " (the kernels are built for sm_100a; device " +
+                    std::to_string(dev->ordinal) + " is sm_" +
+                    std::to_string(major) + std::to_string(minor) + ")");
+    return nullptr;
+  }
+  struct Need {
+    CUfunction *slot;
+    const char *name;
+  } needs[] = {
+      {&lib->linear_tma, "hexir_linear_f64_tma"},
+      {&lib->linear_guarded, "hexir_linear_f64_guarded"},
+      {&lib->splitk_reduce, "hexir_linear_f64_splitk_reduce"},
+      {&lib->relu, "hexir_relu_f64"},
+      {&lib->add, "hexir_add_f64"},
+      {&lib->dmma_probe, "hexir_dmma_peak_probe"},
+  };
+  CUfunction marker = nullptr;
+  if (d.ModuleGetFunction(&marker, lib->module, "hexir_b200_abi_v1") !=
+      CUDA_SUCCESS) {
+    d.ModuleUnload(lib->module);
+    fail(error, "device image is not a hexir-b200 kernel library (launch ABI "
+                "version 1)");
+    return nullptr;
+  }
+  for (const Need &need : needs) {
+    r = d.ModuleGetFunction(need.slot, lib->module, need.name);
+    if (r != CUDA_SUCCESS) {
+      d.ModuleUnload(lib->module);
+      fail(error, std::string("kernel library image lacks ") + need.name);
+      return nullptr;
+    }
+  }
+  size_t word_bytes = 0;
+  r = d.ModuleGetGlobal(&lib->error_word, &word_bytes, lib->module,
+                        "hexir_device_error_word");
+  if (r == CUDA_SUCCESS)
+    r = d.FuncSetAttribute(lib->linear_tma,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_LINEAR_SMEM_BYTES);
+  if (r == CUDA_SUCCESS)
+    r = d.FuncSetAttribute(lib->linear_guarded,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_LINEAR_G_SMEM_BYTES);
+  if (r != CUDA_SUCCESS) {
+    d.ModuleUnload(lib->module);
+    fail(error, cuda_message("kernel library setup", r));
+    return nullptr;
+  }
+  KernelLib *raw = lib.get();
+  dev->libs[key] = std::move(lib);
+  return raw;
+}
+
+KernelLib *embedded_library(DeviceState *dev, std::string *error) {
+  if (dev->embedded)
+    return dev->embedded;
+  KernelLib *lib = library_for_image(dev, embedded_image_data(),
+                                     embedded_image_size(), error);
+  if (lib) {
+    std::lock_guard<std::mutex> lock(dev->mu);
+    dev->embedded = lib;
+  }
+  return lib;
+}
+
+MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
+                       const double *c, uint32_t m, uint32_t n, uint32_t k,
+                       uint32_t flags) {
+  MatmulPlan p;
+  // TMA needs 16-byte aligned bases and row strides (k, n even).
+  const bool tma_ok = (k % 2 == 0) && (n % 2 == 0) && aligned16(a) &&
+                      aligned16(b) && aligned16(c);
+  p.variant = tma_ok ? 1 : 2;
+  if ((flags & HEXIR_MATMUL_FORCE_GUARDED) || !tma_ok)
+    p.variant = 2;
+  if (p.variant == 1) {
+    p.bm = HEXIR_LINEAR_BM;
+    p.bn = HEXIR_LINEAR_BN;
+    p.bk = HEXIR_LINEAR_BK;
+  } else {
+    p.bm = HEXIR_LINEAR_G_BM;
+    p.bn = HEXIR_LINEAR_G_BN;
+    p.bk = HEXIR_LINEAR_G_BK;
+  }
+  p.tiles_m = ceil_div(m, p.bm);
+  p.tiles_n = ceil_div(n, p.bn);
+  p.k_tiles = ceil_div(k, p.bk);
+  const uint64_t tiles = static_cast<uint64_t>(p.tiles_m) * p.tiles_n;
+  uint32_t split = (flags >> 16) & 0xFFu;
+  const int sms = dev ? std::max(dev->sm_count, 1) : 148;
+  if (split == 0) {
+    split = 1;
+    // Too few output tiles to fill the GPU: split k, keeping >= 4 k-tiles
+    // per piece so the pipeline still streams.
+    if (tiles < static_cast<uint64_t>(sms) && p.k_tiles >= 8) {
+      split = static_cast<uint32_t>(sms / tiles);
+      split = std::min<uint32_t>(split, p.k_tiles / 4);
+      split = std::min<uint32_t>(split, 32);
+      split = std::max<uint32_t>(split, 1);
+    }
+  }
+  split = std::max<uint32_t>(1, std::min(split, std::max<uint32_t>(p.k_tiles, 1)));
+  p.k_tiles_per_split = std::max<uint32_t>(1, ceil_div(p.k_tiles, split));
+  // No empty pieces.
+  p.split_k = std::max<uint32_t>(1, ceil_div(std::max<uint32_t>(p.k_tiles, 1),
+                                             p.k_tiles_per_split));
+  return p;
+}
+
+hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
+                             const double *b, double *c, uint32_t m, uint32_t n,
+                             uint32_t k, uint32_t flags, CUstream stream,
+                             std::string *error) {
+  const Driver &d = driver();
+  if (m == 0 || n == 0)
+    return HEXIR_OK;
+  if (!a || !b || !c)
+    return fail(error, "matmul: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
+  if ((flags & HEXIR_MATMUL_FORCE_TMA) &&
+      plan_matmul(dev, a, b, c, m, n, k, flags & ~HEXIR_MATMUL_FORCE_TMA)
+              .variant != 1)
+    return fail(error,
+                "matmul: the TMA kernel needs even k and n and 16-byte aligned "
+                "pointers",
+                HEXIR_ERROR_INVALID_ARGUMENT);
+  const size_t out_bytes = static_cast<size_t>(m) * n * sizeof(double);
+  if (k == 0) {
+    // An empty sum is 0 and relu(0) = 0.
+    CUresult r = d.MemsetD8Async(reinterpret_cast<CUdeviceptr>(c), 0, out_bytes,
+                                 stream);
+    return r == CUDA_SUCCESS ? HEXIR_OK
+                             : fail(error, cuda_message("cuMemsetD8Async", r));
+  }
+  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags);
+
+  hexir_linear_args_t args;
+  std::memset(&args, 0, sizeof(args));
+  args.a = a;
+  args.b = b;
+  args.c = c;
+  args.m = m;
+  args.n = n;
+  args.k = k;
+  args.epilogue = (flags & HEXIR_MATMUL_RELU) ? HEXIR_EPILOGUE_RELU : 0u;
+  args.tiles_m = p.tiles_m;
+  args.tiles_n = p.tiles_n;
+  args.group_m = std::min<uint32_t>(8, p.tiles_m);
+  args.k_tiles = p.k_tiles;
+  args.split_k = p.split_k;
+  args.k_tiles_per_split = p.k_tiles_per_split;
+  args.error = reinterpret_cast<unsigned int *>(lib->error_word);
+  args.timeout_ns = kWaitTimeoutNs;
+
+  std::unique_lock<std::mutex> ws_lock(dev->mu, std::defer_lock);
+  if (p.split_k > 1) {
+    ws_lock.lock();
+    hexir_status_t s = ensure_workspace(
+        dev, static_cast<size_t>(p.split_k) * out_bytes, error);
+    if (s != HEXIR_OK)
+      return s;
+    // The previous user of the workspace may be another stream.
+    d.StreamWaitEvent(stream, dev->ws_ready, 0);
+    args.c = reinterpret_cast<double *>(dev->workspace);
+  }
+
+  const unsigned grid_x = p.tiles_m * p.tiles_n;
+  hexir_status_t status;
+  if (p.variant == 1) {
+    CUtensorMap map_a, map_b;
+    const cuuint64_t a_dims[2] = {k, m};
+    const cuuint64_t a_strides[1] = {static_cast<cuuint64_t>(k) * 8};
+    const cuuint32_t a_box[2] = {8, HEXIR_LINEAR_BM};
+    const cuuint64_t b_dims[2] = {n, k};
+    const cuuint64_t b_strides[1] = {static_cast<cuuint64_t>(n) * 8};
+    const cuuint32_t b_box[2] = {16, HEXIR_LINEAR_BK};
+    const cuuint32_t unit[2] = {1, 1};
+    CUresult r = d.TensorMapEncodeTiled(
+        &map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(a),
+        a_dims, a_strides, a_box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+      r = d.TensorMapEncodeTiled(
+          &map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(b),
+          b_dims, b_strides, b_box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(error, cuda_message("cuTensorMapEncodeTiled", r));
+    void *params[] = {&map_a, &map_b, &args};
+    status = launch(lib->linear_tma, grid_x, p.split_k, HEXIR_LINEAR_THREADS,
+                    HEXIR_LINEAR_SMEM_BYTES, stream, params,
+                    "launch hexir_linear_f64_tma", error);
+  } else {
+    void *params[] = {&args};
+    status = launch(lib->linear_guarded, grid_x, p.split_k,
+                    HEXIR_LINEAR_G_THREADS, HEXIR_LINEAR_G_SMEM_BYTES, stream,
+                    params, "launch hexir_linear_f64_guarded", error);
+  }
+  if (status != HEXIR_OK || p.split_k == 1)
+    return status;
+
+  hexir_reduce_args_t red;
+  red.partials = reinterpret_cast<const double *>(dev->workspace);
+  red.c = c;
+  red.count = static_cast<uint64_t>(m) * n;
+  red.split = p.split_k;
+  red.epilogue = args.epilogue;
+  void *params[] = {&red};
+  const uint64_t want = (red.count + 255) / 256;
+  const unsigned grid = static_cast<unsigned>(std::max<uint64_t>(
+      1, std::min<uint64_t>(want, static_cast<uint64_t>(dev->sm_count) * 8)));
+  status = launch(lib->splitk_reduce, grid, 1, 256, 0, stream, params,
+                  "launch hexir_linear_f64_splitk_reduce", error);
+  d.EventRecord(dev->ws_ready, stream);
+  return status;
+}
+
+hexir_status_t launch_relu(DeviceState *dev, KernelLib *lib, const double *x,
+                           double *y, size_t n, CUstream stream,
+                           std::string *error) {
+  if (n == 0)
+    return HEXIR_OK;
+  if (!x || !y)
+    return fail(error, "relu: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
+  hexir_elementwise_args_t args{x, nullptr, y, static_cast<uint64_t>(n)};
+  void *params[] = {&args};
+  return launch(lib->relu, stream_grid(dev, n / 2), 1, 256, 0, stream, params,
+                "launch hexir_relu_f64", error);
+}
+
+hexir_status_t launch_add(DeviceState *dev, KernelLib *lib, const double *a,
+                          const double *b, double *c, size_t n, CUstream stream,
+                          std::string *error) {
+  if (n == 0)
+    return HEXIR_OK;
+  if (!a || !b || !c)
+    return fail(error, "add: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
+  hexir_elementwise_args_t args{a, b, c, static_cast<uint64_t>(n)};
+  void *params[] = {&args};
+  return launch(lib->add, stream_grid(dev, n / 2), 1, 256, 0, stream, params,
+                "launch hexir_add_f64", error);
+}
+
+hexir_status_t check_device(DeviceState *dev, CUstream stream,
+                            std::string *error) {
+  const Driver &d = driver();
+  ContextGuard guard(dev->context);
+  CUresult r = d.StreamSynchronize(stream);
+  if (r != CUDA_SUCCESS)
+    return fail(error, cuda_message("kernel execution", r));
+  std::lock_guard<std::mutex> lock(dev->mu);
+  unsigned int bits = 0;
+  for (auto &entry : dev->libs) {
+    KernelLib *lib = entry.second.get();
+    unsigned int word = 0;
+    r = d.MemcpyDtoHAsync(&word, lib->error_word, sizeof(word), stream);
+    if (r == CUDA_SUCCESS)
+      r = d.StreamSynchronize(stream);
+    if (r != CUDA_SUCCESS)
+      return fail(error, cuda_message("reading the device error word", r));
+    if (word) {
+      bits |= word;
+      d.MemsetD8Async(lib->error_word, 0, sizeof(word), stream);
+      d.StreamSynchronize(stream);
+    }
+  }
+  if (bits & HEXIR_KERR_WAIT_TIMEOUT)
+    return fail(error, "a kernel pipeline wait ran out of time (device error "
+                       "word " + std::to_string(bits) + ")");
+  if (bits)
+    return fail(error, "a kernel reported device error word " +
+                           std::to_string(bits));
+  return HEXIR_OK;
+}
+
+}  // namespace hexir
+
+// ---- kernel-level C ABI --------------------------------------------------
+
+using namespace hexir;
+
+namespace {
+
+struct Call {
+  DeviceState *dev = nullptr;
+  KernelLib *lib = nullptr;
+  std::string error;
+  bool open(int ordinal) {
+    dev = device_state(ordinal, &error);
+    if (!dev)
+      return false;
+    lib = embedded_library(dev, &error);
+    return lib != nullptr;
+  }
+  hexir_status_t finish(hexir_status_t status) {
+    if (status != HEXIR_OK)
+      set_last_error(error.empty() ? hexir_status_string(status) : error);
+    return status;
+  }
+};
+
+}  // namespace
+
+extern "C" hexir_status_t hexir_cuda_matmul_f64(int ordinal, const double *a,
+                                                const double *b, double *c,
+                                                uint32_t m, uint32_t n,
+                                                uint32_t k, uint32_t flags,
+                                                void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_matmul(call.dev, call.lib, a, b, c, m, n, k, flags,
+                                   static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,
+                                             const double *b, double *c,
+                                             size_t n, void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_add(call.dev, call.lib, a, b, c, n,
+                                static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_relu_f64(int ordinal, const double *x,
+                                              double *y, size_t n,
+                                              void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_relu(call.dev, call.lib, x, y, n,
+                                 static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream) {
+  Call call;
+  call.dev = device_state(ordinal, &call.error);
+  if (!call.dev)
+    return call.finish(HEXIR_ERROR_DEVICE);
+  return call.finish(
+      check_device(call.dev, static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
+                                                 const double *b, double *c,
+                                                 uint32_t m, uint32_t n,
+                                                 uint32_t k, uint32_t flags,
+                                                 int *variant,
+                                                 uint32_t *split_k) {
+  std::string error;
+  DeviceState *dev = device_state(ordinal, &error);
+  MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags);
+  if (variant)
+    *variant = p.variant;
+  if (split_k)
+    *split_k = p.split_k;
+  return HEXIR_OK;
+}
+
+extern "C" hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out,
+                                                uint32_t blocks, uint32_t iters,
+                                                void *stream, double *flops) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  if (!out || blocks == 0)
+    return call.finish(HEXIR_ERROR_INVALID_ARGUMENT);
+  ContextGuard guard(call.dev->context);
+  void *params[] = {&out, &iters};
+  hexir_status_t s = launch(call.lib->dmma_probe, blocks, 1, 256, 0,
+                            static_cast<CUstream>(stream), params,
+                            "launch hexir_dmma_peak_probe", &call.error);
+  if (flops)
+    *flops = static_cast<double>(blocks) * (256 / 32) * iters * 8.0 *
+             (2.0 * 16 * 8 * 8);
+  return call.finish(s);
+}
+
+extern "C" uint64_t hexir_cuda_launch_count(void) {
+  return g_launches.load(std::memory_order_relaxed);
+}
+
+extern "C" int hexir_cuda_sm_count(int ordinal) {
+  std::string error;
+  DeviceState *dev = device_state(ordinal, &error);
+  return dev ? dev->sm_count : 0;
+}
+
+extern "C" hexir_status_t hexir_cuda_kernel_image(const void **data,
+                                                  size_t *size) {
+  if (!data || !size)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  *data = embedded_image_data();
+  *size = embedded_image_size();
+  return HEXIR_OK;
+}
+
+extern "C" const char *hexir_cuda_last_error(void) {
+  return g_last_error.c_str();
+}

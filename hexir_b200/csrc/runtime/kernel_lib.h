@@ -1,0 +1,100 @@
+// kernel_lib.h -- per-GPU state and the launchers of the sm_100a kernels.
+//
+// One DeviceState per CUDA ordinal, created on first use and kept for the
+// life of the process: the retained primary context (shared with any other
+// library in the process, e.g. NCCL or PyTorch), the SM count, the loaded
+// kernel modules keyed by image content, and the split-K workspace.
+#pragma once
+
+#include <cuda.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+
+#include "hexir_runtime/status.h"
+
+namespace hexir {
+
+struct KernelLib {
+  CUmodule module = nullptr;
+  CUfunction linear_tma = nullptr;
+  CUfunction linear_guarded = nullptr;
+  CUfunction splitk_reduce = nullptr;
+  CUfunction relu = nullptr;
+  CUfunction add = nullptr;
+  CUfunction dmma_probe = nullptr;
+  CUdeviceptr error_word = 0;
+};
+
+struct DeviceState {
+  int ordinal = -1;
+  CUdevice device = 0;
+  CUcontext context = nullptr;
+  int sm_count = 0;
+  std::string name;
+
+  std::mutex mu;
+  std::map<uint64_t, std::unique_ptr<KernelLib>> libs;  // by image hash
+  KernelLib *embedded = nullptr;
+
+  // split-K partial sums; reuse across streams is ordered by `ws_ready`.
+  CUdeviceptr workspace = 0;
+  size_t workspace_bytes = 0;
+  CUevent ws_ready = nullptr;
+};
+
+// Per-ordinal state; nullptr (and *error set) if the GPU cannot be opened.
+DeviceState *device_state(int ordinal, std::string *error);
+
+// The kernel module for `image` on this device, loading it on first use.
+// Returns nullptr with *error set if the image does not load or lacks the
+// kernels of launch ABI version 1.
+KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
+                             std::string *error);
+
+// The library's own embedded image on this device.
+KernelLib *embedded_library(DeviceState *dev, std::string *error);
+
+struct MatmulPlan {
+  int variant = 0;  // 1 TMA, 2 guarded
+  uint32_t split_k = 1;
+  uint32_t tiles_m = 0, tiles_n = 0, k_tiles = 0, k_tiles_per_split = 0;
+  uint32_t bm = 0, bn = 0, bk = 0;
+};
+
+MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
+                       const double *c, uint32_t m, uint32_t n, uint32_t k,
+                       uint32_t flags);
+
+// Launchers.  The caller has made dev->context current.  All asynchronous.
+hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
+                             const double *b, double *c, uint32_t m, uint32_t n,
+                             uint32_t k, uint32_t flags, CUstream stream,
+                             std::string *error);
+hexir_status_t launch_relu(DeviceState *dev, KernelLib *lib, const double *x,
+                           double *y, size_t n, CUstream stream,
+                           std::string *error);
+hexir_status_t launch_add(DeviceState *dev, KernelLib *lib, const double *a,
+                          const double *b, double *c, size_t n, CUstream stream,
+                          std::string *error);
+
+// Synchronise `stream` and collect (and clear) the device error word of
+// every module loaded on this device.
+hexir_status_t check_device(DeviceState *dev, CUstream stream,
+                            std::string *error);
+
+void count_launch();
+void set_last_error(const std::string &message);
+
+// 64-bit FNV-1a over a byte range (image identity).
+uint64_t hash_bytes(const void *data, size_t size);
+
+// The CUBIN linked into this library (embedded_image.S).
+const void *embedded_image_data();
+size_t embedded_image_size();
+
+}  // namespace hexir

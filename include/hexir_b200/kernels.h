@@ -1,0 +1,99 @@
+/*
+ * hexir_b200/kernels.h -- kernel-level C ABI of the sm_100a hot path.
+ *
+ * These are the GPU counterparts of the reference runtime's CPU kernels
+ * (runtime/src/kernels/reference_kernels.h:17-19):
+ *
+ *   hexir_ref_matmul_f64(a, b, c, m, n, k)   -> hexir_cuda_matmul_f64
+ *   hexir_ref_add_f64(a, b, c, n)            -> hexir_cuda_add_f64
+ *   hexir_ref_relu_f64(x, y, n)              -> hexir_cuda_relu_f64
+ *
+ * with the same argument order and meaning, plus the CUDA ordinal the device
+ * pointers belong to, a CUstream (NULL = the legacy default stream) and, for
+ * matmul, flags.  Pointers are device addresses (from hexir_buffer_device_pointer,
+ * cuMemAlloc, or any allocator using the device's primary context, e.g.
+ * PyTorch).  Calls are asynchronous; hexir_cuda_synchronize waits and reports
+ * kernel-side errors.
+ *
+ * Results: add and relu are bit-for-bit the reference's.  matmul sums each
+ * output in a different order than the reference's sequential k loop, so it
+ * agrees to f64 rounding (max |err| / max |c| <= 1e-12 in this project's
+ * tests), not bit for bit.
+ *
+ * There is no CPU fallback: without a CUDA driver and an sm_100 GPU every call
+ * returns HEXIR_ERROR_DEVICE with a message in hexir_cuda_last_error().
+ */
+#ifndef HEXIR_B200_KERNELS_H
+#define HEXIR_B200_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "hexir_runtime/status.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* matmul flags */
+#define HEXIR_MATMUL_RELU 0x1u          /* c = relu(a . b), reference relu */
+#define HEXIR_MATMUL_FORCE_TMA 0x100u   /* tests: only the TMA kernel */
+#define HEXIR_MATMUL_FORCE_GUARDED 0x200u /* tests: only the guarded kernel */
+/* tests: split the k range into S pieces (1..255); 0 = choose automatically */
+#define HEXIR_MATMUL_SPLIT_K(S) (((uint32_t)(S) & 0xFFu) << 16)
+
+/* c[m x n] = a[m x k] . b[k x n] (row-major f64), optionally relu'd.
+ * Replaces hexir_ref_matmul_f64 (runtime/src/kernels/reference_kernels.c:3).
+ * k == 0 gives zeros.  May use a per-device split-K workspace that the
+ * library allocates once and grows on demand. */
+hexir_status_t hexir_cuda_matmul_f64(int ordinal, const double *a,
+                                     const double *b, double *c, uint32_t m,
+                                     uint32_t n, uint32_t k, uint32_t flags,
+                                     void *stream);
+
+/* c[i] = a[i] + b[i] for i < n.  Replaces hexir_ref_add_f64
+ * (runtime/src/kernels/reference_kernels.c:15). */
+hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,
+                                  const double *b, double *c, size_t n,
+                                  void *stream);
+
+/* y[i] = x[i] > 0 ? x[i] : 0 for i < n.  Replaces hexir_ref_relu_f64
+ * (runtime/src/kernels/reference_kernels.c:20). */
+hexir_status_t hexir_cuda_relu_f64(int ordinal, const double *x, double *y,
+                                   size_t n, void *stream);
+
+/* Wait for `stream` and report any error a kernel of this library recorded
+ * on the device since the last check (the error word is then cleared). */
+hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream);
+
+/* Which matmul kernel a call with these arguments would launch:
+ * 1 = TMA pipeline, 2 = guarded; *split_k receives the k split. */
+hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
+                                      const double *b, double *c, uint32_t m,
+                                      uint32_t n, uint32_t k, uint32_t flags,
+                                      int *variant, uint32_t *split_k);
+
+/* FP64 tensor-core throughput probe: one launch of `blocks` CTAs x 256
+ * threads, each warp running `iters` rounds of 8 dependent-free DMMAs.
+ * *flops receives the launch's FLOP count.  `out` must hold blocks*256 f64. */
+hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out, uint32_t blocks,
+                                     uint32_t iters, void *stream,
+                                     double *flops);
+
+/* Kernel launches issued by this library since the process started. */
+uint64_t hexir_cuda_launch_count(void);
+
+/* Multiprocessor count of a device (0 if unavailable). */
+int hexir_cuda_sm_count(int ordinal);
+
+/* The sm_100a kernel image this library launches (a CUBIN built from
+ * hexir_b200/csrc/kernels/kernels.cu), as embedded in the library. */
+hexir_status_t hexir_cuda_kernel_image(const void **data, size_t *size);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *hexir_cuda_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXIR_B200_KERNELS_H */

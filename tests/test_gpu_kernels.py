@@ -1,0 +1,200 @@
+"""GPU parity of the kernel-level C ABI (include/hexir_b200/kernels.h) against
+the CPU oracle (oracle/hexir_oracle.c, a restatement of
+runtime/src/kernels/reference_kernels.c).
+
+Bars:
+  relu, add          bit-exact (compared as uint64 bit patterns)
+  matmul             normwise  max|c - c_ref| / max|c_ref| <= 1e-12
+  fused relu         bit-exact against relu of the unfused kernel's output
+"""
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+from hexir_b200 import _ffi
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-12  # normwise relative error bar for f64 linear
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float64).view(np.uint64)
+
+
+def run_matmul(dev, a, b, flags=0, offset_bytes=0):
+    m, k = a.shape
+    n = b.shape[1]
+    pad = offset_bytes
+    ba = dev.buffer(a.nbytes + pad + 8)
+    bb = dev.buffer(b.nbytes + pad + 8)
+    bc = dev.buffer(m * n * 8 + pad + 8)
+    if pad:
+        # Write through a host staging array so the data starts at +pad.
+        for buf, arr in ((ba, a), (bb, b)):
+            stage = np.zeros((arr.nbytes + pad + 8) // 8, dtype=np.float64)
+            stage[pad // 8: pad // 8 + arr.size] = arr.ravel()
+            buf.write(stage)
+    else:
+        ba.write(a)
+        bb.write(b)
+    hx.cuda_matmul(0, ba.ptr + pad, bb.ptr + pad, bc.ptr + pad, m, n, k, flags,
+                   dev.stream)
+    hx.cuda_synchronize(0, dev.stream)
+    out = bc.read((m * n * 8 + pad + 8) // 8)
+    return out[pad // 8: pad // 8 + m * n].reshape(m, n)
+
+
+SHAPES = [
+    (1, 1, 1), (2, 2, 2), (3, 5, 7), (37, 53, 29), (64, 64, 64),
+    (128, 128, 128), (129, 257, 67), (130, 258, 64), (256, 256, 256),
+    (300, 200, 1000), (16, 2048, 2048), (1, 1024, 4096), (513, 130, 96),
+]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_matmul_matches_oracle(gpu, m, n, k):
+    rng = np.random.default_rng(m * 1000003 + n * 1009 + k)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    want = oracle.matmul(a, b)
+    got = run_matmul(gpu, a, b)
+    assert oracle.normwise_error(got, want) <= TOL
+
+
+@pytest.mark.parametrize("variant", ["tma", "guarded"])
+@pytest.mark.parametrize("split", [0, 1, 3])
+def test_matmul_variants_and_split(gpu, variant, split):
+    m, n, k = 200, 136, 520
+    rng = np.random.default_rng(7 + split)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    flags = _ffi.MATMUL_FORCE_TMA if variant == "tma" else _ffi.MATMUL_FORCE_GUARDED
+    flags |= _ffi.MATMUL_SPLIT_K(split)
+    want = oracle.matmul(a, b)
+    got = run_matmul(gpu, a, b, flags)
+    assert oracle.normwise_error(got, want) <= TOL
+    # The plan reports the kernel that the flags select.
+    v, s = hx.matmul_plan(m, n, k, flags)
+    assert v == (1 if variant == "tma" else 2)
+    if split:
+        assert s == split
+
+
+def test_plan_picks_tma_for_aligned_even_shapes(gpu):
+    assert hx.matmul_plan(8192, 8192, 8192)[0] == 1
+    assert hx.matmul_plan(64, 64, 63)[0] == 2      # odd k: row stride not 16 B
+    assert hx.matmul_plan(64, 63, 64)[0] == 2      # odd n
+    assert hx.matmul_plan(16, 8192, 8192)[1] > 1   # too few tiles: split k
+
+
+def test_misaligned_pointers_use_guarded_kernel(gpu):
+    rng = np.random.default_rng(11)
+    a = rng.uniform(-1, 1, (70, 48))
+    b = rng.uniform(-1, 1, (48, 90))
+    got = run_matmul(gpu, a, b, offset_bytes=8)
+    assert oracle.normwise_error(got, oracle.matmul(a, b)) <= TOL
+
+
+@pytest.mark.parametrize("variant", [_ffi.MATMUL_FORCE_TMA,
+                                     _ffi.MATMUL_FORCE_GUARDED,
+                                     _ffi.MATMUL_SPLIT_K(4)])
+def test_fused_relu_is_relu_of_unfused(gpu, variant):
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (190, 256))
+    b = rng.uniform(-1, 1, (256, 144))
+    plain = run_matmul(gpu, a, b, variant)
+    fused = run_matmul(gpu, a, b, variant | _ffi.MATMUL_RELU)
+    assert np.array_equal(bits(fused), bits(oracle.relu(plain)))
+    assert oracle.normwise_error(fused, oracle.relu(oracle.matmul(a, b))) <= TOL
+
+
+def test_matmul_k_zero_gives_zeros(gpu):
+    m, n = 5, 6
+    bc = gpu.buffer(m * n * 8)
+    bc.write(np.full((m, n), 7.0))
+    ba, bb = gpu.buffer(8), gpu.buffer(8)
+    hx.cuda_matmul(0, ba.ptr, bb.ptr, bc.ptr, m, n, 0, 0, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    assert np.array_equal(bc.read((m, n)), np.zeros((m, n)))
+
+
+def test_matmul_exact_integers(gpu):
+    # [[3,1],[2,2]] . [[1,5],[5,2]] = [[8,17],[12,14]]
+    # (runtime/test/hxb-cuda.mlir:19-30, known answer).
+    a = np.array([[3.0, 1.0], [2.0, 2.0]])
+    b = np.array([[1.0, 5.0], [5.0, 2.0]])
+    assert np.array_equal(run_matmul(gpu, a, b), [[8.0, 17.0], [12.0, 14.0]])
+
+
+SPECIALS = np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, np.nan, -np.nan,
+                     5e-324, -5e-324, 2.2250738585072014e-308, 1e308, -1e308,
+                     np.float64(np.frombuffer(b"\x01\x00\x00\x00\x00\x00\xf8\x7f",
+                                              dtype=np.float64)[0])])
+
+
+@pytest.mark.parametrize("n", [0, 1, 2, 3, 15, 1024, 1025, 100003])
+@pytest.mark.parametrize("offset", [0, 8])
+def test_relu_bit_exact(gpu, n, offset):
+    rng = np.random.default_rng(n + offset)
+    x = rng.standard_normal(n)
+    if n >= SPECIALS.size:
+        x[:SPECIALS.size] = SPECIALS
+    bx = gpu.buffer(x.nbytes + 16)
+    by = gpu.buffer(x.nbytes + 16)
+    stage = np.zeros(n + 2)
+    stage[offset // 8: offset // 8 + n] = x
+    bx.write(stage)
+    hx.cuda_relu(0, bx.ptr + offset, by.ptr + offset, n, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    got = by.read(n + 2)[offset // 8: offset // 8 + n]
+    assert np.array_equal(bits(got), bits(oracle.relu(x)))
+
+
+@pytest.mark.parametrize("n", [1, 7, 4096, 99991])
+def test_add_bit_exact(gpu, n):
+    rng = np.random.default_rng(n)
+    a = rng.standard_normal(n) * 1e3
+    b = rng.standard_normal(n)
+    if n >= 8:
+        a[:6] = [np.inf, -np.inf, 1e308, -0.0, 5e-324, 0.0]
+        b[:6] = [1.0, 2.0, 1e308, -0.0, 5e-324, -0.0]
+    ba, bb, bc = gpu.upload(a), gpu.upload(b), gpu.buffer(a.nbytes)
+    hx.cuda_add(0, ba.ptr, bb.ptr, bc.ptr, n, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    assert np.array_equal(bits(bc.read(n)), bits(oracle.add(a, b)))
+
+
+def test_add_nan_inputs_give_nan(gpu):
+    # NaN payloads are not part of the contract (the GPU returns a canonical
+    # NaN); NaN-ness is.
+    a = np.array([np.nan, 1.0, np.inf, np.nan])
+    b = np.array([1.0, np.nan, -np.inf, np.nan])
+    ba, bb, bc = gpu.upload(a), gpu.upload(b), gpu.buffer(a.nbytes)
+    hx.cuda_add(0, ba.ptr, bb.ptr, bc.ptr, 4, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    assert np.isnan(bc.read(4)).all()
+
+
+def test_large_gemm_sampled_rows(gpu):
+    """4096^3 through the TMA pipeline; 24 spread rows checked against the
+    oracle (cost is linear in rows), plus a size-independent identity:
+    sum over rows of c equals (column sums of a) . b."""
+    m = n = k = 4096
+    r = hx.Rng(1)
+    a = r.uniform((m, k))
+    b = r.uniform((k, n))
+    got = run_matmul(gpu, a, b)
+    rows = np.linspace(0, m - 1, 24).astype(int)
+    want = oracle.matmul(a[rows], b)
+    assert oracle.normwise_error(got[rows], want) <= TOL
+    colsum = oracle.matmul(a.sum(axis=0, keepdims=True), b)[0]
+    assert oracle.normwise_error(got.sum(axis=0), colsum) <= 1e-10
+
+
+def test_launch_counter_counts(gpu):
+    before = hx.launch_count()
+    run_matmul(gpu, np.ones((4, 4)), np.ones((4, 4)))
+    assert hx.launch_count() > before
