@@ -1,0 +1,250 @@
+"""The .hxb writer against the reference format.
+
+The reference serializer (compiler/Serialization/ModuleSerializer.cpp) cannot
+be built here, but its output for the built-in program is checked into the
+reference as runtime/test/fixtures/mlp-cpu.hxb; the writer must reproduce it
+byte for byte (size and sha256 recorded in tests/golden/golden.json).  The
+rest pins the layout rules the serializer follows.
+"""
+
+import hashlib
+import json
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+from hexir_b200 import _ffi
+from oracle import oracle
+from tests.conftest import bin_path
+
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden.json")))
+
+
+def test_builtin_program_is_byte_identical_to_reference_fixture(tmp_path):
+    out = tmp_path / "builtin.hxb"
+    subprocess.run([bin_path("hexir-mkhxb"), "-emit=hxb", "-o", str(out)],
+                   check=True)
+    blob = out.read_bytes()
+    ref = GOLDEN["reference_fixture"]
+    assert len(blob) == ref["size"]
+    assert hashlib.sha256(blob).hexdigest() == ref["sha256"]
+
+
+def two_by_two(p):
+    a = p.constant(np.array([[3.0, 1.0], [2.0, 2.0]]))
+    b = p.constant(np.array([[1.0, 5.0], [5.0, 2.0]]))
+    return a, b
+
+
+def test_sections_are_aligned_and_in_reference_order():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.relu(p.add(p.linear(a, b), b)))
+    for placement in ["", "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda"]:
+        blob = p.emit(placement)
+        magic, version, flags, count, _ = struct.unpack_from("<8sIIII", blob)
+        assert magic == b"HEXIRMOD" and version == 3 and flags == 0
+        kinds = []
+        for i in range(count):
+            kind, sflags, off, size = struct.unpack_from("<IIQQ", blob, 24 + 24 * i)
+            assert off % 8 == 0 and off + size <= len(blob)
+            kinds.append(kind)
+        assert kinds[:4] == [1, 2, 3, 4]
+        assert kinds[4:] == ([5] if placement else [])
+
+
+def test_executable_names_kinds_and_fusion():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    m = p.linear(a, b)
+    r = p.relu(m)
+    s = p.add(r, b)
+    p.print(p.relu(s))
+    cpu = hx.read_executables(p.emit())
+    assert [(e.name, e.kind, e.device) for e in cpu] == [
+        ("linear_0", 1, 0), ("relu_1", 3, 0), ("add_2", 2, 0), ("relu_3", 3, 0)]
+    gpu = hx.read_executables(p.emit("hexir.linear=cuda,hexir.relu=cuda,"
+                                     "hexir.add=cuda"))
+    # linear -> relu folds into one matmul_relu executable named after the
+    # linear; later kernels keep their walk-order numbers.
+    assert [(e.name, e.kind, e.device) for e in gpu] == [
+        ("linear_0", 4, 1), ("add_2", 2, 1), ("relu_3", 3, 1)]
+    # One shared image for every cuda entry.
+    assert len({(e.image_offset, e.image_size) for e in gpu}) == 1
+    assert gpu[0].image_size == len(hx.kernel_image())
+    nofuse = hx.read_executables(p.emit("hexir.linear=cuda,hexir.relu=cuda,"
+                                        "hexir.add=cuda", _ffi.EMIT_NO_FUSE))
+    assert [e.name for e in nofuse] == ["linear_0", "relu_1", "add_2", "relu_3"]
+    # Different devices never fuse.
+    mixed = hx.read_executables(p.emit("hexir.linear=cuda,hexir.relu=cpu"))
+    assert [(e.name, e.device) for e in mixed][:2] == [("linear_0", 1),
+                                                       ("relu_1", 0)]
+
+
+def test_linear_with_second_user_is_not_fused():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    m = p.linear(a, b)
+    p.print(p.relu(m))
+    p.print(m)
+    exes = hx.read_executables(p.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    assert [e.kind for e in exes] == [1, 3]
+
+
+def test_program_commands_follow_serializer():
+    p = hx.Program()
+    p.constant(np.ones((1, 2)))  # unused: dropped
+    a, b = two_by_two(p)
+    m = p.linear(a, b)
+    p.print(m)
+    cmds = hx.read_program(p.emit())
+    assert cmds == [(2, (0, 0, 32)), (2, (1, 32, 32)), (1, (2, 32)),
+                    (3, (0, 3, 0, 1, 2)), (4, (2, 2, 2)), (0, ())]
+
+
+def test_splat_is_expanded():
+    p = hx.Program()
+    s = p.splat(2.0, 3, 4)
+    p.print(s)
+    blob = p.emit()
+    off, size = hx.read_sections(blob)[3]
+    assert size == 3 * 4 * 8
+    assert np.array_equal(np.frombuffer(blob[off:off + size]), np.full(12, 2.0))
+
+
+def test_launch_section_records_devices():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.relu(p.linear(a, b)))
+    blob = p.emit("hexir.linear=cuda:2-5,hexir.relu=cuda:2-5")
+    off, size = hx.read_sections(blob)[5]
+    count, _ = struct.unpack_from("<II", blob, off)
+    assert count == 1
+    abi, flags, first, n = struct.unpack_from("<4I", blob, off + 8)
+    assert (abi, flags, first, n) == (1, 1, 2, 4)
+
+
+@pytest.mark.parametrize("bad,msg", [
+    ("hexir.linear", "is not of the form <op-name>=<device>"),
+    ("hexir.linear=tpu", "'tpu' is not a device; expected cpu, cuda or gpu"),
+    ("hexir.softmax=cuda", "'hexir.softmax' is not a placeable op"),
+    ("hexir.linear=cuda:3-1", "is not a device"),
+])
+def test_placement_errors_use_reference_wording(bad, msg):
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.linear(a, b)
+    with pytest.raises(ValueError, match=msg.replace("(", r"\(").replace(")", r"\)")):
+        p.emit(bad)
+
+
+def test_gpu_alias_and_ordinals_parse():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.linear(a, b)
+    for dev in ["gpu", "cuda", "cuda:0", "cuda:7", "gpu:1-2"]:
+        assert hx.read_executables(p.emit(f"hexir.linear={dev}"))[0].device == 1
+
+
+TEXT = """
+// comment
+func.func @main() {
+  %a = hexir.constant dense<[[3.0, 1.0], [2.0, 2.0]]> : tensor<2x2xf64>
+  %b = hexir.constant dense<[[1.0, 5.0], [5.0, 2.0]]> : tensor<2x2xf64>
+  %m = hexir.linear %a, %b : tensor<2x2xf64>
+  %s = hexir.add %m, %b : tensor<2x2xf64>
+  %r = hexir.relu %s : tensor<2x2xf64>
+  hexir.print %r : tensor<2x2xf64>
+  return
+}
+"""
+
+
+def test_text_program_matches_builder():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.relu(p.add(p.linear(a, b), b)))
+    assert hx.parse(TEXT).emit() == p.emit()
+
+
+def test_text_functional_type_and_splat():
+    text = """func.func @main() {
+      %x = hexir.constant dense<1.000000e+00> : tensor<3x4xf64>
+      %w = hexir.constant dense<2.0> : tensor<4x5xf64>
+      %m = hexir.linear %x, %w : (tensor<3x4xf64>, tensor<4x5xf64>) -> tensor<3x5xf64>
+      return
+    }"""
+    exe = hx.read_executables(hx.parse(text).emit())[0]
+    assert (exe.m, exe.n, exe.k) == (3, 5, 4)
+
+
+def test_text_unlowered_op_is_refused_like_the_reference():
+    text = """func.func @main() {
+      %a = hexir.constant dense<[[3.0, 1.0], [2.0, 2.0]]> : tensor<2x2xf64>
+      %s = hexir.sigmoid %a : tensor<2x2xf64>
+      hexir.print %s : tensor<2x2xf64>
+      return
+    }"""
+    with pytest.raises(ValueError, match="cannot serialize this op into a host program"):
+        hx.parse(text)
+
+
+def test_shape_mismatch_is_refused():
+    p = hx.Program()
+    a = p.constant(np.ones((2, 3)))
+    with pytest.raises(ValueError, match="linear"):
+        p.linear(a, p.constant(np.ones((2, 3))))
+
+
+def test_multiple_functions_share_slots_and_rodata():
+    p = hx.Program()
+    p.function("first")
+    a, b = two_by_two(p)
+    p.print(p.linear(a, b))
+    p.function("second")
+    c = p.constant(np.eye(2))
+    p.print(p.relu(c))
+    blob = p.emit()
+    assert hx.read_program(blob, "first")[2] == (1, (2, 32))
+    # Slot numbers continue across functions, as the serializer's counter.
+    assert hx.read_program(blob, "second")[0][1][0] == 3
+    assert [e.name for e in hx.read_executables(blob)] == ["linear_0", "relu_1"]
+
+
+def test_rng_stream_is_stable():
+    r = hx.Rng(0)
+    first = r.uniform(4)
+    again = hx.Rng(0).uniform(8)
+    assert np.array_equal(first, again[:4])
+    assert np.all((again >= -1) & (again < 1))
+    # a then w continue one stream.
+    r2 = hx.Rng(0)
+    r2.uniform(4)
+    assert np.array_equal(r2.uniform(4), again[4:])
+    n = hx.Rng(5).normal(20000)
+    assert abs(n.mean()) < 0.05 and abs(n.std() - 1) < 0.05
+
+
+def test_reference_runtime_runs_our_cpu_modules(tmp_path):
+    """Drop-in check: modules from this writer run on the reference runtime
+    and print what the reference's own tests expect."""
+    if not oracle.have_reference():
+        pytest.skip("reference runtime not built here")
+    for case in GOLDEN["known_answers"]:
+        p = hx.Program()
+        a = p.constant(np.array(case["a"]))
+        b = p.constant(np.array(case["b"]))
+        v = p.linear(a, b)
+        for op in case["ops"][1:]:
+            v = p.add(v, b) if op == "add_b" else p.relu(v)
+        p.print(v)
+        path = tmp_path / (case["name"] + ".hxb")
+        p.emit_file(str(path))
+        res = subprocess.run([oracle.REF_RUN, "--quiet", str(path)],
+                             capture_output=True, text=True, check=True)
+        assert res.stdout == case["stdout_quiet"]

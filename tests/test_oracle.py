@@ -1,0 +1,106 @@
+"""The oracle is pinned before it is trusted.
+
+oracle/hexir_oracle.c restates runtime/src/kernels/reference_kernels.c.  It is
+checked here against
+  - tests/golden/golden.json: outputs of the reference's own hexir_ref_*_f64
+    kernels (built from the reference sources) on seeded inputs, as sha256 of
+    the output bytes, and the relu of IEEE special values;
+  - the reference library itself (oracle/_ref/libhexir_ref.so) when it is
+    present, on further random and special inputs.
+"""
+
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+from oracle import oracle
+
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden.json")))
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.mark.parametrize("vec", GOLDEN["matmul_vectors"],
+                         ids=lambda v: f"{v['m']}x{v['n']}x{v['k']}")
+def test_oracle_matches_reference_vectors(vec):
+    rng = hx.Rng(vec["seed"])
+    a = rng.uniform((vec["m"], vec["k"]))
+    b = rng.uniform((vec["k"], vec["n"]))
+    c = oracle.matmul(a, b)
+    assert sha(c) == vec["matmul_sha256"]
+    assert sha(oracle.relu(c)) == vec["relu_sha256"]
+    assert sha(oracle.add(c, c[::-1].copy())) == vec["add_reversed_rows_sha256"]
+    for i, j, v in vec["samples"]:
+        assert c[i, j] == v
+
+
+def test_oracle_relu_specials_match_reference():
+    spec = GOLDEN["relu_specials"]
+    x = np.array([float.fromhex(h) if h not in ("inf", "-inf", "nan")
+                  else float(h) for h in spec["input_hex"]])
+    got = oracle.relu(x).view(np.uint64)
+    assert [int(v) for v in got] == spec["output_bits"]
+    # NaN and -0.0 both become +0.0 (bit pattern 0).
+    assert got[1] == 0 and got[6] == 0
+
+
+@pytest.mark.parametrize("threads", [1, 2, 3, 8])
+def test_oracle_threads_do_not_change_bits(threads):
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((61, 77))
+    b = rng.standard_normal((77, 45))
+    one = oracle.matmul(a, b, threads=1)
+    assert np.array_equal(oracle.matmul(a, b, threads=threads).view(np.uint64),
+                          one.view(np.uint64))
+
+
+def test_oracle_rows_slice_matches_full():
+    rng = np.random.default_rng(4)
+    a = rng.uniform(-1, 1, (40, 33))
+    b = rng.uniform(-1, 1, (33, 21))
+    full = oracle.matmul(a, b)
+    assert np.array_equal(oracle.matmul_rows(a, b, 7, 19), full[7:19])
+
+
+needs_ref = pytest.mark.skipif(not oracle.have_reference(),
+                               reason="reference library not built here")
+
+
+@needs_ref
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (3, 4, 5), (33, 17, 65),
+                                   (128, 96, 200)])
+def test_oracle_bit_identical_to_reference_library(m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)) * 10
+    b = rng.standard_normal((k, n))
+    if m * k > 4:
+        a.flat[:4] = [np.inf, -0.0, 1e-310, np.nan]
+    want = oracle.ref_matmul(a, b)
+    got = oracle.matmul(a, b)
+    assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+
+
+@needs_ref
+def test_oracle_elementwise_bit_identical_to_reference_library():
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(10007)
+    x[:8] = [0.0, -0.0, np.nan, -np.nan, np.inf, -np.inf, 5e-324, -5e-324]
+    y = rng.standard_normal(10007)
+    assert np.array_equal(oracle.relu(x).view(np.uint64),
+                          oracle.ref_relu(x).view(np.uint64))
+    assert np.array_equal(oracle.add(x, y).view(np.uint64),
+                          oracle.ref_add(x, y).view(np.uint64))
+
+
+def test_normwise_error_definition():
+    want = np.array([[1.0, -4.0], [2.0, 0.0]])
+    got = want + np.array([[0.0, 4e-12], [0.0, 0.0]])
+    assert oracle.normwise_error(got, want) == pytest.approx(1e-12)
+    assert oracle.normwise_error(np.zeros(3), np.zeros(3)) == 0.0
