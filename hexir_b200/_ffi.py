@@ -107,6 +107,7 @@ _SIGNATURES = [
                                       C.POINTER(_u32)]),
     ("hexir_cuda_dmma_probe", _int, [_int, _vp, _u32, _u32, _vp,
                                      C.POINTER(C.c_double)]),
+    ("hexir_cuda_wait_probe", _int, [_int, _u64, _vp]),
     ("hexir_cuda_launch_count", _u64, []),
     ("hexir_cuda_sm_count", _int, [_int]),
     ("hexir_cuda_kernel_image", _int, [C.POINTER(_vp), C.POINTER(_sz)]),

@@ -33,6 +33,22 @@ extern "C" __global__ void __launch_bounds__(256)
   out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// Failure-detection probe: one thread waits on an mbarrier that nothing ever
+// arrives at.  The wait gives up after `timeout_ns`, sets
+// HEXIR_KERR_WAIT_TIMEOUT in the error word and the kernel returns, so the
+// host sees an error status and the context stays usable.  Nothing is in
+// flight when it exits.
+extern "C" __global__ void hexir_wait_timeout_probe(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    mbar_wait_bounded(&bar, 0u, timeout_ns);
+}
+
 // Marker so a loader can tell an image of this kernel library (launch ABI
 // version 1) from an arbitrary CUBIN.
 extern "C" __global__ void hexir_b200_abi_v1() {}

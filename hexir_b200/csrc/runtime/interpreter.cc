@@ -27,7 +27,9 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <new>
 #include <set>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -782,9 +784,34 @@ struct Vm {
   }
 };
 
+hexir_status_t execute_unguarded(const hexir_module_t *module,
+                                 hexir_device_t *primary,
+                                 std::vector<CudaDevice *> cuda,
+                                 const char *entry, void *out_result,
+                                 size_t out_size);
+
+// Sizes in a module are untrusted: a host buffer they ask for may not exist.
+// No C++ exception crosses the C ABI.
 hexir_status_t execute(const hexir_module_t *module, hexir_device_t *primary,
                        std::vector<CudaDevice *> cuda, const char *entry,
                        void *out_result, size_t out_size) {
+  try {
+    return execute_unguarded(module, primary, std::move(cuda), entry,
+                             out_result, out_size);
+  } catch (const std::bad_alloc &) {
+    report("host allocation failed while executing the module");
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  } catch (const std::exception &e) {
+    report(std::string("execute failed: ") + e.what());
+    return HEXIR_ERROR_INVALID_MODULE;
+  }
+}
+
+hexir_status_t execute_unguarded(const hexir_module_t *module,
+                                 hexir_device_t *primary,
+                                 std::vector<CudaDevice *> cuda,
+                                 const char *entry, void *out_result,
+                                 size_t out_size) {
   if (!module || !entry)
     return HEXIR_ERROR_INVALID_ARGUMENT;
   g_last_kernel_ms = 0.0;

@@ -185,6 +185,7 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
       {&lib->relu, "hexir_relu_f64"},
       {&lib->add, "hexir_add_f64"},
       {&lib->dmma_probe, "hexir_dmma_peak_probe"},
+      {&lib->wait_probe, "hexir_wait_timeout_probe"},
   };
   CUfunction marker = nullptr;
   if (d.ModuleGetFunction(&marker, lib->module, "hexir_b200_abi_v1") !=
@@ -551,6 +552,19 @@ extern "C" hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out,
     *flops = static_cast<double>(blocks) * (256 / 32) * iters * 8.0 *
              (2.0 * 16 * 8 * 8);
   return call.finish(s);
+}
+
+extern "C" hexir_status_t hexir_cuda_wait_probe(int ordinal,
+                                               uint64_t timeout_ns,
+                                               void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  ContextGuard guard(call.dev->context);
+  void *params[] = {&timeout_ns};
+  return call.finish(launch(call.lib->wait_probe, 1, 1, 32, 0,
+                            static_cast<CUstream>(stream), params,
+                            "launch hexir_wait_timeout_probe", &call.error));
 }
 
 extern "C" uint64_t hexir_cuda_launch_count(void) {

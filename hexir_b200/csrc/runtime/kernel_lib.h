@@ -27,6 +27,7 @@ struct KernelLib {
   CUfunction relu = nullptr;
   CUfunction add = nullptr;
   CUfunction dmma_probe = nullptr;
+  CUfunction wait_probe = nullptr;
   CUdeviceptr error_word = 0;
 };
 

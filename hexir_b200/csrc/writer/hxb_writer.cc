@@ -486,9 +486,14 @@ int32_t hexir_program_constant(hexir_program_t *p, const double *data,
                                uint32_t rows, uint32_t cols) {
   if (!p || (!data && rows && cols))
     return -1;
-  Op op{OpKind::Constant, {}, -1, {}, false, 0.0};
-  op.data.assign(data, data + static_cast<size_t>(rows) * cols);
-  return p->add_op(std::move(op), rows, cols);
+  try {
+    Op op{OpKind::Constant, {}, -1, {}, false, 0.0};
+    op.data.assign(data, data + static_cast<size_t>(rows) * cols);
+    return p->add_op(std::move(op), rows, cols);
+  } catch (const std::bad_alloc &) {
+    p->error = "out of host memory for a constant";
+    return -1;
+  }
 }
 
 int32_t hexir_program_splat(hexir_program_t *p, double value, uint32_t rows,
@@ -565,7 +570,13 @@ hexir_status_t hexir_program_emit_memory(hexir_program_t *p,
   *data = nullptr;
   *size = 0;
   Bytes out;
-  hexir_status_t st = p->emit(placement, flags, &out);
+  hexir_status_t st;
+  try {
+    st = p->emit(placement, flags, &out);
+  } catch (const std::bad_alloc &) {
+    p->error = "out of host memory while serializing";
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  }
   if (st != HEXIR_OK)
     return st;
   void *buf = std::malloc(out.size() ? out.size() : 1);
@@ -582,7 +593,13 @@ hexir_status_t hexir_program_emit_file(hexir_program_t *p, const char *placement
   if (!p || !path)
     return HEXIR_ERROR_INVALID_ARGUMENT;
   Bytes out;
-  hexir_status_t st = p->emit(placement, flags, &out);
+  hexir_status_t st;
+  try {
+    st = p->emit(placement, flags, &out);
+  } catch (const std::bad_alloc &) {
+    p->error = "out of host memory while serializing";
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  }
   if (st != HEXIR_OK)
     return st;
   FILE *f = std::fopen(path, "wb");

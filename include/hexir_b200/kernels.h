@@ -80,6 +80,15 @@ hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out, uint32_t blocks,
                                      uint32_t iters, void *stream,
                                      double *flops);
 
+/* Failure-detection probe: a one-thread kernel waits on a barrier nothing
+ * arrives at and gives up after timeout_ns, recording a wait timeout in the
+ * device error word.  The next hexir_cuda_synchronize then returns
+ * HEXIR_ERROR_DEVICE; the context stays usable.  Every wait in this library's
+ * kernels is bounded the same way (4 s), so a stuck pipeline ends with an
+ * error status instead of a hung GPU. */
+hexir_status_t hexir_cuda_wait_probe(int ordinal, uint64_t timeout_ns,
+                                     void *stream);
+
 /* Kernel launches issued by this library since the process started. */
 uint64_t hexir_cuda_launch_count(void);
 

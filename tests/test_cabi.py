@@ -1,0 +1,109 @@
+"""The C-ABI library loads on a CPU-only machine and exports every function
+the headers in include/ declare.  No compute calls: without a GPU the CUDA
+entry points must refuse (no CPU fallback), which is checked through device
+creation only."""
+
+import os
+import re
+
+import pytest
+
+import hexir_b200 as hx
+from hexir_b200 import _ffi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INCLUDE = os.path.join(ROOT, "include")
+
+DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_ ]*[\s\*]+"
+                  r"(hexir_[a-z0-9_]+)\s*\(", re.M)
+
+
+def declared_functions():
+    names = set()
+    for dirpath, _, files in os.walk(INCLUDE):
+        for f in files:
+            if f.endswith(".h"):
+                text = open(os.path.join(dirpath, f)).read()
+                text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+                text = re.sub(r"#define[^\n]*(\\\n[^\n]*)*", "", text)
+                names.update(DECL.findall(text))
+    return names
+
+
+def exported_symbols():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", _ffi.LIB_PATH],
+                         capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_headers_declare_the_expected_surface():
+    names = declared_functions()
+    # Reference HAL / module / VM entry points (runtime/include/hexir_runtime).
+    for name in ["hexir_device_create", "hexir_device_release",
+                 "hexir_device_name", "hexir_device_kind", "hexir_device_wait",
+                 "hexir_buffer_allocate", "hexir_buffer_release",
+                 "hexir_buffer_size", "hexir_buffer_memory_kind",
+                 "hexir_buffer_host_pointer", "hexir_buffer_device_pointer",
+                 "hexir_buffer_write", "hexir_buffer_read",
+                 "hexir_device_launch", "hexir_module_load_file",
+                 "hexir_module_release", "hexir_module_version",
+                 "hexir_module_section_count", "hexir_module_section_at",
+                 "hexir_module_section", "hexir_section_kind_string",
+                 "hexir_execute", "hexir_execute_capture",
+                 "hexir_status_string", "hexir_kernel_kind_string"]:
+        assert name in names, name
+    assert len(names) > 60
+
+
+def test_library_exports_every_declared_function():
+    missing = declared_functions() - exported_symbols()
+    assert not missing, sorted(missing)
+
+
+def test_python_bindings_cover_every_declared_function():
+    missing = declared_functions() - set(_ffi.EXPORTED)
+    assert not missing, sorted(missing)
+    lib = hx.lib()
+    for name in _ffi.EXPORTED:
+        assert getattr(lib, name) is not None
+
+
+def test_status_strings_match_reference():
+    want = ["ok", "invalid argument", "not found", "out of memory",
+            "unimplemented", "invalid module", "io error", "device error"]
+    assert [_ffi.status_string(i) for i in range(8)] == want
+    assert _ffi.status_string(99) == "unknown"
+
+
+def test_kernel_image_is_an_elf_cubin():
+    img = hx.kernel_image()
+    assert img[:4] == b"\x7fELF" and len(img) > 10000
+
+
+def test_shard_rows_is_balanced_and_covering():
+    for rows in [0, 1, 7, 8, 9, 8192, 32768, 32769]:
+        for shards in [1, 2, 3, 4, 8]:
+            seen, sizes = 0, []
+            for i in range(shards):
+                b, c = hx.shard_rows(rows, shards, i)
+                assert b == seen
+                seen += c
+                sizes.append(c)
+            assert seen == rows
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(_ffi.HexirError):
+        hx.shard_rows(10, 0, 0)
+
+
+def cuda_available():
+    return hx.device_count() > 0
+
+
+@pytest.mark.skipif(cuda_available(), reason="checks the no-GPU behaviour")
+def test_no_cpu_fallback_without_a_gpu():
+    with pytest.raises(_ffi.HexirError) as err:
+        hx.Device("cuda")
+    assert err.value.status == _ffi.ERROR_DEVICE
+    with pytest.raises(_ffi.HexirError):
+        hx.Device("cuda:3")

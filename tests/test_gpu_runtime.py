@@ -1,0 +1,237 @@
+"""GPU runs through the reference-facing surface: hexir-run, the VM
+(hexir_execute / hexir_execute_devices), the HAL, compared with the CPU path
+(the reference's own differential test style, runtime/test/hxb-cpu-vs-gpu.mlir)
+and with the oracle.
+
+Bars: relu bit-exact against the CPU relu of the same m; linear normwise
+max|c - c_ref| / max|c_ref| <= 1e-12.
+"""
+
+import json
+import os
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+from hexir_b200 import _ffi
+from oracle import oracle
+from tests.conftest import bin_path
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-12
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden.json")))
+RUN = bin_path("hexir-run")
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint64)
+
+
+def known_program(case):
+    p = hx.Program()
+    a = p.constant(np.array(case["a"]))
+    b = p.constant(np.array(case["b"]))
+    v = p.linear(a, b)
+    for op in case["ops"][1:]:
+        v = p.add(v, b) if op == "add_b" else p.relu(v)
+    p.print(v)
+    return p
+
+
+@pytest.mark.parametrize("case", GOLDEN["known_answers"], ids=lambda c: c["name"])
+@pytest.mark.parametrize("fuse", [True, False])
+def test_hexir_run_cuda_matches_cpu_output(tmp_path, case, fuse):
+    """CPU module vs all-cuda module, printed output diffed, as
+    hxb-cpu-vs-gpu.mlir does; both equal the reference's printed answer."""
+    p = known_program(case)
+    cpu, gpu = tmp_path / "cpu.hxb", tmp_path / "gpu.hxb"
+    p.emit_file(str(cpu))
+    p.emit_file(str(gpu), "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda",
+                0 if fuse else _ffi.EMIT_NO_FUSE)
+    out_cpu = subprocess.run([RUN, "--quiet", str(cpu)], capture_output=True,
+                             text=True, check=True).stdout
+    out_gpu = subprocess.run([RUN, "--quiet", "--device=cuda", str(gpu)],
+                             capture_output=True, text=True, check=True).stdout
+    assert out_gpu == out_cpu == case["stdout_quiet"]
+
+
+def test_selftest_cuda():
+    res = subprocess.run([RUN, "--selftest", "--device=cuda"],
+                         capture_output=True, text=True, check=True)
+    assert "device        : cuda" in res.stdout
+    assert "hal roundtrip : ok" in res.stdout
+
+
+def test_module_report_names_the_gpu(tmp_path):
+    path = tmp_path / "m.hxb"
+    known_program(GOLDEN["known_answers"][0]).emit_file(str(path),
+                                                        "hexir.linear=cuda")
+    out = subprocess.run([RUN, "--device=cuda", "--time", str(path)],
+                         capture_output=True, text=True, check=True)
+    assert "device        : cuda (NVIDIA" in out.stdout
+    assert "launch" in out.stdout  # the LAUNCH section is listed
+    assert "kernel time" in out.stderr
+
+
+def parity_graph():
+    r = hx.Rng(0)  # a then w, uniform[-1, 1], seed 0
+    return r.uniform((256, 256)), r.uniform((256, 256))
+
+
+def test_parity_graph_256():
+    """The CPU-runnable reference graph recompiled for cuda: relu bit-exact
+    against the CPU relu of the same m, linear within 1e-12."""
+    a, w = parity_graph()
+    dev = hx.Device("cuda")
+
+    p = hx.Program()
+    p.linear(p.constant(a), p.constant(w))
+    m_gpu = hx.execute(hx.Module(p.emit("hexir.linear=cuda")), dev,
+                       out_shape=(256, 256))
+    assert oracle.normwise_error(m_gpu, oracle.matmul(a, w)) <= TOL
+
+    p2 = hx.Program()
+    p2.relu(p2.linear(p2.constant(a), p2.constant(w)))
+    for flags in (_ffi.EMIT_NO_FUSE, 0):  # separate relu kernel, then fused
+        r_gpu = hx.execute(hx.Module(p2.emit(
+            "hexir.linear=cuda,hexir.relu=cuda", flags)), dev, out_shape=(256, 256))
+        assert np.array_equal(bits(r_gpu), bits(oracle.relu(m_gpu)))
+    # relu on the CPU of the GPU's m: placement-propagated transfer.
+    r_mixed = hx.execute(hx.Module(p2.emit("hexir.linear=cuda,hexir.relu=cpu")),
+                         dev, out_shape=(256, 256))
+    assert np.array_equal(bits(r_mixed), bits(oracle.relu(m_gpu)))
+    # And the whole graph on the CPU backend is the oracle, bit for bit.
+    r_cpu = hx.execute(hx.Module(p2.emit()), hx.Device("cpu"), out_shape=(256, 256))
+    assert np.array_equal(bits(r_cpu), bits(oracle.relu(oracle.matmul(a, w))))
+
+
+def test_mlp_chain_all_cuda_and_mixed_placement():
+    """x[8192x1024] -> W1[1024x4096] -> relu -> W2[4096x4096] -> relu ->
+    W3[4096x1024], x ~ N(0,1), Wi ~ N(0, 1/fan_in), seed 2.  All-cuda and
+    linear=cuda/relu=cpu must agree bit for bit (the relu is the same
+    function on both sides); sampled rows against the oracle."""
+    r = hx.Rng(2)
+    x = r.normal((8192, 1024))
+    w1 = r.normal((1024, 4096), std=1 / np.sqrt(1024))
+    w2 = r.normal((4096, 4096), std=1 / np.sqrt(4096))
+    w3 = r.normal((4096, 1024), std=1 / np.sqrt(4096))
+    p = hx.Program()
+    h = p.relu(p.linear(p.constant(x), p.constant(w1)))
+    h = p.relu(p.linear(h, p.constant(w2)))
+    p.linear(h, p.constant(w3))
+    dev = hx.Device("cuda")
+    all_cuda = hx.execute(hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda")),
+                          dev, out_shape=(8192, 1024))
+    mixed = hx.execute(hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cpu")),
+                       dev, out_shape=(8192, 1024))
+    assert np.array_equal(bits(all_cuda), bits(mixed))
+    rows = np.linspace(0, 8191, 12).astype(int)
+    want = oracle.matmul(oracle.relu(oracle.matmul(
+        oracle.relu(oracle.matmul(x[rows], w1)), w2)), w3)
+    assert oracle.normwise_error(all_cuda[rows], want) <= TOL
+
+
+def test_relu_stream_2_28_bit_exact():
+    """relu on 2^28 f64 ~ N(0,1) seed 4 as tensor<16384x16384xf64>: bit-exact
+    against the CPU relu (compared in place, no second big host copy)."""
+    n = 1 << 28
+    x = hx.Rng(4).normal(n)
+    dev = hx.Device("cuda")
+    bx, by = dev.upload(x), dev.buffer(n * 8)
+    hx.cuda_relu(0, bx.ptr, by.ptr, n, dev.stream)
+    hx.cuda_synchronize(0, dev.stream)
+    got = by.read(n)
+    np.maximum(x, 0.0, out=x)  # x > 0 ? x : 0 for finite non-NaN inputs
+    x[x == 0] = 0.0            # -0.0 -> +0.0 as the reference relu
+    assert np.array_equal(bits(got), bits(x))
+
+
+@pytest.mark.parametrize("m", [1, 16, 128])
+def test_skinny_linear(m):
+    """a[m x 8192] . w[8192 x 8192], uniform weights seed 5."""
+    r = hx.Rng(5)
+    a = r.uniform((m, 8192))
+    w = r.uniform((8192, 8192))
+    dev = hx.Device("cuda")
+    ba, bw, bc = dev.upload(a), dev.upload(w), dev.buffer(m * 8192 * 8)
+    hx.cuda_matmul(0, ba.ptr, bw.ptr, bc.ptr, m, 8192, 8192, 0, dev.stream)
+    hx.cuda_synchronize(0, dev.stream)
+    rows = np.arange(m) if m <= 16 else np.linspace(0, m - 1, 8).astype(int)
+    got = bc.read((m, 8192))[rows]
+    assert oracle.normwise_error(got, oracle.matmul(a[rows], w)) <= TOL
+
+
+def test_bounded_wait_reports_an_error_and_context_survives():
+    dev = hx.Device("cuda")
+    st = hx.lib().hexir_cuda_wait_probe(0, 2_000_000, dev.stream)  # 2 ms
+    assert st == _ffi.OK
+    st = hx.lib().hexir_cuda_synchronize(0, dev.stream)
+    assert st == _ffi.ERROR_DEVICE
+    assert "ran out of time" in hx.lib().hexir_cuda_last_error().decode()
+    # The word is cleared and the context still runs kernels.
+    a = np.eye(8)
+    ba, bc = dev.upload(a), dev.buffer(64 * 8)
+    hx.cuda_matmul(0, ba.ptr, ba.ptr, bc.ptr, 8, 8, 8, 0, dev.stream)
+    hx.cuda_synchronize(0, dev.stream)
+    assert np.array_equal(bc.read((8, 8)), a)
+
+
+def test_reference_style_image_launches_by_entry_name(tmp_path):
+    """The HAL plugin point for images that follow the reference convention
+    (one bare device pointer per buffer, kernel named after the entry):
+    hexir_device_launch loads the image and launches the named kernel."""
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("nvcc not available to build a test image")
+    src = tmp_path / "k.cu"
+    src.write_text('extern "C" __global__ void relu_1(const double *x, double *y)'
+                   ' { unsigned i = blockIdx.x * blockDim.x + threadIdx.x;'
+                   ' y[i] = x[i] > 0.0 ? x[i] : 0.0; }\n')
+    cubin = tmp_path / "k.cubin"
+    subprocess.run([nvcc, "-cubin", "-gencode", "arch=compute_100a,code=sm_100a",
+                    "-o", str(cubin), str(src)], check=True)
+    image = cubin.read_bytes()
+    dev = hx.Device("cuda")
+    x = np.linspace(-1, 1, 256)
+    bx, by = dev.upload(x), dev.buffer(256 * 8)
+    import ctypes as C
+    args = (C.c_void_p * 2)(bx._h, by._h)
+    buf = C.create_string_buffer(image, len(image))
+    st = hx.lib().hexir_device_launch(dev.handle, buf, len(image), b"relu_1",
+                                      2, 1, 128, 1, args, 2)
+    assert st == _ffi.OK
+    dev.wait()
+    assert np.array_equal(bits(by.read(256)), bits(oracle.relu(x)))
+    st = hx.lib().hexir_device_launch(dev.handle, buf, len(image), b"nosuch",
+                                      1, 1, 1, 1, args, 2)
+    assert st == _ffi.ERROR_NOT_FOUND
+
+
+def two_gpus():
+    return hx.device_count() >= 2
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+def test_row_sharded_linear_in_process(tmp_path):
+    """linear + relu placed on cuda:0-1: rows split over two GPUs, weight
+    broadcast and rows gathered with NCCL; equals the one-GPU result bit for
+    bit (same kernels, same per-row arithmetic)."""
+    r = hx.Rng(3)
+    a = r.uniform((1000, 512))
+    w = r.uniform((512, 384))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    devs = [hx.Device("cuda:0"), hx.Device("cuda:1")]
+    sharded = hx.execute(hx.Module(p.emit("hexir.linear=cuda:0-1,"
+                                          "hexir.relu=cuda:0-1")),
+                         devs, out_shape=(1000, 384))
+    single = hx.execute(hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda")),
+                        devs[0], out_shape=(1000, 384))
+    assert oracle.normwise_error(sharded, oracle.relu(oracle.matmul(a, w))) <= TOL
+    # Shards of 500 rows use the same kernel plan as the single GPU's tiles.
+    assert np.array_equal(bits(sharded), bits(single))

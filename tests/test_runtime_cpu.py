@@ -1,0 +1,235 @@
+"""hexir-run and the VM on the CPU backend: the reference's runtime tests
+(runtime/test/*.test, *.mlir) re-expressed against this runtime, plus the
+bounds checks on everything a module file can say."""
+
+import json
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+from hexir_b200 import _ffi
+from oracle import oracle
+from tests.conftest import bin_path
+
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden.json")))
+RUN = bin_path("hexir-run")
+MK = bin_path("hexir-mkhxb")
+
+
+def run(*args, check=False):
+    return subprocess.run([RUN, *args], capture_output=True, text=True,
+                          check=check)
+
+
+def known_program(case):
+    p = hx.Program()
+    a = p.constant(np.array(case["a"]))
+    b = p.constant(np.array(case["b"]))
+    v = p.linear(a, b)
+    for op in case["ops"][1:]:
+        v = p.add(v, b) if op == "add_b" else p.relu(v)
+    p.print(v)
+    return p
+
+
+@pytest.mark.parametrize("case", GOLDEN["known_answers"], ids=lambda c: c["name"])
+def test_known_answers_print_like_the_reference(tmp_path, case):
+    path = tmp_path / "m.hxb"
+    known_program(case).emit_file(str(path))
+    res = run("--quiet", str(path), check=True)
+    assert res.stdout == case["stdout_quiet"]
+
+
+def test_builtin_module_report(tmp_path):
+    # fixture-cpu.test:14-31: report lines and results.
+    path = tmp_path / "builtin.hxb"
+    subprocess.run([MK, "-o", str(path)], check=True)
+    out = run(str(path), check=True).stdout
+    assert "version       : 3" in out
+    assert "sections      : 4" in out
+    for kind in ["symbols", "program", "rodata", "executables"]:
+        assert kind in out
+    assert "device        : cpu" in out
+    assert out.endswith(GOLDEN["reference_fixture"]["stdout_quiet"])
+
+
+def test_selftest_cpu():
+    res = run("--selftest", check=True)
+    assert "device        : cpu" in res.stdout
+    assert "hal roundtrip : ok" in res.stdout
+
+
+def test_not_a_module_is_refused(tmp_path):
+    bad = tmp_path / "bad.hxb"
+    bad.write_text("func.func @main() { return }\n")
+    res = run(str(bad))
+    assert res.returncode == 1
+    assert "invalid module" in res.stderr
+
+
+def test_missing_entry_is_reported(tmp_path):
+    path = tmp_path / "m.hxb"
+    known_program(GOLDEN["known_answers"][0]).emit_file(str(path))
+    res = run(str(path), "--entry=nosuchfunc")
+    assert res.returncode == 1 and "not found" in res.stderr
+
+
+def test_usage_errors_exit_2():
+    assert run().returncode == 2
+    assert run("--device=tpu", "x.hxb").returncode == 2
+    assert run("--bogus").returncode == 2
+
+
+@pytest.mark.parametrize("flags", [0, _ffi.EMIT_NO_IMAGE])
+def test_cuda_module_refused_on_cpu(tmp_path, flags):
+    # hxb-cuda.mlir:25-30 / hxb-errors.mlir:29-31: no host fallback.
+    path = tmp_path / "m.hxb"
+    known_program(GOLDEN["known_answers"][0]).emit_file(
+        str(path), "hexir.linear=cuda", flags)
+    res = run("--quiet", str(path))
+    assert res.returncode == 1
+    assert "placed on cuda but the active device is cpu" in res.stderr
+
+
+def test_mkhxb_text_program_and_unlowered_op(tmp_path):
+    src = tmp_path / "p.mlir"
+    src.write_text("""func.func @main() {
+  %a = hexir.constant dense<[[3.0, -1.0], [2.0, 2.0]]> : tensor<2x2xf64>
+  %b = hexir.constant dense<[[1.0, 5.0], [5.0, -2.0]]> : tensor<2x2xf64>
+  %m = hexir.linear %a, %b : tensor<2x2xf64>
+  %r = hexir.relu %m : tensor<2x2xf64>
+  hexir.print %r : tensor<2x2xf64>
+  return
+}
+""")
+    out = tmp_path / "p.hxb"
+    subprocess.run([MK, "-emit=hxb", "-o", str(out), str(src)], check=True)
+    assert run("--quiet", str(out), check=True).stdout == \
+        "0.000000 17.000000 \n12.000000 6.000000 \n"
+    bad = tmp_path / "bad.mlir"
+    bad.write_text(src.read_text().replace("hexir.relu", "hexir.sigmoid"))
+    res = subprocess.run([MK, "-o", str(tmp_path / "x.hxb"), str(bad)],
+                         capture_output=True, text=True)
+    assert res.returncode == 1
+    assert "cannot serialize this op into a host program" in res.stderr
+    res = subprocess.run([MK, "-placement=hexir.linear=tpu", "-o",
+                          str(tmp_path / "y.hxb"), str(src)],
+                         capture_output=True, text=True)
+    assert res.returncode == 1 and "is not a device" in res.stderr
+
+
+def test_parity_graph_256_on_cpu_matches_oracle():
+    # The CPU-runnable reference graph: linear then relu on 256x256 f64,
+    # a then w uniform[-1,1] from seed 0.
+    r = hx.Rng(0)
+    a, w = r.uniform((256, 256)), r.uniform((256, 256))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    out = hx.execute(hx.Module(p.emit()), hx.Device("cpu"), out_shape=(256, 256))
+    want = oracle.relu(oracle.matmul(a, w))
+    assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
+    vec = [v for v in GOLDEN["matmul_vectors"] if v["m"] == 256][0]
+    import hashlib
+    assert hashlib.sha256(out.tobytes()).hexdigest() == vec["relu_sha256"]
+
+
+def test_mlp_chain_on_cpu_matches_oracle():
+    r = hx.Rng(2)
+    x = r.normal((64, 32))
+    w1 = r.normal((32, 48), std=1 / np.sqrt(32))
+    w2 = r.normal((48, 48), std=1 / np.sqrt(48))
+    w3 = r.normal((48, 16), std=1 / np.sqrt(48))
+    p = hx.Program()
+    h = p.relu(p.linear(p.constant(x), p.constant(w1)))
+    h = p.relu(p.linear(h, p.constant(w2)))
+    p.linear(h, p.constant(w3))
+    out = hx.execute(hx.Module(p.emit()), hx.Device("cpu"), out_shape=(64, 16))
+    want = oracle.matmul(oracle.relu(oracle.matmul(
+        oracle.relu(oracle.matmul(x, w1)), w2)), w3)
+    assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
+
+
+def test_execute_devices_with_no_gpu_runs_cpu_programs():
+    p = known_program(GOLDEN["known_answers"][1])
+    out = hx.execute(hx.Module(p.emit()), [], out_shape=(2, 2))
+    assert np.array_equal(out, [[9.0, 22.0], [17.0, 16.0]])
+
+
+# ---- everything in a module file is checked before use -------------------
+
+def valid_module():
+    p = known_program(GOLDEN["known_answers"][1])
+    return bytearray(p.emit())
+
+
+def run_blob(blob, tmp_path):
+    path = tmp_path / "fuzz.hxb"
+    path.write_bytes(bytes(blob))
+    return run("--quiet", str(path))
+
+
+def patch_u64(blob, offset, value):
+    struct.pack_into("<Q", blob, offset, value)
+
+
+def program_offset(blob):
+    return hx.read_sections(bytes(blob))[2][0]
+
+
+def test_truncated_module_is_invalid(tmp_path):
+    blob = valid_module()
+    for cut in [0, 10, 24, 100, len(blob) - 8]:
+        res = run_blob(blob[:cut], tmp_path)
+        assert res.returncode == 1
+        assert "invalid module" in res.stderr or "io error" in res.stderr
+
+
+def test_bad_section_bounds_are_invalid(tmp_path):
+    blob = valid_module()
+    struct.pack_into("<Q", blob, 24 + 8, len(blob) + 100)  # symbols offset
+    res = run_blob(blob, tmp_path)
+    assert res.returncode == 1 and "invalid module" in res.stderr
+
+
+@pytest.mark.parametrize("field,value", [
+    ("const_slot", 300), ("const_offset", 1 << 40), ("const_bytes", 1 << 40),
+    ("dispatch_index", 99), ("dispatch_argc", 9), ("dispatch_slot", 255)])
+def test_bad_operands_are_invalid(tmp_path, field, value):
+    blob = valid_module()
+    base = program_offset(blob)
+    # Program: CONST(0) CONST(1) ALLOC(2) DISPATCH(linear) ...
+    const0 = base + 8
+    alloc = base + 2 * (8 + 24)
+    dispatch = alloc + 8 + 16
+    where = {"const_slot": const0, "const_offset": const0 + 8,
+             "const_bytes": const0 + 16, "dispatch_index": dispatch + 8,
+             "dispatch_argc": dispatch + 16, "dispatch_slot": dispatch + 24}[field]
+    patch_u64(blob, where, value)
+    res = run_blob(blob, tmp_path)
+    assert res.returncode == 1
+    assert "invalid module" in res.stderr
+
+
+def test_extent_larger_than_buffers_is_invalid(tmp_path):
+    blob = valid_module()
+    off, _ = hx.read_sections(bytes(blob))[4]
+    # executable 0 is the 2x2 matmul: claim m = 1000.
+    struct.pack_into("<I", blob, off + 8 + 32 + 8, 1000)
+    res = run_blob(blob, tmp_path)
+    assert res.returncode == 1 and "invalid module" in res.stderr
+
+
+def test_random_byte_flips_never_crash(tmp_path):
+    rng = np.random.default_rng(0)
+    base = valid_module()
+    for _ in range(150):
+        blob = bytearray(base)
+        for pos in rng.integers(0, len(blob), size=3):
+            blob[pos] = int(rng.integers(0, 256))
+        res = run_blob(blob, tmp_path)
+        assert res.returncode in (0, 1), res.stderr  # never a signal
