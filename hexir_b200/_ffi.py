@@ -101,6 +101,8 @@ _SIGNATURES = [
                                      _u32, _vp]),
     ("hexir_cuda_add_f64", _int, [_int, _vp, _vp, _vp, _sz, _vp]),
     ("hexir_cuda_relu_f64", _int, [_int, _vp, _vp, _sz, _vp]),
+    ("hexir_cuda_matmul_f64_noalloc", _int, [_int, _vp, _vp, _vp, _u32, _u32,
+                                             _u32, _u32, _vp]),
     ("hexir_cuda_synchronize", _int, [_int, _vp]),
     ("hexir_cuda_matmul_plan", _int, [_int, _vp, _vp, _vp, _u32, _u32, _u32,
                                       _u32, C.POINTER(_int),

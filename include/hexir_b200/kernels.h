@@ -89,6 +89,39 @@ hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out, uint32_t blocks,
 hexir_status_t hexir_cuda_wait_probe(int ordinal, uint64_t timeout_ns,
                                      void *stream);
 
+/* Size of the fixed scratch array behind hexir_cuda_matmul_f64_noalloc. */
+#define HEXIR_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* c = a . b like hexir_cuda_matmul_f64, for callers that cannot allocate
+ * device memory.  No counterpart in the reference.
+ *
+ * Who needs it: code that runs where allocating is not allowed or not
+ * affordable -- an application whose device memory is fully owned by its own
+ * pool allocator, a latency-bound service that cannot take the device-wide
+ * synchronisation cudaFree implies, a caller that budgets all device memory
+ * at start-up.  hexir_cuda_matmul_f64 may allocate (and grow) a split-K
+ * workspace; this entry point never calls cudaMalloc, cudaFree or any other
+ * allocating routine.  Its split-K partial sums go to a fixed
+ * HEXIR_NOALLOC_SCRATCH_BYTES array of device memory that comes with the
+ * library's device code: each GPU the library's device code is loaded on
+ * holds it until the process exits.
+ *
+ * The caller still provides a, b and c.  Shapes whose partial sums do not fit
+ * the array (split * m * n * 8 bytes) are rejected with
+ * HEXIR_ERROR_INVALID_ARGUMENT and a message in hexir_cuda_last_error().
+ * The kernel is the bounds-checked DMMA GEMM (any shape and alignment), so
+ * results agree with hexir_cuda_matmul_f64 to f64 rounding, not bit for bit.
+ *
+ * The first call on a device sets that device up (looks up the array's device
+ * address with the device current); make it before any stream capture.
+ * Every call on a device shares the one array, which keeps the last call's
+ * contents; nothing in it needs to start at zero, but calls whose kernels
+ * overlap on the GPU race on it and must be serialised by the caller. */
+hexir_status_t hexir_cuda_matmul_f64_noalloc(int ordinal, const double *a,
+                                             const double *b, double *c,
+                                             uint32_t m, uint32_t n, uint32_t k,
+                                             uint32_t flags, void *stream);
+
 /* Kernel launches issued by this library since the process started. */
 uint64_t hexir_cuda_launch_count(void);
 
