@@ -60,6 +60,11 @@ def parse_args():
                    help="rows of a per GPU (default 8192)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-relu", action="store_true")
+    p.add_argument("--suite", action="store_true",
+                   help="instead of the bench line, one JSON line per "
+                        "configuration: GEMM sweep 1024-8192, relu 2^28, "
+                        "skinny linear M=1/16/128, 3-layer MLP chain")
     return p.parse_args()
 
 
@@ -399,6 +404,9 @@ def run_hexir(args):
         line["vendor"] = {"cublas_dgemm_tflops": round(
             cublas_dgemm_tflops(a, w), 3)}
 
+    if rank == 0 and not args.no_relu:
+        line["relu"] = relu_stream(ordinal)
+
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg)
 
@@ -507,10 +515,177 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg):
             "timing": "host wall clock around synchronous calls, max over ranks"}
 
 
+def timed_ms(fn, steps: int, warmup: int = 3) -> float:
+    """Average device time of fn() (launches on torch's current stream)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / steps
+
+
+MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+HBM_FALLBACK_GBS = 6650.0
+
+
+def hbm_peak_gbs():
+    """Measured copy bandwidth of this pool's B200s, else the fallback."""
+    if os.path.exists(MEASURED_PEAKS):
+        with open(MEASURED_PEAKS) as f:
+            v = json.load(f).get("hbm_gbs")
+        if v:
+            return float(v), "MEASURED_PEAKS.json hbm_gbs"
+    return HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
+
+
+def relu_stream(ordinal: int, log2n: int = 28) -> dict:
+    """hexir.relu over 2^28 f64 ~ N(0,1) (seed 4): HBM GB/s, 16 B/element."""
+    import torch
+    import hexir_b200 as hx
+    n = 1 << log2n
+    x = torch.from_numpy(hx.Rng(4).normal(n)).cuda()
+    y = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = timed_ms(lambda: hx.cuda_relu(ordinal, x.data_ptr(), y.data_ptr(), n,
+                                       stream), steps=20)
+    hx.cuda_synchronize(ordinal, stream)
+    ok = bool(torch.equal(y, torch.where(x > 0, x, torch.zeros_like(x))))
+    gbs = 16.0 * n / (ms * 1e-3) / 1e9
+    peak, src = hbm_peak_gbs()
+    return {"value": round(gbs, 1), "unit": "GB/s", "elements": n,
+            "bytes_per_launch": 16 * n, "ms_per_launch": round(ms, 4),
+            "frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_source": src,
+            "frac_of_8tbs_nominal": round(gbs / 8000.0, 4),
+            "kernel": "hexir_relu_f64", "checked": ok}
+
+
+def run_suite(args):
+    """One JSON line per configuration of the benchmark plan (1 GPU)."""
+    import numpy as np
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+    from oracle import oracle
+    ordinal = 0
+    torch.cuda.set_device(ordinal)
+    stream = torch.cuda.current_stream().cuda_stream
+    peak = dmma_peak_tflops(ordinal)
+    hbm, hbm_src = hbm_peak_gbs()
+    out = []
+
+    # GEMM sweep, square, relu fused (uniform[-1,1], seed 1, a then w).
+    for size in (1024, 2048, 4096, 8192):
+        r = hx.Rng(1)
+        a_h, w_h = r.uniform((size, size)), r.uniform((size, size))
+        a, w = torch.from_numpy(a_h).cuda(), torch.from_numpy(w_h).cuda()
+        c = torch.empty_like(a)
+        steps = max(3, int(2e12 / (2.0 * size ** 3)))
+        steps = min(steps, 200)
+        ms = timed_ms(lambda: hx.cuda_matmul(ordinal, a.data_ptr(), w.data_ptr(),
+                                             c.data_ptr(), size, size, size,
+                                             _ffi.MATMUL_RELU, stream), steps)
+        rows = np.linspace(0, size - 1, 4).astype(int)
+        err = oracle.normwise_error(c.cpu().numpy()[rows],
+                                    oracle.relu(oracle.matmul(a_h[rows], w_h)))
+        tf = 2.0 * size ** 3 / (ms * 1e-3) / 1e12
+        out.append({"suite": "gemm_sweep", "m": size, "n": size, "k": size,
+                    "ms": round(ms, 4), "tflops": round(tf, 3),
+                    "frac_dmma_peak": round(tf / peak, 4),
+                    "cublas_tflops": round(cublas_dgemm_tflops(a, w), 3),
+                    "max_normwise_err_sampled": err})
+        del a, w, c
+
+    # relu stream.
+    out.append({"suite": "relu_2^28", **relu_stream(ordinal)})
+
+    # Skinny linear: weight-read bandwidth.
+    r = hx.Rng(5)
+    w_h = None
+    for m in (1, 16, 128):
+        r = hx.Rng(5)
+        a_h = r.uniform((m, 8192))
+        w_h = r.uniform((8192, 8192))
+        a, w = torch.from_numpy(a_h).cuda(), torch.from_numpy(w_h).cuda()
+        c = torch.empty((m, 8192), dtype=torch.float64, device="cuda")
+        ms = timed_ms(lambda: hx.cuda_matmul(ordinal, a.data_ptr(), w.data_ptr(),
+                                             c.data_ptr(), m, 8192, 8192, 0,
+                                             stream), 50)
+        err = oracle.normwise_error(c.cpu().numpy()[:4],
+                                    oracle.matmul(a_h[:4], w_h))
+        variant, split = hx.matmul_plan(m, 8192, 8192)
+        wbytes = 8.0 * 8192 * 8192
+        out.append({"suite": "skinny", "m": m, "n": 8192, "k": 8192,
+                    "ms": round(ms, 4),
+                    "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                    "weight_frac_hbm": round(wbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                    "total_gbs": round(8.0 * (m * 8192 * 2 + 8192 * 8192) /
+                                       (ms * 1e-3) / 1e9, 1),
+                    "tflops": round(2.0 * m * 8192 * 8192 / (ms * 1e-3) / 1e12, 3),
+                    "plan": {"variant": variant, "split_k": split},
+                    "cublas_tflops": round(cublas_dgemm_tflops(a, w, 20), 3),
+                    "max_normwise_err": err})
+        del a, w, c
+
+    # 3-layer MLP through the VM: all-cuda and linear=cuda / relu=cpu.
+    r = hx.Rng(2)
+    x = r.normal((8192, 1024))
+    w1 = r.normal((1024, 4096), std=1 / np.sqrt(1024))
+    w2 = r.normal((4096, 4096), std=1 / np.sqrt(4096))
+    w3 = r.normal((4096, 1024), std=1 / np.sqrt(4096))
+    prog = hx.Program()
+    h = prog.relu(prog.linear(prog.constant(x), prog.constant(w1)))
+    h = prog.relu(prog.linear(h, prog.constant(w2)))
+    prog.linear(h, prog.constant(w3))
+    flops = 2.0 * 8192 * (1024 * 4096 + 4096 * 4096 + 4096 * 1024)
+    dev = hx.Device("cuda")
+    results = {}
+    for name, placement in (("all_cuda", "hexir.linear=cuda,hexir.relu=cuda"),
+                            ("mixed", "hexir.linear=cuda,hexir.relu=cpu")):
+        module = hx.Module(prog.emit(placement))
+        res = hx.execute(module, dev, out_shape=(8192, 1024))
+        kms, wall = [], []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            hx.execute(module, dev, out_shape=(8192, 1024))
+            wall.append((time.perf_counter() - t0) * 1e3)
+            kms.append(hx.last_kernel_ms())
+        results[name] = res
+        out.append({"suite": "mlp_chain", "placement": placement,
+                    "kernel_ms": round(statistics.median(kms), 3),
+                    "kernel_tflops": round(flops / (statistics.median(kms) * 1e-3)
+                                           / 1e12, 3),
+                    "e2e_ms": round(statistics.median(wall), 3),
+                    "e2e_tflops": round(flops / (statistics.median(wall) * 1e-3)
+                                        / 1e12, 3)})
+        module.close()
+    rows = np.linspace(0, 8191, 8).astype(int)
+    want = oracle.matmul(oracle.relu(oracle.matmul(
+        oracle.relu(oracle.matmul(x[rows], w1)), w2)), w3)
+    out.append({"suite": "mlp_chain_check",
+                "all_cuda_equals_mixed_bitwise": bool(np.array_equal(
+                    results["all_cuda"].view(np.uint64),
+                    results["mixed"].view(np.uint64))),
+                "max_normwise_err_sampled": oracle.normwise_error(
+                    results["all_cuda"][rows], want)})
+    for o in out:
+        o["dmma_peak_tflops"] = round(peak, 3)
+        print(json.dumps(o), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.suite:
+        return run_suite(args)
     return run_hexir(args)
 
 

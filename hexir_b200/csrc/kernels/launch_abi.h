@@ -28,6 +28,13 @@ extern "C" {
 #define HEXIR_LINEAR_SMEM_BYTES \
   (HEXIR_LINEAR_STAGES * HEXIR_LINEAR_STAGE_BYTES + 1024 + 256)
 
+/* Shared memory of the 64-row (4 stages) and 16-row (3 stages, two CTAs per
+ * SM) variants. */
+#define HEXIR_LINEAR_M64_SMEM_BYTES \
+  (4 * ((64 * 32 + 32 * 128) * 8) + 1024 + 256)
+#define HEXIR_LINEAR_M16_SMEM_BYTES \
+  (3 * ((16 * 32 + 32 * 128) * 8) + 1024 + 256)
+
 /* Tile shape of the guarded GEMM for shapes TMA cannot describe. */
 #define HEXIR_LINEAR_G_BM 64
 #define HEXIR_LINEAR_G_BN 64

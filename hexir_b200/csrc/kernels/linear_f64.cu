@@ -9,9 +9,11 @@
 // agree with the CPU to within f64 rounding, not bit for bit.
 //
 // Kernels:
-//   hexir_linear_f64_tma      TMA-fed 3-stage mbarrier ring, 8 DMMA warps
-//                             (thread 0 also issues the TMA boxes),
-//                             128x128x32 CTA tile, one CTA per SM.
+//   hexir_linear_f64_tma      TMA-fed mbarrier ring, 8 DMMA warps (thread 0
+//   hexir_linear_f64_tma_m64  also issues the TMA boxes), one CTA per SM;
+//   hexir_linear_f64_tma_m16  CTA tiles 128x128x32 (3 stages), 64x128x32 (4)
+//                             and 16x128x32 (3, two CTAs per SM) for tall,
+//                             medium and skinny row counts.
 //                             Needs k and n even and 16-byte aligned bases.
 //   hexir_linear_f64_guarded  any shape and alignment: bounds-checked loads,
 //                             64x64x16 tile, double-buffered shared memory.
@@ -35,19 +37,6 @@
 
 namespace hexir {
 
-namespace lin {
-constexpr int BM = HEXIR_LINEAR_BM;
-constexpr int BN = HEXIR_LINEAR_BN;
-constexpr int BK = HEXIR_LINEAR_BK;
-constexpr int STAGES = HEXIR_LINEAR_STAGES;
-constexpr int A_SLAB = BM * 8;   // doubles in one A slab (one TMA box)
-constexpr int B_SLAB = BK * 16;  // doubles in one B slab (one TMA box)
-constexpr int A_STAGE = BM * BK; // doubles
-constexpr int B_STAGE = BK * BN;
-constexpr uint32_t STAGE_BYTES = HEXIR_LINEAR_STAGE_BYTES;
-static_assert(STAGE_BYTES == (A_STAGE + B_STAGE) * 8, "stage size");
-static_assert((B_SLAB * 8) % 1024 == 0, "B slabs must keep 1024-B alignment");
-}  // namespace lin
 
 // Grouped raster: group_m row-tiles share each sweep over the column tiles,
 // so concurrently running CTAs reuse the same A and B panels from L2.
@@ -151,18 +140,50 @@ __device__ __forceinline__ void store_warp_tile(
 
 using namespace hexir;
 
-extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
-    hexir_linear_f64_tma(const __grid_constant__ CUtensorMap map_a,
-                         const __grid_constant__ CUtensorMap map_b,
-                         const hexir_linear_args_t args) {
-  using namespace hexir::lin;
+namespace hexir {
+
+// Tile configurations of the TMA pipeline.  All use 8 DMMA warps (256
+// threads, one CTA per SM); thread 0 also issues the TMA boxes.
+//   BM x BN x BK  CTA tile; STAGES smem ring depth
+//   WARPS_M x WARPS_N  warp grid; warp tile (BM/WARPS_M) x (BN/WARPS_N)
+template <int BM_, int BN_, int BK_, int STAGES_, int WARPS_M_>
+struct TmaTile {
+  static constexpr int BM = BM_, BN = BN_, BK = BK_, STAGES = STAGES_;
+  static constexpr int WARPS_M = WARPS_M_, WARPS_N = 8 / WARPS_M_;
+  static constexpr int WTM = BM / WARPS_M, WTN = BN / WARPS_N;  // warp tile
+  static constexpr int MI = WTM / 16, NP = WTN / 16;
+  static constexpr int A_SLAB = BM * 8, B_SLAB = BK * 16;  // doubles per box
+  static constexpr int A_STAGE = BM * BK, B_STAGE = BK * BN;
+  static constexpr uint32_t STAGE_BYTES = (A_STAGE + B_STAGE) * 8;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(MI >= 1 && NP >= 1 && WTM % 16 == 0 && WTN % 16 == 0,
+                "warp tile must be a multiple of 16 x 16");
+  static_assert((B_SLAB * 8) % 1024 == 0 && (A_STAGE * 8) % 1024 == 0,
+                "slabs must keep the 1024-B swizzle alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
+
+using Tile128 = TmaTile<HEXIR_LINEAR_BM, HEXIR_LINEAR_BN, HEXIR_LINEAR_BK,
+                        HEXIR_LINEAR_STAGES, 2>;
+using Tile64 = TmaTile<64, 128, 32, 4, 2>;
+using Tile16 = TmaTile<16, 128, 32, 3, 1>;
+static_assert(Tile128::SMEM_BYTES == HEXIR_LINEAR_SMEM_BYTES, "smem");
+static_assert(Tile64::SMEM_BYTES == HEXIR_LINEAR_M64_SMEM_BYTES, "smem");
+static_assert(Tile16::SMEM_BYTES == HEXIR_LINEAR_M16_SMEM_BYTES, "smem");
+
+template <class T>
+__device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
+                                                const CUtensorMap *map_b,
+                                                const hexir_linear_args_t &args) {
+  constexpr int BM = T::BM, BN = T::BN, BK = T::BK, STAGES = T::STAGES;
+  constexpr int MI = T::MI, NP = T::NP;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align the ring to the 1024-byte swizzle atom.
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   double *sa = reinterpret_cast<double *>(smem);
-  double *sb = sa + STAGES * A_STAGE;
-  uint64_t *full = reinterpret_cast<uint64_t *>(sb + STAGES * B_STAGE);
+  double *sb = sa + STAGES * T::A_STAGE;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sb + STAGES * T::B_STAGE);
   uint64_t *empty = full + STAGES;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -177,8 +198,8 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
   const uint32_t m0 = tm * BM, n0 = tn * BN;
 
   if (issuer) {
-    prefetch_tensormap(&map_a);
-    prefetch_tensormap(&map_b);
+    prefetch_tensormap(map_a);
+    prefetch_tensormap(map_b);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], HEXIR_LINEAR_CONSUMER_WARPS);
@@ -191,16 +212,16 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
   // of [BM][8] and BN/16 B boxes of [BK][16] (128-byte swizzled).
   auto issue = [&](int32_t i) {
     const int s = i % STAGES;
-    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+    mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
     const int32_t k0 = (int32_t)((kt_begin + i) * BK);
-    double *as = sa + s * A_STAGE;
-    double *bs = sb + s * B_STAGE;
+    double *as = sa + s * T::A_STAGE;
+    double *bs = sb + s * T::B_STAGE;
 #pragma unroll
     for (int j = 0; j < BK / 8; ++j)
-      tma_load_2d(as + j * A_SLAB, &map_a, k0 + j * 8, (int32_t)m0, &full[s]);
+      tma_load_2d(as + j * T::A_SLAB, map_a, k0 + j * 8, (int32_t)m0, &full[s]);
 #pragma unroll
     for (int j = 0; j < BN / 16; ++j)
-      tma_load_2d(bs + j * B_SLAB, &map_b, (int32_t)(n0 + j * 16), k0,
+      tma_load_2d(bs + j * T::B_SLAB, map_b, (int32_t)(n0 + j * 16), k0,
                   &full[s]);
   };
   int32_t issued = 0;
@@ -209,14 +230,13 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
       issue(issued);
   }
 
-  // 8 DMMA warps as 2 (rows) x 4 (columns), warp tile 64 x 32.
   const uint32_t g = lane >> 2, t = lane & 3;
-  const uint32_t wm = warp >> 2, wn = warp & 3;
-  double acc[4][4][4];
+  const uint32_t wm = warp / T::WARPS_N, wn = warp % T::WARPS_N;
+  double acc[MI][2 * NP][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < MI; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2 * NP; ++j)
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         acc[i][j][q] = 0.0;
@@ -230,12 +250,13 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
       ok = false;
       break;
     }
-    const uint32_t a_stage = sa_addr + s * A_STAGE * 8;
-    const uint32_t b_stage = sb_addr + s * B_STAGE * 8 + (wn * 2) * B_SLAB * 8;
+    const uint32_t a_stage = sa_addr + s * T::A_STAGE * 8;
+    const uint32_t b_stage =
+        sb_addr + s * T::B_STAGE * 8 + (wn * NP) * T::B_SLAB * 8;
 #pragma unroll
     for (int kk = 0; kk < BK / 8; ++kk)
-      dmma_k8_step<4, 2>(acc, a_stage + kk * A_SLAB * 8, wm * 64, b_stage,
-                         B_SLAB * 8, kk * 8, g, t);
+      dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
+                           b_stage, T::B_SLAB * 8, kk * 8, g, t);
     __syncwarp();
     if (lane == 0)
       mbar_arrive(&empty[s]);
@@ -271,8 +292,37 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
     dst += (size_t)split * args.m * args.n;
     relu = false;
   }
-  store_warp_tile<4, 2, true>(acc, dst, args.m, args.n, m0 + wm * 64,
-                              n0 + wn * 32, relu, g, t);
+  store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
+                                n0 + wn * T::WTN, relu, g, t);
+}
+
+}  // namespace hexir
+
+// 128 x 128 x 32 CTA tile: square and tall shapes (warp tile 64 x 32).
+extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
+    hexir_linear_f64_tma(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b,
+                         const hexir_linear_args_t args) {
+  linear_tma_body<Tile128>(&map_a, &map_b, args);
+}
+
+// 64 x 128 x 32, 4 stages: 17..64 rows (warp tile 32 x 32).
+extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
+    hexir_linear_f64_tma_m64(const __grid_constant__ CUtensorMap map_a,
+                             const __grid_constant__ CUtensorMap map_b,
+                             const hexir_linear_args_t args) {
+  linear_tma_body<Tile64>(&map_a, &map_b, args);
+}
+
+// 16 x 128 x 32, 3 stages, two CTAs per SM: up to 16 rows, where the weight
+// stream is the whole cost (warp tile 16 x 16, one m16 DMMA row block).  Two
+// resident CTAs hide each other's pipeline fill; measured 6.4 TB/s on the
+// weight read at m = 1, against 4.4-4.8 TB/s for one 6-stage CTA per SM.
+extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 2)
+    hexir_linear_f64_tma_m16(const __grid_constant__ CUtensorMap map_a,
+                             const __grid_constant__ CUtensorMap map_b,
+                             const hexir_linear_args_t args) {
+  linear_tma_body<Tile16>(&map_a, &map_b, args);
 }
 
 // Guarded variant: every global load is bounds checked, so any m, n, k and

@@ -1,6 +1,7 @@
 // comm.cc -- row-shard planning and the multi-process sharded linear
 // (include/hexir_b200/comm.h).
 
+#include <algorithm>
 #include <cstring>
 #include <new>
 #include <string>
@@ -13,11 +14,21 @@
 
 using namespace hexir;
 
+namespace {
+// Output rows leave for the root in this many pieces, so that all but the
+// last piece's transfer hides behind the GEMM of the next.
+constexpr uint32_t kGatherChunks = 4;
+constexpr uint64_t kMinChunkRows = 256;
+}  // namespace
+
 struct hexir_comm_t {
   ncclComm_t comm = nullptr;
   int nranks = 0;
   int rank = 0;
   int ordinal = 0;
+  CUstream gather_stream = nullptr;  // row sends / receives
+  CUevent chunk_done[kGatherChunks] = {};
+  CUevent gather_done = nullptr;
 };
 
 extern "C" {
@@ -82,6 +93,17 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   comm->nranks = nranks;
   comm->rank = rank;
   comm->ordinal = ordinal;
+  const Driver &d = driver();
+  CUresult cr = d.StreamCreate(&comm->gather_stream, CU_STREAM_NON_BLOCKING);
+  for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kGatherChunks; ++i)
+    cr = d.EventCreate(&comm->chunk_done[i], CU_EVENT_DISABLE_TIMING);
+  if (cr == CUDA_SUCCESS)
+    cr = d.EventCreate(&comm->gather_done, CU_EVENT_DISABLE_TIMING);
+  if (cr != CUDA_SUCCESS) {
+    set_last_error(cuda_message("gather stream set-up", cr));
+    hexir_comm_release(comm);
+    return HEXIR_ERROR_DEVICE;
+  }
   *out = comm;
   return HEXIR_OK;
 }
@@ -89,6 +111,21 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
 void hexir_comm_release(hexir_comm_t *comm) {
   if (!comm)
     return;
+  std::string error;
+  DeviceState *dev = device_state(comm->ordinal, &error);
+  if (dev) {
+    ContextGuard guard(dev->context);
+    const Driver &d = driver();
+    if (comm->gather_stream) {
+      d.StreamSynchronize(comm->gather_stream);
+      d.StreamDestroy(comm->gather_stream);
+    }
+    for (CUevent ev : comm->chunk_done)
+      if (ev)
+        d.EventDestroy(ev);
+    if (comm->gather_done)
+      d.EventDestroy(comm->gather_done);
+  }
   if (comm->comm && nccl().ok)
     nccl().CommDestroy(comm->comm);
   delete comm;
@@ -130,36 +167,72 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
     set_last_error(nccl_message("ncclBroadcast", r));
     return HEXIR_ERROR_DEVICE;
   }
-  // 2. This rank's rows; the root writes straight into its part of c.
-  if (rows) {
-    hexir_status_t st = launch_matmul(dev, lib, a_rows, w, c,
-                                      static_cast<uint32_t>(rows), n, k,
-                                      flags & HEXIR_MATMUL_RELU, s, &error);
-    if (st != HEXIR_OK) {
-      set_last_error(error);
-      return st;
-    }
+  // 2. This rank's rows in up to kGatherChunks pieces; the root writes
+  //    straight into its part of c.  3. Each finished piece goes to the root
+  //    on the gather stream while the next piece computes.  Every rank splits
+  //    its rows by the same rule, so the root knows each peer's pieces.
+  const Driver &d = driver();
+  auto chunks_of = [](uint64_t r) -> uint32_t {
+    const uint64_t by_size = r / kMinChunkRows;
+    return static_cast<uint32_t>(
+        std::max<uint64_t>(1, std::min<uint64_t>(kGatherChunks, by_size)));
+  };
+  const uint32_t my_chunks = chunks_of(rows);
+  uint32_t max_chunks = 0;
+  for (uint32_t peer = 0; peer < ranks; ++peer) {
+    uint64_t pb = 0, pr = 0;
+    hexir_shard_rows(m, ranks, peer, &pb, &pr);
+    max_chunks = std::max(max_chunks, chunks_of(pr));
   }
-  // 3. Rows back to the root.
-  if (ranks > 1) {
+  cudaStream_t gs = reinterpret_cast<cudaStream_t>(comm->gather_stream);
+  for (uint32_t i = 0; i < max_chunks; ++i) {
+    if (i < my_chunks && rows) {
+      uint64_t cb = 0, cr = 0;
+      hexir_shard_rows(rows, my_chunks, i, &cb, &cr);
+      if (cr) {
+        hexir_status_t st = launch_matmul(
+            dev, lib, a_rows + cb * k, w, c + cb * n, static_cast<uint32_t>(cr),
+            n, k, flags & HEXIR_MATMUL_RELU, s, &error);
+        if (st != HEXIR_OK) {
+          set_last_error(error);
+          return st;
+        }
+      }
+    }
+    if (ranks == 1)
+      continue;
+    d.EventRecord(comm->chunk_done[i], s);
+    d.StreamWaitEvent(comm->gather_stream, comm->chunk_done[i], 0);
     nc.GroupStart();
     if (comm->rank == 0) {
       for (uint32_t peer = 1; peer < ranks; ++peer) {
         uint64_t pb = 0, pr = 0;
         hexir_shard_rows(m, ranks, peer, &pb, &pr);
-        if (pr)
-          nc.Recv(c + pb * n, pr * n, ncclDouble, static_cast<int>(peer),
-                  comm->comm, reinterpret_cast<cudaStream_t>(s));
+        const uint32_t pc = chunks_of(pr);
+        if (i >= pc || !pr)
+          continue;
+        uint64_t cb = 0, cr = 0;
+        hexir_shard_rows(pr, pc, i, &cb, &cr);
+        if (cr)
+          nc.Recv(c + (pb + cb) * n, cr * n, ncclDouble, static_cast<int>(peer),
+                  comm->comm, gs);
       }
-    } else if (rows) {
-      nc.Send(c, rows * n, ncclDouble, 0, comm->comm,
-              reinterpret_cast<cudaStream_t>(s));
+    } else if (i < my_chunks && rows) {
+      uint64_t cb = 0, cr = 0;
+      hexir_shard_rows(rows, my_chunks, i, &cb, &cr);
+      if (cr)
+        nc.Send(c + cb * n, cr * n, ncclDouble, 0, comm->comm, gs);
     }
     r = nc.GroupEnd();
     if (r != ncclSuccess) {
       set_last_error(nccl_message("ncclGroupEnd (row gather)", r));
       return HEXIR_ERROR_DEVICE;
     }
+  }
+  if (ranks > 1) {
+    // The caller's stream completes only after the gather.
+    d.EventRecord(comm->gather_done, comm->gather_stream);
+    d.StreamWaitEvent(s, comm->gather_done, 0);
   }
   return HEXIR_OK;
 }

@@ -61,6 +61,8 @@ void load() {
             bind(lib, d.MemFree, "cuMemFree_v2", e) &&
             bind(lib, d.MemAllocHost, "cuMemAllocHost_v2", e) &&
             bind(lib, d.MemFreeHost, "cuMemFreeHost", e) &&
+            bind(lib, d.MemHostRegister, "cuMemHostRegister_v2", e) &&
+            bind(lib, d.MemHostUnregister, "cuMemHostUnregister", e) &&
             bind(lib, d.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2", e) &&
             bind(lib, d.MemcpyDtoHAsync, "cuMemcpyDtoHAsync_v2", e) &&
             bind(lib, d.MemcpyDtoDAsync, "cuMemcpyDtoDAsync_v2", e) &&

@@ -39,6 +39,8 @@ struct Driver {
   CUresult (*MemFree)(CUdeviceptr) = nullptr;
   CUresult (*MemAllocHost)(void **, size_t) = nullptr;
   CUresult (*MemFreeHost)(void *) = nullptr;
+  CUresult (*MemHostRegister)(void *, size_t, unsigned int) = nullptr;
+  CUresult (*MemHostUnregister)(void *) = nullptr;
   CUresult (*MemcpyHtoDAsync)(CUdeviceptr, const void *, size_t, CUstream) =
       nullptr;
   CUresult (*MemcpyDtoHAsync)(void *, CUdeviceptr, size_t, CUstream) = nullptr;

@@ -90,8 +90,43 @@ CudaDevice::~CudaDevice() {
   if (stream) {
     ContextGuard guard(state->context);
     driver().StreamSynchronize(stream);
+    for (auto &kv : pool)
+      driver().MemFree(kv.second);
+    pool.clear();
     driver().StreamDestroy(stream);
   }
+}
+
+hexir_status_t CudaDevice::allocate_pooled(size_t size, hexir_buffer_t **out) {
+  auto it = pool.find(size);
+  if (it == pool.end()) {
+    hexir_status_t st = allocate_raw(size, out);
+    if (st == HEXIR_ERROR_OUT_OF_MEMORY && !pool.empty()) {
+      // Give the pool back and try once more.
+      ContextGuard guard(state->context);
+      driver().StreamSynchronize(stream);
+      for (auto &kv : pool)
+        driver().MemFree(kv.second);
+      pool.clear();
+      pool_bytes = 0;
+      st = allocate_raw(size, out);
+    }
+    if (st == HEXIR_OK)
+      (*out)->pooled = true;
+    return st;
+  }
+  auto *buffer = new (std::nothrow) hexir_buffer_t;
+  if (!buffer)
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  buffer->device = this;
+  buffer->size = size;
+  buffer->memory = HEXIR_MEMORY_DEVICE_LOCAL;
+  buffer->impl = reinterpret_cast<void *>(static_cast<uintptr_t>(it->second));
+  buffer->pooled = true;
+  pool_bytes -= size;
+  pool.erase(it);
+  *out = buffer;
+  return HEXIR_OK;
 }
 
 hexir_status_t CudaDevice::allocate_raw(size_t size, hexir_buffer_t **out) {
@@ -137,6 +172,12 @@ hexir_status_t CudaDevice::buffer_allocate(size_t size, hexir_memory_kind_t,
 }
 
 void CudaDevice::buffer_release(hexir_buffer_t *buffer) {
+  if (buffer->pooled && buffer->impl) {
+    pool.emplace(buffer->size, reinterpret_cast<CUdeviceptr>(buffer->impl));
+    pool_bytes += buffer->size;
+    delete buffer;
+    return;
+  }
   if (buffer->impl) {
     ContextGuard guard(state->context);
     // Work queued on this stream may still use the buffer.

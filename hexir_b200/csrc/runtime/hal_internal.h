@@ -8,6 +8,7 @@
 #include <cuda.h>
 
 #include <cstddef>
+#include <map>
 #include <string>
 
 #include "hexir_runtime/hal.h"
@@ -47,6 +48,7 @@ struct hexir_buffer_t {
   size_t size = 0;
   hexir_memory_kind_t memory = HEXIR_MEMORY_HOST_LOCAL;
   void *impl = nullptr;  // host pointer (CPU) or CUdeviceptr (CUDA)
+  bool pooled = false;   // VM buffer: returns to the device's pool on release
 };
 
 namespace hexir {
@@ -76,6 +78,13 @@ struct CudaDevice : hexir_device_t {
   hexir_status_t write_async(CUdeviceptr dst, const void *src, size_t size);
   // Allocate without zeroing (the VM zeroes lazily where it must).
   hexir_status_t allocate_raw(size_t size, hexir_buffer_t **out);
+  // Same, from the device's pool of released VM buffers when one of exactly
+  // this size is free.  Pooled blocks are reused in stream order (every VM
+  // use is on this device's stream) and freed with the device.
+  hexir_status_t allocate_pooled(size_t size, hexir_buffer_t **out);
+
+  std::multimap<size_t, CUdeviceptr> pool;
+  size_t pool_bytes = 0;
 };
 
 CudaDevice *as_cuda(hexir_device_t *device);

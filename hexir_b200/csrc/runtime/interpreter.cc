@@ -40,6 +40,7 @@
 #include "hexir_runtime/program.h"
 #include "hexir_runtime/vm.h"
 #include "kernel_lib.h"
+#include "module_internal.h"
 #include "nccl_shim.h"
 
 namespace hexir {
@@ -81,6 +82,58 @@ hexir_status_t comms_for(const std::vector<int> &ordinals,
   return HEXIR_OK;
 }
 
+// Page-locked RODATA, set up the first time a program copies a large
+// constant to a GPU and kept until the module is released, so every upload
+// runs at pinned-memory speed.  The module's bytes are registered in place
+// when the driver accepts that (heap copies); a file mapping it refuses is
+// copied once into pinned host memory.  Without either, uploads stay on the
+// driver's pageable path.
+struct PinnedRodata {
+  const uint8_t *src = nullptr;  // RODATA in the module
+  uint64_t size = 0;
+  void *registered = nullptr;    // page-aligned base registered in place
+  uint8_t *copy = nullptr;       // pinned copy of RODATA
+};
+
+void *pin_rodata(const hexir_module_t *module) {
+  auto *pin = new (std::nothrow) PinnedRodata;
+  if (!pin)
+    return nullptr;
+  const void *data = nullptr;
+  uint64_t size = 0;
+  const Driver &d = driver();
+  if (!d.ok ||
+      hexir_module_section(module, HEXIR_SECTION_RODATA, &data, &size) != HEXIR_OK)
+    return pin;
+  pin->src = static_cast<const uint8_t *>(data);
+  pin->size = size;
+  const uintptr_t page = 4096;
+  const uintptr_t begin = reinterpret_cast<uintptr_t>(data) & ~(page - 1);
+  const uintptr_t end =
+      (reinterpret_cast<uintptr_t>(data) + size + page - 1) & ~(page - 1);
+  if (d.MemHostRegister(reinterpret_cast<void *>(begin), end - begin,
+                        CU_MEMHOSTREGISTER_PORTABLE |
+                            CU_MEMHOSTREGISTER_READ_ONLY) == CUDA_SUCCESS) {
+    pin->registered = reinterpret_cast<void *>(begin);
+    return pin;
+  }
+  void *host = nullptr;
+  if (d.MemAllocHost(&host, size) == CUDA_SUCCESS) {
+    std::memcpy(host, data, size);
+    pin->copy = static_cast<uint8_t *>(host);
+  }
+  return pin;
+}
+
+void unpin_rodata(void *p) {
+  auto *pin = static_cast<PinnedRodata *>(p);
+  if (pin->registered)
+    driver().MemHostUnregister(pin->registered);
+  if (pin->copy)
+    driver().MemFreeHost(pin->copy);
+  delete pin;
+}
+
 struct Slot {
   bool defined = false;
   uint64_t bytes = 0;
@@ -98,6 +151,7 @@ struct Span {
 };
 
 struct Vm {
+  const hexir_module_t *module = nullptr;
   const uint8_t *rodata = nullptr;
   uint64_t rodata_size = 0;
   const hexir_executable_entry_t *exes = nullptr;
@@ -181,7 +235,7 @@ struct Vm {
     auto it = s.dev.find(o);
     if (it == s.dev.end()) {
       hexir_buffer_t *b = nullptr;
-      hexir_status_t st = cuda[o]->allocate_raw(bytes, &b);
+      hexir_status_t st = cuda[o]->allocate_pooled(bytes, &b);
       if (st != HEXIR_OK)
         return st;
       it = s.dev.emplace(o, b).first;
@@ -192,7 +246,7 @@ struct Vm {
 
   hexir_status_t temp_on(int o, uint64_t bytes, CUdeviceptr *out) {
     hexir_buffer_t *b = nullptr;
-    hexir_status_t st = cuda[o]->allocate_raw(bytes, &b);
+    hexir_status_t st = cuda[o]->allocate_pooled(bytes, &b);
     if (st != HEXIR_OK)
       return st;
     temps.emplace_back(cuda[o], b);
@@ -213,7 +267,14 @@ struct Vm {
     if (s.zero) {
       r = d.MemsetD8Async(dst, 0, bytes, to->stream);
     } else if (s.rodata) {
-      return to->write_async(dst, s.rodata + offset, bytes);
+      const uint8_t *src = s.rodata + offset;
+      if (module && bytes >= (1u << 20)) {
+        auto *pin = static_cast<PinnedRodata *>(
+            module_attached(module, pin_rodata, unpin_rodata));
+        if (pin && pin->copy && src >= pin->src && src + bytes <= pin->src + pin->size)
+          src = pin->copy + (src - pin->src);
+      }
+      return to->write_async(dst, src, bytes);
     } else if (s.host_valid) {
       return to->write_async(
           dst, reinterpret_cast<const uint8_t *>(s.host.data()) + offset, bytes);
@@ -824,6 +885,7 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
     return HEXIR_ERROR_INVALID_MODULE;
 
   auto vm = std::make_unique<Vm>();
+  vm->module = module;
   vm->primary = primary;
   vm->cuda = std::move(cuda);
   const char *trace = std::getenv("HEXIR_TRACE");

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstring>
 
 #include "../kernels/launch_abi.h"
@@ -180,6 +181,8 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
     const char *name;
   } needs[] = {
       {&lib->linear_tma, "hexir_linear_f64_tma"},
+      {&lib->linear_tma_m64, "hexir_linear_f64_tma_m64"},
+      {&lib->linear_tma_m16, "hexir_linear_f64_tma_m16"},
       {&lib->linear_guarded, "hexir_linear_f64_guarded"},
       {&lib->splitk_reduce, "hexir_linear_f64_splitk_reduce"},
       {&lib->relu, "hexir_relu_f64"},
@@ -210,6 +213,14 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
     r = d.FuncSetAttribute(lib->linear_tma,
                            CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
                            HEXIR_LINEAR_SMEM_BYTES);
+  if (r == CUDA_SUCCESS)
+    r = d.FuncSetAttribute(lib->linear_tma_m64,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_LINEAR_M64_SMEM_BYTES);
+  if (r == CUDA_SUCCESS)
+    r = d.FuncSetAttribute(lib->linear_tma_m16,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_LINEAR_M16_SMEM_BYTES);
   if (r == CUDA_SUCCESS)
     r = d.FuncSetAttribute(lib->linear_guarded,
                            CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
@@ -243,33 +254,65 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   // TMA needs 16-byte aligned bases and row strides (k, n even).
   const bool tma_ok = (k % 2 == 0) && (n % 2 == 0) && aligned16(a) &&
                       aligned16(b) && aligned16(c);
-  p.variant = tma_ok ? 1 : 2;
-  if ((flags & HEXIR_MATMUL_FORCE_GUARDED) || !tma_ok)
-    p.variant = 2;
-  if (p.variant == 1) {
-    p.bm = HEXIR_LINEAR_BM;
-    p.bn = HEXIR_LINEAR_BN;
-    p.bk = HEXIR_LINEAR_BK;
-  } else {
+  if ((flags & HEXIR_MATMUL_FORCE_GUARDED) || !tma_ok) {
+    p.variant = kGuarded;
     p.bm = HEXIR_LINEAR_G_BM;
     p.bn = HEXIR_LINEAR_G_BN;
     p.bk = HEXIR_LINEAR_G_BK;
+  } else {
+    // Row tile to the row count: a skinny a streams the weight once through
+    // 16-row tiles instead of multiplying 112 rows of zero fill.
+    p.variant = m <= 16 ? kTma16 : (m <= 64 ? kTma64 : kTma128);
+    p.bm = p.variant == kTma16 ? 16u : (p.variant == kTma64 ? 64u : 128u);
+    p.bn = HEXIR_LINEAR_BN;
+    p.bk = HEXIR_LINEAR_BK;
   }
   p.tiles_m = ceil_div(m, p.bm);
   p.tiles_n = ceil_div(n, p.bn);
   p.k_tiles = ceil_div(k, p.bk);
   const uint64_t tiles = static_cast<uint64_t>(p.tiles_m) * p.tiles_n;
   uint32_t split = (flags >> 16) & 0xFFu;
-  const int sms = dev ? std::max(dev->sm_count, 1) : 148;
+  const uint64_t sms = dev ? static_cast<uint64_t>(std::max(dev->sm_count, 1)) : 148;
+  // CTAs resident per SM: one for the 128- and 64-row TMA tiles (192 KiB of
+  // shared memory), two for the 16-row tile (109 KiB), three for the guarded
+  // kernel (register bound).
+  const uint64_t slots =
+      sms * (p.variant == kGuarded ? 3 : (p.variant == kTma16 ? 2 : 1));
   if (split == 0) {
+    // Pick the k split that minimises the modelled time, in units of one
+    // CTA's k-tile: waves of CTAs, each running its share of k-tiles plus a
+    // pipeline fill of 0.6 k-tile, plus the split-K reduction's HBM traffic
+    // ((split + 1) * m * n * 8 bytes at ~6.4 TB/s).  Pieces keep >= 4
+    // k-tiles so the pipeline still streams.  The constants were fitted to
+    // B200 measurements of 1024^3, 2048^3, 8192x1024x4096 and m = 1..128
+    // rows against 8192^2 (within ~5 %).
+    // Seconds per k-tile per CTA: DMMA time of the tile at 64 FMA/clk and
+    // ~1.9 GHz (the 16-row tile is bound instead by its 36 KiB weight stream,
+    // two CTAs sharing an SM's ~43 GB/s share of HBM).
+    double t_ktile = 4.3e-6;
+    if (p.variant == kTma64)
+      t_ktile = 2.15e-6;
+    else if (p.variant == kTma16)
+      t_ktile = 1.7e-6;
+    else if (p.variant == kGuarded)
+      t_ktile = 1.6e-6;
     split = 1;
-    // Too few output tiles to fill the GPU: split k, keeping >= 4 k-tiles
-    // per piece so the pipeline still streams.
-    if (tiles < static_cast<uint64_t>(sms) && p.k_tiles >= 8) {
-      split = static_cast<uint32_t>(sms / tiles);
-      split = std::min<uint32_t>(split, p.k_tiles / 4);
-      split = std::min<uint32_t>(split, 32);
-      split = std::max<uint32_t>(split, 1);
+    if (tiles < 4 * slots) {
+      const uint32_t max_split =
+          std::min<uint32_t>(64, std::max<uint32_t>(1, p.k_tiles / 4));
+      double best = 0.0;
+      for (uint32_t s = 1; s <= max_split; ++s) {
+        const uint64_t ctas = tiles * s;
+        const uint64_t waves = (ctas + slots - 1) / slots;
+        const double per_cta = std::ceil(static_cast<double>(p.k_tiles) / s) + 0.6;
+        double t = static_cast<double>(waves) * per_cta;
+        if (s > 1)
+          t += (s + 1.0) * m * n * 8.0 / 6.4e12 / t_ktile;
+        if (s == 1 || t < best * 0.99) {  // a larger split must win by 1 %
+          best = t;
+          split = s;
+        }
+      }
     }
   }
   split = std::max<uint32_t>(1, std::min(split, std::max<uint32_t>(p.k_tiles, 1)));
@@ -291,7 +334,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     return fail(error, "matmul: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
   if ((flags & HEXIR_MATMUL_FORCE_TMA) &&
       plan_matmul(dev, a, b, c, m, n, k, flags & ~HEXIR_MATMUL_FORCE_TMA)
-              .variant != 1)
+              .variant == kGuarded)
     return fail(error,
                 "matmul: the TMA kernel needs even k and n and 16-byte aligned "
                 "pointers",
@@ -338,11 +381,11 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
 
   const unsigned grid_x = p.tiles_m * p.tiles_n;
   hexir_status_t status;
-  if (p.variant == 1) {
+  if (p.variant != kGuarded) {
     CUtensorMap map_a, map_b;
     const cuuint64_t a_dims[2] = {k, m};
     const cuuint64_t a_strides[1] = {static_cast<cuuint64_t>(k) * 8};
-    const cuuint32_t a_box[2] = {8, HEXIR_LINEAR_BM};
+    const cuuint32_t a_box[2] = {8, p.bm};
     const cuuint64_t b_dims[2] = {n, k};
     const cuuint64_t b_strides[1] = {static_cast<cuuint64_t>(n) * 8};
     const cuuint32_t b_box[2] = {16, HEXIR_LINEAR_BK};
@@ -361,9 +404,20 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     if (r != CUDA_SUCCESS)
       return fail(error, cuda_message("cuTensorMapEncodeTiled", r));
     void *params[] = {&map_a, &map_b, &args};
-    status = launch(lib->linear_tma, grid_x, p.split_k, HEXIR_LINEAR_THREADS,
-                    HEXIR_LINEAR_SMEM_BYTES, stream, params,
-                    "launch hexir_linear_f64_tma", error);
+    CUfunction fn = lib->linear_tma;
+    unsigned smem = HEXIR_LINEAR_SMEM_BYTES;
+    const char *what = "launch hexir_linear_f64_tma";
+    if (p.variant == kTma16) {
+      fn = lib->linear_tma_m16;
+      smem = HEXIR_LINEAR_M16_SMEM_BYTES;
+      what = "launch hexir_linear_f64_tma_m16";
+    } else if (p.variant == kTma64) {
+      fn = lib->linear_tma_m64;
+      smem = HEXIR_LINEAR_M64_SMEM_BYTES;
+      what = "launch hexir_linear_f64_tma_m64";
+    }
+    status = launch(fn, grid_x, p.split_k, HEXIR_LINEAR_THREADS, smem, stream,
+                    params, what, error);
   } else {
     void *params[] = {&args};
     status = launch(lib->linear_guarded, grid_x, p.split_k,

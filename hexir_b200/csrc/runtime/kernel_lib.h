@@ -21,7 +21,9 @@ namespace hexir {
 
 struct KernelLib {
   CUmodule module = nullptr;
-  CUfunction linear_tma = nullptr;
+  CUfunction linear_tma = nullptr;      // 128-row tiles
+  CUfunction linear_tma_m64 = nullptr;  // 64-row tiles
+  CUfunction linear_tma_m16 = nullptr;  // 16-row tiles
   CUfunction linear_guarded = nullptr;
   CUfunction splitk_reduce = nullptr;
   CUfunction relu = nullptr;
@@ -60,8 +62,16 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
 // The library's own embedded image on this device.
 KernelLib *embedded_library(DeviceState *dev, std::string *error);
 
+// Matmul kernel variants (hexir_cuda_matmul_plan reports these numbers).
+enum MatmulVariant {
+  kTma128 = 1,   // hexir_linear_f64_tma, 128 x 128 x 32
+  kGuarded = 2,  // hexir_linear_f64_guarded, 64 x 64 x 16, any shape
+  kTma16 = 3,    // hexir_linear_f64_tma_m16, 16 x 128 x 32
+  kTma64 = 4,    // hexir_linear_f64_tma_m64, 64 x 128 x 32
+};
+
 struct MatmulPlan {
-  int variant = 0;  // 1 TMA, 2 guarded
+  int variant = 0;  // MatmulVariant
   uint32_t split_k = 1;
   uint32_t tiles_m = 0, tiles_n = 0, k_tiles = 0, k_tiles_per_split = 0;
   uint32_t bm = 0, bn = 0, bk = 0;

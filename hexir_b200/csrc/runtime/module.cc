@@ -13,9 +13,12 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "hexir_runtime/module.h"
+
+#include "module_internal.h"
 
 struct hexir_module_t {
   void *mapping = nullptr;  // mmap'd file, or nullptr for a memory copy
@@ -24,7 +27,28 @@ struct hexir_module_t {
   size_t size = 0;
   hexir_module_header_t header;  // copied: the mapping may be unaligned-safe
   const hexir_section_entry_t *sections = nullptr;
+  // Runtime state tied to the module's lifetime (pinned RODATA); released
+  // before the bytes are unmapped.
+  std::mutex attach_mu;
+  void *attached = nullptr;
+  void (*detach)(void *) = nullptr;
 };
+
+namespace hexir {
+
+void *module_attached(const hexir_module_t *module, void *(*make)(const hexir_module_t *),
+                      void (*detach)(void *)) {
+  auto *m = const_cast<hexir_module_t *>(module);
+  std::lock_guard<std::mutex> lock(m->attach_mu);
+  if (!m->attached) {
+    m->attached = make(module);
+    if (m->attached)
+      m->detach = detach;
+  }
+  return m->attached;
+}
+
+}  // namespace hexir
 
 namespace {
 
@@ -133,6 +157,8 @@ hexir_status_t hexir_module_load_memory(const void *data, uint64_t size,
 void hexir_module_release(hexir_module_t *module) {
   if (!module)
     return;
+  if (module->attached && module->detach)
+    module->detach(module->attached);
   if (module->mapping)
     munmap(module->mapping, module->size);
   std::free(module->copy);

@@ -67,7 +67,9 @@ hexir_status_t hexir_cuda_relu_f64(int ordinal, const double *x, double *y,
 hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream);
 
 /* Which matmul kernel a call with these arguments would launch:
- * 1 = TMA pipeline, 2 = guarded; *split_k receives the k split. */
+ * 1 = TMA pipeline with 128-row tiles, 2 = guarded (any shape/alignment),
+ * 3 = TMA with 16-row tiles (m <= 16), 4 = TMA with 64-row tiles
+ * (16 < m <= 64); *split_k receives the k split. */
 hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
                                       const double *b, double *c, uint32_t m,
                                       uint32_t n, uint32_t k, uint32_t flags,

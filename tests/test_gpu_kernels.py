@@ -51,7 +51,25 @@ SHAPES = [
     (1, 1, 1), (2, 2, 2), (3, 5, 7), (37, 53, 29), (64, 64, 64),
     (128, 128, 128), (129, 257, 67), (130, 258, 64), (256, 256, 256),
     (300, 200, 1000), (16, 2048, 2048), (1, 1024, 4096), (513, 130, 96),
+    (17, 130, 96), (40, 200, 3000), (5, 6, 8), (2, 4098, 512),
 ]
+
+
+@pytest.mark.parametrize("m", [1, 7, 16, 17, 33, 64, 65])
+@pytest.mark.parametrize("flags", [0, _ffi.MATMUL_SPLIT_K(3),
+                                   _ffi.MATMUL_RELU | _ffi.MATMUL_SPLIT_K(1)])
+def test_row_tile_variants(gpu, m, flags):
+    """16-, 64- and 128-row TMA tiles chosen by m, each against the oracle."""
+    n, k = 264, 1024
+    rng = np.random.default_rng(1000 + m)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    variant, split = hx.matmul_plan(m, n, k, flags)
+    assert variant == (3 if m <= 16 else 4 if m <= 64 else 1)
+    want = oracle.matmul(a, b)
+    if flags & _ffi.MATMUL_RELU:
+        want = oracle.relu(want)
+    assert oracle.normwise_error(run_matmul(gpu, a, b, flags), want) <= TOL
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
@@ -78,7 +96,7 @@ def test_matmul_variants_and_split(gpu, variant, split):
     assert oracle.normwise_error(got, want) <= TOL
     # The plan reports the kernel that the flags select.
     v, s = hx.matmul_plan(m, n, k, flags)
-    assert v == (1 if variant == "tma" else 2)
+    assert v == (1 if variant == "tma" else 2)  # m = 200: 128-row tiles
     if split:
         assert s == split
 
@@ -88,6 +106,8 @@ def test_plan_picks_tma_for_aligned_even_shapes(gpu):
     assert hx.matmul_plan(64, 64, 63)[0] == 2      # odd k: row stride not 16 B
     assert hx.matmul_plan(64, 63, 64)[0] == 2      # odd n
     assert hx.matmul_plan(16, 8192, 8192)[1] > 1   # too few tiles: split k
+    assert hx.matmul_plan(16, 8192, 8192)[0] == 3  # 16-row tiles
+    assert hx.matmul_plan(48, 8192, 8192)[0] == 4  # 64-row tiles
 
 
 def test_misaligned_pointers_use_guarded_kernel(gpu):
