@@ -86,7 +86,21 @@ CudaDevice *as_cuda(hexir_device_t *device) {
              : nullptr;
 }
 
+CUstream CudaDevice::copy_stream() {
+  if (!copies) {
+    ContextGuard guard(state->context);
+    if (driver().StreamCreate(&copies, CU_STREAM_NON_BLOCKING) != CUDA_SUCCESS)
+      copies = nullptr;
+  }
+  return copies;
+}
+
 CudaDevice::~CudaDevice() {
+  if (copies) {
+    ContextGuard guard(state->context);
+    driver().StreamSynchronize(copies);
+    driver().StreamDestroy(copies);
+  }
   if (stream) {
     ContextGuard guard(state->context);
     driver().StreamSynchronize(stream);

@@ -85,6 +85,11 @@ struct CudaDevice : hexir_device_t {
 
   std::multimap<size_t, CUdeviceptr> pool;
   size_t pool_bytes = 0;
+
+  // Second stream for copies that overlap the kernels on `stream` (the VM's
+  // pipelined upload / download of a large dispatch); created on first use.
+  CUstream copy_stream();
+  CUstream copies = nullptr;
 };
 
 CudaDevice *as_cuda(hexir_device_t *device);

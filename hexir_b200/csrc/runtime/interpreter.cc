@@ -21,6 +21,7 @@
 //   c rows  -> each GPU computes its rows with no collective; ncclSend/Recv
 //              gathers them into c on the first GPU
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -169,6 +170,15 @@ struct Vm {
   std::vector<Span> spans;
   bool trace = false;
 
+  // Capture target of hexir_execute_capture and the program offset of the
+  // entry's last DISPATCH, whose destination is what gets captured: a large
+  // last dispatch copies its rows out as they finish (see run_pipelined).
+  void *capture_out = nullptr;
+  size_t capture_size = 0;
+  uint64_t last_dispatch_pc = UINT64_MAX;
+  uint64_t current_pc = 0;
+  bool capture_done = false;
+
   ~Vm() { release(); }
 
   void release() {
@@ -254,6 +264,19 @@ struct Vm {
     return HEXIR_OK;
   }
 
+  // Where to upload RODATA bytes from: the pinned copy of RODATA when the
+  // module has one (large uploads set it up), else the module's own bytes.
+  const uint8_t *rodata_source(const Slot &s, uint64_t offset, uint64_t bytes) {
+    const uint8_t *src = s.rodata + offset;
+    if (module && bytes >= (1u << 20)) {
+      auto *pin = static_cast<PinnedRodata *>(
+          module_attached(module, pin_rodata, unpin_rodata));
+      if (pin && pin->copy && src >= pin->src && src + bytes <= pin->src + pin->size)
+        src = pin->copy + (src - pin->src);
+    }
+    return src;
+  }
+
   // Copy bytes [offset, offset + bytes) of slot s to `dst` on GPU o, from
   // wherever the slot is valid.  Asynchronous on o's stream.
   hexir_status_t copy_range_to(Slot &s, uint64_t offset, uint64_t bytes, int o,
@@ -267,14 +290,7 @@ struct Vm {
     if (s.zero) {
       r = d.MemsetD8Async(dst, 0, bytes, to->stream);
     } else if (s.rodata) {
-      const uint8_t *src = s.rodata + offset;
-      if (module && bytes >= (1u << 20)) {
-        auto *pin = static_cast<PinnedRodata *>(
-            module_attached(module, pin_rodata, unpin_rodata));
-        if (pin && pin->copy && src >= pin->src && src + bytes <= pin->src + pin->size)
-          src = pin->copy + (src - pin->src);
-      }
-      return to->write_async(dst, src, bytes);
+      return to->write_async(dst, rodata_source(s, offset, bytes), bytes);
     } else if (s.host_valid) {
       return to->write_async(
           dst, reinterpret_cast<const uint8_t *>(s.host.data()) + offset, bytes);
@@ -471,8 +487,149 @@ struct Vm {
     return HEXIR_OK;
   }
 
+  // A large matmul whose `a` still lives on the host, or whose result is the
+  // one being captured, runs as a pipeline of row chunks: chunk i of `a`
+  // uploads on the device's copy stream while chunk i-1 computes, and each
+  // finished chunk of the result copies out to the capture buffer on the
+  // copy stream while the next chunk computes.  Same kernels, same per-row
+  // arithmetic as the one-shot launch.
+  static constexpr uint64_t kPipelineBytes = 64ull << 20;
+  static constexpr uint32_t kPipelineChunks = 4;
+
+  bool want_pipeline(const hexir_executable_entry_t &exe, Slot *const *args,
+                     int o, bool *upload_a, bool *stream_out) {
+    if (exe.kind != HEXIR_KERNEL_MATMUL && exe.kind != HEXIR_KERNEL_MATMUL_RELU)
+      return false;
+    Slot &a = *args[0];
+    Slot &dst = *args[2];
+    if (&dst == args[0] || &dst == args[1] || exe.m < kPipelineChunks * 256)
+      return false;
+    *upload_a = !a.dev_valid.count(o) && !a.zero && (a.rodata || a.host_valid) &&
+                a.bytes >= kPipelineBytes;
+    *stream_out = capture_out && capture_size && current_pc == last_dispatch_pc &&
+                  dst.bytes >= kPipelineBytes;
+    return *upload_a || *stream_out;
+  }
+
+  hexir_status_t run_pipelined(uint32_t index, int o, Slot *const *args,
+                               bool upload_a, bool stream_out) {
+    const hexir_executable_entry_t &exe = exes[index];
+    KernelLib *lib = library(index, o);
+    if (!lib)
+      return HEXIR_ERROR_DEVICE;
+    CudaDevice *dev = cuda[o];
+    const Driver &d = driver();
+    Slot &as = *args[0];
+    Slot &dst = *args[2];
+    CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
+    hexir_status_t st = on_device(*args[1], o, &w_dev);
+    if (st == HEXIR_OK)
+      st = upload_a ? buffer_on(as, o, as.bytes, &a_dev) : on_device(as, o, &a_dev);
+    if (st == HEXIR_OK)
+      st = buffer_on(dst, o, dst.bytes, &c_dev);
+    if (st != HEXIR_OK)
+      return st;
+    CUstream cs = dev->copy_stream();
+    if (!cs)
+      return HEXIR_ERROR_DEVICE;
+    ContextGuard guard(dev->state->context);
+    std::vector<CUevent> events;
+    auto event = [&](CUstream on) -> CUevent {
+      CUevent ev = nullptr;
+      if (d.EventCreate(&ev, CU_EVENT_DISABLE_TIMING) != CUDA_SUCCESS)
+        return nullptr;
+      d.EventRecord(ev, on);
+      events.push_back(ev);
+      return ev;
+    };
+    // The copy stream starts after everything queued on the main stream
+    // (the buffers may be reused pool blocks).
+    CUevent ready = event(dev->stream);
+    if (!ready)
+      return HEXIR_ERROR_DEVICE;
+    d.StreamWaitEvent(cs, ready, 0);
+    Span *span = begin_span(dev);
+    const uint64_t row_a = static_cast<uint64_t>(exe.k) * 8;
+    const uint64_t row_c = static_cast<uint64_t>(exe.n) * 8;
+    uint64_t r0[kPipelineChunks], rows[kPipelineChunks];
+    std::vector<CUevent> a_ready(kPipelineChunks, nullptr);
+    for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+      hexir_shard_rows(exe.m, kPipelineChunks, i, &r0[i], &rows[i]);
+      if (!upload_a || !rows[i])
+        continue;
+      const uint64_t off = r0[i] * row_a, bytes = rows[i] * row_a;
+      const uint8_t *src =
+          as.rodata ? rodata_source(as, off, bytes)
+                    : reinterpret_cast<const uint8_t *>(as.host.data()) + off;
+      if (d.MemcpyHtoDAsync(a_dev + off, src, bytes, cs) != CUDA_SUCCESS)
+        return HEXIR_ERROR_DEVICE;
+      a_ready[i] = event(cs);
+    }
+    std::string error;
+    std::vector<CUevent> c_ready(kPipelineChunks, nullptr);
+    // Every chunk uses the k split the whole matmul would use, so each
+    // element is summed exactly as by the one-shot launch (chunks of >= 256
+    // rows keep the same 128-row tile kernel).
+    uint32_t flags = exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU : 0u;
+    const MatmulPlan whole = plan_matmul(
+        dev->state, reinterpret_cast<const double *>(a_dev),
+        reinterpret_cast<const double *>(w_dev),
+        reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k, flags);
+    flags |= HEXIR_MATMUL_SPLIT_K(whole.split_k);
+    for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+      if (!rows[i])
+        continue;
+      if (a_ready[i])
+        d.StreamWaitEvent(dev->stream, a_ready[i], 0);
+      st = launch_matmul(
+          dev->state, lib,
+          reinterpret_cast<const double *>(a_dev + r0[i] * row_a),
+          reinterpret_cast<const double *>(w_dev),
+          reinterpret_cast<double *>(c_dev + r0[i] * row_c),
+          static_cast<uint32_t>(rows[i]), exe.n, exe.k, flags, dev->stream,
+          &error);
+      if (st != HEXIR_OK) {
+        report(std::string("kernel '") + exe.name + "': " + error);
+        return st;
+      }
+      if (stream_out)
+        c_ready[i] = event(dev->stream);
+    }
+    end_span(span);
+    if (stream_out) {
+      // Rows out to the capture buffer as their chunk finishes.
+      for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+        if (!c_ready[i])
+          continue;
+        const uint64_t begin = r0[i] * row_c;
+        if (begin >= capture_size)
+          break;
+        const uint64_t bytes = std::min<uint64_t>(rows[i] * row_c,
+                                                  capture_size - begin);
+        d.StreamWaitEvent(cs, c_ready[i], 0);
+        if (d.MemcpyDtoHAsync(static_cast<uint8_t *>(capture_out) + begin,
+                              c_dev + begin, bytes, cs) != CUDA_SUCCESS)
+          return HEXIR_ERROR_DEVICE;
+      }
+      capture_done = true;
+    }
+    // The main stream covers the copies from here on.
+    CUevent copies_done = event(cs);
+    if (copies_done)
+      d.StreamWaitEvent(dev->stream, copies_done, 0);
+    for (CUevent ev : events)
+      d.EventDestroy(ev);  // released once complete
+    if (upload_a)
+      as.dev_valid.insert(o);
+    written_on_device(dst, o);
+    return HEXIR_OK;
+  }
+
   hexir_status_t run_device(uint32_t index, int o, Slot *const *args) {
     const hexir_executable_entry_t &exe = exes[index];
+    bool upload_a = false, stream_out = false;
+    if (want_pipeline(exe, args, o, &upload_a, &stream_out))
+      return run_pipelined(index, o, args, upload_a, stream_out);
     KernelLib *lib = library(index, o);
     if (!lib)
       return HEXIR_ERROR_DEVICE;
@@ -942,9 +1099,29 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
     return HEXIR_ERROR_NOT_FOUND;
 
   const uint8_t *program = static_cast<const uint8_t *>(program_data);
+  // Find the entry's last DISPATCH: its destination is what a capture copies
+  // out, so that dispatch may stream its result straight to out_result.
+  if (out_result && out_size) {
+    uint64_t scan = pc;
+    while (scan + sizeof(hexir_command_header_t) <= program_size) {
+      hexir_command_header_t h;
+      std::memcpy(&h, program + scan, sizeof(h));
+      const uint64_t next = scan + sizeof(h) + static_cast<uint64_t>(h.operand_count) * 8;
+      if (next > program_size)
+        break;
+      if (h.kind == HEXIR_CMD_DISPATCH)
+        vm->last_dispatch_pc = scan;
+      if (h.kind == HEXIR_CMD_END)
+        break;
+      scan = next;
+    }
+    vm->capture_out = out_result;
+    vm->capture_size = out_size;
+  }
   hexir_status_t status = HEXIR_OK;
   int64_t result_slot = -1;
   while (status == HEXIR_OK) {
+    vm->current_pc = pc;
     if (pc + sizeof(hexir_command_header_t) > program_size) {
       status = HEXIR_ERROR_INVALID_MODULE;
       break;
@@ -968,7 +1145,7 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
       hexir_status_t settled = vm->settle();
       if (settled != HEXIR_OK)
         return settled;
-      if (out_result && out_size && result_slot >= 0)
+      if (out_result && out_size && result_slot >= 0 && !vm->capture_done)
         status = vm->capture(static_cast<uint64_t>(result_slot), out_result,
                              out_size);
       return status;

@@ -136,6 +136,29 @@ def test_mlp_chain_all_cuda_and_mixed_placement():
     assert oracle.normwise_error(all_cuda[rows], want) <= TOL
 
 
+@pytest.mark.parametrize("m,n,k,capture_rows", [
+    (4096, 2048, 2048, 4096),   # 64 MiB a uploads in chunks; 64 MiB result streams out
+    (4096, 2048, 2048, 1000),   # partial capture: only the first 1000 rows
+    (2048, 1024, 4096, 2048),   # a pipelined, result too small to stream
+])
+def test_pipelined_dispatch(m, n, k, capture_rows):
+    """A large host-sourced linear runs as an upload / compute / download
+    pipeline of row chunks; the captured rows equal the oracle's."""
+    r = hx.Rng(7)
+    a = r.uniform((m, k))
+    w = r.uniform((k, n))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    dev = hx.Device("cuda")
+    module = hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    first = hx.execute(module, dev, out_shape=(capture_rows, n))
+    again = hx.execute(module, dev, out_shape=(capture_rows, n))  # pinned + pooled
+    assert np.array_equal(bits(first), bits(again))
+    rows = np.linspace(0, capture_rows - 1, 16).astype(int)
+    want = oracle.relu(oracle.matmul(a[rows], w))
+    assert oracle.normwise_error(first[rows], want) <= TOL
+
+
 def test_relu_stream_2_28_bit_exact():
     """relu on 2^28 f64 ~ N(0,1) seed 4 as tensor<16384x16384xf64>: bit-exact
     against the CPU relu (compared in place, no second big host copy)."""
