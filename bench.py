@@ -61,6 +61,11 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-relu", action="store_true")
+    p.add_argument("--profile", choices=["relu", "skinny", "linear"],
+                   help="run only one kernel a few times (the small cases the "
+                        "committed ncu summaries capture)")
+    p.add_argument("--log2n", type=int, default=26,
+                   help="--profile relu: 2^log2n elements")
     p.add_argument("--suite", action="store_true",
                    help="instead of the bench line, one JSON line per "
                         "configuration: GEMM sweep 1024-8192, relu 2^28, "
@@ -680,10 +685,41 @@ def run_suite(args):
     return 0
 
 
+def run_profile(args):
+    """One kernel, 5 launches, nothing else: the command line ncu captures."""
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream().cuda_stream
+    if args.profile == "relu":
+        n = 1 << args.log2n
+        x = torch.from_numpy(hx.Rng(4).normal(n)).cuda()
+        y = torch.empty_like(x)
+        run = lambda: hx.cuda_relu(0, x.data_ptr(), y.data_ptr(), n, stream)
+        what = f"relu 2^{args.log2n} f64"
+    else:
+        m = args.m
+        r = hx.Rng(5 if args.profile == "skinny" else 1)
+        a = torch.from_numpy(r.uniform((m, K_DIM))).cuda()
+        w = torch.from_numpy(r.uniform((K_DIM, N_DIM))).cuda()
+        c = torch.empty((m, N_DIM), dtype=torch.float64, device="cuda")
+        flags = _ffi.MATMUL_RELU if args.profile == "linear" else 0
+        run = lambda: hx.cuda_matmul(0, a.data_ptr(), w.data_ptr(), c.data_ptr(),
+                                     m, N_DIM, K_DIM, flags, stream)
+        what = f"linear {m}x{N_DIM}x{K_DIM} plan {hx.matmul_plan(m, N_DIM, K_DIM, flags)}"
+    ms = timed_ms(run, steps=3, warmup=2)
+    hx.cuda_synchronize(0, stream)
+    print(json.dumps({"profile": what, "ms": round(ms, 4)}))
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return run_profile(args)
     if args.suite:
         return run_suite(args)
     return run_hexir(args)
