@@ -239,6 +239,19 @@ def cpu_reference_rate(rows: int, steps: int = 1, warmup: int = 0):
 
 # ------------------------------------------------------------------ arms
 
+def workload_config(world: int, m_rows: int) -> dict:
+    """The `config` of both arms' JSON lines for N = world GPUs."""
+    m_total = m_rows * world
+    return {"workload": f"hexir.linear+relu f64 row-sharded "
+                        f"a[{m_total}x{K_DIM}] . w[{K_DIM}x{N_DIM}] "
+                        f"({m_rows} rows per GPU)",
+            "m": m_total, "n": N_DIM, "k": K_DIM,
+            "parallelism": f"rows x{world}" + (
+                ", w broadcast + row gather over NVLink (NCCL)"
+                if world > 1 else ""),
+            "l2": "inputs larger than L2 (a+w = 1 GiB per GPU)"}
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -254,9 +267,8 @@ def run_reference(args):
         "ms_per_step": round(statistics.median(times) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f64", "data": "synthetic uniform[-1,1]",
-        "config": {"workload": "hexir.linear f64 8192x8192x8192 (reference CPU "
-                               "kernel on a row sample)",
-                   "sample_rows": rows},
+        "config": {**workload_config(args.gpus, args.m),
+                   "reference_sample_rows_per_step": rows},
         "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s",
                          "cores": used, "kind": kind, "sample": sample},
         "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s",
@@ -367,14 +379,7 @@ def run_hexir(args):
             "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic: uniform[-1,1], SplitMix64 seed 1 (a then w)",
-            "config": {"workload": f"hexir.linear+relu f64 row-sharded "
-                                   f"a[{m_total}x{K_DIM}] . w[{K_DIM}x{N_DIM}] "
-                                   f"({m_rows} rows per GPU)",
-                       "m": m_total, "n": N_DIM, "k": K_DIM,
-                       "parallelism": f"rows x{world}" + (
-                           ", w broadcast + row gather over NVLink (NCCL)"
-                           if world > 1 else ""),
-                       "l2": "inputs larger than L2 (a+w = 1 GiB per GPU)"},
+            "config": workload_config(world, m_rows),
             "gpu_launches": launches,
             "clocks": clock_info}
 

@@ -15,10 +15,42 @@
 using namespace hexir;
 
 namespace {
-// Output rows leave for the root in this many pieces, so that all but the
-// last piece's transfer hides behind the GEMM of the next.
-constexpr uint32_t kGatherChunks = 4;
+// A rank's output rows leave for the root in up to kGatherChunks pieces of
+// geometrically shrinking size (1/2, 1/4, 1/8, 1/16, 1/16 of its rows), so
+// every transfer but the last hides behind the GEMM of the next piece and the
+// exposed last one is small.  Pieces keep >= kMinChunkRows rows.
+constexpr uint32_t kGatherChunks = 5;
 constexpr uint64_t kMinChunkRows = 256;
+
+// Piece `i` of `rows` rows: [*begin, *begin + *count).  Returns the number of
+// pieces.  Deterministic, so the root computes every peer's pieces.
+uint32_t gather_piece(uint64_t rows, uint32_t i, uint64_t *begin,
+                      uint64_t *count) {
+  uint32_t pieces = 1;
+  uint64_t bounds[kGatherChunks + 1] = {0};
+  uint64_t done = 0;
+  for (uint32_t p = 0; p < kGatherChunks; ++p) {
+    const uint64_t left = rows - done;
+    uint64_t take = p + 1 == kGatherChunks ? left : left / 2;
+    // Round to 128-row tiles; the remainder must stay a worthwhile piece.
+    take = (take / 128) * 128;
+    if (take < kMinChunkRows || left - take < kMinChunkRows)
+      take = left;
+    done += take;
+    bounds[p + 1] = done;
+    pieces = p + 1;
+    if (done == rows)
+      break;
+  }
+  if (i >= pieces) {
+    *begin = rows;
+    *count = 0;
+  } else {
+    *begin = bounds[i];
+    *count = bounds[i + 1] - bounds[i];
+  }
+  return pieces;
+}
 }  // namespace
 
 struct hexir_comm_t {
@@ -172,23 +204,20 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   //    on the gather stream while the next piece computes.  Every rank splits
   //    its rows by the same rule, so the root knows each peer's pieces.
   const Driver &d = driver();
-  auto chunks_of = [](uint64_t r) -> uint32_t {
-    const uint64_t by_size = r / kMinChunkRows;
-    return static_cast<uint32_t>(
-        std::max<uint64_t>(1, std::min<uint64_t>(kGatherChunks, by_size)));
-  };
-  const uint32_t my_chunks = chunks_of(rows);
+  uint64_t ignore_b = 0, ignore_c = 0;
+  const uint32_t my_chunks = rows ? gather_piece(rows, 0, &ignore_b, &ignore_c) : 0;
   uint32_t max_chunks = 0;
   for (uint32_t peer = 0; peer < ranks; ++peer) {
     uint64_t pb = 0, pr = 0;
     hexir_shard_rows(m, ranks, peer, &pb, &pr);
-    max_chunks = std::max(max_chunks, chunks_of(pr));
+    if (pr)
+      max_chunks = std::max(max_chunks, gather_piece(pr, 0, &ignore_b, &ignore_c));
   }
   cudaStream_t gs = reinterpret_cast<cudaStream_t>(comm->gather_stream);
   for (uint32_t i = 0; i < max_chunks; ++i) {
-    if (i < my_chunks && rows) {
+    if (i < my_chunks) {
       uint64_t cb = 0, cr = 0;
-      hexir_shard_rows(rows, my_chunks, i, &cb, &cr);
+      gather_piece(rows, i, &cb, &cr);
       if (cr) {
         hexir_status_t st = launch_matmul(
             dev, lib, a_rows + cb * k, w, c + cb * n, static_cast<uint32_t>(cr),
@@ -208,18 +237,17 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       for (uint32_t peer = 1; peer < ranks; ++peer) {
         uint64_t pb = 0, pr = 0;
         hexir_shard_rows(m, ranks, peer, &pb, &pr);
-        const uint32_t pc = chunks_of(pr);
-        if (i >= pc || !pr)
-          continue;
         uint64_t cb = 0, cr = 0;
-        hexir_shard_rows(pr, pc, i, &cb, &cr);
+        if (!pr)
+          continue;
+        gather_piece(pr, i, &cb, &cr);
         if (cr)
           nc.Recv(c + (pb + cb) * n, cr * n, ncclDouble, static_cast<int>(peer),
                   comm->comm, gs);
       }
-    } else if (i < my_chunks && rows) {
+    } else if (i < my_chunks) {
       uint64_t cb = 0, cr = 0;
-      hexir_shard_rows(rows, my_chunks, i, &cb, &cr);
+      gather_piece(rows, i, &cb, &cr);
       if (cr)
         nc.Send(c + cb * n, cr * n, ncclDouble, 0, comm->comm, gs);
     }
