@@ -178,6 +178,25 @@ def read_sections(blob: bytes) -> dict:
     return out
 
 
+@dataclass
+class LaunchEntry:
+    abi: int
+    flags: int
+    device_first: int
+    device_count: int
+
+
+def read_launch(blob: bytes) -> List[LaunchEntry]:
+    """The LAUNCH section (kind 5), one entry per executable; [] if absent."""
+    sections = read_sections(blob)
+    if 5 not in sections:
+        return []
+    off, _size = sections[5]
+    count, _ = struct.unpack_from("<II", blob, off)
+    return [LaunchEntry(*LAUNCH_ENTRY.unpack_from(blob, off + 8 + 32 * i)[:4])
+            for i in range(count)]
+
+
 def read_program(blob: bytes, entry: str = "main") -> List[tuple]:
     """Commands of an entry point as (kind, operands) tuples."""
     sections = read_sections(blob)

@@ -127,6 +127,12 @@ def test_launch_section_records_devices():
     assert count == 1
     abi, flags, first, n = struct.unpack_from("<4I", blob, off + 8)
     assert (abi, flags, first, n) == (1, 1, 2, 4)
+    assert hx.read_launch(blob)[0].device_count == 4
+    # cpu entries get an empty launch record; all-cpu modules no section.
+    mixed = p.emit("hexir.linear=cuda:1,hexir.relu=cpu", _ffi.EMIT_NO_FUSE)
+    recs = hx.read_launch(mixed)
+    assert [(r.abi, r.device_first) for r in recs] == [(1, 1), (0, 0)]
+    assert hx.read_launch(p.emit()) == []
 
 
 @pytest.mark.parametrize("bad,msg", [

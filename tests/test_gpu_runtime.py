@@ -258,3 +258,61 @@ def test_row_sharded_linear_in_process(tmp_path):
     assert oracle.normwise_error(sharded, oracle.relu(oracle.matmul(a, w))) <= TOL
     # Shards of 500 rows use the same kernel plan as the single GPU's tiles.
     assert np.array_equal(bits(sharded), bits(single))
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+@pytest.mark.parametrize("m", [1, 3, 257, 1001])
+def test_row_sharded_odd_rows_and_elementwise(m):
+    """Row splits that do not divide evenly, and add / relu placed on a GPU
+    range: each shard's rows, gathered on the first GPU, equal the oracle."""
+    r = hx.Rng(11 + m)
+    a = r.uniform((m, 96))
+    w = r.uniform((96, 130))
+    b = r.uniform((m, 130))
+    p = hx.Program()
+    lin = p.linear(p.constant(a), p.constant(w))
+    p.relu(p.add(lin, p.constant(b)))
+    devs = [hx.Device("cuda:0"), hx.Device("cuda:1")]
+    out = hx.execute(hx.Module(p.emit("hexir.linear=cuda:0-1,hexir.add=cuda:0-1,"
+                                      "hexir.relu=cuda:0-1")),
+                     devs, out_shape=(m, 130))
+    m_ref = oracle.matmul(a, w)
+    want = oracle.relu(oracle.add(m_ref, b))
+    assert oracle.normwise_error(out, want) <= TOL
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+def test_kernels_on_the_second_gpu():
+    """A linear placed on cuda:1 runs there (kernel-level C ABI and VM)."""
+    r = hx.Rng(12)
+    a, w = r.uniform((200, 64)), r.uniform((64, 72))
+    dev1 = hx.Device("cuda:1")
+    ba, bw, bc = dev1.upload(a), dev1.upload(w), dev1.buffer(200 * 72 * 8)
+    hx.cuda_matmul(1, ba.ptr, bw.ptr, bc.ptr, 200, 72, 64, 0, dev1.stream)
+    hx.cuda_synchronize(1, dev1.stream)
+    assert oracle.normwise_error(bc.read((200, 72)), oracle.matmul(a, w)) <= TOL
+    p = hx.Program()
+    p.linear(p.constant(a), p.constant(w))
+    devs = [hx.Device("cuda:0"), dev1]
+    out = hx.execute(hx.Module(p.emit("hexir.linear=cuda:1")), devs,
+                     out_shape=(200, 72))
+    assert oracle.normwise_error(out, oracle.matmul(a, w)) <= TOL
+
+
+def test_hexir_bench_tool_verifies_and_times(tmp_path):
+    """The extended reference benchmark tool on a cuda module: sampled
+    verification, end-to-end and kernel time, cuBLAS line, JSON output."""
+    r = hx.Rng(13)
+    a, w = r.uniform((512, 512)), r.uniform((512, 512))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    path = tmp_path / "m.hxb"
+    p.emit_file(str(path), "hexir.linear=cuda,hexir.relu=cuda")
+    res = subprocess.run([bin_path("hexir-bench"), str(path), "--iters=3",
+                          "--json"], capture_output=True, text=True, check=True)
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["verify_ok"] is True and line["verify_max_rel_err"] < 1e-12
+    assert line["kernel"] == "matmul_relu" and line["m"] == 512
+    assert line["e2e_ms"] > 0 and line["kernel_ms"] > 0
+    assert line["cublas_ms"] > 0
+
