@@ -80,7 +80,9 @@ struct CudaDevice : hexir_device_t {
   hexir_status_t allocate_raw(size_t size, hexir_buffer_t **out);
   // Same, from the device's pool of released VM buffers when one of exactly
   // this size is free.  Pooled blocks are reused in stream order (every VM
-  // use is on this device's stream) and freed with the device.
+  // use is on this device's stream), capped at 32 GiB per device, and freed
+  // with the device.  A device object serves one thread at a time, as in the
+  // reference runtime.
   hexir_status_t allocate_pooled(size_t size, hexir_buffer_t **out);
 
   std::multimap<size_t, CUdeviceptr> pool;

@@ -49,7 +49,6 @@ namespace hexir {
 namespace {
 
 constexpr int kMaxSlots = 256;  // as the reference (interpreter.c:20)
-constexpr int kHost = -1;
 
 thread_local double g_last_kernel_ms = 0.0;
 
