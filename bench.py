@@ -7,8 +7,10 @@ Workload (per GPU): hexir.linear a[8192 x 8192] . w[8192 x 8192] f64 with
 the relu fused in the epilogue, a and w uniform[-1, 1] from the writer's
 seeded stream (seed 1, a then w).  At N GPUs the job is the row-sharded
 linear a[8192N x 8192] . w: each GPU holds its 8192 rows of a, w is
-broadcast from GPU 0 over NVLink (NCCL) and the output rows are gathered back
-to GPU 0 every step (weak scaling; N = 4 is the 32768 x 8192 x 8192 shape).
+broadcast from GPU 0 over NVLink (NCCL) and every GPU's kernel stores its
+output tiles straight into GPU 0's output over NVLink (CUDA IPC mapping;
+`--gather nccl` sends the rows with NCCL instead) every step (weak scaling;
+N = 4 is the 32768 x 8192 x 8192 shape).
 
 One JSON line on rank 0:
   value      GFLOP/s of the whole job, inputs resident in HBM, device time
@@ -16,8 +18,8 @@ One JSON line on rank 0:
   e2e        the same through the public API with host buffers: a .hxb module
              run by hexir_execute_capture (constants copied host->device,
              result copied back) at N = 1; host->device copies of each rank's
-             rows, the sharded linear and the gather, result copied to the
-             host, at N > 1
+             rows, the sharded linear, result copied from GPU 0 to the host,
+             at N > 1
   roofline   the GEMM kernel's FLOP rate against the FP64 tensor-core (DMMA)
              peak measured on this GPU by a register-only DMMA probe
   cpu_baseline  the reference's own CPU kernel (hexir_ref_matmul_f64, built
@@ -58,6 +60,9 @@ def parse_args():
     p.add_argument("--impl", choices=["hexir", "reference"], default="hexir")
     p.add_argument("--m", type=int, default=M_PER_GPU,
                    help="rows of a per GPU (default 8192)")
+    p.add_argument("--gather", choices=["auto", "nccl"], default="auto",
+                   help="N > 1: how output rows reach GPU 0 (auto: kernel "
+                        "stores through a CUDA IPC mapping where possible)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-relu", action="store_true")
@@ -145,8 +150,20 @@ class ClockSampler:
 def make_w(world: int, m_rows: int):
     import hexir_b200 as hx
     rng = hx.Rng(SEED)
-    rng.uniform((world * m_rows, K_DIM))
+    rng.skip(world * m_rows * K_DIM)
     return rng.uniform((K_DIM, N_DIM))
+
+
+def a_rows(rows):
+    """Rows `rows` (global indices) of the synthetic a."""
+    import numpy as np
+    import hexir_b200 as hx
+    out = np.empty((len(rows), K_DIM))
+    for i, g in enumerate(rows):
+        rng = hx.Rng(SEED)
+        rng.skip(int(g) * K_DIM)
+        out[i] = rng.uniform(K_DIM)
+    return out
 
 
 def dmma_peak_tflops(ordinal: int) -> float:
@@ -247,8 +264,8 @@ def workload_config(world: int, m_rows: int) -> dict:
                         f"({m_rows} rows per GPU)",
             "m": m_total, "n": N_DIM, "k": K_DIM,
             "parallelism": f"rows x{world}" + (
-                ", w broadcast + row gather over NVLink (NCCL)"
-                if world > 1 else ""),
+                ", w broadcast over NVLink (NCCL), output rows to GPU 0 over "
+                "NVLink" if world > 1 else ""),
             "l2": "inputs larger than L2 (a+w = 1 GiB per GPU)"}
 
 
@@ -312,12 +329,15 @@ def run_hexir(args):
         _ffi.check(hx.lib().hexir_comm_init_rank(uid, 128, world, rank, ordinal,
                                                  C.byref(h)), "comm init")
         comm = h.value
+    shard_flags = _ffi.MATMUL_RELU | (_ffi.SHARD_GATHER_NCCL
+                                      if args.gather == "nccl" else 0)
+    direct = bool(comm) and args.gather != "nccl" and bool(
+        hx.lib().hexir_comm_direct_stores(comm))
 
     # Inputs: this rank's rows of a; w on every rank (rank 0's is the source
     # of the broadcast; the others' buffers are overwritten every step).
     rng = hx.Rng(SEED)
-    if rank:
-        rng.uniform((rank * m_rows, K_DIM))
+    rng.skip(rank * m_rows * K_DIM)
     a_host = rng.uniform((m_rows, K_DIM))
     w_host = make_w(world, m_rows)
     a = torch.from_numpy(a_host).cuda()
@@ -333,7 +353,7 @@ def run_hexir(args):
         else:
             _ffi.check(hx.lib().hexir_sharded_linear_f64(
                 comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
-                K_DIM, _ffi.MATMUL_RELU, stream), "sharded linear")
+                K_DIM, shard_flags, stream), "sharded linear")
 
     for _ in range(args.warmup):
         step()
@@ -363,13 +383,16 @@ def run_hexir(args):
         ms = float(t.item())
         pg.barrier()
 
-    # The timed kernel computes the right thing: spread rows vs the oracle.
-    rows = np.linspace(0, m_rows - 1, 4).astype(int)
-    got = c[:m_rows].cpu().numpy()[rows]
-    want = oracle.relu(oracle.matmul(a_host[rows], w_host))
-    err = oracle.normwise_error(got, want)
-    if not err <= 1e-12:
-        raise SystemExit(f"bench output wrong: normwise error {err}")
+    # The timed step computes the right thing: rows spread over every
+    # rank's block of the root's output against the oracle.
+    if rank == 0:
+        rows = np.concatenate([p * m_rows + np.linspace(0, m_rows - 1, 3)
+                               .astype(int) for p in range(world)])
+        got = c[torch.from_numpy(rows).cuda()].cpu().numpy()
+        want = oracle.relu(oracle.matmul(a_rows(rows), w_host))
+        err = oracle.normwise_error(got, want)
+        if not err <= 1e-12:
+            raise SystemExit(f"bench output wrong: normwise error {err}")
 
     flops_total = 2.0 * m_total * N_DIM * K_DIM
     value = flops_total / (ms * 1e-3) / 1e9
@@ -382,6 +405,10 @@ def run_hexir(args):
             "config": workload_config(world, m_rows),
             "gpu_launches": launches,
             "clocks": clock_info}
+    if world > 1:
+        line["rows_to_gpu0"] = ("kernel stores over NVLink into GPU 0's output "
+                                "(CUDA IPC mapping)" if direct else
+                                "NCCL send/receive in pieces behind the GEMM")
 
     if rank == 0:
         # Roofline of the dominant kernel (hexir_linear_f64_tma): one launch
@@ -418,7 +445,8 @@ def run_hexir(args):
         line["relu"] = relu_stream(ordinal)
 
     if not args.no_e2e:
-        line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg)
+        line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg,
+                              shard_flags)
 
     if rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -437,7 +465,7 @@ def run_hexir(args):
     return 0
 
 
-def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg):
+def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg, shard_flags):
     """Same metric through the public API with host buffers."""
     import numpy as np
     import torch
@@ -497,7 +525,7 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg):
                 w.copy_(w_pin, non_blocking=True)
             _ffi.check(hx.lib().hexir_sharded_linear_f64(
                 comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
-                K_DIM, _ffi.MATMUL_RELU, stream), "sharded linear")
+                K_DIM, shard_flags, stream), "sharded linear")
             if rank == 0:
                 out.copy_(c, non_blocking=True)
             torch.cuda.synchronize()

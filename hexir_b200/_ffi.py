@@ -34,6 +34,8 @@ MEMORY_DEVICE_LOCAL = 1
 MATMUL_RELU = 0x1
 MATMUL_FORCE_TMA = 0x100
 MATMUL_FORCE_GUARDED = 0x200
+MATMUL_REMOTE_OUTPUT = 0x400
+SHARD_GATHER_NCCL = 0x1000
 
 
 def MATMUL_SPLIT_K(s: int) -> int:
@@ -123,6 +125,7 @@ _SIGNATURES = [
     ("hexir_comm_release", None, [_vp]),
     ("hexir_comm_rank", _int, [_vp]),
     ("hexir_comm_size", _int, [_vp]),
+    ("hexir_comm_direct_stores", _int, [_vp]),
     ("hexir_sharded_linear_f64", _int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32,
                                         _u32, _vp]),
     # hexir_b200/hxb_writer.h

@@ -121,6 +121,11 @@ class Rng:
                                 out.size, lo, hi)
         return out
 
+    def skip(self, draws: int) -> None:
+        """Advance the stream by `draws` draws without producing them (the
+        SplitMix64 state moves by a constant per draw)."""
+        self._r.state = (self._r.state + draws * 0x9E3779B97F4A7C15) % (1 << 64)
+
     def normal(self, shape, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
         out = np.empty(shape, dtype=np.float64)
         lib().hexir_rng_normal(C.byref(self._r),

@@ -45,6 +45,10 @@ extern "C" {
         HEXIR_LINEAR_G_BK * HEXIR_LINEAR_G_BN) * 8 + 1024)
 
 #define HEXIR_EPILOGUE_RELU 0x1u
+/* c is another GPU's memory (peer / IPC mapping): fence the stores at system
+ * scope before the CTA exits, so the owner sees them once it has synchronised
+ * with this kernel's completion. */
+#define HEXIR_EPILOGUE_SYSTEM_FENCE 0x2u
 
 /* Error bits a kernel ORs into the device error word. */
 #define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */

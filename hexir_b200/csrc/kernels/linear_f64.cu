@@ -294,6 +294,8 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   }
   store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
                                 n0 + wn * T::WTN, relu, g, t);
+  if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
+    __threadfence_system();
 }
 
 }  // namespace hexir
@@ -429,6 +431,8 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
   }
   store_warp_tile<2, 2, false>(acc, dst, m, n, m0 + wm * 32, n0 + wn * 32,
                                relu, g, t);
+  if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
+    __threadfence_system();
 }
 
 // c[i] = epilogue(sum over s in 0..split-1 of partials[s][i]), summed in
@@ -444,4 +448,6 @@ extern "C" __global__ void __launch_bounds__(256)
       s = __dadd_rn(s, args.partials[(size_t)p * args.count + i]);
     args.c[i] = relu ? relu_ref(s) : s;
   }
+  if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)
+    __threadfence_system();
 }

@@ -51,6 +51,29 @@ uint32_t gather_piece(uint64_t rows, uint32_t i, uint64_t *begin,
   }
   return pieces;
 }
+
+// Where the root's output lives, as the peers need it to store their rows
+// there directly: a CUDA IPC handle of the allocation holding c and c's
+// offset in it.  Broadcast from the root every call (its c may change).
+struct RootOutput {
+  uint32_t magic;
+  uint32_t valid;  // 0: this call gathers with NCCL
+  uint64_t offset;
+  CUipcMemHandle handle;
+};
+constexpr uint32_t kRootOutputMagic = 0x4f525848u;  // "HXRO"
+constexpr size_t kDescBytes = 128;
+static_assert(sizeof(RootOutput) <= kDescBytes, "descriptor too large");
+// Pinned descriptor slots, reused round robin once their copy has finished.
+constexpr uint32_t kDescSlots = 8;
+// Root allocations a peer keeps mapped.
+constexpr size_t kMaxMapped = 4;
+
+struct MappedOutput {
+  CUipcMemHandle handle;
+  CUdeviceptr base;
+  uint64_t last_use;
+};
 }  // namespace
 
 struct hexir_comm_t {
@@ -61,7 +84,122 @@ struct hexir_comm_t {
   CUstream gather_stream = nullptr;  // row sends / receives
   CUevent chunk_done[kGatherChunks] = {};
   CUevent gather_done = nullptr;
+  // Direct row stores into the root's c (all ranks on one host, IPC works).
+  bool direct = false;
+  CUdeviceptr scratch = 0;  // descriptor [kDescBytes] + completion word
+  RootOutput *desc_host = nullptr;  // pinned [kDescSlots]
+  CUevent desc_done[kDescSlots] = {};
+  uint32_t desc_next = 0;
+  MappedOutput mapped[kMaxMapped] = {};
+  size_t mapped_count = 0;
+  uint64_t calls = 0;
 };
+
+namespace {
+
+hexir_status_t comm_fail(const std::string &message) {
+  set_last_error(message);
+  return HEXIR_ERROR_DEVICE;
+}
+
+// The pinned descriptor slot for this call, once its previous copy is done.
+RootOutput *next_desc(hexir_comm_t *comm, CUevent *done) {
+  const uint32_t i = comm->desc_next++ % kDescSlots;
+  driver().EventSynchronize(comm->desc_done[i]);
+  *done = comm->desc_done[i];
+  return &comm->desc_host[i];
+}
+
+// The root's allocation `handle` mapped into this peer, opened on first use.
+// At most kMaxMapped stay open; the least recently used one is closed after
+// the context has finished every kernel that could store through it.
+hexir_status_t map_root_output(hexir_comm_t *comm, const CUipcMemHandle &handle,
+                               CUdeviceptr *base) {
+  const Driver &d = driver();
+  ++comm->calls;
+  for (size_t i = 0; i < comm->mapped_count; ++i)
+    if (std::memcmp(&comm->mapped[i].handle, &handle, sizeof(handle)) == 0) {
+      comm->mapped[i].last_use = comm->calls;
+      *base = comm->mapped[i].base;
+      return HEXIR_OK;
+    }
+  size_t slot = comm->mapped_count;
+  if (slot == kMaxMapped) {
+    slot = 0;
+    for (size_t i = 1; i < kMaxMapped; ++i)
+      if (comm->mapped[i].last_use < comm->mapped[slot].last_use)
+        slot = i;
+    CUresult r = d.CtxSynchronize();
+    if (r == CUDA_SUCCESS)
+      r = d.IpcCloseMemHandle(comm->mapped[slot].base);
+    if (r != CUDA_SUCCESS)
+      return comm_fail(cuda_message("closing a mapping of the root's output", r));
+    --comm->mapped_count;
+    comm->mapped[slot] = comm->mapped[comm->mapped_count];
+    slot = comm->mapped_count;
+  }
+  CUdeviceptr p = 0;
+  const CUresult r =
+      d.IpcOpenMemHandle(&p, handle, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("mapping the root's output (IPC)", r));
+  comm->mapped[slot] = {handle, p, comm->calls};
+  ++comm->mapped_count;
+  *base = p;
+  return HEXIR_OK;
+}
+
+// Once, at set-up: the root exports its scratch buffer and every peer tries
+// to map it.  Direct stores are used only if all of them could.
+hexir_status_t probe_direct(hexir_comm_t *comm) {
+  const Driver &d = driver();
+  const Nccl &nc = nccl();
+  CUstream s = comm->gather_stream;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(s);
+  RootOutput *desc = &comm->desc_host[0];
+  std::memset(desc, 0, sizeof(*desc));
+  if (comm->rank == 0) {
+    desc->magic = kRootOutputMagic;
+    desc->valid = d.IpcGetMemHandle(&desc->handle, comm->scratch) == CUDA_SUCCESS;
+    CUresult r = d.MemcpyHtoDAsync(comm->scratch, desc, sizeof(*desc), s);
+    if (r != CUDA_SUCCESS)
+      return comm_fail(cuda_message("probe descriptor", r));
+  }
+  void *buf = reinterpret_cast<void *>(comm->scratch);
+  ncclResult_t nr = nc.Broadcast(buf, buf, kDescBytes, ncclUint8, 0, comm->comm, cs);
+  if (nr != ncclSuccess)
+    return comm_fail(nccl_message("ncclBroadcast (probe)", nr));
+  CUresult r = d.MemcpyDtoHAsync(desc, comm->scratch, sizeof(*desc), s);
+  if (r == CUDA_SUCCESS)
+    r = d.StreamSynchronize(s);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("probe descriptor", r));
+  int32_t ok = desc->magic == kRootOutputMagic && desc->valid;
+  if (ok && comm->rank != 0) {
+    CUdeviceptr p = 0;
+    ok = d.IpcOpenMemHandle(&p, desc->handle,
+                            CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS) == CUDA_SUCCESS;
+    if (ok)
+      d.IpcCloseMemHandle(p);
+  }
+  const CUdeviceptr word = comm->scratch + kDescBytes;
+  r = d.MemcpyHtoDAsync(word, &ok, sizeof(ok), s);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("probe vote", r));
+  void *w = reinterpret_cast<void *>(word);
+  nr = nc.AllReduce(w, w, 1, ncclInt32, ncclMin, comm->comm, cs);
+  if (nr != ncclSuccess)
+    return comm_fail(nccl_message("ncclAllReduce (probe)", nr));
+  r = d.MemcpyDtoHAsync(&ok, word, sizeof(ok), s);
+  if (r == CUDA_SUCCESS)
+    r = d.StreamSynchronize(s);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("probe vote", r));
+  comm->direct = ok == 1;
+  return HEXIR_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -131,10 +269,24 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
     cr = d.EventCreate(&comm->chunk_done[i], CU_EVENT_DISABLE_TIMING);
   if (cr == CUDA_SUCCESS)
     cr = d.EventCreate(&comm->gather_done, CU_EVENT_DISABLE_TIMING);
+  for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kDescSlots; ++i)
+    cr = d.EventCreate(&comm->desc_done[i], CU_EVENT_DISABLE_TIMING);
+  if (cr == CUDA_SUCCESS)
+    cr = d.MemAlloc(&comm->scratch, kDescBytes + 16);
+  if (cr == CUDA_SUCCESS)
+    cr = d.MemAllocHost(reinterpret_cast<void **>(&comm->desc_host),
+                        kDescSlots * sizeof(RootOutput));
   if (cr != CUDA_SUCCESS) {
     set_last_error(cuda_message("gather stream set-up", cr));
     hexir_comm_release(comm);
     return HEXIR_ERROR_DEVICE;
+  }
+  if (nranks > 1) {
+    hexir_status_t st = probe_direct(comm);
+    if (st != HEXIR_OK) {
+      hexir_comm_release(comm);
+      return st;
+    }
   }
   *out = comm;
   return HEXIR_OK;
@@ -157,6 +309,19 @@ void hexir_comm_release(hexir_comm_t *comm) {
         d.EventDestroy(ev);
     if (comm->gather_done)
       d.EventDestroy(comm->gather_done);
+    if (comm->mapped_count)
+      d.CtxSynchronize();
+    for (size_t i = 0; i < comm->mapped_count; ++i)
+      d.IpcCloseMemHandle(comm->mapped[i].base);
+    for (CUevent ev : comm->desc_done)
+      if (ev) {
+        d.EventSynchronize(ev);
+        d.EventDestroy(ev);
+      }
+    if (comm->desc_host)
+      d.MemFreeHost(comm->desc_host);
+    if (comm->scratch)
+      d.MemFree(comm->scratch);
   }
   if (comm->comm && nccl().ok)
     nccl().CommDestroy(comm->comm);
@@ -166,6 +331,9 @@ void hexir_comm_release(hexir_comm_t *comm) {
 int hexir_comm_rank(const hexir_comm_t *comm) { return comm ? comm->rank : -1; }
 int hexir_comm_size(const hexir_comm_t *comm) {
   return comm ? comm->nranks : 0;
+}
+int hexir_comm_direct_stores(const hexir_comm_t *comm) {
+  return comm && comm->direct ? 1 : 0;
 }
 
 hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows,
@@ -188,22 +356,94 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   }
   ContextGuard guard(dev->context);
   CUstream s = static_cast<CUstream>(stream);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(s);
+  const Driver &d = driver();
   const uint32_t ranks = static_cast<uint32_t>(comm->nranks);
   uint64_t begin = 0, rows = 0;
   hexir_shard_rows(m, ranks, static_cast<uint32_t>(comm->rank), &begin, &rows);
 
+  // 0. Whether this call's rows are stored straight into the root's c: the
+  //    root describes c (IPC handle + offset) and every rank reads that
+  //    description, so all of them take the same branch.
+  bool direct = false;
+  CUdeviceptr remote_c = 0;
+  hexir_status_t peer_status = HEXIR_OK;
+  if (ranks > 1 && comm->direct) {
+    CUevent done = nullptr;
+    RootOutput *desc = next_desc(comm, &done);
+    std::memset(desc, 0, sizeof(*desc));
+    CUresult cr = CUDA_SUCCESS;
+    if (comm->rank == 0) {
+      CUdeviceptr base = 0;
+      size_t size = 0;
+      const CUdeviceptr cp = reinterpret_cast<CUdeviceptr>(c);
+      desc->magic = kRootOutputMagic;
+      desc->valid = !(flags & HEXIR_SHARD_GATHER_NCCL) &&
+                    d.MemGetAddressRange(&base, &size, cp) == CUDA_SUCCESS &&
+                    d.IpcGetMemHandle(&desc->handle, base) == CUDA_SUCCESS;
+      desc->offset = desc->valid ? cp - base : 0;
+      cr = d.MemcpyHtoDAsync(comm->scratch, desc, sizeof(*desc), s);
+    }
+    if (cr != CUDA_SUCCESS)
+      return comm_fail(cuda_message("output descriptor", cr));
+    void *buf = reinterpret_cast<void *>(comm->scratch);
+    ncclResult_t nr =
+        nc.Broadcast(buf, buf, kDescBytes, ncclUint8, 0, comm->comm, cs);
+    if (nr != ncclSuccess)
+      return comm_fail(nccl_message("ncclBroadcast (output descriptor)", nr));
+    if (comm->rank != 0)
+      cr = d.MemcpyDtoHAsync(desc, comm->scratch, sizeof(*desc), s);
+    if (cr == CUDA_SUCCESS)
+      cr = d.EventRecord(done, s);
+    // A peer waits here until the root's stream has reached this call.
+    if (cr == CUDA_SUCCESS && comm->rank != 0)
+      cr = d.EventSynchronize(done);
+    if (cr != CUDA_SUCCESS)
+      return comm_fail(cuda_message("output descriptor", cr));
+    direct = desc->magic == kRootOutputMagic && desc->valid;
+    if (direct && comm->rank != 0) {
+      peer_status = map_root_output(comm, desc->handle, &remote_c);
+      remote_c += desc->offset;
+    }
+  }
+
   // 1. Weight from the root to everyone, over NVLink.
   ncclResult_t r = nc.Broadcast(w, w, static_cast<size_t>(k) * n, ncclDouble, 0,
-                                comm->comm, reinterpret_cast<cudaStream_t>(s));
+                                comm->comm, cs);
   if (r != ncclSuccess) {
     set_last_error(nccl_message("ncclBroadcast", r));
     return HEXIR_ERROR_DEVICE;
   }
+
+  if (direct) {
+    // 2'. One launch over this rank's rows; a peer's kernel stores its tiles
+    //     into the root's c over NVLink as they finish (system-scope fence
+    //     before each CTA retires).  3'. A one-word all-reduce orders the
+    //     root's stream after every peer's kernel.  A rank whose launch
+    //     failed still joins it, so no rank waits for ever.
+    if (rows && peer_status == HEXIR_OK) {
+      double *out = comm->rank == 0
+                        ? c
+                        : reinterpret_cast<double *>(remote_c) + begin * n;
+      const uint32_t kflags = (flags & HEXIR_MATMUL_RELU) |
+                              (comm->rank ? HEXIR_MATMUL_REMOTE_OUTPUT : 0u);
+      peer_status = launch_matmul(dev, lib, a_rows, w, out,
+                                  static_cast<uint32_t>(rows), n, k, kflags, s,
+                                  &error);
+      if (peer_status != HEXIR_OK)
+        set_last_error(error);
+    }
+    void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
+    r = nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
+    if (r != ncclSuccess)
+      return comm_fail(nccl_message("ncclAllReduce (row stores done)", r));
+    return peer_status;
+  }
+
   // 2. This rank's rows in up to kGatherChunks pieces; the root writes
   //    straight into its part of c.  3. Each finished piece goes to the root
   //    on the gather stream while the next piece computes.  Every rank splits
   //    its rows by the same rule, so the root knows each peer's pieces.
-  const Driver &d = driver();
   uint64_t ignore_b = 0, ignore_c = 0;
   const uint32_t my_chunks = rows ? gather_piece(rows, 0, &ignore_b, &ignore_c) : 0;
   uint32_t max_chunks = 0;

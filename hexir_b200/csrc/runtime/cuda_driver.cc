@@ -69,6 +69,10 @@ void load() {
             bind(lib, d.MemcpyPeerAsync, "cuMemcpyPeerAsync", e) &&
             bind(lib, d.MemsetD8Async, "cuMemsetD8Async", e) &&
             bind(lib, d.PointerGetAttribute, "cuPointerGetAttribute", e) &&
+            bind(lib, d.MemGetAddressRange, "cuMemGetAddressRange_v2", e) &&
+            bind(lib, d.IpcGetMemHandle, "cuIpcGetMemHandle", e) &&
+            bind(lib, d.IpcOpenMemHandle, "cuIpcOpenMemHandle_v2", e) &&
+            bind(lib, d.IpcCloseMemHandle, "cuIpcCloseMemHandle", e) &&
             bind(lib, d.ModuleLoadData, "cuModuleLoadData", e) &&
             bind(lib, d.ModuleUnload, "cuModuleUnload", e) &&
             bind(lib, d.ModuleGetFunction, "cuModuleGetFunction", e) &&

@@ -52,6 +52,11 @@ struct Driver {
       nullptr;
   CUresult (*PointerGetAttribute)(void *, CUpointer_attribute,
                                   CUdeviceptr) = nullptr;
+  CUresult (*MemGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr) = nullptr;
+  CUresult (*IpcGetMemHandle)(CUipcMemHandle *, CUdeviceptr) = nullptr;
+  CUresult (*IpcOpenMemHandle)(CUdeviceptr *, CUipcMemHandle, unsigned int) =
+      nullptr;
+  CUresult (*IpcCloseMemHandle)(CUdeviceptr) = nullptr;
   CUresult (*ModuleLoadData)(CUmodule *, const void *) = nullptr;
   CUresult (*ModuleUnload)(CUmodule) = nullptr;
   CUresult (*ModuleGetFunction)(CUfunction *, CUmodule, const char *) = nullptr;

@@ -18,8 +18,9 @@
 //   weight  -> first GPU, then ncclBroadcast to the rest of the range
 //   a rows  -> each GPU gets its rows (hexir_shard_rows) straight from where
 //              a lives
-//   c rows  -> each GPU computes its rows with no collective; ncclSend/Recv
-//              gathers them into c on the first GPU
+//   c rows  -> each GPU computes its rows with no collective and stores them
+//              straight into c on the first GPU over NVLink (peer access);
+//              without peer access, ncclSend/Recv gathers them instead
 
 #include <algorithm>
 #include <cstdint>
@@ -238,6 +239,32 @@ struct Vm {
       return HEXIR_ERROR_DEVICE;
     }
     return HEXIR_OK;
+  }
+
+  // Whether `from` may load and store `to`'s memory directly (NVLink peer
+  // access), enabling it on first use.
+  static bool peer_access(CudaDevice *from, CudaDevice *to) {
+    static std::mutex mu;
+    static std::map<std::pair<CUcontext, CUcontext>, bool> known;
+    if (from->state == to->state)
+      return true;
+    const auto key = std::make_pair(from->state->context, to->state->context);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = known.find(key);
+    if (it != known.end())
+      return it->second;
+    const Driver &d = driver();
+    int can = 0;
+    bool ok = d.DeviceCanAccessPeer(&can, from->state->device,
+                                    to->state->device) == CUDA_SUCCESS &&
+              can;
+    if (ok) {
+      ContextGuard guard(from->state->context);
+      const CUresult r = d.CtxEnablePeerAccess(to->state->context, 0);
+      ok = r == CUDA_SUCCESS || r == CUDA_ERROR_PEER_ACCESS_ALREADY_ENABLED;
+    }
+    known[key] = ok;
+    return ok;
   }
 
   hexir_status_t buffer_on(Slot &s, int o, uint64_t bytes, CUdeviceptr *out) {
@@ -754,6 +781,7 @@ struct Vm {
     const uint64_t row_out = static_cast<uint64_t>(exe.n) * 8;
     std::vector<CUdeviceptr> c_part(count, 0);
     std::vector<uint64_t> begin(count), rows(count);
+    std::vector<char> direct(count, 0);
     for (int r = 0; r < count; ++r) {
       hexir_shard_rows(exe.m, static_cast<uint32_t>(count),
                        static_cast<uint32_t>(r), &begin[r], &rows[r]);
@@ -777,9 +805,13 @@ struct Vm {
         }
         (i == 0 ? x : y) = p;
       }
+      // With peer access to the first GPU, the shard's kernel stores its rows
+      // straight into the result there over NVLink, tile by tile as they are
+      // computed; otherwise it writes a local block for the NCCL gather below.
       CUdeviceptr out = 0;
-      if (r == 0) {
-        out = c_root;
+      direct[r] = r == 0 || peer_access(cuda[o], root);
+      if (direct[r]) {
+        out = c_root + begin[r] * row_out;
       } else if ((st = temp_on(o, rows[r] * row_out, &out)) != HEXIR_OK) {
         return st;
       }
@@ -794,8 +826,9 @@ struct Vm {
         st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(x),
                            reinterpret_cast<const double *>(w[r]),
                            reinterpret_cast<double *>(out), m, exe.n, exe.k,
-                           exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
-                                                                : 0u,
+                           (exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
+                                                                 : 0u) |
+                               (r && direct[r] ? HEXIR_MATMUL_REMOTE_OUTPUT : 0u),
                            dev->stream, &error);
         break;
       case HEXIR_KERNEL_ADD:
@@ -816,11 +849,23 @@ struct Vm {
         return st;
       }
     }
-    // Rows back to the root.
-    if (count > 1) {
+    // The root's stream continues once every shard has finished; shards
+    // that wrote directly only need that ordering, the rest send their rows.
+    bool any_gather = false;
+    for (int r = 1; r < count; ++r) {
+      if (!rows[r])
+        continue;
+      if (direct[r]) {
+        if ((st = order_after(cuda[first + r], root)) != HEXIR_OK)
+          return st;
+      } else {
+        any_gather = true;
+      }
+    }
+    if (any_gather) {
       nc.GroupStart();
       for (int r = 1; r < count; ++r) {
-        if (!rows[r])
+        if (!rows[r] || direct[r])
           continue;
         nc.Send(reinterpret_cast<void *>(c_part[r]), rows[r] * exe.n, ncclDouble,
                 0, comms[r],

@@ -370,7 +370,9 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   args.m = m;
   args.n = n;
   args.k = k;
-  args.epilogue = (flags & HEXIR_MATMUL_RELU) ? HEXIR_EPILOGUE_RELU : 0u;
+  args.epilogue = ((flags & HEXIR_MATMUL_RELU) ? HEXIR_EPILOGUE_RELU : 0u) |
+                  ((flags & HEXIR_MATMUL_REMOTE_OUTPUT) ? HEXIR_EPILOGUE_SYSTEM_FENCE
+                                                        : 0u);
   args.tiles_m = p.tiles_m;
   args.tiles_n = p.tiles_n;
   args.group_m = std::min<uint32_t>(8, p.tiles_m);

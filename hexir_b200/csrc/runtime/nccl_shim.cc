@@ -46,6 +46,7 @@ void load() {
          bind(lib, n.GroupEnd, "ncclGroupEnd", e) &&
          bind(lib, n.Broadcast, "ncclBroadcast", e) &&
          bind(lib, n.Send, "ncclSend", e) && bind(lib, n.Recv, "ncclRecv", e) &&
+         bind(lib, n.AllReduce, "ncclAllReduce", e) &&
          bind(lib, n.GetErrorString, "ncclGetErrorString", e);
 }
 

@@ -24,6 +24,8 @@ struct Nccl {
                             ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t,
                        cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t,
+                            ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t,
                        cudaStream_t) = nullptr;
   const char *(*GetErrorString)(ncclResult_t) = nullptr;

@@ -6,8 +6,11 @@
  * interpreter.c:85-92).  This header adds the one strategy the hot path
  * needs: the rows of a[m x k] (and so of c[m x n]) are split over GPUs, the
  * weight b[k x n] is broadcast from the first GPU over NVLink with NCCL, every
- * GPU computes its rows with no collective, and the output rows are gathered
- * back to the first GPU.
+ * GPU computes its rows with no collective, and the output rows land on the
+ * first GPU.  Where the GPUs can reach the first GPU's memory (peer access in
+ * one process, a CUDA IPC mapping across processes of one host), each GPU's
+ * kernel stores its output tiles there directly over NVLink as it computes
+ * them; otherwise the rows are gathered with NCCL send/receive.
  *
  * Two ways in:
  *   - in one process, a module whose linear is placed on "cuda:F-L" run with
@@ -40,21 +43,40 @@ typedef struct hexir_comm_t hexir_comm_t;
 hexir_status_t hexir_comm_unique_id(void *id, size_t size);
 
 /* Join a communicator of `nranks` processes as `rank`, driving GPU
- * `ordinal`. */
+ * `ordinal`.  Collective; also checks once whether the peers can map rank
+ * 0's memory for direct row stores. */
 hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
                                     int rank, int ordinal, hexir_comm_t **out);
 void hexir_comm_release(hexir_comm_t *comm);
 int hexir_comm_rank(const hexir_comm_t *comm);
 int hexir_comm_size(const hexir_comm_t *comm);
+/* 1 when the set-up check found that every peer can map rank 0's memory, so
+ * hexir_sharded_linear_f64 can store rows into the root's c directly. */
+int hexir_comm_direct_stores(const hexir_comm_t *comm);
+
+/* Rank 0's flag: gather the rows with NCCL send/receive even where they
+ * could be stored into its c directly. */
+#define HEXIR_SHARD_GATHER_NCCL 0x1000u
 
 /* Collective over all ranks of `comm` (rank 0 is the root):
  *   w      [k x n] on every rank; the root's contents are broadcast into the
  *          others' buffers.
  *   a_rows this rank's rows of a, rows hexir_shard_rows(m, size, rank).
- *   c      root: the whole [m x n] output; other ranks: [rows x n] for their
- *          own rows, which are then sent to the root.
- * flags: HEXIR_MATMUL_RELU as for hexir_cuda_matmul_f64.  Asynchronous on
- * `stream`. */
+ *   c      root: the whole [m x n] output; other ranks: [rows x n] staging
+ *          for their own rows, used only when the rows travel by NCCL (its
+ *          contents are unspecified afterwards).
+ * flags: HEXIR_MATMUL_RELU as for hexir_cuda_matmul_f64, HEXIR_SHARD_GATHER_NCCL.
+ *
+ * Rows go to the root's c directly when hexir_comm_init_rank found that
+ * every peer can map rank 0's memory (same host, CUDA IPC) and the root's c
+ * is exportable (a cuMemAlloc / cudaMalloc allocation); the root's stream
+ * continues after every peer's kernel has finished storing.  Otherwise they
+ * are gathered with NCCL on a side stream, piece by piece behind the GEMM.
+ * Asynchronous on `stream`, except that with direct stores a peer's call
+ * returns only once the root's stream has reached the same call (the root
+ * sends the location of c every call).  Peers write the root's c only after
+ * the root's `stream` reaches the call, so the root orders its own use of c
+ * on that stream. */
 hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows,
                                         double *w, double *c, uint32_t m,
                                         uint32_t n, uint32_t k, uint32_t flags,

@@ -39,6 +39,9 @@ extern "C" {
 #define HEXIR_MATMUL_RELU 0x1u          /* c = relu(a . b), reference relu */
 #define HEXIR_MATMUL_FORCE_TMA 0x100u   /* tests: only the TMA kernel */
 #define HEXIR_MATMUL_FORCE_GUARDED 0x200u /* tests: only the guarded kernel */
+/* c is another GPU's memory (a peer or IPC mapping): the kernels fence their
+ * stores at system scope before finishing. */
+#define HEXIR_MATMUL_REMOTE_OUTPUT 0x400u
 /* tests: split the k range into S pieces (1..255); 0 = choose automatically */
 #define HEXIR_MATMUL_SPLIT_K(S) (((uint32_t)(S) & 0xFFu) << 16)
 

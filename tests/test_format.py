@@ -232,6 +232,9 @@ def test_rng_stream_is_stable():
     r2 = hx.Rng(0)
     r2.uniform(4)
     assert np.array_equal(r2.uniform(4), again[4:])
+    r3 = hx.Rng(0)
+    r3.skip(5)
+    assert np.array_equal(r3.uniform(3), again[5:])
     n = hx.Rng(5).normal(20000)
     assert abs(n.mean()) < 0.05 and abs(n.std() - 1) < 0.05
 

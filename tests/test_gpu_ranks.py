@@ -1,0 +1,125 @@
+"""hexir_sharded_linear_f64 with one process per GPU (2 GPUs).
+
+Each rank is a spawned process driving its own GPU; the NCCL unique id
+travels over a gloo group on 127.0.0.1.  Rank 0 holds the whole output.
+The same call runs twice: rows stored by every rank straight into rank 0's
+output through a CUDA IPC mapping (the default where the set-up check
+passes), and rows gathered with NCCL send/receive (HEXIR_SHARD_GATHER_NCCL).
+Both must equal the oracle within the normwise tolerance.  With direct
+stores every rank runs one launch over its rows, so each block of rows must
+equal, bit for bit, the same launch on one GPU; and a second call into a
+different output buffer must land there (the root sends its output's
+location every call).  The NCCL path computes in pieces whose k-split may
+differ, so it is held to the tolerance only.
+"""
+
+import ctypes as C
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import hexir_b200 as hx
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-12
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, m, n, k, result_path):
+    import torch.distributed as dist
+    from hexir_b200 import _ffi
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    lib = hx.lib()
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        _ffi.check(lib.hexir_comm_unique_id(uid, 128), "unique id")
+    obj = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    uid = C.create_string_buffer(obj[0], 128)
+    comm = C.c_void_p()
+    _ffi.check(lib.hexir_comm_init_rank(uid, 128, world, rank, rank,
+                                        C.byref(comm)), "comm init")
+    comm = comm.value
+    direct = lib.hexir_comm_direct_stores(comm)
+
+    rng = hx.Rng(31)
+    a = rng.uniform((m, k))
+    w = rng.uniform((k, n))
+    begin, rows = hx.shard_rows(m, world, rank)
+    dev = hx.Device(f"cuda:{rank}")
+    ba = dev.upload(a[begin:begin + rows] if rows else np.zeros(1))
+    bw = dev.upload(w if rank == 0 else np.zeros_like(w))
+    out_rows = m if rank == 0 else max(rows, 1)
+    outs = [dev.buffer(out_rows * n * 8) for _ in range(2)]
+    results = {}
+    for name, buf, flags in [
+            ("direct", outs[0], _ffi.MATMUL_RELU),
+            ("nccl", outs[1], _ffi.MATMUL_RELU | _ffi.SHARD_GATHER_NCCL),
+            ("direct_again", outs[1], _ffi.MATMUL_RELU)]:
+        if rank == 0:
+            buf.write(np.full((m, n), np.nan))
+        dist.barrier()
+        _ffi.check(lib.hexir_sharded_linear_f64(comm, ba.ptr, bw.ptr, buf.ptr,
+                                                m, n, k, flags, dev.stream),
+                   "sharded linear " + name)
+        hx.cuda_synchronize(rank, dev.stream)
+        if rank == 0:
+            results[name] = buf.read((m, n))
+    lib.hexir_comm_release(comm)
+    if rank == 0:
+        # Every rank's block as one launch on this GPU alone.
+        single = np.empty((m, n))
+        for r in range(world):
+            rb, rr = hx.shard_rows(m, world, r)
+            if not rr:
+                continue
+            xa = dev.upload(a[rb:rb + rr])
+            xc = dev.buffer(rr * n * 8)
+            hx.cuda_matmul(0, xa.ptr, bw.ptr, xc.ptr, rr, n, k,
+                           _ffi.MATMUL_RELU, dev.stream)
+            hx.cuda_synchronize(0, dev.stream)
+            single[rb:rb + rr] = xc.read((rr, n))
+        results["single"] = single
+    if rank == 0:
+        np.savez(result_path, direct_flag=np.array([direct]), a=a, w=w,
+                 **results)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def two_gpus():
+    return hx.device_count() >= 2
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+@pytest.mark.parametrize("m,n,k", [(1000, 384, 512), (3, 130, 96),
+                                   (2048, 1024, 1024)])
+def test_two_processes_sharded_linear(tmp_path, m, n, k):
+    import torch.multiprocessing as mp
+    from oracle import oracle
+    path = str(tmp_path / "out.npz")
+    mp.start_processes(_rank, args=(2, free_port(), m, n, k, path), nprocs=2,
+                       join=True, start_method="spawn")
+    r = np.load(path)
+    # Two processes on one host: the peers can map rank 0's memory.
+    assert int(r["direct_flag"][0]) == 1
+    want = oracle.relu(oracle.matmul(r["a"], r["w"]))
+    for name in ["direct", "nccl", "direct_again"]:
+        got = r[name]
+        assert not np.isnan(got).any(), name
+        assert oracle.normwise_error(got, want) <= TOL, name
+    bits = lambda x: x.view(np.uint64)
+    assert np.array_equal(bits(r["direct"]), bits(r["single"]))
+    assert np.array_equal(bits(r["direct"]), bits(r["direct_again"]))
