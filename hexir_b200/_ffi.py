@@ -98,6 +98,8 @@ _SIGNATURES = [
     ("hexir_execute_devices", _int, [_vp, C.POINTER(_vp), C.c_uint,
                                      C.c_char_p, _vp, _sz]),
     ("hexir_last_execute_kernel_ms", C.c_double, []),
+    ("hexir_module_keep_constants", _int, [_vp, _int]),
+    ("hexir_module_kept_bytes", _sz, [_vp]),
     # hexir_b200/kernels.h
     ("hexir_cuda_matmul_f64", _int, [_int, _vp, _vp, _vp, _u32, _u32, _u32,
                                      _u32, _vp]),

@@ -251,6 +251,16 @@ class Module:
     def version(self) -> int:
         return lib().hexir_module_version(self._h)
 
+    def keep_constants(self, enable: bool = True) -> None:
+        """Keep CONST uploads on the GPUs between executes
+        (hexir_module_keep_constants); False frees them."""
+        check(lib().hexir_module_keep_constants(self._h, int(enable)),
+              "hexir_module_keep_constants")
+
+    @property
+    def kept_bytes(self) -> int:
+        return lib().hexir_module_kept_bytes(self._h)
+
     def sections(self) -> List[tuple]:
         out = []
         for i in range(lib().hexir_module_section_count(self._h)):

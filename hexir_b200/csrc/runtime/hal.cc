@@ -186,6 +186,10 @@ hexir_status_t CudaDevice::buffer_allocate(size_t size, hexir_memory_kind_t,
 }
 
 void CudaDevice::buffer_release(hexir_buffer_t *buffer) {
+  if (buffer->borrowed) {
+    delete buffer;
+    return;
+  }
   // The pool keeps at most kPoolCapBytes; beyond that blocks are freed.
   constexpr size_t kPoolCapBytes = 32ull << 30;
   if (buffer->pooled && buffer->impl && pool_bytes + buffer->size <= kPoolCapBytes) {

@@ -49,6 +49,8 @@ struct hexir_buffer_t {
   hexir_memory_kind_t memory = HEXIR_MEMORY_HOST_LOCAL;
   void *impl = nullptr;  // host pointer (CPU) or CUdeviceptr (CUDA)
   bool pooled = false;   // VM buffer: returns to the device's pool on release
+  bool borrowed = false; // VM view of memory it does not own (a constant the
+                         // module keeps on the device): release frees no memory
 };
 
 namespace hexir {

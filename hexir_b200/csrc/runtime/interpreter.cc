@@ -23,6 +23,7 @@
 //              without peer access, ncclSend/Recv gathers them instead
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -96,7 +97,7 @@ struct PinnedRodata {
   uint8_t *copy = nullptr;       // pinned copy of RODATA
 };
 
-void *pin_rodata(const hexir_module_t *module) {
+PinnedRodata *pin_rodata(const hexir_module_t *module) {
   auto *pin = new (std::nothrow) PinnedRodata;
   if (!pin)
     return nullptr;
@@ -126,13 +127,75 @@ void *pin_rodata(const hexir_module_t *module) {
   return pin;
 }
 
-void unpin_rodata(void *p) {
-  auto *pin = static_cast<PinnedRodata *>(p);
+void unpin_rodata(PinnedRodata *pin) {
   if (pin->registered)
     driver().MemHostUnregister(pin->registered);
   if (pin->copy)
     driver().MemFreeHost(pin->copy);
   delete pin;
+}
+
+// A constant kept on one GPU between executes of its module.
+struct ResidentConst {
+  DeviceState *device = nullptr;
+  uint64_t offset = 0, bytes = 0;  // range of RODATA
+  CUdeviceptr ptr = 0;
+  CUevent ready = nullptr;  // the upload, recorded on the uploading stream
+};
+
+// Runtime state attached to a loaded module for its lifetime: the pinned
+// RODATA (set up by the first large upload) and, when the caller asked for
+// it (hexir_module_keep_constants), device copies of its constants.
+struct ModuleState {
+  const hexir_module_t *module = nullptr;
+  std::once_flag pin_once;
+  PinnedRodata *pin = nullptr;
+  std::atomic<bool> keep_constants{false};
+  std::mutex mu;  // guards resident
+  std::vector<ResidentConst> resident;
+
+  PinnedRodata *pinned() {
+    std::call_once(pin_once, [this] { pin = pin_rodata(module); });
+    return pin;
+  }
+
+  // Frees every resident copy once the GPU has finished using it.  Callers
+  // hold mu.
+  void drop_resident() {
+    const Driver &d = driver();
+    for (ResidentConst &rc : resident) {
+      ContextGuard guard(rc.device->context);
+      d.CtxSynchronize();
+      if (rc.ready)
+        d.EventDestroy(rc.ready);
+      d.MemFree(rc.ptr);
+    }
+    resident.clear();
+  }
+};
+
+void *make_module_state(const hexir_module_t *module) {
+  auto *ms = new (std::nothrow) ModuleState;
+  if (ms)
+    ms->module = module;
+  return ms;
+}
+
+void free_module_state(void *p) {
+  auto *ms = static_cast<ModuleState *>(p);
+  {
+    std::lock_guard<std::mutex> lock(ms->mu);
+    ms->drop_resident();
+  }
+  if (ms->pin)
+    unpin_rodata(ms->pin);
+  delete ms;
+}
+
+ModuleState *module_state(const hexir_module_t *module) {
+  return module ? static_cast<ModuleState *>(module_attached(
+                      module, make_module_state, free_module_state))
+                : nullptr;
 }
 
 struct Slot {
@@ -294,9 +357,9 @@ struct Vm {
   // module has one (large uploads set it up), else the module's own bytes.
   const uint8_t *rodata_source(const Slot &s, uint64_t offset, uint64_t bytes) {
     const uint8_t *src = s.rodata + offset;
-    if (module && bytes >= (1u << 20)) {
-      auto *pin = static_cast<PinnedRodata *>(
-          module_attached(module, pin_rodata, unpin_rodata));
+    ModuleState *ms = bytes >= (1u << 20) ? module_state(module) : nullptr;
+    if (ms) {
+      PinnedRodata *pin = ms->pinned();
       if (pin && pin->copy && src >= pin->src && src + bytes <= pin->src + pin->size)
         src = pin->copy + (src - pin->src);
     }
@@ -347,9 +410,102 @@ struct Vm {
     return HEXIR_OK;
   }
 
+  // Attach the resident copy of constant slot s on GPU o, uploading it on
+  // first use, when the module keeps its constants.  *done is false when the
+  // slot is not served that way (the caller uploads as usual).
+  hexir_status_t resident_on(Slot &s, int o, CUdeviceptr *out, bool *done) {
+    *done = false;
+    ModuleState *ms = s.rodata && s.bytes ? module_state(module) : nullptr;
+    if (!ms || !ms->keep_constants.load() || s.dev.count(o))
+      return HEXIR_OK;
+    CudaDevice *dev = cuda[o];
+    const Driver &d = driver();
+    const uint64_t offset = static_cast<uint64_t>(s.rodata - rodata);
+    std::lock_guard<std::mutex> lock(ms->mu);
+    ContextGuard guard(dev->state->context);
+    ResidentConst *rc = nullptr;
+    for (ResidentConst &r : ms->resident)
+      if (r.device == dev->state && r.offset == offset && r.bytes == s.bytes)
+        rc = &r;
+    auto *b = new (std::nothrow) hexir_buffer_t;
+    if (!b)
+      return HEXIR_ERROR_OUT_OF_MEMORY;
+    if (!rc) {
+      ResidentConst fresh;
+      fresh.device = dev->state;
+      fresh.offset = offset;
+      fresh.bytes = s.bytes;
+      if (d.MemAlloc(&fresh.ptr, s.bytes) != CUDA_SUCCESS) {
+        delete b;  // no room to keep it: upload per execute as usual
+        return HEXIR_OK;
+      }
+      hexir_status_t st = dev->write_async(fresh.ptr, rodata_source(s, 0, s.bytes),
+                                           s.bytes);
+      CUresult r = st == HEXIR_OK
+                       ? d.EventCreate(&fresh.ready, CU_EVENT_DISABLE_TIMING)
+                       : CUDA_SUCCESS;
+      if (st == HEXIR_OK && r == CUDA_SUCCESS)
+        r = d.EventRecord(fresh.ready, dev->stream);
+      if (st != HEXIR_OK || r != CUDA_SUCCESS) {
+        d.StreamSynchronize(dev->stream);
+        if (fresh.ready)
+          d.EventDestroy(fresh.ready);
+        d.MemFree(fresh.ptr);
+        delete b;
+        if (st == HEXIR_OK)
+          report(cuda_message("resident constant upload", r));
+        return st == HEXIR_OK ? HEXIR_ERROR_DEVICE : st;
+      }
+      ms->resident.push_back(fresh);
+      rc = &ms->resident.back();
+    } else if (d.StreamWaitEvent(dev->stream, rc->ready, 0) != CUDA_SUCCESS) {
+      delete b;
+      return HEXIR_ERROR_DEVICE;
+    }
+    b->device = dev;
+    b->size = s.bytes;
+    b->memory = HEXIR_MEMORY_DEVICE_LOCAL;
+    b->impl = reinterpret_cast<void *>(rc->ptr);
+    b->borrowed = true;
+    s.dev[o] = b;
+    s.dev_valid.insert(o);
+    *out = rc->ptr;
+    *done = true;
+    return HEXIR_OK;
+  }
+
+  // Resident copies are shared by every execute: a slot that is about to be
+  // written lets go of them first (they stay with the module).
+  static void drop_borrowed(Slot &s) {
+    for (auto it = s.dev.begin(); it != s.dev.end();) {
+      if (it->second->borrowed) {
+        s.dev_valid.erase(it->first);
+        delete it->second;
+        it = s.dev.erase(it);
+      } else {
+        ++it;
+      }
+    }
+  }
+
+  // A buffer of slot s on GPU o that may be written.
+  hexir_status_t writable_on(Slot &s, int o, uint64_t bytes, CUdeviceptr *out) {
+    auto it = s.dev.find(o);
+    if (it != s.dev.end() && it->second->borrowed) {
+      s.dev_valid.erase(o);
+      delete it->second;
+      s.dev.erase(it);
+    }
+    return buffer_on(s, o, bytes, out);
+  }
+
   // Make slot s valid on GPU o and return its address there.
   hexir_status_t on_device(Slot &s, int o, CUdeviceptr *out) {
-    hexir_status_t st = buffer_on(s, o, s.bytes, out);
+    bool resident = false;
+    hexir_status_t st = resident_on(s, o, out, &resident);
+    if (st != HEXIR_OK || resident)
+      return st;
+    st = buffer_on(s, o, s.bytes, out);
     if (st != HEXIR_OK || s.dev_valid.count(o))
       return st;
     st = copy_range_to(s, 0, s.bytes, o, *out);
@@ -381,6 +537,7 @@ struct Vm {
 
   // The destination of a dispatch becomes valid only where it is written.
   void written_on_device(Slot &s, int o) {
+    drop_borrowed(s);
     s.zero = false;
     s.rodata = nullptr;
     s.host_valid = false;
@@ -388,6 +545,7 @@ struct Vm {
     s.dev_valid.insert(o);
   }
   double *written_on_host(Slot &s) {
+    drop_borrowed(s);
     s.host.resize((s.bytes + 7) / 8);
     s.zero = false;
     s.rodata = nullptr;
@@ -530,8 +688,11 @@ struct Vm {
     Slot &dst = *args[2];
     if (&dst == args[0] || &dst == args[1] || exe.m < kPipelineChunks * 256)
       return false;
+    // A constant the module keeps on the device is uploaded whole, once.
+    ModuleState *ms = a.rodata ? module_state(module) : nullptr;
+    const bool kept = ms && ms->keep_constants.load();
     *upload_a = !a.dev_valid.count(o) && !a.zero && (a.rodata || a.host_valid) &&
-                a.bytes >= kPipelineBytes;
+                a.bytes >= kPipelineBytes && !kept;
     *stream_out = capture_out && capture_size && current_pc == last_dispatch_pc &&
                   dst.bytes >= kPipelineBytes;
     return *upload_a || *stream_out;
@@ -550,9 +711,9 @@ struct Vm {
     CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
     hexir_status_t st = on_device(*args[1], o, &w_dev);
     if (st == HEXIR_OK)
-      st = upload_a ? buffer_on(as, o, as.bytes, &a_dev) : on_device(as, o, &a_dev);
+      st = upload_a ? writable_on(as, o, as.bytes, &a_dev) : on_device(as, o, &a_dev);
     if (st == HEXIR_OK)
-      st = buffer_on(dst, o, dst.bytes, &c_dev);
+      st = writable_on(dst, o, dst.bytes, &c_dev);
     if (st != HEXIR_OK)
       return st;
     CUstream cs = dev->copy_stream();
@@ -674,7 +835,7 @@ struct Vm {
       if ((st = temp_on(o, dst.bytes, &tmp)) != HEXIR_OK)
         return st;
       out = tmp;
-    } else if ((st = buffer_on(dst, o, dst.bytes, &out)) != HEXIR_OK) {
+    } else if ((st = writable_on(dst, o, dst.bytes, &out)) != HEXIR_OK) {
       return st;
     }
     std::string error;
@@ -706,7 +867,7 @@ struct Vm {
     if (out != reinterpret_cast<CUdeviceptr>(dst.dev.count(o) ? dst.dev[o]->impl
                                                               : nullptr)) {
       CUdeviceptr home = 0;
-      if ((st = buffer_on(dst, o, dst.bytes, &home)) != HEXIR_OK)
+      if ((st = writable_on(dst, o, dst.bytes, &home)) != HEXIR_OK)
         return st;
       driver().MemcpyDtoDAsync(home, out, dst.bytes, dev->stream);
     }
@@ -751,11 +912,14 @@ struct Vm {
       if ((st = on_device(ws, first, &w[0])) != HEXIR_OK)
         return st;
       bool everywhere = true;
-      for (int r = 1; r < count; ++r) {
-        if ((st = buffer_on(ws, first + r, ws.bytes, &w[r])) != HEXIR_OK)
-          return st;
+      for (int r = 1; r < count; ++r)
         everywhere &= ws.dev_valid.count(first + r) > 0;
-      }
+      // The broadcast writes every peer's copy, so those must be writable.
+      for (int r = 1; r < count; ++r)
+        if ((st = everywhere ? buffer_on(ws, first + r, ws.bytes, &w[r])
+                             : writable_on(ws, first + r, ws.bytes, &w[r])) !=
+            HEXIR_OK)
+          return st;
       if (!everywhere) {
         const size_t elemsw = static_cast<size_t>(exe.k) * exe.n;
         nc.GroupStart();
@@ -774,7 +938,7 @@ struct Vm {
     }
 
     CUdeviceptr c_root = 0;
-    if ((st = buffer_on(dst, first, dst.bytes, &c_root)) != HEXIR_OK)
+    if ((st = writable_on(dst, first, dst.bytes, &c_root)) != HEXIR_OK)
       return st;
     const uint64_t row_in = matmul ? static_cast<uint64_t>(exe.k) * 8
                                    : static_cast<uint64_t>(exe.n) * 8;
@@ -955,7 +1119,7 @@ struct Vm {
         CUdeviceptr p = 0;
         hexir_status_t st;
         if (i + 1 == argc) {
-          st = buffer_on(*args[i], 0, args[i]->bytes, &p);
+          st = writable_on(*args[i], 0, args[i]->bytes, &p);
           if (st == HEXIR_OK && !args[i]->dev_valid.count(0))
             st = copy_range_to(*args[i], 0, args[i]->bytes, 0, p);
         } else {
@@ -1296,5 +1460,29 @@ hexir_status_t hexir_execute_devices(const hexir_module_t *module,
 }
 
 double hexir_last_execute_kernel_ms(void) { return g_last_kernel_ms; }
+
+hexir_status_t hexir_module_keep_constants(hexir_module_t *module, int enable) {
+  if (!module)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  ModuleState *ms = module_state(module);
+  if (!ms)
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  std::lock_guard<std::mutex> lock(ms->mu);
+  ms->keep_constants.store(enable != 0);
+  if (!enable)
+    ms->drop_resident();
+  return HEXIR_OK;
+}
+
+size_t hexir_module_kept_bytes(const hexir_module_t *module) {
+  ModuleState *ms = module_state(module);
+  if (!ms)
+    return 0;
+  std::lock_guard<std::mutex> lock(ms->mu);
+  size_t total = 0;
+  for (const ResidentConst &rc : ms->resident)
+    total += rc.bytes;
+  return total;
+}
 
 }  // extern "C"

@@ -39,8 +39,9 @@ hexir_status_t hexir_execute_capture(const hexir_module_t *module,
  * A kernel placed on cuda:N needs N < device_count; a row-sharded kernel
  * needs its whole ordinal range.  cpu-placed kernels run on the host.  Row
  * sharding uses NCCL (libnccl.so.2, loaded on first use) to broadcast the
- * weight from the first device of the range and to gather the output rows
- * back to it. */
+ * weight from the first device of the range; the output rows land on that
+ * device through peer stores from each GPU's kernel (NCCL send/receive where
+ * peer access is unavailable). */
 hexir_status_t hexir_execute_devices(const hexir_module_t *module,
                                      hexir_device_t *const *devices,
                                      unsigned device_count, const char *entry,
@@ -50,6 +51,20 @@ hexir_status_t hexir_execute_devices(const hexir_module_t *module,
  * in milliseconds, summed over dispatches (CUDA events around each DISPATCH
  * on the launching stream).  0 when nothing ran on a GPU. */
 double hexir_last_execute_kernel_ms(void);
+
+/* extension: keep the module's constants on the device between executes.
+ * With `enable` set, the first execute that needs a CONST on a GPU uploads it
+ * into memory that stays with the module, and later executes of the module
+ * on that GPU (through any device object, from any thread) read it there
+ * instead of copying RODATA again; the reference re-uploads every constant
+ * on every execute (runtime/src/vm/interpreter.c:300-315).  A dispatch
+ * whose destination is a CONST slot writes a private buffer, never the kept
+ * copy.  `enable` = 0 frees the kept copies (after the GPUs finish with
+ * them), as does hexir_module_release.  Off by default. */
+hexir_status_t hexir_module_keep_constants(hexir_module_t *module, int enable);
+
+/* extension: bytes of constants currently kept on GPUs for `module`. */
+size_t hexir_module_kept_bytes(const hexir_module_t *module);
 
 #ifdef __cplusplus
 }

@@ -10,6 +10,7 @@ max|c - c_ref| / max|c_ref| <= 1e-12.
 import json
 import os
 import shutil
+import struct
 import subprocess
 
 import numpy as np
@@ -316,3 +317,73 @@ def test_hexir_bench_tool_verifies_and_times(tmp_path):
     assert line["e2e_ms"] > 0 and line["kernel_ms"] > 0
     assert line["cublas_ms"] > 0
 
+
+
+def test_kept_constants_are_reused_and_bit_identical():
+    """hexir_module_keep_constants: the first execute uploads a and w into
+    memory kept with the module; later executes (also through another device
+    object for the same GPU) reuse it and give the same bits."""
+    r = hx.Rng(41)
+    a = r.uniform((1000, 512))
+    w = r.uniform((512, 384))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    mod = hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    dev = hx.Device("cuda")
+    base = hx.execute(mod, dev, out_shape=(1000, 384))
+    assert mod.kept_bytes == 0
+    mod.keep_constants(True)
+    first = hx.execute(mod, dev, out_shape=(1000, 384))
+    assert mod.kept_bytes == a.nbytes + w.nbytes
+    second = hx.execute(mod, dev, out_shape=(1000, 384))
+    other = hx.Device("cuda:0")
+    third = hx.execute(mod, other, out_shape=(1000, 384))
+    assert mod.kept_bytes == a.nbytes + w.nbytes
+    for out in (first, second, third):
+        assert np.array_equal(bits(out), bits(base))
+    assert oracle.normwise_error(base, oracle.relu(oracle.matmul(a, w))) <= TOL
+    mod.keep_constants(False)
+    assert mod.kept_bytes == 0
+    assert np.array_equal(bits(hx.execute(mod, dev, out_shape=(1000, 384))),
+                          bits(base))
+    other.close()
+    mod.close()
+
+
+def _dispatch_into_constant_slot(blob: bytes) -> bytes:
+    """The module with its first DISPATCH's destination replaced by the slot
+    of its first operand (a CONST): the serializer never emits this, a
+    hand-made module can."""
+    sections = hx.read_sections(blob)
+    poff, _ = sections[2]
+    out = bytearray(blob)
+    pc = 0
+    while True:
+        kind, argc = struct.unpack_from("<II", blob, poff + pc)
+        if kind == 3:  # DISPATCH: index, argc, args...
+            ops = struct.unpack_from(f"<{argc}Q", blob, poff + pc + 8)
+            struct.pack_into("<Q", out, poff + pc + 8 + 8 * (argc - 1), ops[2])
+            return bytes(out)
+        assert kind != 0
+        pc += 8 + 8 * argc
+
+
+def test_dispatch_into_a_kept_constant_never_changes_it():
+    """A dispatch whose destination is a CONST slot writes a private buffer:
+    the kept copy, and so the next execute, still see the module's bytes."""
+    r = hx.Rng(42)
+    a = r.uniform((256, 256))
+    w = r.uniform((256, 256))
+    p = hx.Program()
+    p.linear(p.constant(a), p.constant(w))
+    blob = _dispatch_into_constant_slot(p.emit("hexir.linear=cuda"))
+    mod = hx.Module(blob)
+    mod.keep_constants(True)
+    dev = hx.Device("cuda")
+    want = oracle.matmul(a, w)
+    outs = [hx.execute(mod, dev, out_shape=(256, 256)) for _ in range(3)]
+    for out in outs:
+        assert oracle.normwise_error(out, want) <= TOL
+        assert np.array_equal(bits(out), bits(outs[0]))
+    assert mod.kept_bytes == a.nbytes + w.nbytes
+    mod.close()

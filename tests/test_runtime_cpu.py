@@ -233,3 +233,17 @@ def test_random_byte_flips_never_crash(tmp_path):
             blob[pos] = int(rng.integers(0, 256))
         res = run_blob(blob, tmp_path)
         assert res.returncode in (0, 1), res.stderr  # never a signal
+
+
+def test_keep_constants_on_a_cpu_run_keeps_nothing():
+    """hexir_module_keep_constants only concerns GPU copies: a CPU execute is
+    unchanged and keeps no bytes; the call checks its argument."""
+    p = known_program(GOLDEN["known_answers"][1])
+    mod = hx.Module(p.emit())
+    mod.keep_constants(True)
+    for _ in range(2):
+        out = hx.execute(mod, hx.Device("cpu"), out_shape=(2, 2))
+        assert np.array_equal(out, [[9.0, 22.0], [17.0, 16.0]])
+    assert mod.kept_bytes == 0
+    mod.keep_constants(False)
+    assert hx.lib().hexir_module_keep_constants(None, 1) == _ffi.ERROR_INVALID_ARGUMENT
