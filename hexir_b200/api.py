@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes as C
 import struct
+import weakref
 from dataclasses import dataclass
 from typing import Iterable, List, Optional, Sequence
 
@@ -289,6 +290,9 @@ class Device:
         check(st, f"hexir_device_create({spec})")
         self._h = h.value
         self.spec = spec
+        # Buffers still alive when the device closes are released first (a
+        # buffer must not outlive its device in the C ABI).
+        self._buffers = weakref.WeakSet()
 
     @property
     def handle(self) -> int:
@@ -311,6 +315,8 @@ class Device:
 
     def close(self) -> None:
         if getattr(self, "_h", None):
+            for b in list(getattr(self, "_buffers", ())):
+                b.close()
             lib().hexir_device_release(self._h)
             self._h = None
 
@@ -337,6 +343,7 @@ class Buffer:
         self._h = h.value
         self.device = device
         self.nbytes = nbytes
+        device._buffers.add(self)
 
     @property
     def ptr(self) -> int:
@@ -399,6 +406,16 @@ def cuda_matmul(ordinal: int, a: int, b: int, c: int, m: int, n: int, k: int,
     """c = a . b on device pointers (hexir_cuda_matmul_f64)."""
     check(lib().hexir_cuda_matmul_f64(ordinal, a, b, c, m, n, k, flags,
                                       stream or None), "hexir_cuda_matmul_f64")
+
+
+def cuda_matmul_acc(ordinal: int, a: int, lda: int, b: int, c_in: int, c: int,
+                    m: int, n: int, k: int, flags: int = 0,
+                    stream: int = 0) -> None:
+    """c = epilogue(c_in + a . b) with a's row stride lda
+    (hexir_cuda_matmul_acc_f64); c_in 0 starts the sums at zero."""
+    check(lib().hexir_cuda_matmul_acc_f64(ordinal, a, lda, b, c_in or None, c,
+                                          m, n, k, flags, stream or None),
+          "hexir_cuda_matmul_acc_f64")
 
 
 def cuda_relu(ordinal: int, x: int, y: int, n: int, stream: int = 0) -> None:

@@ -67,6 +67,14 @@ typedef struct {
   uint32_t k_tiles_per_split;
   unsigned int *error;   /* device error word */
   uint64_t timeout_ns;   /* bound on every pipeline wait */
+  /* Non-null: each element's sum starts from c_in (same [m][n] layout as c,
+   * may equal c) instead of 0.0, so a product computed over consecutive k
+   * ranges, each launch continuing from the last one's output, performs the
+   * same operations in the same order as one launch over all of k.  Only
+   * with split_k == 1. */
+  const double *c_in;
+  uint32_t lda;          /* row stride of a in elements (>= k) */
+  uint32_t reserved;
 } hexir_linear_args_t;
 
 typedef struct {

@@ -136,6 +136,50 @@ __device__ __forceinline__ void store_warp_tile(
   }
 }
 
+// Start a warp tile's sums from c_in: the inverse of store_warp_tile's
+// mapping (elements outside m x n stay 0 and are never stored).
+template <int MI, int NP, bool VEC>
+__device__ __forceinline__ void load_warp_tile(
+    double (&acc)[MI][2 * NP][4], const double *__restrict__ c_in, uint32_t m,
+    uint32_t n, uint32_t row0, uint32_t col0, uint32_t g, uint32_t t) {
+#pragma unroll
+  for (int mi = 0; mi < MI; ++mi) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t row = row0 + mi * 16 + g + half * 8;
+      if (row >= m)
+        continue;
+      const double *crow = c_in + (size_t)row * n;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const uint32_t col = col0 + p * 16 + 4 * t;
+        double v[4] = {0.0, 0.0, 0.0, 0.0};
+        if (VEC) {
+          if (col < n) {
+            const double2 x = *reinterpret_cast<const double2 *>(crow + col);
+            v[0] = x.x;
+            v[1] = x.y;
+          }
+          if (col + 2 < n) {
+            const double2 x = *reinterpret_cast<const double2 *>(crow + col + 2);
+            v[2] = x.x;
+            v[3] = x.y;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (col + q < n)
+              v[q] = crow[col + q];
+        }
+        acc[mi][2 * p][2 * half] = v[0];
+        acc[mi][2 * p + 1][2 * half] = v[1];
+        acc[mi][2 * p][2 * half + 1] = v[2];
+        acc[mi][2 * p + 1][2 * half + 1] = v[3];
+      }
+    }
+  }
+}
+
 }  // namespace hexir
 
 using namespace hexir;
@@ -240,6 +284,9 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         acc[i][j][q] = 0.0;
+  if (args.c_in)
+    load_warp_tile<MI, NP, true>(acc, args.c_in, args.m, args.n,
+                                 m0 + wm * T::WTM, n0 + wn * T::WTN, g, t);
 
   const uint32_t sa_addr = smem_addr(sa), sb_addr = smem_addr(sb);
   bool ok = true;
@@ -353,6 +400,7 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
   const uint32_t kt_end = min(k_tiles, kt_begin + args.k_tiles_per_split);
   const uint32_t m0 = tm * BM, n0 = tn * BN;
   const uint32_t m = args.m, n = args.n, k = args.k;
+  const size_t lda = args.lda ? args.lda : k;
   const double *__restrict__ a = args.a;
   const double *__restrict__ b = args.b;
 
@@ -364,7 +412,7 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
       const uint32_t e = tid + i * HEXIR_LINEAR_G_THREADS;
       const uint32_t row = e / BK, kc = e % BK;
       const uint32_t gr = m0 + row, gk = k0 + kc;
-      ra[i] = (gr < m && gk < k) ? a[(size_t)gr * k + gk] : 0.0;
+      ra[i] = (gr < m && gk < k) ? a[(size_t)gr * lda + gk] : 0.0;
     }
 #pragma unroll
     for (int i = 0; i < PER_THREAD_B; ++i) {
@@ -400,6 +448,9 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         acc[i][j][q] = 0.0;
+  if (args.c_in)
+    load_warp_tile<2, 2, false>(acc, args.c_in, m, n, m0 + wm * 32,
+                                n0 + wn * 32, g, t);
 
   if (kt_begin < kt_end) {
     load_tile(kt_begin);

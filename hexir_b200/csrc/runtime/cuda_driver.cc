@@ -66,6 +66,7 @@ void load() {
             bind(lib, d.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2", e) &&
             bind(lib, d.MemcpyDtoHAsync, "cuMemcpyDtoHAsync_v2", e) &&
             bind(lib, d.MemcpyDtoDAsync, "cuMemcpyDtoDAsync_v2", e) &&
+            bind(lib, d.Memcpy2DAsync, "cuMemcpy2DAsync_v2", e) &&
             bind(lib, d.MemcpyPeerAsync, "cuMemcpyPeerAsync", e) &&
             bind(lib, d.MemsetD8Async, "cuMemsetD8Async", e) &&
             bind(lib, d.PointerGetAttribute, "cuPointerGetAttribute", e) &&

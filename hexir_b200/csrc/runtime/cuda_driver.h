@@ -46,6 +46,7 @@ struct Driver {
   CUresult (*MemcpyDtoHAsync)(void *, CUdeviceptr, size_t, CUstream) = nullptr;
   CUresult (*MemcpyDtoDAsync)(CUdeviceptr, CUdeviceptr, size_t, CUstream) =
       nullptr;
+  CUresult (*Memcpy2DAsync)(const CUDA_MEMCPY2D *, CUstream) = nullptr;
   CUresult (*MemcpyPeerAsync)(CUdeviceptr, CUcontext, CUdeviceptr, CUcontext,
                               size_t, CUstream) = nullptr;
   CUresult (*MemsetD8Async)(CUdeviceptr, unsigned char, size_t, CUstream) =

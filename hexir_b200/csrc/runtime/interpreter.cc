@@ -671,35 +671,72 @@ struct Vm {
     return HEXIR_OK;
   }
 
-  // A large matmul whose `a` still lives on the host, or whose result is the
-  // one being captured, runs as a pipeline of row chunks: chunk i of `a`
-  // uploads on the device's copy stream while chunk i-1 computes, and each
-  // finished chunk of the result copies out to the capture buffer on the
-  // copy stream while the next chunk computes.  Same kernels, same per-row
-  // arithmetic as the one-shot launch.
+  // A large matmul whose operands still live on the host, or whose result is
+  // the one being captured, runs as a pipeline on two streams: uploads on the
+  // device's copy stream, kernels on its main stream, downloads of finished
+  // rows on the copy stream.
+  //   - Weight still on the host (and the one-shot launch has no k split):
+  //     phase 1 runs k in [0, K1) over all rows in pieces of growing length,
+  //     each piece's rows of w (and columns of a) uploading while the
+  //     previous piece computes, every launch continuing the previous one's
+  //     sums; phase 2 runs k in [K1, K) per row chunk, continuing from phase
+  //     1, with the relu, and each finished chunk downloads while the next
+  //     computes.  Only the first, short piece's upload and the last chunk's
+  //     download are exposed.
+  //   - Otherwise: w whole first, then row chunks of a upload while the
+  //     previous chunk computes, and finished chunks download.
+  // Both perform each element's operations in the one-shot order (no k
+  // split, or the one-shot's own split for every row chunk), so results are
+  // bit-identical to a single launch.
   static constexpr uint64_t kPipelineBytes = 64ull << 20;
   static constexpr uint32_t kPipelineChunks = 4;
+  static constexpr uint32_t kPieceMinK = 2048;
+
+  // Slot s's bytes are on the host and would be uploaded by this dispatch.
+  bool host_upload(const Slot &s, int o) {
+    ModuleState *ms = s.rodata ? module_state(module) : nullptr;
+    const bool kept = ms && ms->keep_constants.load();  // uploaded once, whole
+    return !s.dev_valid.count(o) && !s.zero && (s.rodata || s.host_valid) &&
+           s.bytes >= kPipelineBytes && !kept;
+  }
 
   bool want_pipeline(const hexir_executable_entry_t &exe, Slot *const *args,
-                     int o, bool *upload_a, bool *stream_out) {
+                     int o, bool *upload_a, bool *upload_w, bool *stream_out) {
     if (exe.kind != HEXIR_KERNEL_MATMUL && exe.kind != HEXIR_KERNEL_MATMUL_RELU)
       return false;
-    Slot &a = *args[0];
     Slot &dst = *args[2];
-    if (&dst == args[0] || &dst == args[1] || exe.m < kPipelineChunks * 256)
+    if (&dst == args[0] || &dst == args[1] || args[0] == args[1] ||
+        exe.m < kPipelineChunks * 256)
       return false;
-    // A constant the module keeps on the device is uploaded whole, once.
-    ModuleState *ms = a.rodata ? module_state(module) : nullptr;
-    const bool kept = ms && ms->keep_constants.load();
-    *upload_a = !a.dev_valid.count(o) && !a.zero && (a.rodata || a.host_valid) &&
-                a.bytes >= kPipelineBytes && !kept;
+    *upload_a = host_upload(*args[0], o);
+    *upload_w = host_upload(*args[1], o) && exe.k >= kPieceMinK;
     *stream_out = capture_out && capture_size && current_pc == last_dispatch_pc &&
                   dst.bytes >= kPipelineBytes;
-    return *upload_a || *stream_out;
+    return *upload_a || *upload_w || *stream_out;
+  }
+
+  // Bounds of phase 1's k pieces over [0, k1): 256 first, then each piece at
+  // most 256 + 0.7 x the k done so far (rounded to the 32-wide k tile), so a
+  // piece's upload (a column slice plus w rows, ~2.25 ms per 1024 k at 8192
+  // rows and columns over PCIe) ends before the previous pieces' compute
+  // (~3.9 ms per 1024 k) does.
+  static std::vector<uint32_t> k_piece_bounds(uint32_t k1) {
+    std::vector<uint32_t> b{0};
+    const uint32_t first = std::min<uint32_t>(256, k1);
+    uint32_t done = 0;
+    while (done < k1) {
+      uint32_t len = done == 0 ? first : (first + done * 7 / 10) / 32 * 32;
+      len = std::max<uint32_t>(len, 32);
+      if (done + len >= k1 || k1 - (done + len) < len / 2)
+        len = k1 - done;
+      done += len;
+      b.push_back(done);
+    }
+    return b;
   }
 
   hexir_status_t run_pipelined(uint32_t index, int o, Slot *const *args,
-                               bool upload_a, bool stream_out) {
+                               bool upload_a, bool upload_w, bool stream_out) {
     const hexir_executable_entry_t &exe = exes[index];
     KernelLib *lib = library(index, o);
     if (!lib)
@@ -707,15 +744,30 @@ struct Vm {
     CudaDevice *dev = cuda[o];
     const Driver &d = driver();
     Slot &as = *args[0];
+    Slot &ws = *args[1];
     Slot &dst = *args[2];
     CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
-    hexir_status_t st = on_device(*args[1], o, &w_dev);
+    hexir_status_t st = upload_w ? writable_on(ws, o, ws.bytes, &w_dev)
+                                 : on_device(ws, o, &w_dev);
     if (st == HEXIR_OK)
       st = upload_a ? writable_on(as, o, as.bytes, &a_dev) : on_device(as, o, &a_dev);
     if (st == HEXIR_OK)
       st = writable_on(dst, o, dst.bytes, &c_dev);
     if (st != HEXIR_OK)
       return st;
+    const uint32_t relu =
+        exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU : 0u;
+    const MatmulPlan whole = plan_matmul(
+        dev->state, reinterpret_cast<const double *>(a_dev),
+        reinterpret_cast<const double *>(w_dev),
+        reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k, relu);
+    const bool pieces = upload_w && whole.split_k == 1;
+    if (upload_w && !pieces) {
+      // The one-shot launch splits k: upload w whole before the row chunks.
+      if ((st = copy_range_to(ws, 0, ws.bytes, o, w_dev)) != HEXIR_OK)
+        return st;
+      ws.dev_valid.insert(o);
+    }
     CUstream cs = dev->copy_stream();
     if (!cs)
       return HEXIR_ERROR_DEVICE;
@@ -729,6 +781,10 @@ struct Vm {
       events.push_back(ev);
       return ev;
     };
+    auto release_events = [&] {
+      for (CUevent ev : events)
+        d.EventDestroy(ev);  // released once complete
+    };
     // The copy stream starts after everything queued on the main stream
     // (the buffers may be reused pool blocks).
     CUevent ready = event(dev->stream);
@@ -736,51 +792,131 @@ struct Vm {
       return HEXIR_ERROR_DEVICE;
     d.StreamWaitEvent(cs, ready, 0);
     Span *span = begin_span(dev);
-    const uint64_t row_a = static_cast<uint64_t>(exe.k) * 8;
-    const uint64_t row_c = static_cast<uint64_t>(exe.n) * 8;
+    const uint64_t K = exe.k, N = exe.n;
+    const uint64_t row_a = K * 8;
+    const uint64_t row_c = N * 8;
     uint64_t r0[kPipelineChunks], rows[kPipelineChunks];
-    std::vector<CUevent> a_ready(kPipelineChunks, nullptr);
-    for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+    for (uint32_t i = 0; i < kPipelineChunks; ++i)
       hexir_shard_rows(exe.m, kPipelineChunks, i, &r0[i], &rows[i]);
-      if (!upload_a || !rows[i])
-        continue;
-      const uint64_t off = r0[i] * row_a, bytes = rows[i] * row_a;
-      const uint8_t *src =
-          as.rodata ? rodata_source(as, off, bytes)
-                    : reinterpret_cast<const uint8_t *>(as.host.data()) + off;
-      if (d.MemcpyHtoDAsync(a_dev + off, src, bytes, cs) != CUDA_SUCCESS)
-        return HEXIR_ERROR_DEVICE;
-      a_ready[i] = event(cs);
-    }
-    std::string error;
-    std::vector<CUevent> c_ready(kPipelineChunks, nullptr);
-    // Every chunk uses the k split the whole matmul would use, so each
-    // element is summed exactly as by the one-shot launch (chunks of >= 256
-    // rows keep the same 128-row tile kernel).
-    uint32_t flags = exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU : 0u;
-    const MatmulPlan whole = plan_matmul(
-        dev->state, reinterpret_cast<const double *>(a_dev),
-        reinterpret_cast<const double *>(w_dev),
-        reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k, flags);
-    flags |= HEXIR_MATMUL_SPLIT_K(whole.split_k);
-    for (uint32_t i = 0; i < kPipelineChunks; ++i) {
-      if (!rows[i])
-        continue;
-      if (a_ready[i])
-        d.StreamWaitEvent(dev->stream, a_ready[i], 0);
-      st = launch_matmul(
-          dev->state, lib,
-          reinterpret_cast<const double *>(a_dev + r0[i] * row_a),
-          reinterpret_cast<const double *>(w_dev),
-          reinterpret_cast<double *>(c_dev + r0[i] * row_c),
-          static_cast<uint32_t>(rows[i]), exe.n, exe.k, flags, dev->stream,
-          &error);
-      if (st != HEXIR_OK) {
+    auto host_bytes = [&](Slot &s, uint64_t off, uint64_t bytes) {
+      return s.rodata ? rodata_source(s, off, bytes)
+                      : reinterpret_cast<const uint8_t *>(s.host.data()) + off;
+    };
+    // Uploads of w's rows [k0, k1) and of a's columns [k0, k1) for rows
+    // [ra, ra + nr), on the copy stream.
+    auto upload_w_rows = [&](uint64_t k0, uint64_t k1) -> bool {
+      const uint64_t off = k0 * row_c, bytes = (k1 - k0) * row_c;
+      return d.MemcpyHtoDAsync(w_dev + off, host_bytes(ws, off, bytes), bytes,
+                               cs) == CUDA_SUCCESS;
+    };
+    auto upload_a_cols = [&](uint64_t ra, uint64_t nr, uint64_t k0,
+                             uint64_t k1) -> bool {
+      if (!nr)
+        return true;
+      CUDA_MEMCPY2D cp;
+      std::memset(&cp, 0, sizeof(cp));
+      cp.srcMemoryType = CU_MEMORYTYPE_HOST;
+      cp.srcHost = host_bytes(as, ra * row_a, nr * row_a) + k0 * 8;
+      cp.srcPitch = row_a;
+      cp.dstMemoryType = CU_MEMORYTYPE_DEVICE;
+      cp.dstDevice = a_dev + ra * row_a + k0 * 8;
+      cp.dstPitch = row_a;
+      cp.WidthInBytes = (k1 - k0) * 8;
+      cp.Height = nr;
+      return d.Memcpy2DAsync(&cp, cs) == CUDA_SUCCESS;
+    };
+    auto fail_copy = [&]() {
+      report("host to device copy failed (pipelined dispatch)");
+      release_events();
+      return HEXIR_ERROR_DEVICE;
+    };
+    auto launch = [&](uint64_t ra, uint64_t nr, uint64_t k0, uint64_t k1,
+                      uint32_t flags, bool cont) -> hexir_status_t {
+      std::string error;
+      double *c = reinterpret_cast<double *>(c_dev + ra * row_c);
+      hexir_status_t ls = launch_matmul(
+          dev->state, lib, reinterpret_cast<const double *>(a_dev + ra * row_a + k0 * 8),
+          reinterpret_cast<const double *>(w_dev + k0 * row_c), c,
+          static_cast<uint32_t>(nr), exe.n, static_cast<uint32_t>(k1 - k0),
+          flags | HEXIR_MATMUL_SPLIT_K(1), dev->stream, &error, exe.k,
+          cont ? c : nullptr);
+      if (ls != HEXIR_OK)
         report(std::string("kernel '") + exe.name + "': " + error);
-        return st;
+      return ls;
+    };
+    std::vector<CUevent> c_ready(kPipelineChunks, nullptr);
+    if (pieces) {
+      const uint64_t k1 = K / 2 / 32 * 32;
+      const std::vector<uint32_t> b = k_piece_bounds(static_cast<uint32_t>(k1));
+      std::vector<CUevent> piece_ready;
+      for (size_t j = 0; j + 1 < b.size(); ++j) {
+        if (!upload_w_rows(b[j], b[j + 1]) ||
+            (upload_a && !upload_a_cols(0, exe.m, b[j], b[j + 1])))
+          return fail_copy();
+        piece_ready.push_back(event(cs));
       }
-      if (stream_out)
-        c_ready[i] = event(dev->stream);
+      if (!upload_w_rows(k1, K))
+        return fail_copy();
+      std::vector<CUevent> chunk_ready(kPipelineChunks, nullptr);
+      CUevent w_ready = event(cs);
+      for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+        if (upload_a && !upload_a_cols(r0[i], rows[i], k1, K))
+          return fail_copy();
+        chunk_ready[i] = upload_a ? event(cs) : w_ready;
+      }
+      for (size_t j = 0; j + 1 < b.size(); ++j) {
+        d.StreamWaitEvent(dev->stream, piece_ready[j], 0);
+        if ((st = launch(0, exe.m, b[j], b[j + 1], 0u, j > 0)) != HEXIR_OK) {
+          release_events();
+          return st;
+        }
+      }
+      for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+        if (!rows[i])
+          continue;
+        d.StreamWaitEvent(dev->stream, chunk_ready[i], 0);
+        if ((st = launch(r0[i], rows[i], k1, K, relu, k1 > 0)) != HEXIR_OK) {
+          release_events();
+          return st;
+        }
+        if (stream_out)
+          c_ready[i] = event(dev->stream);
+      }
+    } else {
+      std::vector<CUevent> a_ready(kPipelineChunks, nullptr);
+      for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+        if (!upload_a || !rows[i])
+          continue;
+        const uint64_t off = r0[i] * row_a, bytes = rows[i] * row_a;
+        if (d.MemcpyHtoDAsync(a_dev + off, host_bytes(as, off, bytes), bytes,
+                              cs) != CUDA_SUCCESS)
+          return fail_copy();
+        a_ready[i] = event(cs);
+      }
+      // Every chunk uses the k split the whole matmul would use, so each
+      // element is summed exactly as by the one-shot launch.
+      const uint32_t flags = relu | HEXIR_MATMUL_SPLIT_K(whole.split_k);
+      for (uint32_t i = 0; i < kPipelineChunks; ++i) {
+        if (!rows[i])
+          continue;
+        if (a_ready[i])
+          d.StreamWaitEvent(dev->stream, a_ready[i], 0);
+        std::string error;
+        st = launch_matmul(
+            dev->state, lib,
+            reinterpret_cast<const double *>(a_dev + r0[i] * row_a),
+            reinterpret_cast<const double *>(w_dev),
+            reinterpret_cast<double *>(c_dev + r0[i] * row_c),
+            static_cast<uint32_t>(rows[i]), exe.n, exe.k, flags, dev->stream,
+            &error);
+        if (st != HEXIR_OK) {
+          report(std::string("kernel '") + exe.name + "': " + error);
+          release_events();
+          return st;
+        }
+        if (stream_out)
+          c_ready[i] = event(dev->stream);
+      }
     }
     end_span(span);
     if (stream_out) {
@@ -795,8 +931,10 @@ struct Vm {
                                                   capture_size - begin);
         d.StreamWaitEvent(cs, c_ready[i], 0);
         if (d.MemcpyDtoHAsync(static_cast<uint8_t *>(capture_out) + begin,
-                              c_dev + begin, bytes, cs) != CUDA_SUCCESS)
+                              c_dev + begin, bytes, cs) != CUDA_SUCCESS) {
+          release_events();
           return HEXIR_ERROR_DEVICE;
+        }
       }
       capture_done = true;
     }
@@ -804,19 +942,20 @@ struct Vm {
     CUevent copies_done = event(cs);
     if (copies_done)
       d.StreamWaitEvent(dev->stream, copies_done, 0);
-    for (CUevent ev : events)
-      d.EventDestroy(ev);  // released once complete
+    release_events();
     if (upload_a)
       as.dev_valid.insert(o);
+    if (upload_w)
+      ws.dev_valid.insert(o);
     written_on_device(dst, o);
     return HEXIR_OK;
   }
 
   hexir_status_t run_device(uint32_t index, int o, Slot *const *args) {
     const hexir_executable_entry_t &exe = exes[index];
-    bool upload_a = false, stream_out = false;
-    if (want_pipeline(exe, args, o, &upload_a, &stream_out))
-      return run_pipelined(index, o, args, upload_a, stream_out);
+    bool upload_a = false, upload_w = false, stream_out = false;
+    if (want_pipeline(exe, args, o, &upload_a, &upload_w, &stream_out))
+      return run_pipelined(index, o, args, upload_a, upload_w, stream_out);
     KernelLib *lib = library(index, o);
     if (!lib)
       return HEXIR_ERROR_DEVICE;

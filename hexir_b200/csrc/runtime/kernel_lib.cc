@@ -262,11 +262,14 @@ KernelLib *embedded_library(DeviceState *dev, std::string *error) {
 
 MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
                        const double *c, uint32_t m, uint32_t n, uint32_t k,
-                       uint32_t flags) {
+                       uint32_t flags, uint32_t lda, const double *c_in) {
   MatmulPlan p;
-  // TMA needs 16-byte aligned bases and row strides (k, n even).
-  const bool tma_ok = (k % 2 == 0) && (n % 2 == 0) && aligned16(a) &&
-                      aligned16(b) && aligned16(c);
+  if (lda == 0)
+    lda = k;
+  // TMA needs 16-byte aligned bases and row strides (k, lda, n even).
+  const bool tma_ok = (k % 2 == 0) && (lda % 2 == 0) && (n % 2 == 0) &&
+                      aligned16(a) && aligned16(b) && aligned16(c) &&
+                      aligned16(c_in);
   if ((flags & HEXIR_MATMUL_FORCE_GUARDED) || !tma_ok) {
     p.variant = kGuarded;
     p.bm = HEXIR_LINEAR_G_BM;
@@ -284,7 +287,7 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   p.tiles_n = ceil_div(n, p.bn);
   p.k_tiles = ceil_div(k, p.bk);
   const uint64_t tiles = static_cast<uint64_t>(p.tiles_m) * p.tiles_n;
-  uint32_t split = (flags >> 16) & 0xFFu;
+  uint32_t split = c_in ? 1u : (flags >> 16) & 0xFFu;
   const uint64_t sms = dev ? static_cast<uint64_t>(std::max(dev->sm_count, 1)) : 148;
   // CTAs resident per SM: one for the 128- and 64-row TMA tiles (192 KiB of
   // shared memory), two for the 16-row tile (109 KiB), three for the guarded
@@ -339,28 +342,48 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
 hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              const double *b, double *c, uint32_t m, uint32_t n,
                              uint32_t k, uint32_t flags, CUstream stream,
-                             std::string *error) {
+                             std::string *error, uint32_t lda,
+                             const double *c_in) {
   const Driver &d = driver();
   if (m == 0 || n == 0)
     return HEXIR_OK;
   if (!a || !b || !c)
     return fail(error, "matmul: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
+  if (lda == 0)
+    lda = k;
+  if (lda < k)
+    return fail(error, "matmul: lda is smaller than k",
+                HEXIR_ERROR_INVALID_ARGUMENT);
+  if (c_in && (flags & 0xFF0000u) && ((flags >> 16) & 0xFFu) != 1)
+    return fail(error, "matmul: a continued sum cannot be split over k",
+                HEXIR_ERROR_INVALID_ARGUMENT);
   if ((flags & HEXIR_MATMUL_FORCE_TMA) &&
-      plan_matmul(dev, a, b, c, m, n, k, flags & ~HEXIR_MATMUL_FORCE_TMA)
+      plan_matmul(dev, a, b, c, m, n, k, flags & ~HEXIR_MATMUL_FORCE_TMA, lda,
+                  c_in)
               .variant == kGuarded)
     return fail(error,
-                "matmul: the TMA kernel needs even k and n and 16-byte aligned "
-                "pointers",
+                "matmul: the TMA kernel needs even k, lda and n and 16-byte "
+                "aligned pointers",
                 HEXIR_ERROR_INVALID_ARGUMENT);
   const size_t out_bytes = static_cast<size_t>(m) * n * sizeof(double);
   if (k == 0) {
-    // An empty sum is 0 and relu(0) = 0.
-    CUresult r = d.MemsetD8Async(reinterpret_cast<CUdeviceptr>(c), 0, out_bytes,
-                                 stream);
+    // An empty sum is 0 (or c_in) and relu(0) = 0.
+    CUresult r;
+    if (!c_in) {
+      r = d.MemsetD8Async(reinterpret_cast<CUdeviceptr>(c), 0, out_bytes, stream);
+    } else if (!(flags & HEXIR_MATMUL_RELU)) {
+      r = c_in == c ? CUDA_SUCCESS
+                    : d.MemcpyDtoDAsync(reinterpret_cast<CUdeviceptr>(c),
+                                        reinterpret_cast<CUdeviceptr>(c_in),
+                                        out_bytes, stream);
+    } else {
+      return launch_relu(dev, lib, c_in, c, static_cast<size_t>(m) * n, stream,
+                         error);
+    }
     return r == CUDA_SUCCESS ? HEXIR_OK
-                             : fail(error, cuda_message("cuMemsetD8Async", r));
+                             : fail(error, cuda_message("empty matmul", r));
   }
-  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags);
+  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in);
 
   hexir_linear_args_t args;
   std::memset(&args, 0, sizeof(args));
@@ -381,6 +404,8 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   args.k_tiles_per_split = p.k_tiles_per_split;
   args.error = reinterpret_cast<unsigned int *>(lib->error_word);
   args.timeout_ns = kWaitTimeoutNs;
+  args.c_in = c_in;
+  args.lda = lda;
 
   std::unique_lock<std::mutex> ws_lock(dev->mu, std::defer_lock);
   if (p.split_k > 1) {
@@ -399,7 +424,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   if (p.variant != kGuarded) {
     CUtensorMap map_a, map_b;
     const cuuint64_t a_dims[2] = {k, m};
-    const cuuint64_t a_strides[1] = {static_cast<cuuint64_t>(k) * 8};
+    const cuuint64_t a_strides[1] = {static_cast<cuuint64_t>(lda) * 8};
     const cuuint32_t a_box[2] = {8, p.bm};
     const cuuint64_t b_dims[2] = {n, k};
     const cuuint64_t b_strides[1] = {static_cast<cuuint64_t>(n) * 8};
@@ -555,6 +580,26 @@ extern "C" hexir_status_t hexir_cuda_matmul_f64(int ordinal, const double *a,
   ContextGuard guard(call.dev->context);
   return call.finish(launch_matmul(call.dev, call.lib, a, b, c, m, n, k, flags,
                                    static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_matmul_acc_f64(
+    int ordinal, const double *a, uint32_t lda, const double *b,
+    const double *c_in, double *c, uint32_t m, uint32_t n, uint32_t k,
+    uint32_t flags, void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  // Never split over k, with or without c_in: every piece of a product
+  // computed in k ranges must sum its range in one pass.
+  if (((flags >> 16) & 0xFFu) > 1) {
+    call.error = "matmul: a continued sum cannot be split over k";
+    return call.finish(HEXIR_ERROR_INVALID_ARGUMENT);
+  }
+  flags = (flags & ~0xFF0000u) | HEXIR_MATMUL_SPLIT_K(1);
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_matmul(call.dev, call.lib, a, b, c, m, n, k, flags,
+                                   static_cast<CUstream>(stream), &call.error,
+                                   lda, c_in));
 }
 
 extern "C" hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,

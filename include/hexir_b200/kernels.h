@@ -54,6 +54,22 @@ hexir_status_t hexir_cuda_matmul_f64(int ordinal, const double *a,
                                      uint32_t n, uint32_t k, uint32_t flags,
                                      void *stream);
 
+/* c = epilogue(c_in + a . b), with a's rows `lda` elements apart (lda >= k,
+ * 0 = k) and c_in NULL (sums start at 0), equal to c, or another [m x n]
+ * buffer.  Extension, no reference counterpart: it lets a product be
+ * computed over consecutive k ranges -- a + k0 with lda = K, b + k0 * n,
+ * each call continuing from the previous one's c -- while the next range of
+ * the operands is still being copied or broadcast.  This call never splits
+ * its k range (HEXIR_MATMUL_SPLIT_K(S) with S > 1 is refused), so the pieces
+ * perform exactly the operations of one hexir_cuda_matmul_f64 call over all
+ * of K whose plan has no k split (k0 a multiple of 32), and the result has
+ * the same bits; HEXIR_MATMUL_RELU belongs on the last piece only. */
+hexir_status_t hexir_cuda_matmul_acc_f64(int ordinal, const double *a,
+                                         uint32_t lda, const double *b,
+                                         const double *c_in, double *c,
+                                         uint32_t m, uint32_t n, uint32_t k,
+                                         uint32_t flags, void *stream);
+
 /* c[i] = a[i] + b[i] for i < n.  Replaces hexir_ref_add_f64
  * (runtime/src/kernels/reference_kernels.c:15). */
 hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,

@@ -218,3 +218,63 @@ def test_launch_counter_counts(gpu):
     before = hx.launch_count()
     run_matmul(gpu, np.ones((4, 4)), np.ones((4, 4)))
     assert hx.launch_count() > before
+
+
+@pytest.mark.parametrize("m,n,k,cuts,force", [
+    (1000, 384, 1024, [256, 512, 768], 0),
+    (1000, 384, 1000, [256, 512, 768], 0),         # ragged last piece
+    (40, 264, 2048, [1024], 0),                    # 64-row tile
+    (9, 264, 512, [128, 384], 0),                  # 16-row tile
+    (77, 131, 301, [64, 160], _ffi.MATMUL_FORCE_GUARDED),
+])
+def test_matmul_over_k_pieces_is_bit_identical(gpu, m, n, k, cuts, force):
+    """hexir_cuda_matmul_acc_f64 over consecutive k ranges (a + k0 with
+    lda = K, b + k0 * n, each piece continuing from c, relu on the last) gives
+    the bits of one unsplit launch over all of k."""
+    rng = np.random.default_rng(m + 7 * k)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    whole = run_matmul(gpu, a, b, _ffi.MATMUL_RELU | _ffi.MATMUL_SPLIT_K(1) |
+                       force)
+    ba, bb = gpu.upload(a), gpu.upload(b)
+    bc = gpu.buffer(m * n * 8)
+    bounds = [0] + cuts + [k]
+    for i in range(len(bounds) - 1):
+        k0, k1 = bounds[i], bounds[i + 1]
+        last = i == len(bounds) - 2
+        hx.cuda_matmul_acc(0, ba.ptr + 8 * k0, k, bb.ptr + 8 * k0 * n,
+                           bc.ptr if i else 0, bc.ptr, m, n, k1 - k0,
+                           (_ffi.MATMUL_RELU if last else 0) | force, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    got = bc.read((m, n))
+    assert np.array_equal(bits(got), bits(whole))
+    assert oracle.normwise_error(got, oracle.relu(oracle.matmul(a, b))) <= TOL
+
+
+def test_matmul_acc_separate_input_and_errors(gpu):
+    """c_in distinct from c; an empty k copies (or relus) c_in; lda < k and a
+    requested k split are refused."""
+    rng = np.random.default_rng(5)
+    m, n, k = 70, 96, 64
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    c0 = rng.uniform(-1, 1, (m, n))
+    ba, bb, bi = gpu.upload(a), gpu.upload(b), gpu.upload(c0)
+    bc = gpu.buffer(m * n * 8)
+    hx.cuda_matmul_acc(0, ba.ptr, k, bb.ptr, bi.ptr, bc.ptr, m, n, k, 0,
+                       gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    want = oracle.add(c0, oracle.matmul(a, b))
+    assert oracle.normwise_error(bc.read((m, n)), want) <= TOL
+    assert np.array_equal(bits(bi.read((m, n))), bits(c0))  # input untouched
+    hx.cuda_matmul_acc(0, ba.ptr, k, bb.ptr, bi.ptr, bc.ptr, m, n, 0,
+                       _ffi.MATMUL_RELU, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    assert np.array_equal(bits(bc.read((m, n))), bits(oracle.relu(c0)))
+    lib = hx.lib()
+    assert lib.hexir_cuda_matmul_acc_f64(0, ba.ptr, k - 2, bb.ptr, None, bc.ptr,
+                                         m, n, k, 0, None) == \
+        _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_cuda_matmul_acc_f64(0, ba.ptr, k, bb.ptr, bi.ptr, bc.ptr,
+                                         m, n, k, _ffi.MATMUL_SPLIT_K(2),
+                                         None) == _ffi.ERROR_INVALID_ARGUMENT

@@ -160,6 +160,38 @@ def test_pipelined_dispatch(m, n, k, capture_rows):
     assert oracle.normwise_error(first[rows], want) <= TOL
 
 
+@pytest.mark.parametrize("m,n,k,capture_rows", [
+    (4096, 4096, 2048, 4096),
+    (4096, 4096, 4100, 3000),   # ragged last k tile, partial capture
+])
+def test_weight_streamed_pipeline_is_bit_identical(gpu, m, n, k, capture_rows):
+    """With w still on the host and no k split in the one-shot plan, the VM
+    runs k in pieces while w's rows (and a's columns) upload, then the second
+    half of k per row chunk while rows download: every element sees the
+    one-shot launch's operations in the same order, so the captured rows
+    equal hexir_cuda_matmul_f64's bit for bit."""
+    assert hx.matmul_plan(m, n, k, _ffi.MATMUL_RELU)[1] == 1
+    r = hx.Rng(8)
+    a = r.uniform((m, k))
+    w = r.uniform((k, n))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    module = hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    dev = hx.Device("cuda")
+    got = hx.execute(module, dev, out_shape=(capture_rows, n))
+    ba, bw = gpu.upload(a), gpu.upload(w)
+    bc = gpu.buffer(m * n * 8)
+    hx.cuda_matmul(0, ba.ptr, bw.ptr, bc.ptr, m, n, k, _ffi.MATMUL_RELU,
+                   gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    one_shot = bc.read((m, n))[:capture_rows]
+    assert np.array_equal(bits(got), bits(one_shot))
+    rows = np.linspace(0, capture_rows - 1, 8).astype(int)
+    want = oracle.relu(oracle.matmul(a[rows], w))
+    assert oracle.normwise_error(got[rows], want) <= TOL
+    module.close()
+
+
 def test_relu_stream_2_28_bit_exact():
     """relu on 2^28 f64 ~ N(0,1) seed 4 as tensor<16384x16384xf64>: bit-exact
     against the CPU relu (compared in place, no second big host copy)."""
