@@ -113,6 +113,20 @@ __device__ __forceinline__ void dmma_16x8x8(double (&d)[4], double a0,
       : "d"(a0), "d"(a1), "d"(a2), "d"(a3), "d"(b0), "d"(b1));
 }
 
+// 256-bit global accesses (sm_100): four consecutive f64, 32-byte aligned.
+__device__ __forceinline__ void stg256(double *p, double a, double b, double c,
+                                       double d) {
+  asm volatile("st.global.v4.f64 [%0], {%1, %2, %3, %4};" ::"l"(p), "d"(a),
+               "d"(b), "d"(c), "d"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void ldg256(const double *p, double (&v)[4]) {
+  asm volatile("ld.global.v4.f64 {%0, %1, %2, %3}, [%4];"
+               : "=d"(v[0]), "=d"(v[1]), "=d"(v[2]), "=d"(v[3])
+               : "l"(p));
+}
+
 __device__ __forceinline__ double2 lds128(uint32_t addr) {
   double2 v;
   asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];"

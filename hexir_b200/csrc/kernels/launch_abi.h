@@ -49,6 +49,10 @@ extern "C" {
  * scope before the CTA exits, so the owner sees them once it has synchronised
  * with this kernel's completion. */
 #define HEXIR_EPILOGUE_SYSTEM_FENCE 0x2u
+/* c (and c_in) rows start on 32-byte boundaries (n % 4 == 0, 32-byte aligned
+ * base): the TMA kernels move each thread's four consecutive outputs with one
+ * 256-bit access, so a warp's store covers whole 128-byte lines. */
+#define HEXIR_EPILOGUE_VEC4 0x4u
 
 /* Error bits a kernel ORs into the device error word. */
 #define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */

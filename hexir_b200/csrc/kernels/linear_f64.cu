@@ -98,7 +98,7 @@ template <int MI, int NP, bool VEC>
 __device__ __forceinline__ void store_warp_tile(
     const double (&acc)[MI][2 * NP][4], double *__restrict__ c, uint32_t m,
     uint32_t n, uint32_t row0, uint32_t col0, bool relu, uint32_t g,
-    uint32_t t) {
+    uint32_t t, bool vec4 = false) {
 #pragma unroll
   for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
@@ -118,7 +118,11 @@ __device__ __forceinline__ void store_warp_tile(
           for (int q = 0; q < 4; ++q)
             v[q] = relu_ref(v[q]);
         }
-        if (VEC) {
+        if (VEC && vec4) {
+          // n % 4 == 0 and rows 32-byte aligned: quads never straddle n.
+          if (col < n)
+            stg256(crow + col, v[0], v[1], v[2], v[3]);
+        } else if (VEC) {
           // n is even and the base 16-byte aligned: pairs never straddle n.
           if (col < n)
             *reinterpret_cast<double2 *>(crow + col) = make_double2(v[0], v[1]);
@@ -141,7 +145,8 @@ __device__ __forceinline__ void store_warp_tile(
 template <int MI, int NP, bool VEC>
 __device__ __forceinline__ void load_warp_tile(
     double (&acc)[MI][2 * NP][4], const double *__restrict__ c_in, uint32_t m,
-    uint32_t n, uint32_t row0, uint32_t col0, uint32_t g, uint32_t t) {
+    uint32_t n, uint32_t row0, uint32_t col0, uint32_t g, uint32_t t,
+    bool vec4 = false) {
 #pragma unroll
   for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
@@ -154,7 +159,10 @@ __device__ __forceinline__ void load_warp_tile(
       for (int p = 0; p < NP; ++p) {
         const uint32_t col = col0 + p * 16 + 4 * t;
         double v[4] = {0.0, 0.0, 0.0, 0.0};
-        if (VEC) {
+        if (VEC && vec4) {
+          if (col < n)
+            ldg256(crow + col, v);
+        } else if (VEC) {
           if (col < n) {
             const double2 x = *reinterpret_cast<const double2 *>(crow + col);
             v[0] = x.x;
@@ -284,9 +292,10 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         acc[i][j][q] = 0.0;
+  const bool vec4 = (args.epilogue & HEXIR_EPILOGUE_VEC4) != 0;
   if (args.c_in)
     load_warp_tile<MI, NP, true>(acc, args.c_in, args.m, args.n,
-                                 m0 + wm * T::WTM, n0 + wn * T::WTN, g, t);
+                                 m0 + wm * T::WTM, n0 + wn * T::WTN, g, t, vec4);
 
   const uint32_t sa_addr = smem_addr(sa), sb_addr = smem_addr(sb);
   bool ok = true;
@@ -340,7 +349,7 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
     relu = false;
   }
   store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
-                                n0 + wn * T::WTN, relu, g, t);
+                                n0 + wn * T::WTN, relu, g, t, vec4);
   if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
     __threadfence_system();
 }

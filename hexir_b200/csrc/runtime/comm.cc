@@ -199,6 +199,104 @@ hexir_status_t probe_direct(hexir_comm_t *comm) {
   return HEXIR_OK;
 }
 
+// The weight's k pieces for a broadcast that peers compute behind: a short
+// first piece (512 of k) whose transfer is the only exposed one, then the
+// rest, which lands long before the first piece's GEMM ends (8192 x 8192 on
+// B200: the 480 MiB rest crosses NVLink in ~0.8 ms, the first piece takes
+// ~2 ms of DMMA time on 8192 rows).  Each extra piece costs ~0.2 ms there
+// (every CTA stores and reloads its partial sums, one more tail wave), so
+// there are two.  Multiples of the 32-wide k tile.  Returns the count.
+constexpr uint32_t kBroadcastPieceMinK = 2048;
+uint32_t broadcast_pieces(uint32_t k, uint32_t bounds[3]) {
+  bounds[0] = 0;
+  if (k < kBroadcastPieceMinK) {
+    bounds[1] = k;
+    return 1;
+  }
+  bounds[1] = 512;
+  bounds[2] = k;
+  return 2;
+}
+
+// Direct row stores (see hexir_sharded_linear_f64).  The weight is broadcast
+// in k pieces on the comm's high-priority side stream.  Every rank runs one
+// launch per piece, each continuing the previous one's sums (same operations
+// as one unsplit launch): a peer waits for each piece to land and keeps its
+// partial sums in its staging rows `c`, the last piece storing into the
+// root's output over NVLink; the root needs no broadcast and sums in its own
+// rows of c at once, its short first pieces leaving SMs free for the
+// broadcast's NCCL kernels.  Where a rank's one-shot plan would split k it
+// runs that plan instead (a peer after the whole weight has landed).  A
+// one-word all-reduce then orders the root's stream after every peer's
+// kernels.  A rank whose launch failed still takes every collective step, so
+// no rank waits for ever.
+hexir_status_t direct_rows(hexir_comm_t *comm, DeviceState *dev, KernelLib *lib,
+                           const double *a_rows, double *w, double *c,
+                           CUdeviceptr remote_c, uint64_t begin, uint64_t rows,
+                           uint32_t n, uint32_t k, uint32_t flags, CUstream s,
+                           hexir_status_t status) {
+  const Driver &d = driver();
+  const Nccl &nc = nccl();
+  std::string error;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(s);
+  CUstream bs = comm->gather_stream;
+  cudaStream_t bcs = reinterpret_cast<cudaStream_t>(bs);
+  uint32_t bounds[3];
+  const uint32_t pieces = broadcast_pieces(k, bounds);
+  // The side stream starts after the caller's queued work (w's contents).
+  CUevent start = comm->chunk_done[0];
+  CUresult cr = d.EventRecord(start, s);
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamWaitEvent(bs, start, 0);
+  if (cr != CUDA_SUCCESS)
+    return comm_fail(cuda_message("broadcast stream", cr));
+  for (uint32_t j = 0; j < pieces; ++j) {
+    double *wp = w + static_cast<size_t>(bounds[j]) * n;
+    ncclResult_t nr =
+        nc.Broadcast(wp, wp, static_cast<size_t>(bounds[j + 1] - bounds[j]) * n,
+                     ncclDouble, 0, comm->comm, bcs);
+    if (nr != ncclSuccess)
+      return comm_fail(nccl_message("ncclBroadcast (weight piece)", nr));
+    d.EventRecord(comm->chunk_done[1 + j], bs);
+  }
+  d.EventRecord(comm->gather_done, bs);
+
+  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
+  const uint32_t m = static_cast<uint32_t>(rows);
+  if (rows && status == HEXIR_OK) {
+    const bool root = comm->rank == 0;
+    double *out = root ? c : reinterpret_cast<double *>(remote_c) + begin * n;
+    const uint32_t remote = root ? 0u : HEXIR_MATMUL_REMOTE_OUTPUT;
+    const MatmulPlan one = plan_matmul(dev, a_rows, w, out, m, n, k, relu);
+    if (pieces == 1 || one.split_k != 1) {
+      if (!root)
+        d.StreamWaitEvent(s, comm->gather_done, 0);
+      status = launch_matmul(dev, lib, a_rows, w, out, m, n, k, relu | remote, s,
+                             &error);
+    } else {
+      for (uint32_t j = 0; j < pieces && status == HEXIR_OK; ++j) {
+        const bool last = j + 1 == pieces;
+        if (!root)
+          d.StreamWaitEvent(s, comm->chunk_done[1 + j], 0);
+        status = launch_matmul(
+            dev, lib, a_rows + bounds[j], w + static_cast<size_t>(bounds[j]) * n,
+            last ? out : c, m, n, bounds[j + 1] - bounds[j],
+            (last ? relu | remote : 0u) | HEXIR_MATMUL_SPLIT_K(1), s, &error, k,
+            j ? c : nullptr);
+      }
+    }
+    if (status != HEXIR_OK)
+      set_last_error(error);
+  }
+  // Later work on the caller's stream (a new w) waits for the broadcast.
+  d.StreamWaitEvent(s, comm->gather_done, 0);
+  void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
+  ncclResult_t nr = nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
+  if (nr != ncclSuccess)
+    return comm_fail(nccl_message("ncclAllReduce (row stores done)", nr));
+  return status;
+}
+
 }  // namespace
 
 extern "C" {
@@ -264,7 +362,14 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   comm->rank = rank;
   comm->ordinal = ordinal;
   const Driver &d = driver();
-  CUresult cr = d.StreamCreate(&comm->gather_stream, CU_STREAM_NON_BLOCKING);
+  // The side stream carries the weight pieces that peers' GEMMs wait for:
+  // highest priority, so its NCCL kernels take SMs as soon as GEMM CTAs
+  // retire instead of after the whole GEMM grid has been dispatched.
+  int least = 0, greatest = 0;
+  CUresult cr = d.CtxGetStreamPriorityRange(&least, &greatest);
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamCreateWithPriority(&comm->gather_stream, CU_STREAM_NON_BLOCKING,
+                                    greatest);
   for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kGatherChunks; ++i)
     cr = d.EventCreate(&comm->chunk_done[i], CU_EVENT_DISABLE_TIMING);
   if (cr == CUDA_SUCCESS)
@@ -407,37 +512,16 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
     }
   }
 
+  if (direct)
+    return direct_rows(comm, dev, lib, a_rows, w, c, remote_c, begin, rows, n, k,
+                       flags, s, peer_status);
+
   // 1. Weight from the root to everyone, over NVLink.
   ncclResult_t r = nc.Broadcast(w, w, static_cast<size_t>(k) * n, ncclDouble, 0,
                                 comm->comm, cs);
   if (r != ncclSuccess) {
     set_last_error(nccl_message("ncclBroadcast", r));
     return HEXIR_ERROR_DEVICE;
-  }
-
-  if (direct) {
-    // 2'. One launch over this rank's rows; a peer's kernel stores its tiles
-    //     into the root's c over NVLink as they finish (system-scope fence
-    //     before each CTA retires).  3'. A one-word all-reduce orders the
-    //     root's stream after every peer's kernel.  A rank whose launch
-    //     failed still joins it, so no rank waits for ever.
-    if (rows && peer_status == HEXIR_OK) {
-      double *out = comm->rank == 0
-                        ? c
-                        : reinterpret_cast<double *>(remote_c) + begin * n;
-      const uint32_t kflags = (flags & HEXIR_MATMUL_RELU) |
-                              (comm->rank ? HEXIR_MATMUL_REMOTE_OUTPUT : 0u);
-      peer_status = launch_matmul(dev, lib, a_rows, w, out,
-                                  static_cast<uint32_t>(rows), n, k, kflags, s,
-                                  &error);
-      if (peer_status != HEXIR_OK)
-        set_last_error(error);
-    }
-    void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
-    r = nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
-    if (r != ncclSuccess)
-      return comm_fail(nccl_message("ncclAllReduce (row stores done)", r));
-    return peer_status;
   }
 
   // 2. This rank's rows in up to kGatherChunks pieces; the root writes

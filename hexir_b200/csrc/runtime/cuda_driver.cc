@@ -54,6 +54,8 @@ void load() {
             bind(lib, d.CtxEnablePeerAccess, "cuCtxEnablePeerAccess", e) &&
             bind(lib, d.DeviceCanAccessPeer, "cuDeviceCanAccessPeer", e) &&
             bind(lib, d.StreamCreate, "cuStreamCreate", e) &&
+            bind(lib, d.StreamCreateWithPriority, "cuStreamCreateWithPriority", e) &&
+            bind(lib, d.CtxGetStreamPriorityRange, "cuCtxGetStreamPriorityRange", e) &&
             bind(lib, d.StreamDestroy, "cuStreamDestroy_v2", e) &&
             bind(lib, d.StreamSynchronize, "cuStreamSynchronize", e) &&
             bind(lib, d.StreamWaitEvent, "cuStreamWaitEvent", e) &&

@@ -32,6 +32,8 @@ struct Driver {
   CUresult (*CtxEnablePeerAccess)(CUcontext, unsigned int) = nullptr;
   CUresult (*DeviceCanAccessPeer)(int *, CUdevice, CUdevice) = nullptr;
   CUresult (*StreamCreate)(CUstream *, unsigned int) = nullptr;
+  CUresult (*StreamCreateWithPriority)(CUstream *, unsigned int, int) = nullptr;
+  CUresult (*CtxGetStreamPriorityRange)(int *, int *) = nullptr;
   CUresult (*StreamDestroy)(CUstream) = nullptr;
   CUresult (*StreamSynchronize)(CUstream) = nullptr;
   CUresult (*StreamWaitEvent)(CUstream, CUevent, unsigned int) = nullptr;

@@ -406,6 +406,11 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   args.timeout_ns = kWaitTimeoutNs;
   args.c_in = c_in;
   args.lda = lda;
+  // 256-bit epilogue accesses where every row of c (the split-K partials
+  // included) and c_in starts on a 32-byte boundary.
+  const bool rows32 = n % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(c) & 31u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(c_in) & 31u) == 0;
 
   std::unique_lock<std::mutex> ws_lock(dev->mu, std::defer_lock);
   if (p.split_k > 1) {
@@ -418,6 +423,8 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     d.StreamWaitEvent(stream, dev->ws_ready, 0);
     args.c = reinterpret_cast<double *>(dev->workspace);
   }
+  if (rows32 && (reinterpret_cast<uintptr_t>(args.c) & 31u) == 0)
+    args.epilogue |= HEXIR_EPILOGUE_VEC4;
 
   const unsigned grid_x = p.tiles_m * p.tiles_n;
   hexir_status_t status;

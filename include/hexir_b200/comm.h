@@ -63,15 +63,19 @@ int hexir_comm_direct_stores(const hexir_comm_t *comm);
  *          others' buffers.
  *   a_rows this rank's rows of a, rows hexir_shard_rows(m, size, rank).
  *   c      root: the whole [m x n] output; other ranks: [rows x n] staging
- *          for their own rows, used only when the rows travel by NCCL (its
- *          contents are unspecified afterwards).
+ *          for their own rows (partial sums, or rows that travel by NCCL;
+ *          its contents are unspecified afterwards).
  * flags: HEXIR_MATMUL_RELU as for hexir_cuda_matmul_f64, HEXIR_SHARD_GATHER_NCCL.
  *
  * Rows go to the root's c directly when hexir_comm_init_rank found that
  * every peer can map rank 0's memory (same host, CUDA IPC) and the root's c
  * is exportable (a cuMemAlloc / cudaMalloc allocation); the root's stream
- * continues after every peer's kernel has finished storing.  Otherwise they
- * are gathered with NCCL on a side stream, piece by piece behind the GEMM.
+ * continues after every peer's kernel has finished storing.  Then, for
+ * k >= 2048, w is broadcast in two k pieces (512, rest) and a peer computes
+ * each piece as it lands, continuing its sums in its staging c, so only the
+ * first piece's transfer is exposed; the result has the bits of one launch
+ * over the rank's rows.  Otherwise rows are gathered with NCCL on a side
+ * stream, piece by piece behind the GEMM.
  * Asynchronous on `stream`, except that with direct stores a peer's call
  * returns only once the root's stream has reached the same call (the root
  * sends the location of c every call).  Peers write the root's c only after
