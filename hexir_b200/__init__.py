@@ -10,7 +10,7 @@ this package is a thin Python face over it.
 
 from ._ffi import HexirError, lib  # noqa: F401
 from .api import (Buffer, Device, Module, Program, Rng, cuda_add,  # noqa: F401
-                  cuda_matmul, cuda_matmul_acc, cuda_relu,
+                  cuda_matmul, cuda_matmul_acc, cuda_matmul_add, cuda_relu,
                   cuda_synchronize, device_count,
                   execute, kernel_image, last_kernel_ms, launch_count,
                   matmul_plan, parse, read_executables, read_launch,

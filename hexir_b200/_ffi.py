@@ -105,6 +105,8 @@ _SIGNATURES = [
                                      _u32, _vp]),
     ("hexir_cuda_matmul_acc_f64", _int, [_int, _vp, _u32, _vp, _vp, _vp, _u32,
                                          _u32, _u32, _u32, _vp]),
+    ("hexir_cuda_matmul_add_f64", _int, [_int, _vp, _vp, _vp, _vp, _u32, _u32,
+                                         _u32, _u32, _vp]),
     ("hexir_cuda_add_f64", _int, [_int, _vp, _vp, _vp, _sz, _vp]),
     ("hexir_cuda_relu_f64", _int, [_int, _vp, _vp, _sz, _vp]),
     ("hexir_cuda_matmul_f64_noalloc", _int, [_int, _vp, _vp, _vp, _u32, _u32,

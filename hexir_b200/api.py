@@ -418,6 +418,14 @@ def cuda_matmul_acc(ordinal: int, a: int, lda: int, b: int, c_in: int, c: int,
           "hexir_cuda_matmul_acc_f64")
 
 
+def cuda_matmul_add(ordinal: int, a: int, b: int, addend: int, c: int, m: int,
+                    n: int, k: int, flags: int = 0, stream: int = 0) -> None:
+    """c = epilogue(a . b + addend) (hexir_cuda_matmul_add_f64)."""
+    check(lib().hexir_cuda_matmul_add_f64(ordinal, a, b, addend, c, m, n, k,
+                                          flags, stream or None),
+          "hexir_cuda_matmul_add_f64")
+
+
 def cuda_relu(ordinal: int, x: int, y: int, n: int, stream: int = 0) -> None:
     check(lib().hexir_cuda_relu_f64(ordinal, x, y, n, stream or None),
           "hexir_cuda_relu_f64")

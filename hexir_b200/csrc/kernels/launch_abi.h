@@ -53,6 +53,10 @@ extern "C" {
  * base): the TMA kernels move each thread's four consecutive outputs with one
  * 256-bit access, so a warp's store covers whole 128-byte lines. */
 #define HEXIR_EPILOGUE_VEC4 0x4u
+/* c = a . b + addend (then the relu, if set): a linear and the add that is
+ * its only user, fused.  Same rounding as the two kernels: the sum is an f64
+ * before the add. */
+#define HEXIR_EPILOGUE_ADD 0x8u
 
 /* Error bits a kernel ORs into the device error word. */
 #define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */
@@ -79,6 +83,7 @@ typedef struct {
   const double *c_in;
   uint32_t lda;          /* row stride of a in elements (>= k) */
   uint32_t reserved;
+  const double *addend;  /* [m][n], with HEXIR_EPILOGUE_ADD */
 } hexir_linear_args_t;
 
 typedef struct {
@@ -87,6 +92,7 @@ typedef struct {
   uint64_t count;         /* m * n */
   uint32_t split;
   uint32_t epilogue;
+  const double *addend;   /* [m*n], with HEXIR_EPILOGUE_ADD */
 } hexir_reduce_args_t;
 
 typedef struct {

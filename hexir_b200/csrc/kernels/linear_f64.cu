@@ -98,7 +98,7 @@ template <int MI, int NP, bool VEC>
 __device__ __forceinline__ void store_warp_tile(
     const double (&acc)[MI][2 * NP][4], double *__restrict__ c, uint32_t m,
     uint32_t n, uint32_t row0, uint32_t col0, bool relu, uint32_t g,
-    uint32_t t, bool vec4 = false) {
+    uint32_t t, bool vec4 = false, const double *__restrict__ addend = nullptr) {
 #pragma unroll
   for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
@@ -113,6 +113,34 @@ __device__ __forceinline__ void store_warp_tile(
         double v[4] = {acc[mi][2 * p][2 * half], acc[mi][2 * p + 1][2 * half],
                        acc[mi][2 * p][2 * half + 1],
                        acc[mi][2 * p + 1][2 * half + 1]};
+        if (addend) {
+          // The fused add: the same rounding as adding the stored product.
+          const double *arow = addend + (size_t)row * n;
+          double b[4] = {0.0, 0.0, 0.0, 0.0};
+          if (VEC && vec4) {
+            if (col < n)
+              ldg256(arow + col, b);
+          } else if (VEC) {
+            if (col < n) {
+              const double2 x = *reinterpret_cast<const double2 *>(arow + col);
+              b[0] = x.x;
+              b[1] = x.y;
+            }
+            if (col + 2 < n) {
+              const double2 x = *reinterpret_cast<const double2 *>(arow + col + 2);
+              b[2] = x.x;
+              b[3] = x.y;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (col + q < n)
+                b[q] = arow[col + q];
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            v[q] = __dadd_rn(v[q], b[q]);
+        }
         if (relu) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -344,12 +372,15 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
 
   double *dst = args.c;
   bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
+  const double *addend =
+      (args.epilogue & HEXIR_EPILOGUE_ADD) ? args.addend : nullptr;
   if (args.split_k > 1) {
     dst += (size_t)split * args.m * args.n;
     relu = false;
+    addend = nullptr;
   }
   store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
-                                n0 + wn * T::WTN, relu, g, t, vec4);
+                                n0 + wn * T::WTN, relu, g, t, vec4, addend);
   if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
     __threadfence_system();
 }
@@ -485,18 +516,22 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
 
   double *dst = args.c;
   bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
+  const double *addend =
+      (args.epilogue & HEXIR_EPILOGUE_ADD) ? args.addend : nullptr;
   if (args.split_k > 1) {
     dst += (size_t)split * m * n;
     relu = false;
+    addend = nullptr;
   }
   store_warp_tile<2, 2, false>(acc, dst, m, n, m0 + wm * 32, n0 + wn * 32,
-                               relu, g, t);
+                               relu, g, t, false, addend);
   if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
     __threadfence_system();
 }
 
 // c[i] = epilogue(sum over s in 0..split-1 of partials[s][i]), summed in
-// split order so the result does not depend on scheduling.
+// split order so the result does not depend on scheduling; the epilogue adds
+// addend[i] (HEXIR_EPILOGUE_ADD), then applies the relu.
 extern "C" __global__ void __launch_bounds__(256)
     hexir_linear_f64_splitk_reduce(const hexir_reduce_args_t args) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -506,6 +541,8 @@ extern "C" __global__ void __launch_bounds__(256)
     double s = 0.0;
     for (uint32_t p = 0; p < args.split; ++p)
       s = __dadd_rn(s, args.partials[(size_t)p * args.count + i]);
+    if (args.epilogue & HEXIR_EPILOGUE_ADD)
+      s = __dadd_rn(s, args.addend[i]);
     args.c[i] = relu ? relu_ref(s) : s;
   }
   if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)

@@ -596,6 +596,28 @@ struct Vm {
   }
 
   // Buffer sizes against the kernel's extents.
+  // Operands before the destination, by kernel kind.
+  static int inputs_of(uint32_t kind) {
+    switch (kind) {
+    case HEXIR_KERNEL_RELU: return 1;
+    case HEXIR_KERNEL_MATMUL_ADD:
+    case HEXIR_KERNEL_MATMUL_ADD_RELU: return 3;
+    default: return 2;
+    }
+  }
+  static bool is_matmul(uint32_t kind) {
+    return kind == HEXIR_KERNEL_MATMUL || kind == HEXIR_KERNEL_MATMUL_RELU ||
+           kind == HEXIR_KERNEL_MATMUL_ADD || kind == HEXIR_KERNEL_MATMUL_ADD_RELU;
+  }
+  static uint32_t matmul_flags(uint32_t kind) {
+    return kind == HEXIR_KERNEL_MATMUL_RELU || kind == HEXIR_KERNEL_MATMUL_ADD_RELU
+               ? HEXIR_MATMUL_RELU
+               : 0u;
+  }
+  static bool has_addend(uint32_t kind) {
+    return kind == HEXIR_KERNEL_MATMUL_ADD || kind == HEXIR_KERNEL_MATMUL_ADD_RELU;
+  }
+
   hexir_status_t check_sizes(const hexir_executable_entry_t &exe,
                              Slot *const *args, uint64_t argc) {
     if (exe.elem_size != sizeof(double))
@@ -609,6 +631,15 @@ struct Vm {
       if (args[0]->bytes < static_cast<uint64_t>(exe.m) * exe.k * 8 ||
           args[1]->bytes < static_cast<uint64_t>(exe.k) * exe.n * 8 ||
           args[2]->bytes < mn)
+        return HEXIR_ERROR_INVALID_MODULE;
+      return HEXIR_OK;
+    case HEXIR_KERNEL_MATMUL_ADD:
+    case HEXIR_KERNEL_MATMUL_ADD_RELU:
+      if (argc != 4)
+        return HEXIR_ERROR_INVALID_MODULE;
+      if (args[0]->bytes < static_cast<uint64_t>(exe.m) * exe.k * 8 ||
+          args[1]->bytes < static_cast<uint64_t>(exe.k) * exe.n * 8 ||
+          args[2]->bytes < mn || args[3]->bytes < mn)
         return HEXIR_ERROR_INVALID_MODULE;
       return HEXIR_OK;
     case HEXIR_KERNEL_ADD:
@@ -629,29 +660,26 @@ struct Vm {
   }
 
   hexir_status_t run_host(const hexir_executable_entry_t &exe, Slot *const *args) {
-    const uint8_t *in0 = nullptr, *in1 = nullptr;
-    hexir_status_t st = on_host(*args[0], &in0);
-    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
-    if (st == HEXIR_OK && binary)
-      st = on_host(*args[1], &in1);
+    const int inputs = inputs_of(exe.kind);
+    const uint8_t *in[3] = {nullptr, nullptr, nullptr};
+    hexir_status_t st = HEXIR_OK;
+    for (int i = 0; i < inputs && st == HEXIR_OK; ++i)
+      st = on_host(*args[i], &in[i]);
     if (st != HEXIR_OK)
       return st;
-    Slot &dst = *args[binary ? 2 : 1];
+    Slot &dst = *args[inputs];
     // Inputs may alias the destination slot only in a malformed module; copy
     // them out first so writing cannot corrupt them.
-    std::vector<double> keep0, keep1;
-    if (args[0] == &dst) {
-      keep0.assign(reinterpret_cast<const double *>(in0),
-                   reinterpret_cast<const double *>(in0) + args[0]->bytes / 8);
-      in0 = reinterpret_cast<const uint8_t *>(keep0.data());
-    }
-    if (binary && args[1] == &dst) {
-      keep1.assign(reinterpret_cast<const double *>(in1),
-                   reinterpret_cast<const double *>(in1) + args[1]->bytes / 8);
-      in1 = reinterpret_cast<const uint8_t *>(keep1.data());
-    }
-    const double *a = reinterpret_cast<const double *>(in0);
-    const double *b = reinterpret_cast<const double *>(in1);
+    std::vector<double> keep[3];
+    for (int i = 0; i < inputs; ++i)
+      if (args[i] == &dst) {
+        keep[i].assign(reinterpret_cast<const double *>(in[i]),
+                       reinterpret_cast<const double *>(in[i]) + args[i]->bytes / 8);
+        in[i] = reinterpret_cast<const uint8_t *>(keep[i].data());
+      }
+    const double *a = reinterpret_cast<const double *>(in[0]);
+    const double *b = reinterpret_cast<const double *>(in[1]);
+    const double *d = reinterpret_cast<const double *>(in[2]);
     double *c = written_on_host(dst);
     switch (exe.kind) {
     case HEXIR_KERNEL_MATMUL:
@@ -660,6 +688,13 @@ struct Vm {
     case HEXIR_KERNEL_MATMUL_RELU:
       cpu_matmul_f64(a, b, c, exe.m, exe.n, exe.k);
       cpu_relu_f64(c, c, elems(exe));
+      break;
+    case HEXIR_KERNEL_MATMUL_ADD:
+    case HEXIR_KERNEL_MATMUL_ADD_RELU:
+      cpu_matmul_f64(a, b, c, exe.m, exe.n, exe.k);
+      cpu_add_f64(c, d, c, elems(exe));
+      if (exe.kind == HEXIR_KERNEL_MATMUL_ADD_RELU)
+        cpu_relu_f64(c, c, elems(exe));
       break;
     case HEXIR_KERNEL_ADD:
       cpu_add_f64(a, b, c, elems(exe));
@@ -960,15 +995,18 @@ struct Vm {
     if (!lib)
       return HEXIR_ERROR_DEVICE;
     CudaDevice *dev = cuda[o];
-    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
-    CUdeviceptr in0 = 0, in1 = 0, out = 0;
-    Slot &dst = *args[binary ? 2 : 1];
-    hexir_status_t st = on_device(*args[0], o, &in0);
-    if (st == HEXIR_OK && binary)
-      st = on_device(*args[1], o, &in1);
+    const int inputs = inputs_of(exe.kind);
+    CUdeviceptr in[3] = {0, 0, 0}, out = 0;
+    Slot &dst = *args[inputs];
+    hexir_status_t st = HEXIR_OK;
+    bool aliased = false;
+    for (int i = 0; i < inputs && st == HEXIR_OK; ++i) {
+      st = on_device(*args[i], o, &in[i]);
+      aliased |= args[i] == &dst;
+    }
     if (st != HEXIR_OK)
       return st;
-    if (&dst == args[0] || (binary && &dst == args[1])) {
+    if (aliased) {
       // Malformed aliasing: give the destination a fresh buffer.
       CUdeviceptr tmp = 0;
       if ((st = temp_on(o, dst.bytes, &tmp)) != HEXIR_OK)
@@ -980,16 +1018,19 @@ struct Vm {
     std::string error;
     ContextGuard guard(dev->state->context);
     Span *span = begin_span(dev);
-    const double *a = reinterpret_cast<const double *>(in0);
-    const double *b = reinterpret_cast<const double *>(in1);
+    const double *a = reinterpret_cast<const double *>(in[0]);
+    const double *b = reinterpret_cast<const double *>(in[1]);
     double *c = reinterpret_cast<double *>(out);
     switch (exe.kind) {
     case HEXIR_KERNEL_MATMUL:
     case HEXIR_KERNEL_MATMUL_RELU:
+    case HEXIR_KERNEL_MATMUL_ADD:
+    case HEXIR_KERNEL_MATMUL_ADD_RELU:
       st = launch_matmul(dev->state, lib, a, b, c, exe.m, exe.n, exe.k,
-                         exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
-                                                              : 0u,
-                         dev->stream, &error);
+                         matmul_flags(exe.kind), dev->stream, &error, 0, nullptr,
+                         has_addend(exe.kind)
+                             ? reinterpret_cast<const double *>(in[2])
+                             : nullptr);
       break;
     case HEXIR_KERNEL_ADD:
       st = launch_add(dev->state, lib, a, b, c, elems(exe), dev->stream, &error);
@@ -1028,12 +1069,12 @@ struct Vm {
       report(std::string("kernel '") + exe.name + "': " + error);
       return st;
     }
-    const bool matmul = exe.kind == HEXIR_KERNEL_MATMUL ||
-                        exe.kind == HEXIR_KERNEL_MATMUL_RELU;
-    const bool binary = exe.kind != HEXIR_KERNEL_RELU;
-    Slot &dst = *args[binary ? 2 : 1];
-    if (&dst == args[0] || (binary && &dst == args[1]))
-      return HEXIR_ERROR_INVALID_MODULE;
+    const bool matmul = is_matmul(exe.kind);
+    const int inputs = inputs_of(exe.kind);
+    Slot &dst = *args[inputs];
+    for (int i = 0; i < inputs; ++i)
+      if (&dst == args[i])
+        return HEXIR_ERROR_INVALID_MODULE;
     for (int r = 0; r < count; ++r)
       if (!library(index, first + r))
         return HEXIR_ERROR_DEVICE;
@@ -1079,9 +1120,18 @@ struct Vm {
     CUdeviceptr c_root = 0;
     if ((st = writable_on(dst, first, dst.bytes, &c_root)) != HEXIR_OK)
       return st;
-    const uint64_t row_in = matmul ? static_cast<uint64_t>(exe.k) * 8
-                                   : static_cast<uint64_t>(exe.n) * 8;
     const uint64_t row_out = static_cast<uint64_t>(exe.n) * 8;
+    // The row-split inputs and their row sizes: a (and the addend) of a
+    // matmul, both operands of an add, the input of a relu.
+    std::vector<std::pair<Slot *, uint64_t>> split_in;
+    if (matmul) {
+      split_in.emplace_back(args[0], static_cast<uint64_t>(exe.k) * 8);
+      if (has_addend(exe.kind))
+        split_in.emplace_back(args[2], row_out);
+    } else {
+      for (int i = 0; i < inputs; ++i)
+        split_in.emplace_back(args[i], row_out);
+    }
     std::vector<CUdeviceptr> c_part(count, 0);
     std::vector<uint64_t> begin(count), rows(count);
     std::vector<char> direct(count, 0);
@@ -1094,9 +1144,9 @@ struct Vm {
       CudaDevice *dev = cuda[o];
       // This shard's rows of the row-split inputs.
       CUdeviceptr x = 0, y = 0;
-      const int split_inputs = matmul ? 1 : (binary ? 2 : 1);
-      for (int i = 0; i < split_inputs; ++i) {
-        Slot &in = *args[i];
+      for (size_t i = 0; i < split_in.size(); ++i) {
+        Slot &in = *split_in[i].first;
+        const uint64_t row_in = split_in[i].second;
         CUdeviceptr p = 0;
         if (in.dev_valid.count(o)) {
           p = reinterpret_cast<CUdeviceptr>(in.dev[o]->impl) + begin[r] * row_in;
@@ -1126,13 +1176,17 @@ struct Vm {
       switch (exe.kind) {
       case HEXIR_KERNEL_MATMUL:
       case HEXIR_KERNEL_MATMUL_RELU:
+      case HEXIR_KERNEL_MATMUL_ADD:
+      case HEXIR_KERNEL_MATMUL_ADD_RELU:
         st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(x),
                            reinterpret_cast<const double *>(w[r]),
                            reinterpret_cast<double *>(out), m, exe.n, exe.k,
-                           (exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU
-                                                                 : 0u) |
+                           matmul_flags(exe.kind) |
                                (r && direct[r] ? HEXIR_MATMUL_REMOTE_OUTPUT : 0u),
-                           dev->stream, &error);
+                           dev->stream, &error, 0, nullptr,
+                           has_addend(exe.kind)
+                               ? reinterpret_cast<const double *>(y)
+                               : nullptr);
         break;
       case HEXIR_KERNEL_ADD:
         st = launch_add(dev->state, lib, reinterpret_cast<const double *>(x),
@@ -1555,6 +1609,8 @@ const char *hexir_kernel_kind_string(uint32_t kind) {
   case HEXIR_KERNEL_ADD: return "add";
   case HEXIR_KERNEL_RELU: return "relu";
   case HEXIR_KERNEL_MATMUL_RELU: return "matmul_relu";
+  case HEXIR_KERNEL_MATMUL_ADD: return "matmul_add";
+  case HEXIR_KERNEL_MATMUL_ADD_RELU: return "matmul_add_relu";
   }
   return "unknown";
 }

@@ -262,14 +262,16 @@ KernelLib *embedded_library(DeviceState *dev, std::string *error) {
 
 MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
                        const double *c, uint32_t m, uint32_t n, uint32_t k,
-                       uint32_t flags, uint32_t lda, const double *c_in) {
+                       uint32_t flags, uint32_t lda, const double *c_in,
+                       const double *addend) {
   MatmulPlan p;
   if (lda == 0)
     lda = k;
-  // TMA needs 16-byte aligned bases and row strides (k, lda, n even).
+  // TMA needs 16-byte aligned bases and row strides (k, lda, n even); the
+  // epilogue's paired accesses need the same of c, c_in and the addend.
   const bool tma_ok = (k % 2 == 0) && (lda % 2 == 0) && (n % 2 == 0) &&
                       aligned16(a) && aligned16(b) && aligned16(c) &&
-                      aligned16(c_in);
+                      aligned16(c_in) && aligned16(addend);
   if ((flags & HEXIR_MATMUL_FORCE_GUARDED) || !tma_ok) {
     p.variant = kGuarded;
     p.bm = HEXIR_LINEAR_G_BM;
@@ -343,7 +345,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              const double *b, double *c, uint32_t m, uint32_t n,
                              uint32_t k, uint32_t flags, CUstream stream,
                              std::string *error, uint32_t lda,
-                             const double *c_in) {
+                             const double *c_in, const double *addend) {
   const Driver &d = driver();
   if (m == 0 || n == 0)
     return HEXIR_OK;
@@ -359,13 +361,29 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                 HEXIR_ERROR_INVALID_ARGUMENT);
   if ((flags & HEXIR_MATMUL_FORCE_TMA) &&
       plan_matmul(dev, a, b, c, m, n, k, flags & ~HEXIR_MATMUL_FORCE_TMA, lda,
-                  c_in)
+                  c_in, addend)
               .variant == kGuarded)
     return fail(error,
                 "matmul: the TMA kernel needs even k, lda and n and 16-byte "
                 "aligned pointers",
                 HEXIR_ERROR_INVALID_ARGUMENT);
   const size_t out_bytes = static_cast<size_t>(m) * n * sizeof(double);
+  if (k == 0 && addend) {
+    // An empty sum plus the addend: the add (and relu) kernels' arithmetic.
+    const double *base = c_in;
+    if (!base) {
+      CUresult r = d.MemsetD8Async(reinterpret_cast<CUdeviceptr>(c), 0,
+                                   out_bytes, stream);
+      if (r != CUDA_SUCCESS)
+        return fail(error, cuda_message("empty matmul", r));
+      base = c;
+    }
+    hexir_status_t st = launch_add(dev, lib, base, addend, c,
+                                   static_cast<size_t>(m) * n, stream, error);
+    if (st != HEXIR_OK || !(flags & HEXIR_MATMUL_RELU))
+      return st;
+    return launch_relu(dev, lib, c, c, static_cast<size_t>(m) * n, stream, error);
+  }
   if (k == 0) {
     // An empty sum is 0 (or c_in) and relu(0) = 0.
     CUresult r;
@@ -383,7 +401,8 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     return r == CUDA_SUCCESS ? HEXIR_OK
                              : fail(error, cuda_message("empty matmul", r));
   }
-  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in);
+  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in,
+                                   addend);
 
   hexir_linear_args_t args;
   std::memset(&args, 0, sizeof(args));
@@ -406,11 +425,15 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   args.timeout_ns = kWaitTimeoutNs;
   args.c_in = c_in;
   args.lda = lda;
+  args.addend = addend;
+  if (addend)
+    args.epilogue |= HEXIR_EPILOGUE_ADD;
   // 256-bit epilogue accesses where every row of c (the split-K partials
-  // included) and c_in starts on a 32-byte boundary.
+  // included), c_in and the addend starts on a 32-byte boundary.
   const bool rows32 = n % 4 == 0 &&
                       (reinterpret_cast<uintptr_t>(c) & 31u) == 0 &&
-                      (reinterpret_cast<uintptr_t>(c_in) & 31u) == 0;
+                      (reinterpret_cast<uintptr_t>(c_in) & 31u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(addend) & 31u) == 0;
 
   std::unique_lock<std::mutex> ws_lock(dev->mu, std::defer_lock);
   if (p.split_k > 1) {
@@ -480,6 +503,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   red.count = static_cast<uint64_t>(m) * n;
   red.split = p.split_k;
   red.epilogue = args.epilogue;
+  red.addend = addend;
   void *params[] = {&red};
   const uint64_t want = (red.count + 255) / 256;
   const unsigned grid = static_cast<unsigned>(std::max<uint64_t>(
@@ -607,6 +631,23 @@ extern "C" hexir_status_t hexir_cuda_matmul_acc_f64(
   return call.finish(launch_matmul(call.dev, call.lib, a, b, c, m, n, k, flags,
                                    static_cast<CUstream>(stream), &call.error,
                                    lda, c_in));
+}
+
+extern "C" hexir_status_t hexir_cuda_matmul_add_f64(
+    int ordinal, const double *a, const double *b, const double *addend,
+    double *c, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+    void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  if (!addend && m && n) {
+    call.error = "matmul_add: null addend";
+    return call.finish(HEXIR_ERROR_INVALID_ARGUMENT);
+  }
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_matmul(call.dev, call.lib, a, b, c, m, n, k, flags,
+                                   static_cast<CUstream>(stream), &call.error,
+                                   0, nullptr, addend));
 }
 
 extern "C" hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,

@@ -78,18 +78,21 @@ struct MatmulPlan {
 };
 
 // lda: row stride of a in elements (0 = k).  c_in: when non-null the sums
-// start from c_in (no k split), see hexir_linear_args_t.
+// start from c_in (no k split), see hexir_linear_args_t.  addend: when
+// non-null, c = a . b + addend (before the relu), [m][n] like c.
 MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
                        const double *c, uint32_t m, uint32_t n, uint32_t k,
                        uint32_t flags, uint32_t lda = 0,
-                       const double *c_in = nullptr);
+                       const double *c_in = nullptr,
+                       const double *addend = nullptr);
 
 // Launchers.  The caller has made dev->context current.  All asynchronous.
 hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              const double *b, double *c, uint32_t m, uint32_t n,
                              uint32_t k, uint32_t flags, CUstream stream,
                              std::string *error, uint32_t lda = 0,
-                             const double *c_in = nullptr);
+                             const double *c_in = nullptr,
+                             const double *addend = nullptr);
 hexir_status_t launch_relu(DeviceState *dev, KernelLib *lib, const double *x,
                            double *y, size_t n, CUstream stream,
                            std::string *error);

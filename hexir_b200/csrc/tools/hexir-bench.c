@@ -160,7 +160,12 @@ int main(int argc, char **argv) {
     return 1;
   }
   const int is_gemm = entry.kind == HEXIR_KERNEL_MATMUL ||
-                      entry.kind == HEXIR_KERNEL_MATMUL_RELU;
+                      entry.kind == HEXIR_KERNEL_MATMUL_RELU ||
+                      entry.kind == HEXIR_KERNEL_MATMUL_ADD ||
+                      entry.kind == HEXIR_KERNEL_MATMUL_ADD_RELU;
+  /* The sampled check recomputes a . w from RODATA (a then w). */
+  const int checkable = entry.kind == HEXIR_KERNEL_MATMUL ||
+                        entry.kind == HEXIR_KERNEL_MATMUL_RELU;
   if (!json) {
     printf("module   : %s\n", path);
     printf("kernel   : %.32s  %s  built for %s  %ux%ux%u  elem=%uB\n",
@@ -211,7 +216,7 @@ int main(int argc, char **argv) {
   }
   double err = -1.0;
   int correct = 1;
-  if (result && is_gemm) {
+  if (result && checkable) {
     const void *rodata = NULL;
     uint64_t rodata_bytes = 0;
     size_t a_n = (size_t)entry.m * entry.k, b_n = (size_t)entry.k * entry.n;

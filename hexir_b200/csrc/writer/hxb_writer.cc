@@ -249,26 +249,67 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
         where[oi] = spec[op_key(ops[oi].kind)];
       }
 
-  // linear -> relu fusion on a GPU: the relu's input has no other user.
+  // Fusions on a GPU, each where the intermediate value has no other user and
+  // every op sits on the same device spec:
+  //   linear -> add [-> relu]  one matmul_add[_relu] executable, named after
+  //                            the linear, dispatched where the add stands
+  //                            (its addend may be computed after the linear);
+  //   linear -> relu           one matmul_relu, dispatched where the linear
+  //                            stands.
   std::vector<bool> fused(ops.size(), false), folded(ops.size(), false);
-  std::vector<int> alias(values.size(), -1);  // relu result -> linear result
+  std::vector<uint32_t> fused_kind(ops.size(), 0);  // linear op -> kind
+  std::vector<int> add_linear(ops.size(), -1);  // add op -> its linear op
+  std::vector<int> addend_of(ops.size(), -1);   // add op -> addend value
+  std::vector<int> alias(values.size(), -1);    // folded result -> kept result
+  auto fusable = [&](int value, int user_op) {
+    const int def = values[value].def;
+    return def >= 0 && ops[def].kind == OpKind::Linear && values[value].uses == 1 &&
+           !fused[def] && where[user_op].cuda && where[user_op] == where[def];
+  };
   if (!(flags & HEXIR_EMIT_NO_FUSE)) {
+    for (size_t oi = 0; oi < ops.size(); ++oi) {
+      const Op &add = ops[oi];
+      if (add.kind != OpKind::Add)
+        continue;
+      for (int i = 0; i < 2; ++i) {
+        const int in = add.operands[i];
+        if (!fusable(in, static_cast<int>(oi)))
+          continue;
+        const int def = values[in].def;
+        fused[def] = true;
+        fused_kind[def] = HEXIR_KERNEL_MATMUL_ADD;
+        add_linear[oi] = def;
+        addend_of[oi] = add.operands[1 - i];
+        break;
+      }
+    }
     for (size_t oi = 0; oi < ops.size(); ++oi) {
       const Op &r = ops[oi];
       if (r.kind != OpKind::Relu)
         continue;
       const int in = r.operands[0];
       const int def = values[in].def;
-      if (def < 0 || ops[def].kind != OpKind::Linear || values[in].uses != 1 ||
-          fused[def])
+      if (def < 0 || values[in].uses != 1 || !where[oi].cuda ||
+          !(where[oi] == where[def]))
         continue;
-      if (!where[oi].cuda || !(where[oi] == where[def]))
-        continue;
-      fused[def] = true;
-      folded[oi] = true;
-      alias[r.result] = in;
+      if (ops[def].kind == OpKind::Add && add_linear[def] >= 0) {
+        fused_kind[add_linear[def]] = HEXIR_KERNEL_MATMUL_ADD_RELU;
+        folded[oi] = true;
+        alias[r.result] = in;
+      } else if (ops[def].kind == OpKind::Linear && !fused[def]) {
+        fused[def] = true;
+        fused_kind[def] = HEXIR_KERNEL_MATMUL_RELU;
+        folded[oi] = true;
+        alias[r.result] = in;
+      }
     }
   }
+  // The op whose position carries op oi's dispatch, and the op whose
+  // executable it runs.
+  auto deferred = [&](int oi) {
+    return ops[oi].kind == OpKind::Linear && fused[oi] &&
+           fused_kind[oi] != HEXIR_KERNEL_MATMUL_RELU;
+  };
 
   const void *image = nullptr;
   size_t image_size = 0;
@@ -280,18 +321,21 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
   std::map<int, uint32_t> exe_index;  // op -> executable index
   bool any_library = false;
   for (const Function &f : funcs) {
-    for (int oi : f.ops) {
-      const Op &op = ops[oi];
-      if (!is_compute(op.kind) || folded[oi])
+    for (int at : f.ops) {
+      if (!is_compute(ops[at].kind) || folded[at] || deferred(at))
         continue;
+      // A fused add carries its linear's executable.
+      const int oi = add_linear[at] >= 0 ? add_linear[at] : at;
+      const Op &op = ops[oi];
       hexir_executable_entry_t e;
       std::memset(&e, 0, sizeof(e));
       write_name(e.name, kernel_name[oi]);
-      const Value &dst = values[op.result];
-      e.kind = op.kind == OpKind::Linear
-                   ? (fused[oi] ? HEXIR_KERNEL_MATMUL_RELU : HEXIR_KERNEL_MATMUL)
-                   : (op.kind == OpKind::Add ? HEXIR_KERNEL_ADD
-                                             : HEXIR_KERNEL_RELU);
+      const Value &dst = values[ops[at].result];
+      if (op.kind == OpKind::Linear)
+        e.kind = fused[oi] ? fused_kind[oi]
+                           : static_cast<uint32_t>(HEXIR_KERNEL_MATMUL);
+      else
+        e.kind = op.kind == OpKind::Add ? HEXIR_KERNEL_ADD : HEXIR_KERNEL_RELU;
       e.device = where[oi].cuda ? 1u : 0u;
       e.m = dst.rows;
       e.n = dst.cols;
@@ -327,7 +371,7 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
         l.device_count = where[oi].count;
         any_library = true;
       }
-      exe_index[oi] = static_cast<uint32_t>(entries.size());
+      exe_index[at] = static_cast<uint32_t>(entries.size());
       entries.push_back(e);
       launch.push_back(l);
     }
@@ -391,15 +435,24 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
           slot_of[op.result] = slot_of[alias[op.result]];
           continue;
         }
+        if (deferred(oi))
+          continue;  // dispatched where its add stands
+        // Operands: the op's own, or for a fused add its linear's and then
+        // the addend.
+        std::vector<int> operands = op.operands;
+        if (add_linear[oi] >= 0) {
+          operands = ops[add_linear[oi]].operands;
+          operands.push_back(addend_of[oi]);
+        }
         const Value &dst = values[op.result];
         const uint64_t d = next_slot++;
         slot_of[op.result] = static_cast<int64_t>(d);
         command(HEXIR_CMD_ALLOC, {d, static_cast<uint64_t>(dst.rows) * dst.cols * 8});
         program.u32(HEXIR_CMD_DISPATCH);
-        program.u32(static_cast<uint32_t>(2 + op.operands.size() + 1));
+        program.u32(static_cast<uint32_t>(2 + operands.size() + 1));
         program.u64(exe_index[oi]);
-        program.u64(op.operands.size() + 1);
-        for (int a : op.operands) {
+        program.u64(operands.size() + 1);
+        for (int a : operands) {
           if (slot_of[a] < 0) {
             error = "argument has no slot; it is not produced by a constant or "
                     "a call in this function";

@@ -70,6 +70,19 @@ hexir_status_t hexir_cuda_matmul_acc_f64(int ordinal, const double *a,
                                          uint32_t m, uint32_t n, uint32_t k,
                                          uint32_t flags, void *stream);
 
+/* c = epilogue(a . b + addend), addend [m x n] like c: a linear and the add
+ * that is its only user as one kernel (HEXIR_MATMUL_RELU applies the relu
+ * after the add).  Replaces hexir_ref_matmul_f64 followed by
+ * hexir_ref_add_f64 (runtime/src/kernels/reference_kernels.c:3,15): the
+ * product is rounded to f64 before the add, so the result has the bits of
+ * hexir_cuda_matmul_f64 then hexir_cuda_add_f64 under the same k split.
+ * addend may equal c. */
+hexir_status_t hexir_cuda_matmul_add_f64(int ordinal, const double *a,
+                                         const double *b, const double *addend,
+                                         double *c, uint32_t m, uint32_t n,
+                                         uint32_t k, uint32_t flags,
+                                         void *stream);
+
 /* c[i] = a[i] + b[i] for i < n.  Replaces hexir_ref_add_f64
  * (runtime/src/kernels/reference_kernels.c:15). */
 hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,

@@ -11,6 +11,9 @@
  *     form a linear takes when its only user is a relu on the same device.  A
  *     runtime that does not know kind 4 rejects it instead of silently
  *     dropping the relu.
+ *   - kernel kinds 5 and 6, HEXIR_KERNEL_MATMUL_ADD(_RELU): a . b + d (then
+ *     the relu), a linear whose only user is an add (whose only user is a
+ *     relu) on the same device.  DISPATCH operands: a, b, d, destination.
  *   - the LAUNCH section (module.h kind 5), one hexir_launch_entry_t per
  *     executable, in executable order.
  */
@@ -43,6 +46,8 @@ typedef enum {
   HEXIR_KERNEL_ADD = 2,         /* c = a + b, elementwise over m*n */
   HEXIR_KERNEL_RELU = 3,        /* y = x > 0 ? x : 0, elementwise over m*n */
   HEXIR_KERNEL_MATMUL_RELU = 4, /* extension: c = relu(a . b) */
+  HEXIR_KERNEL_MATMUL_ADD = 5,  /* extension: c = a . b + d */
+  HEXIR_KERNEL_MATMUL_ADD_RELU = 6, /* extension: c = relu(a . b + d) */
 } hexir_kernel_kind_t;
 
 #define HEXIR_NAME_SIZE 32

@@ -257,3 +257,67 @@ def test_reference_runtime_runs_our_cpu_modules(tmp_path):
         res = subprocess.run([oracle.REF_RUN, "--quiet", str(path)],
                              capture_output=True, text=True, check=True)
         assert res.stdout == case["stdout_quiet"]
+
+
+def test_linear_add_relu_fuses_at_the_add():
+    """linear -> add -> relu on one GPU spec: one matmul_add_relu executable
+    named after the linear (kind 6), dispatched where the add stands with
+    operands a, w, addend, destination; the relu is folded."""
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.relu(p.add(p.linear(a, b), b)))
+    blob = p.emit("hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda")
+    exes = hx.read_executables(blob)
+    assert [(e.name, e.kind, e.device, e.m, e.n, e.k) for e in exes] == [
+        ("linear_0", 6, 1, 2, 2, 2)]
+    assert hx.read_program(blob) == [
+        (2, (0, 0, 32)), (2, (1, 32, 32)), (1, (2, 32)),
+        (3, (0, 4, 0, 1, 1, 2)), (4, (2, 2, 2)), (0, ())]
+    # The linear as the add's second operand fuses the same way.
+    p2 = hx.Program()
+    a, b = two_by_two(p2)
+    p2.print(p2.relu(p2.add(b, p2.linear(a, b))))
+    assert [e.kind for e in hx.read_executables(
+        p2.emit("hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda"))] == [6]
+    nofuse = hx.read_executables(p.emit(
+        "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda", _ffi.EMIT_NO_FUSE))
+    assert [(e.name, e.kind) for e in nofuse] == [
+        ("linear_0", 1), ("add_1", 2), ("relu_2", 3)]
+
+
+def test_linear_add_fusion_rules():
+    p = hx.Program()
+    a, b = two_by_two(p)
+    s = p.add(p.linear(a, b), b)
+    p.print(s)
+    p.print(p.relu(s))  # the add has a second user: the relu stays
+    exes = hx.read_executables(p.emit("hexir.linear=cuda,hexir.add=cuda,"
+                                      "hexir.relu=cuda"))
+    assert [(e.name, e.kind) for e in exes] == [("linear_0", 5), ("relu_2", 3)]
+    # Different devices never fuse; a linear with two users never fuses.
+    mixed = hx.read_executables(p.emit("hexir.linear=cuda,hexir.add=cpu"))
+    assert [(e.name, e.kind, e.device) for e in mixed][:2] == [
+        ("linear_0", 1, 1), ("add_1", 2, 0)]
+    p3 = hx.Program()
+    a, b = two_by_two(p3)
+    m = p3.linear(a, b)
+    p3.print(p3.add(m, m))
+    assert [e.kind for e in hx.read_executables(
+        p3.emit("hexir.linear=cuda,hexir.add=cuda"))] == [1, 2]
+
+
+def test_fused_add_waits_for_an_addend_computed_after_the_linear():
+    """The addend is a relu computed after the linear: the fused dispatch
+    stands where the add does, after the relu that defines its addend."""
+    p = hx.Program()
+    a, b = two_by_two(p)
+    lin = p.linear(a, b)
+    x = p.relu(p.constant(np.array([[-1.0, 2.0], [3.0, -4.0]])))
+    p.print(p.add(lin, x))
+    blob = p.emit("hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda")
+    exes = hx.read_executables(blob)
+    assert [(e.name, e.kind) for e in exes] == [("relu_1", 3), ("linear_0", 5)]
+    cmds = hx.read_program(blob)
+    dispatches = [ops for kind, ops in cmds if kind == 3]
+    assert dispatches[0][0] == 0 and dispatches[1][0] == 1  # relu, then fused
+    assert dispatches[1][1] == 4 and dispatches[1][4] == dispatches[0][3]

@@ -278,3 +278,38 @@ def test_matmul_acc_separate_input_and_errors(gpu):
     assert lib.hexir_cuda_matmul_acc_f64(0, ba.ptr, k, bb.ptr, bi.ptr, bc.ptr,
                                          m, n, k, _ffi.MATMUL_SPLIT_K(2),
                                          None) == _ffi.ERROR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("m,n,k,flags", [
+    (256, 256, 256, 0),
+    (300, 200, 1000, _ffi.MATMUL_RELU),                 # 128-row tile
+    (40, 264, 2048, _ffi.MATMUL_RELU),                  # 64-row tile
+    (9, 130, 512, 0),                                   # 16-row tile, n % 4 != 0
+    (1024, 1024, 1024, _ffi.MATMUL_RELU),               # split k
+    (77, 131, 301, _ffi.MATMUL_RELU | _ffi.MATMUL_FORCE_GUARDED),
+    (64, 64, 0, _ffi.MATMUL_RELU),                      # empty sum
+])
+def test_fused_matmul_add_is_matmul_then_add(gpu, m, n, k, flags):
+    """hexir_cuda_matmul_add_f64 = hexir_cuda_matmul_f64, then
+    hexir_cuda_add_f64 (then the relu), bit for bit under the same plan."""
+    rng = np.random.default_rng(m * 31 + n + k)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    d = rng.uniform(-1, 1, (m, n))
+    ba, bb, bd = gpu.upload(a if k else np.zeros(1)), \
+        gpu.upload(b if k else np.zeros(1)), gpu.upload(d)
+    fused, prod, two = (gpu.buffer(m * n * 8) for _ in range(3))
+    hx.cuda_matmul_add(0, ba.ptr, bb.ptr, bd.ptr, fused.ptr, m, n, k, flags,
+                       gpu.stream)
+    hx.cuda_matmul(0, ba.ptr, bb.ptr, prod.ptr, m, n, k,
+                   flags & ~_ffi.MATMUL_RELU, gpu.stream)
+    hx.cuda_add(0, prod.ptr, bd.ptr, two.ptr, m * n, gpu.stream)
+    if flags & _ffi.MATMUL_RELU:
+        hx.cuda_relu(0, two.ptr, two.ptr, m * n, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    got, want2 = fused.read((m, n)), two.read((m, n))
+    assert np.array_equal(bits(got), bits(want2))
+    want = oracle.add(oracle.matmul(a, b) if k else np.zeros((m, n)), d)
+    if flags & _ffi.MATMUL_RELU:
+        want = oracle.relu(want)
+    assert oracle.normwise_error(got, want) <= TOL

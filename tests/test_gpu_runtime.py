@@ -419,3 +419,39 @@ def test_dispatch_into_a_kept_constant_never_changes_it():
         assert np.array_equal(bits(out), bits(outs[0]))
     assert mod.kept_bytes == a.nbytes + w.nbytes
     mod.close()
+
+
+def test_fused_linear_add_relu_module_matches_unfused():
+    """The reference's roundtrip graph shape (linear -> add -> relu) placed
+    on cuda: one fused executable, bit-identical to the three unfused
+    kernels and within the bar of the oracle."""
+    r = hx.Rng(19)
+    a, w, b = r.uniform((700, 512)), r.uniform((512, 384)), r.uniform((700, 384))
+    p = hx.Program()
+    p.relu(p.add(p.linear(p.constant(a), p.constant(w)), p.constant(b)))
+    placement = "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda"
+    fused_blob = p.emit(placement)
+    assert [e.kind for e in hx.read_executables(fused_blob)] == [6]
+    dev = hx.Device("cuda")
+    fused = hx.execute(hx.Module(fused_blob), dev, out_shape=(700, 384))
+    plain = hx.execute(hx.Module(p.emit(placement, _ffi.EMIT_NO_FUSE)), dev,
+                       out_shape=(700, 384))
+    assert np.array_equal(bits(fused), bits(plain))
+    want = oracle.relu(oracle.add(oracle.matmul(a, w), b))
+    assert oracle.normwise_error(fused, want) <= TOL
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+def test_row_sharded_fused_linear_add_relu():
+    """linear -> add -> relu on cuda:0-1: the fused kernel per shard with the
+    addend's rows split like a's; equals the one-GPU fused module."""
+    r = hx.Rng(23)
+    a, w, b = r.uniform((1001, 256)), r.uniform((256, 132)), r.uniform((1001, 132))
+    p = hx.Program()
+    p.relu(p.add(p.linear(p.constant(a), p.constant(w)), p.constant(b)))
+    devs = [hx.Device("cuda:0"), hx.Device("cuda:1")]
+    sharded = hx.execute(hx.Module(p.emit("hexir.linear=cuda:0-1,hexir.add=cuda:0-1,"
+                                          "hexir.relu=cuda:0-1")),
+                         devs, out_shape=(1001, 132))
+    want = oracle.relu(oracle.add(oracle.matmul(a, w), b))
+    assert oracle.normwise_error(sharded, want) <= TOL

@@ -247,3 +247,35 @@ def test_keep_constants_on_a_cpu_run_keeps_nothing():
     assert mod.kept_bytes == 0
     mod.keep_constants(False)
     assert hx.lib().hexir_module_keep_constants(None, 1) == _ffi.ERROR_INVALID_ARGUMENT
+
+
+def _as_host_module(blob: bytes) -> bytes:
+    """The module with every executable moved to the host (device 0, no
+    image): the form a hand-made module takes to run a fused kind on a CPU."""
+    off, _ = hx.read_sections(blob)[4]
+    count, _ = struct.unpack_from("<II", blob, off)
+    out = bytearray(blob)
+    for i in range(count):
+        e = off + 8 + 80 * i
+        struct.pack_into("<I", out, e + 36, 0)           # device
+        struct.pack_into("<II", out, e + 56, 0, 0)       # image offset, size
+    return bytes(out)
+
+
+@pytest.mark.parametrize("relu", [False, True])
+def test_fused_matmul_add_kinds_run_on_the_host(relu):
+    """Kinds 5 and 6 on the host: the reference's matmul, add and relu in
+    sequence, bit for bit."""
+    r = hx.Rng(17)
+    a, w, b = r.uniform((24, 40)), r.uniform((40, 16)), r.uniform((24, 16))
+    p = hx.Program()
+    s = p.add(p.linear(p.constant(a), p.constant(w)), p.constant(b))
+    p.print(p.relu(s) if relu else s)
+    blob = p.emit("hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda")
+    assert [e.kind for e in hx.read_executables(blob)] == [6 if relu else 5]
+    out = hx.execute(hx.Module(_as_host_module(blob)), hx.Device("cpu"),
+                     out_shape=(24, 16))
+    want = oracle.add(oracle.matmul(a, w), b)
+    if relu:
+        want = oracle.relu(want)
+    assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
