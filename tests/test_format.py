@@ -321,3 +321,28 @@ def test_fused_add_waits_for_an_addend_computed_after_the_linear():
     dispatches = [ops for kind, ops in cmds if kind == 3]
     assert dispatches[0][0] == 0 and dispatches[1][0] == 1  # relu, then fused
     assert dispatches[1][1] == 4 and dispatches[1][4] == dispatches[0][3]
+
+
+def test_dump_tool_decodes_fused_kinds_and_launch(tmp_path):
+    """python -m hexir_b200.dump: sections, fused kinds, the LAUNCH range and
+    the command list of each entry; a non-module exits 1."""
+    import sys
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.relu(p.add(p.linear(a, b), b)))
+    path = tmp_path / "m.hxb"
+    p.emit_file(str(path), "hexir.linear=cuda:0-1,hexir.add=cuda:0-1,"
+                           "hexir.relu=cuda:0-1")
+    res = subprocess.run([sys.executable, "-m", "hexir_b200.dump", str(path)],
+                         capture_output=True, text=True, check=True,
+                         cwd=os.path.dirname(os.path.dirname(__file__)))
+    assert "section LAUNCH" in res.stdout
+    assert "linear_0" in res.stdout and "matmul_add_relu" in res.stdout
+    assert "cuda:0-1" in res.stdout
+    assert "DISPATCH linear_0 (0 1 1) -> slot 2" in res.stdout
+    bad = tmp_path / "bad.hxb"
+    bad.write_bytes(b"not a module at all, not even close")
+    res = subprocess.run([sys.executable, "-m", "hexir_b200.dump", str(bad)],
+                         capture_output=True, text=True,
+                         cwd=os.path.dirname(os.path.dirname(__file__)))
+    assert res.returncode == 1 and "not a version 3 hexir module" in res.stderr
