@@ -47,6 +47,9 @@ def format_command(kind: int, ops: tuple, exes: list) -> str:
 
 
 def dump(blob: bytes, out=sys.stdout) -> None:
+    if len(blob) < api.HEADER.size or blob[:8] != b"HEXIRMOD":
+        raise ValueError("not a version 3 hexir module")
+    api.read_sections(blob)  # checks the version and the section table
     magic, version, flags, count, _ = api.HEADER.unpack_from(blob, 0)
     print(f"module: {magic.decode(errors='replace')} v{version} flags={flags} "
           f"{count} sections, {len(blob)} bytes", file=out)
