@@ -35,6 +35,8 @@ MATMUL_RELU = 0x1
 MATMUL_FORCE_TMA = 0x100
 MATMUL_FORCE_GUARDED = 0x200
 MATMUL_REMOTE_OUTPUT = 0x400
+MATMUL_NO_STREAM_K = 0x800
+MATMUL_FORCE_STREAM_K = 0x2000
 SHARD_GATHER_NCCL = 0x1000
 
 

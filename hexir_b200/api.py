@@ -445,7 +445,8 @@ def cuda_synchronize(ordinal: int, stream: int = 0) -> None:
 def matmul_plan(m: int, n: int, k: int, flags: int = 0, ordinal: int = 0,
                 a: int = 0, b: int = 0, c: int = 0) -> tuple:
     """(variant, split_k): 1 = TMA 128-row tiles, 2 = guarded kernel,
-    3 = TMA 16-row tiles, 4 = TMA 64-row tiles."""
+    3 = TMA 16-row tiles, 4 = TMA 64-row tiles, 5 = 128-row tiles as a
+    stream-K launch (split_k: CTAs sharing the k units)."""
     v, s = C.c_int(), C.c_uint32()
     lib().hexir_cuda_matmul_plan(ordinal, a, b, c, m, n, k, flags, C.byref(v),
                                  C.byref(s))

@@ -84,6 +84,15 @@ typedef struct {
   uint32_t lda;          /* row stride of a in elements (>= k) */
   uint32_t reserved;
   const double *addend;  /* [m][n], with HEXIR_EPILOGUE_ADD */
+  /* Stream-K launches (hexir_linear_f64_tma_sk): tiles below sk_dp_tiles go
+   * whole to CTAs c, c + G, ... (G = gridDim.x); the k-tile units of the
+   * rest are dealt out in consecutive runs of sk_units per CTA.  A tile whose
+   * units span CTAs leaves each CTA's partial sums in sk_partials (slot 2c
+   * for the CTA's first tile of the run, 2c + 1 for its last), which
+   * hexir_linear_f64_sk_fixup sums in CTA order. */
+  uint32_t sk_dp_tiles;
+  uint32_t sk_units;
+  double *sk_partials;   /* [2 G][BM][BN] */
 } hexir_linear_args_t;
 
 typedef struct {

@@ -385,6 +385,195 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
     __threadfence_system();
 }
 
+// The k-tile steps of one CTA of a stream-K launch, in the order it runs
+// them: its data-parallel tiles whole, then its run of stream-K units.  The
+// producer and the consumers each walk them with a Cursor, which advances by
+// increments (no division per step: the per-k-tile budget of the DMMA loop
+// has no issue slots to spare).
+struct SkSteps {
+  uint32_t c, grid, dp_tiles, k_tiles, dp_steps, u0, n_steps;
+  __device__ __forceinline__ SkSteps(const hexir_linear_args_t &args) {
+    c = blockIdx.x;
+    grid = gridDim.x;
+    dp_tiles = args.sk_dp_tiles;
+    k_tiles = args.k_tiles;
+    const uint32_t tiles = args.tiles_m * args.tiles_n;
+    const uint32_t my_dp = dp_tiles > c ? (dp_tiles - c - 1) / grid + 1 : 0;
+    dp_steps = my_dp * k_tiles;
+    const uint32_t sk_total = (tiles - dp_tiles) * k_tiles;
+    u0 = min(c * args.sk_units, sk_total);
+    const uint32_t u1 = min(u0 + args.sk_units, sk_total);
+    n_steps = dp_steps + (u1 - u0);
+  }
+  __device__ __forceinline__ uint32_t first_sk_tile() const {
+    return dp_tiles + u0 / k_tiles;
+  }
+  // Position (tile, kt) of step i, advanced one step at a time.
+  struct Cursor {
+    uint32_t i, tile, kt;
+  };
+  __device__ __forceinline__ Cursor begin() const {
+    Cursor p;
+    p.i = 0;
+    if (dp_steps) {
+      p.tile = c;
+      p.kt = 0;
+    } else {
+      p.tile = first_sk_tile();
+      p.kt = u0 % k_tiles;
+    }
+    return p;
+  }
+  __device__ __forceinline__ void next(Cursor &p) const {
+    ++p.i;
+    if (p.i == dp_steps) {
+      p.tile = first_sk_tile();
+      p.kt = u0 % k_tiles;
+    } else if (++p.kt == k_tiles) {
+      p.kt = 0;
+      p.tile += p.i < dp_steps ? grid : 1u;
+    }
+  }
+};
+
+template <class T>
+__device__ __forceinline__ void linear_tma_sk_body(
+    const CUtensorMap *map_a, const CUtensorMap *map_b,
+    const hexir_linear_args_t &args) {
+  constexpr int BM = T::BM, BN = T::BN, BK = T::BK, STAGES = T::STAGES;
+  constexpr int MI = T::MI, NP = T::NP;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  double *sa = reinterpret_cast<double *>(smem);
+  double *sb = sa + STAGES * T::A_STAGE;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sb + STAGES * T::B_STAGE);
+  uint64_t *empty = full + STAGES;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool issuer = threadIdx.x == 0;
+  const SkSteps steps(args);
+  const int32_t nk = (int32_t)steps.n_steps;
+
+  if (issuer) {
+    prefetch_tensormap(map_a);
+    prefetch_tensormap(map_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], HEXIR_LINEAR_CONSUMER_WARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // The producer's cursor and the row / column of its current tile.
+  SkSteps::Cursor prod = steps.begin();
+  uint32_t prod_tile = ~0u, ptm = 0, ptn = 0;
+  auto issue = [&](int32_t i) {
+    const int s = i % STAGES;
+    if (prod.tile != prod_tile) {
+      prod_tile = prod.tile;
+      tile_of(prod_tile, args.tiles_m, args.tiles_n, args.group_m, ptm, ptn);
+    }
+    const uint32_t tm = ptm, tn = ptn, kt = prod.kt;
+    steps.next(prod);
+    mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
+    const int32_t k0 = (int32_t)(kt * BK);
+    double *as = sa + s * T::A_STAGE;
+    double *bs = sb + s * T::B_STAGE;
+#pragma unroll
+    for (int j = 0; j < BK / 8; ++j)
+      tma_load_2d(as + j * T::A_SLAB, map_a, k0 + j * 8, (int32_t)(tm * BM),
+                  &full[s]);
+#pragma unroll
+    for (int j = 0; j < BN / 16; ++j)
+      tma_load_2d(bs + j * T::B_SLAB, map_b, (int32_t)(tn * BN + j * 16), k0,
+                  &full[s]);
+  };
+  int32_t issued = 0;
+  if (issuer) {
+    for (; issued < nk && issued < STAGES; ++issued)
+      issue(issued);
+  }
+
+  const uint32_t g = lane >> 2, t = lane & 3;
+  const uint32_t wm = warp / T::WARPS_N, wn = warp % T::WARPS_N;
+  const bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
+  const bool vec4 = (args.epilogue & HEXIR_EPILOGUE_VEC4) != 0;
+  const double *addend =
+      (args.epilogue & HEXIR_EPILOGUE_ADD) ? args.addend : nullptr;
+  double acc[MI][2 * NP][4];
+  const uint32_t sa_addr = smem_addr(sa), sb_addr = smem_addr(sb);
+  bool ok = true;
+  uint32_t seg_kt0 = 0;  // first k-tile of the current segment
+  SkSteps::Cursor cur = steps.begin();
+  for (int32_t i = 0; i < nk; ++i, steps.next(cur)) {
+    const uint32_t tile = cur.tile, kt = cur.kt;
+    if (kt == 0 || (uint32_t)i == steps.dp_steps) {
+      seg_kt0 = kt;
+#pragma unroll
+      for (int a = 0; a < MI; ++a)
+#pragma unroll
+        for (int b = 0; b < 2 * NP; ++b)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            acc[a][b][q] = 0.0;
+    }
+    const int s = i % STAGES;
+    const uint32_t use = (uint32_t)i / STAGES;
+    if (!mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns)) {
+      ok = false;
+      break;
+    }
+    const uint32_t a_stage = sa_addr + s * T::A_STAGE * 8;
+    const uint32_t b_stage =
+        sb_addr + s * T::B_STAGE * 8 + (wn * NP) * T::B_SLAB * 8;
+#pragma unroll
+    for (int kk = 0; kk < BK / 8; ++kk)
+      dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
+                           b_stage, T::B_SLAB * 8, kk * 8, g, t);
+    __syncwarp();
+    if (lane == 0)
+      mbar_arrive(&empty[s]);
+    if (issuer && issued < nk) {
+      if (!mbar_wait_bounded(&empty[s], use & 1u, args.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      issue(issued++);
+    }
+    __syncwarp();
+    // Segment end: the tile's last k-tile or this CTA's last step.
+    if (kt + 1 == args.k_tiles || i + 1 == nk) {
+      uint32_t tm, tn;
+      tile_of(tile, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+      if (seg_kt0 == 0 && kt + 1 == args.k_tiles) {
+        store_warp_tile<MI, NP, true>(acc, args.c, args.m, args.n,
+                                      tm * BM + wm * T::WTM,
+                                      tn * BN + wn * T::WTN, relu, g, t, vec4,
+                                      addend);
+      } else {
+        const uint32_t slot =
+            2 * steps.c + (tile == steps.first_sk_tile() ? 0u : 1u);
+        store_warp_tile<MI, NP, true>(acc, args.sk_partials + (size_t)slot * BM * BN,
+                                      BM, BN, wm * T::WTM, wn * T::WTN, false, g,
+                                      t, true, nullptr);
+      }
+    }
+  }
+
+  if (issuer) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s)
+      if (issued > s) {
+        const uint32_t uses = (uint32_t)(issued - s + STAGES - 1) / STAGES;
+        mbar_wait_bounded(&full[s], (uses - 1) & 1u, args.timeout_ns);
+      }
+  }
+  if (ok && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
+    __threadfence_system();
+}
+
 }  // namespace hexir
 
 // 128 x 128 x 32 CTA tile: square and tall shapes (warp tile 64 x 32).
@@ -393,6 +582,53 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
                          const __grid_constant__ CUtensorMap map_b,
                          const hexir_linear_args_t args) {
   linear_tma_body<Tile128>(&map_a, &map_b, args);
+}
+
+// The 128 x 128 x 32 pipeline as a persistent stream-K launch (one CTA per
+// SM, see SkSteps): shapes with too few tiles to fill whole waves.
+extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
+    hexir_linear_f64_tma_sk(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b,
+                            const hexir_linear_args_t args) {
+  linear_tma_sk_body<Tile128>(&map_a, &map_b, args);
+}
+
+// Completes the stream-K tiles whose k units were split over CTAs: one CTA
+// per such tile sums the partial tiles in CTA order (the order of k), then
+// applies the epilogue (addend, relu).  Tiles owned by one CTA were stored by
+// it and are skipped.
+extern "C" __global__ void __launch_bounds__(256)
+    hexir_linear_f64_sk_fixup(const hexir_linear_args_t args) {
+  constexpr uint32_t BM = HEXIR_LINEAR_BM, BN = HEXIR_LINEAR_BN;
+  const uint32_t tile = args.sk_dp_tiles + blockIdx.x;
+  const uint32_t k_tiles = args.k_tiles, U = args.sk_units;
+  const uint32_t t0 = blockIdx.x * k_tiles;  // first unit of the tile
+  const uint32_t c0 = t0 / U, c1 = (t0 + k_tiles - 1) / U;
+  if (c0 == c1)
+    return;
+  uint32_t tm, tn;
+  tile_of(tile, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+  const bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
+  const bool add = (args.epilogue & HEXIR_EPILOGUE_ADD) != 0;
+  for (uint32_t e = threadIdx.x; e < BM * BN; e += blockDim.x) {
+    const uint32_t r = e / BN, col = e % BN;
+    const uint32_t row = tm * BM + r, gcol = tn * BN + col;
+    if (row >= args.m || gcol >= args.n)
+      continue;
+    double s = 0.0;
+    for (uint32_t c = c0; c <= c1; ++c) {
+      // The CTA's run starts in this tile: its first-tile slot.
+      const uint32_t first = args.sk_dp_tiles + (c * U) / k_tiles;
+      const uint32_t slot = 2 * c + (tile == first ? 0u : 1u);
+      s = __dadd_rn(s, args.sk_partials[(size_t)slot * BM * BN + e]);
+    }
+    const size_t idx = (size_t)row * args.n + gcol;
+    if (add)
+      s = __dadd_rn(s, args.addend[idx]);
+    args.c[idx] = relu ? relu_ref(s) : s;
+  }
+  if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)
+    __threadfence_system();
 }
 
 // 64 x 128 x 32, 4 stages: 17..64 rows (warp tile 32 x 32).

@@ -268,7 +268,7 @@ hexir_status_t direct_rows(hexir_comm_t *comm, DeviceState *dev, KernelLib *lib,
     double *out = root ? c : reinterpret_cast<double *>(remote_c) + begin * n;
     const uint32_t remote = root ? 0u : HEXIR_MATMUL_REMOTE_OUTPUT;
     const MatmulPlan one = plan_matmul(dev, a_rows, w, out, m, n, k, relu);
-    if (pieces == 1 || one.split_k != 1) {
+    if (pieces == 1 || one.split_k != 1 || one.stream_k()) {
       if (!root)
         d.StreamWaitEvent(s, comm->gather_done, 0);
       status = launch_matmul(dev, lib, a_rows, w, out, m, n, k, relu | remote, s,

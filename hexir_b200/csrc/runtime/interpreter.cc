@@ -796,12 +796,36 @@ struct Vm {
         dev->state, reinterpret_cast<const double *>(a_dev),
         reinterpret_cast<const double *>(w_dev),
         reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k, relu);
-    const bool pieces = upload_w && whole.split_k == 1;
+    const bool pieces = upload_w && whole.split_k == 1 && !whole.stream_k();
     if (upload_w && !pieces) {
       // The one-shot launch splits k: upload w whole before the row chunks.
       if ((st = copy_range_to(ws, 0, ws.bytes, o, w_dev)) != HEXIR_OK)
         return st;
       ws.dev_valid.insert(o);
+    }
+    if (whole.stream_k()) {
+      // A stream-K plan's partial tiles follow the whole matrix's tiles:
+      // row chunks could not reproduce its sums, so the matmul runs as one
+      // launch after the uploads, and the capture copies after it.
+      if (upload_a) {
+        if ((st = copy_range_to(as, 0, as.bytes, o, a_dev)) != HEXIR_OK)
+          return st;
+        as.dev_valid.insert(o);
+      }
+      ContextGuard guard(dev->state->context);
+      Span *span = begin_span(dev);
+      std::string error;
+      st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(a_dev),
+                         reinterpret_cast<const double *>(w_dev),
+                         reinterpret_cast<double *>(c_dev), exe.m, exe.n, exe.k,
+                         relu, dev->stream, &error);
+      end_span(span);
+      if (st != HEXIR_OK) {
+        report(std::string("kernel '") + exe.name + "': " + error);
+        return st;
+      }
+      written_on_device(dst, o);
+      return HEXIR_OK;
     }
     CUstream cs = dev->copy_stream();
     if (!cs)

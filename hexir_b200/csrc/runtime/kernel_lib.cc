@@ -219,6 +219,12 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
       return nullptr;
     }
   }
+  // Optional: images written before the stream-K kernels existed lack them.
+  if (d.ModuleGetFunction(&lib->linear_tma_sk, lib->module,
+                          "hexir_linear_f64_tma_sk") != CUDA_SUCCESS ||
+      d.ModuleGetFunction(&lib->sk_fixup, lib->module,
+                          "hexir_linear_f64_sk_fixup") != CUDA_SUCCESS)
+    lib->linear_tma_sk = lib->sk_fixup = nullptr;
   size_t word_bytes = 0;
   r = d.ModuleGetGlobal(&lib->error_word, &word_bytes, lib->module,
                         "hexir_device_error_word");
@@ -238,6 +244,10 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
     r = d.FuncSetAttribute(lib->linear_guarded,
                            CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
                            HEXIR_LINEAR_G_SMEM_BYTES);
+  if (r == CUDA_SUCCESS && lib->linear_tma_sk)
+    r = d.FuncSetAttribute(lib->linear_tma_sk,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_LINEAR_SMEM_BYTES);
   if (r != CUDA_SUCCESS) {
     d.ModuleUnload(lib->module);
     fail(error, cuda_message("kernel library setup", r));
@@ -338,6 +348,29 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   // No empty pieces.
   p.split_k = std::max<uint32_t>(1, ceil_div(std::max<uint32_t>(p.k_tiles, 1),
                                              p.k_tiles_per_split));
+
+  // Stream-K for the 128-row tiles, on request only: whole waves of tiles
+  // stay data-parallel except the last one or two, whose k-tile units are
+  // dealt out evenly over one CTA per SM (runs of >= 4 units).  Measured on
+  // B200 it loses to the data-parallel and split-k schedules at every shape
+  // tried (2048^3: 29.9 against 31.6 TFLOP/s; 8192^3: 34.4 against 35.2),
+  // so the planner never picks it by itself.
+  if ((flags & HEXIR_MATMUL_FORCE_STREAM_K) && p.variant == kTma128 && !c_in &&
+      ((flags >> 16) & 0xFFu) == 0 && !(flags & HEXIR_MATMUL_NO_STREAM_K) &&
+      sms > 0) {
+    const uint64_t g = sms;
+    const uint64_t dp_tiles = tiles >= 2 * g ? (tiles / g - 1) * g : 0;
+    const uint64_t sk_units_total = (tiles - dp_tiles) * p.k_tiles;
+    const uint64_t units = (sk_units_total + g - 1) / g;
+    if (units >= 4) {
+      p.variant = kTma128Sk;
+      p.split_k = 1;
+      p.k_tiles_per_split = p.k_tiles;
+      p.sk_grid = static_cast<uint32_t>(g);
+      p.sk_dp_tiles = static_cast<uint32_t>(dp_tiles);
+      p.sk_units = static_cast<uint32_t>(units);
+    }
+  }
   return p;
 }
 
@@ -401,8 +434,10 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     return r == CUDA_SUCCESS ? HEXIR_OK
                              : fail(error, cuda_message("empty matmul", r));
   }
-  const MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in,
-                                   addend);
+  MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in, addend);
+  if (p.stream_k() && !lib->linear_tma_sk)  // an image without stream-K
+    p = plan_matmul(dev, a, b, c, m, n, k, flags | HEXIR_MATMUL_NO_STREAM_K, lda,
+                    c_in, addend);
 
   hexir_linear_args_t args;
   std::memset(&args, 0, sizeof(args));
@@ -436,6 +471,20 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                       (reinterpret_cast<uintptr_t>(addend) & 31u) == 0;
 
   std::unique_lock<std::mutex> ws_lock(dev->mu, std::defer_lock);
+  if (p.stream_k()) {
+    // Partial tiles of the k units split over CTAs: two slots per CTA.
+    ws_lock.lock();
+    hexir_status_t s = ensure_workspace(
+        dev, static_cast<size_t>(2) * p.sk_grid * HEXIR_LINEAR_BM *
+                 HEXIR_LINEAR_BN * sizeof(double),
+        error);
+    if (s != HEXIR_OK)
+      return s;
+    d.StreamWaitEvent(stream, dev->ws_ready, 0);
+    args.sk_partials = reinterpret_cast<double *>(dev->workspace);
+    args.sk_dp_tiles = p.sk_dp_tiles;
+    args.sk_units = p.sk_units;
+  }
   if (p.split_k > 1) {
     ws_lock.lock();
     hexir_status_t s = ensure_workspace(
@@ -474,6 +523,18 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     if (r != CUDA_SUCCESS)
       return fail(error, cuda_message("cuTensorMapEncodeTiled", r));
     void *params[] = {&map_a, &map_b, &args};
+    if (p.stream_k()) {
+      status = launch(lib->linear_tma_sk, p.sk_grid, 1, HEXIR_LINEAR_THREADS,
+                      HEXIR_LINEAR_SMEM_BYTES, stream, params,
+                      "launch hexir_linear_f64_tma_sk", error);
+      const unsigned sk_tiles = p.tiles_m * p.tiles_n - p.sk_dp_tiles;
+      void *fix_params[] = {&args};
+      if (status == HEXIR_OK)
+        status = launch(lib->sk_fixup, sk_tiles, 1, 256, 0, stream, fix_params,
+                        "launch hexir_linear_f64_sk_fixup", error);
+      d.EventRecord(dev->ws_ready, stream);
+      return status;
+    }
     CUfunction fn = lib->linear_tma;
     unsigned smem = HEXIR_LINEAR_SMEM_BYTES;
     const char *what = "launch hexir_linear_f64_tma";
@@ -693,7 +754,7 @@ extern "C" hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
   if (variant)
     *variant = p.variant;
   if (split_k)
-    *split_k = p.split_k;
+    *split_k = p.stream_k() ? p.sk_grid : p.split_k;
   return HEXIR_OK;
 }
 

@@ -25,6 +25,8 @@ struct KernelLib {
   CUfunction linear_tma_m64 = nullptr;  // 64-row tiles
   CUfunction linear_tma_m16 = nullptr;  // 16-row tiles
   CUfunction linear_guarded = nullptr;
+  CUfunction linear_tma_sk = nullptr;   // stream-K (absent in older images)
+  CUfunction sk_fixup = nullptr;
   CUfunction splitk_reduce = nullptr;
   CUfunction relu = nullptr;
   CUfunction add = nullptr;
@@ -68,6 +70,7 @@ enum MatmulVariant {
   kGuarded = 2,  // hexir_linear_f64_guarded, 64 x 64 x 16, any shape
   kTma16 = 3,    // hexir_linear_f64_tma_m16, 16 x 128 x 32
   kTma64 = 4,    // hexir_linear_f64_tma_m64, 64 x 128 x 32
+  kTma128Sk = 5, // hexir_linear_f64_tma_sk, 128 x 128 x 32, stream-K
 };
 
 struct MatmulPlan {
@@ -75,6 +78,9 @@ struct MatmulPlan {
   uint32_t split_k = 1;
   uint32_t tiles_m = 0, tiles_n = 0, k_tiles = 0, k_tiles_per_split = 0;
   uint32_t bm = 0, bn = 0, bk = 0;
+  // kTma128Sk: persistent grid, data-parallel tiles, k-tile units per CTA.
+  uint32_t sk_grid = 0, sk_dp_tiles = 0, sk_units = 0;
+  bool stream_k() const { return variant == kTma128Sk; }
 };
 
 // lda: row stride of a in elements (0 = k).  c_in: when non-null the sums

@@ -42,7 +42,15 @@ extern "C" {
 /* c is another GPU's memory (a peer or IPC mapping): the kernels fence their
  * stores at system scope before finishing. */
 #define HEXIR_MATMUL_REMOTE_OUTPUT 0x400u
-/* tests: split the k range into S pieces (1..255); 0 = choose automatically */
+/* Stream-K schedule for 128-row tiles (the k units of the last waves' tiles
+ * dealt out evenly over one CTA per SM, split tiles summed by a fix-up
+ * kernel in CTA order): used only on request -- it measured slower than
+ * the data-parallel and split-k schedules on B200 -- and only where no k
+ * split is requested and no c_in is given.  NO_STREAM_K overrides. */
+#define HEXIR_MATMUL_NO_STREAM_K 0x800u
+#define HEXIR_MATMUL_FORCE_STREAM_K 0x2000u
+/* tests: split the k range into S pieces (1..255; any S rules out stream-K);
+ * 0 = choose automatically */
 #define HEXIR_MATMUL_SPLIT_K(S) (((uint32_t)(S) & 0xFFu) << 16)
 
 /* c[m x n] = a[m x k] . b[k x n] (row-major f64), optionally relu'd.
@@ -101,7 +109,8 @@ hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream);
 /* Which matmul kernel a call with these arguments would launch:
  * 1 = TMA pipeline with 128-row tiles, 2 = guarded (any shape/alignment),
  * 3 = TMA with 16-row tiles (m <= 16), 4 = TMA with 64-row tiles
- * (16 < m <= 64); *split_k receives the k split. */
+ * (16 < m <= 64), 5 = the 128-row pipeline as a stream-K launch; *split_k
+ * receives the k split (for 5: the number of CTAs sharing the k units). */
 hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
                                       const double *b, double *c, uint32_t m,
                                       uint32_t n, uint32_t k, uint32_t flags,

@@ -313,3 +313,47 @@ def test_fused_matmul_add_is_matmul_then_add(gpu, m, n, k, flags):
     if flags & _ffi.MATMUL_RELU:
         want = oracle.relu(want)
     assert oracle.normwise_error(got, want) <= TOL
+
+
+@pytest.mark.parametrize("m,n,k,flags,add", [
+    (2048, 2048, 2048, 0, False),
+    (2048, 1024, 4096, _ffi.MATMUL_RELU, False),
+    (500, 2560, 2048, _ffi.MATMUL_RELU, True),     # ragged row tiles, fused add
+    (640, 2048, 1024, 0, True),
+    (128, 8192, 8192, _ffi.MATMUL_RELU, False),    # one row of tiles, long k
+    (100, 8192, 2048, 0, False),                   # a partial row tile
+])
+def test_stream_k_schedule(gpu, m, n, k, flags, add):
+    """The stream-K schedule (on request): a persistent launch plus fix-up,
+    within the bar of the oracle (rows sampled for the large shapes),
+    deterministic run to run, and within the bar of the planner's own
+    schedule."""
+    flags |= _ffi.MATMUL_FORCE_STREAM_K
+    assert hx.matmul_plan(m, n, k, flags)[0] == 5
+    assert hx.matmul_plan(m, n, k, flags & ~_ffi.MATMUL_FORCE_STREAM_K)[0] == 1
+    rng = np.random.default_rng(m + n + k)
+    a = rng.uniform(-1, 1, (m, k))
+    b = rng.uniform(-1, 1, (k, n))
+    d = rng.uniform(-1, 1, (m, n)) if add else None
+    ba, bb = gpu.upload(a), gpu.upload(b)
+    bd = gpu.upload(d) if add else None
+    outs = []
+    for extra in (0, 0, _ffi.MATMUL_NO_STREAM_K):  # forced, forced, planner
+        bc = gpu.buffer(m * n * 8)
+        if add:
+            hx.cuda_matmul_add(0, ba.ptr, bb.ptr, bd.ptr, bc.ptr, m, n, k,
+                               flags | extra, gpu.stream)
+        else:
+            hx.cuda_matmul(0, ba.ptr, bb.ptr, bc.ptr, m, n, k, flags | extra,
+                           gpu.stream)
+        hx.cuda_synchronize(0, gpu.stream)
+        outs.append(bc.read((m, n)))
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    rows = np.unique(np.linspace(0, m - 1, 40).astype(int))
+    want = oracle.matmul(a[rows], b)
+    if add:
+        want = oracle.add(want, d[rows])
+    if flags & _ffi.MATMUL_RELU:
+        want = oracle.relu(want)
+    assert oracle.normwise_error(outs[0][rows], want) <= TOL
+    assert oracle.normwise_error(outs[0], outs[2]) <= TOL
