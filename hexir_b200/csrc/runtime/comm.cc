@@ -84,6 +84,9 @@ struct hexir_comm_t {
   CUstream gather_stream = nullptr;  // row sends / receives
   CUevent chunk_done[kGatherChunks] = {};
   CUevent gather_done = nullptr;
+  // The weight broadcast on the side stream: its start (after the caller's
+  // queued work), each piece landing, the whole weight landed.
+  CUevent w_start = nullptr, w_piece[2] = {}, w_done = nullptr;
   // Direct row stores into the root's c (all ranks on one host, IPC works).
   bool direct = false;
   CUdeviceptr scratch = 0;  // descriptor [kDescBytes] + completion word
@@ -218,85 +221,6 @@ uint32_t broadcast_pieces(uint32_t k, uint32_t bounds[3]) {
   return 2;
 }
 
-// Direct row stores (see hexir_sharded_linear_f64).  The weight is broadcast
-// in k pieces on the comm's high-priority side stream.  Every rank runs one
-// launch per piece, each continuing the previous one's sums (same operations
-// as one unsplit launch): a peer waits for each piece to land and keeps its
-// partial sums in its staging rows `c`, the last piece storing into the
-// root's output over NVLink; the root needs no broadcast and sums in its own
-// rows of c at once, its short first pieces leaving SMs free for the
-// broadcast's NCCL kernels.  Where a rank's one-shot plan would split k it
-// runs that plan instead (a peer after the whole weight has landed).  A
-// one-word all-reduce then orders the root's stream after every peer's
-// kernels.  A rank whose launch failed still takes every collective step, so
-// no rank waits for ever.
-hexir_status_t direct_rows(hexir_comm_t *comm, DeviceState *dev, KernelLib *lib,
-                           const double *a_rows, double *w, double *c,
-                           CUdeviceptr remote_c, uint64_t begin, uint64_t rows,
-                           uint32_t n, uint32_t k, uint32_t flags, CUstream s,
-                           hexir_status_t status) {
-  const Driver &d = driver();
-  const Nccl &nc = nccl();
-  std::string error;
-  cudaStream_t cs = reinterpret_cast<cudaStream_t>(s);
-  CUstream bs = comm->gather_stream;
-  cudaStream_t bcs = reinterpret_cast<cudaStream_t>(bs);
-  uint32_t bounds[3];
-  const uint32_t pieces = broadcast_pieces(k, bounds);
-  // The side stream starts after the caller's queued work (w's contents).
-  CUevent start = comm->chunk_done[0];
-  CUresult cr = d.EventRecord(start, s);
-  if (cr == CUDA_SUCCESS)
-    cr = d.StreamWaitEvent(bs, start, 0);
-  if (cr != CUDA_SUCCESS)
-    return comm_fail(cuda_message("broadcast stream", cr));
-  for (uint32_t j = 0; j < pieces; ++j) {
-    double *wp = w + static_cast<size_t>(bounds[j]) * n;
-    ncclResult_t nr =
-        nc.Broadcast(wp, wp, static_cast<size_t>(bounds[j + 1] - bounds[j]) * n,
-                     ncclDouble, 0, comm->comm, bcs);
-    if (nr != ncclSuccess)
-      return comm_fail(nccl_message("ncclBroadcast (weight piece)", nr));
-    d.EventRecord(comm->chunk_done[1 + j], bs);
-  }
-  d.EventRecord(comm->gather_done, bs);
-
-  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
-  const uint32_t m = static_cast<uint32_t>(rows);
-  if (rows && status == HEXIR_OK) {
-    const bool root = comm->rank == 0;
-    double *out = root ? c : reinterpret_cast<double *>(remote_c) + begin * n;
-    const uint32_t remote = root ? 0u : HEXIR_MATMUL_REMOTE_OUTPUT;
-    const MatmulPlan one = plan_matmul(dev, a_rows, w, out, m, n, k, relu);
-    if (pieces == 1 || one.split_k != 1 || one.stream_k()) {
-      if (!root)
-        d.StreamWaitEvent(s, comm->gather_done, 0);
-      status = launch_matmul(dev, lib, a_rows, w, out, m, n, k, relu | remote, s,
-                             &error);
-    } else {
-      for (uint32_t j = 0; j < pieces && status == HEXIR_OK; ++j) {
-        const bool last = j + 1 == pieces;
-        if (!root)
-          d.StreamWaitEvent(s, comm->chunk_done[1 + j], 0);
-        status = launch_matmul(
-            dev, lib, a_rows + bounds[j], w + static_cast<size_t>(bounds[j]) * n,
-            last ? out : c, m, n, bounds[j + 1] - bounds[j],
-            (last ? relu | remote : 0u) | HEXIR_MATMUL_SPLIT_K(1), s, &error, k,
-            j ? c : nullptr);
-      }
-    }
-    if (status != HEXIR_OK)
-      set_last_error(error);
-  }
-  // Later work on the caller's stream (a new w) waits for the broadcast.
-  d.StreamWaitEvent(s, comm->gather_done, 0);
-  void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
-  ncclResult_t nr = nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
-  if (nr != ncclSuccess)
-    return comm_fail(nccl_message("ncclAllReduce (row stores done)", nr));
-  return status;
-}
-
 }  // namespace
 
 extern "C" {
@@ -376,6 +300,10 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
     cr = d.EventCreate(&comm->gather_done, CU_EVENT_DISABLE_TIMING);
   for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kDescSlots; ++i)
     cr = d.EventCreate(&comm->desc_done[i], CU_EVENT_DISABLE_TIMING);
+  for (CUevent *ev : {&comm->w_start, &comm->w_piece[0], &comm->w_piece[1],
+                      &comm->w_done})
+    if (cr == CUDA_SUCCESS)
+      cr = d.EventCreate(ev, CU_EVENT_DISABLE_TIMING);
   if (cr == CUDA_SUCCESS)
     cr = d.MemAlloc(&comm->scratch, kDescBytes + 16);
   if (cr == CUDA_SUCCESS)
@@ -414,6 +342,10 @@ void hexir_comm_release(hexir_comm_t *comm) {
         d.EventDestroy(ev);
     if (comm->gather_done)
       d.EventDestroy(comm->gather_done);
+    for (CUevent ev : {comm->w_start, comm->w_piece[0], comm->w_piece[1],
+                       comm->w_done})
+      if (ev)
+        d.EventDestroy(ev);
     if (comm->mapped_count)
       d.CtxSynchronize();
     for (size_t i = 0; i < comm->mapped_count; ++i)
@@ -467,18 +399,31 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   uint64_t begin = 0, rows = 0;
   hexir_shard_rows(m, ranks, static_cast<uint32_t>(comm->rank), &begin, &rows);
 
-  // 0. Whether this call's rows are stored straight into the root's c: the
-  //    root describes c (IPC handle + offset) and every rank reads that
-  //    description, so all of them take the same branch.
+  const bool root = comm->rank == 0;
+  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
+  const uint32_t my_rows = static_cast<uint32_t>(rows);
+  // The weight goes out in k pieces (one for short k or a single rank).  A
+  // rank computes behind them -- one launch per piece, each continuing the
+  // previous one's sums, the same operations as one unsplit launch -- where
+  // its one-shot plan has no k split; otherwise it runs that plan once the
+  // whole weight has landed.
+  uint32_t bounds[3] = {0, k, k};
+  const uint32_t pieces = ranks > 1 ? broadcast_pieces(k, bounds) : 1;
+  const MatmulPlan one = plan_matmul(dev, a_rows, w, c, my_rows, n, k, relu);
+  const bool chain = pieces > 1 && one.split_k == 1 && !one.stream_k();
+
+  // 0. Where the rows go: the root describes its c (IPC handle + offset)
+  //    every call and every rank reads that description, so all of them
+  //    take the same branch.  A peer reads it only after its first piece is
+  //    queued, so the host round trip hides behind that piece.
+  RootOutput *desc = nullptr;
+  CUevent desc_ready = nullptr;
   bool direct = false;
-  CUdeviceptr remote_c = 0;
-  hexir_status_t peer_status = HEXIR_OK;
+  CUresult cr = CUDA_SUCCESS;
   if (ranks > 1 && comm->direct) {
-    CUevent done = nullptr;
-    RootOutput *desc = next_desc(comm, &done);
+    desc = next_desc(comm, &desc_ready);
     std::memset(desc, 0, sizeof(*desc));
-    CUresult cr = CUDA_SUCCESS;
-    if (comm->rank == 0) {
+    if (root) {
       CUdeviceptr base = 0;
       size_t size = 0;
       const CUdeviceptr cp = reinterpret_cast<CUdeviceptr>(c);
@@ -487,6 +432,7 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
                     d.MemGetAddressRange(&base, &size, cp) == CUDA_SUCCESS &&
                     d.IpcGetMemHandle(&desc->handle, base) == CUDA_SUCCESS;
       desc->offset = desc->valid ? cp - base : 0;
+      direct = desc->valid;
       cr = d.MemcpyHtoDAsync(comm->scratch, desc, sizeof(*desc), s);
     }
     if (cr != CUDA_SUCCESS)
@@ -496,38 +442,115 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
         nc.Broadcast(buf, buf, kDescBytes, ncclUint8, 0, comm->comm, cs);
     if (nr != ncclSuccess)
       return comm_fail(nccl_message("ncclBroadcast (output descriptor)", nr));
-    if (comm->rank != 0)
+    if (!root)
       cr = d.MemcpyDtoHAsync(desc, comm->scratch, sizeof(*desc), s);
     if (cr == CUDA_SUCCESS)
-      cr = d.EventRecord(done, s);
-    // A peer waits here until the root's stream has reached this call.
-    if (cr == CUDA_SUCCESS && comm->rank != 0)
-      cr = d.EventSynchronize(done);
+      cr = d.EventRecord(desc_ready, s);
+    if (cr != CUDA_SUCCESS)
+      return comm_fail(cuda_message("output descriptor", cr));
+  }
+
+  // 1. The weight from the root to everyone over NVLink, piece by piece, on
+  //    the high-priority side stream (it starts after the caller's queued
+  //    work, which may have written w).
+  CUstream bs = comm->gather_stream;
+  cudaStream_t bcs = reinterpret_cast<cudaStream_t>(bs);
+  cr = d.EventRecord(comm->w_start, s);
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamWaitEvent(bs, comm->w_start, 0);
+  if (cr != CUDA_SUCCESS)
+    return comm_fail(cuda_message("broadcast stream", cr));
+  for (uint32_t j = 0; j < pieces; ++j) {
+    double *wp = w + static_cast<size_t>(bounds[j]) * n;
+    ncclResult_t nr =
+        nc.Broadcast(wp, wp, static_cast<size_t>(bounds[j + 1] - bounds[j]) * n,
+                     ncclDouble, 0, comm->comm, bcs);
+    if (nr != ncclSuccess)
+      return comm_fail(nccl_message("ncclBroadcast (weight)", nr));
+    d.EventRecord(comm->w_piece[j], bs);
+  }
+  d.EventRecord(comm->w_done, bs);
+
+  // 2. The first piece over all of this rank's rows (the root needs no
+  //    broadcast): partial sums in c (a peer's staging rows).
+  hexir_status_t status = HEXIR_OK;
+  if (chain && my_rows) {
+    if (!root)
+      d.StreamWaitEvent(s, comm->w_piece[0], 0);
+    status = launch_matmul(dev, lib, a_rows, w, c, my_rows, n, bounds[1],
+                           HEXIR_MATMUL_SPLIT_K(1), s, &error, k, nullptr);
+  }
+
+  // 3. A peer learns where its rows go.
+  CUdeviceptr remote_c = 0;
+  if (desc && !root) {
+    cr = d.EventSynchronize(desc_ready);
     if (cr != CUDA_SUCCESS)
       return comm_fail(cuda_message("output descriptor", cr));
     direct = desc->magic == kRootOutputMagic && desc->valid;
-    if (direct && comm->rank != 0) {
-      peer_status = map_root_output(comm, desc->handle, &remote_c);
+    if (direct && status == HEXIR_OK) {
+      status = map_root_output(comm, desc->handle, &remote_c);
       remote_c += desc->offset;
     }
   }
 
-  if (direct)
-    return direct_rows(comm, dev, lib, a_rows, w, c, remote_c, begin, rows, n, k,
-                       flags, s, peer_status);
+  // The rest of a row range [cb, cb + cr) of this rank: the remaining k
+  // pieces continuing the first one's sums, or the one-shot plan.
+  auto finish_rows = [&](uint64_t cb, uint64_t count, double *out,
+                         uint32_t out_flags) -> hexir_status_t {
+    if (!count)
+      return HEXIR_OK;
+    const uint32_t mm = static_cast<uint32_t>(count);
+    if (!chain) {
+      if (!root)
+        d.StreamWaitEvent(s, comm->w_done, 0);
+      return launch_matmul(dev, lib, a_rows + cb * k, w, out, mm, n, k,
+                           relu | out_flags, s, &error);
+    }
+    hexir_status_t st = HEXIR_OK;
+    for (uint32_t j = 1; j < pieces && st == HEXIR_OK; ++j) {
+      const bool last = j + 1 == pieces;
+      if (!root)
+        d.StreamWaitEvent(s, comm->w_piece[j], 0);
+      st = launch_matmul(dev, lib, a_rows + cb * k + bounds[j],
+                         w + static_cast<size_t>(bounds[j]) * n,
+                         last ? out : c + cb * n, mm, n, bounds[j + 1] - bounds[j],
+                         (last ? relu | out_flags : 0u) | HEXIR_MATMUL_SPLIT_K(1),
+                         s, &error, k, c + cb * n);
+    }
+    return st;
+  };
 
-  // 1. Weight from the root to everyone, over NVLink.
-  ncclResult_t r = nc.Broadcast(w, w, static_cast<size_t>(k) * n, ncclDouble, 0,
-                                comm->comm, cs);
-  if (r != ncclSuccess) {
-    set_last_error(nccl_message("ncclBroadcast", r));
-    return HEXIR_ERROR_DEVICE;
+  if (direct) {
+    // 4. Every rank's kernel stores its output tiles into the root's c over
+    //    NVLink (system-scope fence before each CTA retires); a one-word
+    //    all-reduce then orders the root's stream after every peer's
+    //    kernels.  A rank whose launch failed still takes every collective
+    //    step, so no rank waits for ever.
+    if (status == HEXIR_OK) {
+      double *out = root ? c : reinterpret_cast<double *>(remote_c) + begin * n;
+      status = finish_rows(0, my_rows, out, root ? 0u : HEXIR_MATMUL_REMOTE_OUTPUT);
+    }
+    if (status != HEXIR_OK)
+      set_last_error(error.empty() ? hexir_status_string(status) : error);
+    d.StreamWaitEvent(s, comm->w_done, 0);
+    void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
+    ncclResult_t nr =
+        nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
+    if (nr != ncclSuccess)
+      return comm_fail(nccl_message("ncclAllReduce (row stores done)", nr));
+    return status;
+  }
+  if (status != HEXIR_OK) {
+    set_last_error(error);
+    return status;
   }
 
-  // 2. This rank's rows in up to kGatherChunks pieces; the root writes
-  //    straight into its part of c.  3. Each finished piece goes to the root
-  //    on the gather stream while the next piece computes.  Every rank splits
-  //    its rows by the same rule, so the root knows each peer's pieces.
+  // 4'. Rows by NCCL: this rank's rows in up to kGatherChunks pieces of
+  //     shrinking size; the root writes straight into its part of c, and
+  //     each finished piece of a peer goes to the root on the side stream
+  //     while the next piece computes.  Every rank splits its rows by the
+  //     same rule, so the root knows each peer's pieces.
   uint64_t ignore_b = 0, ignore_c = 0;
   const uint32_t my_chunks = rows ? gather_piece(rows, 0, &ignore_b, &ignore_c) : 0;
   uint32_t max_chunks = 0;
@@ -540,16 +563,12 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   cudaStream_t gs = reinterpret_cast<cudaStream_t>(comm->gather_stream);
   for (uint32_t i = 0; i < max_chunks; ++i) {
     if (i < my_chunks) {
-      uint64_t cb = 0, cr = 0;
-      gather_piece(rows, i, &cb, &cr);
-      if (cr) {
-        hexir_status_t st = launch_matmul(
-            dev, lib, a_rows + cb * k, w, c + cb * n, static_cast<uint32_t>(cr),
-            n, k, flags & HEXIR_MATMUL_RELU, s, &error);
-        if (st != HEXIR_OK) {
-          set_last_error(error);
-          return st;
-        }
+      uint64_t cb = 0, cnt = 0;
+      gather_piece(rows, i, &cb, &cnt);
+      hexir_status_t st = finish_rows(cb, cnt, c + cb * n, 0u);
+      if (st != HEXIR_OK) {
+        set_last_error(error);
+        return st;
       }
     }
     if (ranks == 1)
@@ -557,35 +576,33 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
     d.EventRecord(comm->chunk_done[i], s);
     d.StreamWaitEvent(comm->gather_stream, comm->chunk_done[i], 0);
     nc.GroupStart();
-    if (comm->rank == 0) {
+    if (root) {
       for (uint32_t peer = 1; peer < ranks; ++peer) {
         uint64_t pb = 0, pr = 0;
         hexir_shard_rows(m, ranks, peer, &pb, &pr);
-        uint64_t cb = 0, cr = 0;
+        uint64_t cb = 0, cnt = 0;
         if (!pr)
           continue;
-        gather_piece(pr, i, &cb, &cr);
-        if (cr)
-          nc.Recv(c + (pb + cb) * n, cr * n, ncclDouble, static_cast<int>(peer),
+        gather_piece(pr, i, &cb, &cnt);
+        if (cnt)
+          nc.Recv(c + (pb + cb) * n, cnt * n, ncclDouble, static_cast<int>(peer),
                   comm->comm, gs);
       }
     } else if (i < my_chunks) {
-      uint64_t cb = 0, cr = 0;
-      gather_piece(rows, i, &cb, &cr);
-      if (cr)
-        nc.Send(c + cb * n, cr * n, ncclDouble, 0, comm->comm, gs);
+      uint64_t cb = 0, cnt = 0;
+      gather_piece(rows, i, &cb, &cnt);
+      if (cnt)
+        nc.Send(c + cb * n, cnt * n, ncclDouble, 0, comm->comm, gs);
     }
-    r = nc.GroupEnd();
-    if (r != ncclSuccess) {
-      set_last_error(nccl_message("ncclGroupEnd (row gather)", r));
+    ncclResult_t nr = nc.GroupEnd();
+    if (nr != ncclSuccess) {
+      set_last_error(nccl_message("ncclGroupEnd (row gather)", nr));
       return HEXIR_ERROR_DEVICE;
     }
   }
-  if (ranks > 1) {
-    // The caller's stream completes only after the gather.
-    d.EventRecord(comm->gather_done, comm->gather_stream);
-    d.StreamWaitEvent(s, comm->gather_done, 0);
-  }
+  // The caller's stream completes only after the broadcast and the gather.
+  d.EventRecord(comm->gather_done, comm->gather_stream);
+  d.StreamWaitEvent(s, comm->gather_done, 0);
   return HEXIR_OK;
 }
 

@@ -724,7 +724,18 @@ struct Vm {
   // split, or the one-shot's own split for every row chunk), so results are
   // bit-identical to a single launch.
   static constexpr uint64_t kPipelineBytes = 64ull << 20;
-  static constexpr uint32_t kPipelineChunks = 4;
+  // Row chunks: 1/4, 1/4, 1/4, 1/8, 1/8 of the rows (128-row multiples), so
+  // the one download left exposed after the last kernel is an eighth.
+  static constexpr uint32_t kPipelineChunks = 5;
+  static void pipeline_chunk(uint64_t m, uint32_t i, uint64_t *begin,
+                             uint64_t *rows) {
+    static const uint32_t eighths[kPipelineChunks + 1] = {0, 2, 4, 6, 7, 8};
+    auto bound = [&](uint32_t j) {
+      return j == kPipelineChunks ? m : (m * eighths[j] / 8) / 128 * 128;
+    };
+    *begin = bound(i);
+    *rows = bound(i + 1) - *begin;
+  }
   static constexpr uint32_t kPieceMinK = 2048;
 
   // Slot s's bytes are on the host and would be uploaded by this dispatch.
@@ -741,7 +752,7 @@ struct Vm {
       return false;
     Slot &dst = *args[2];
     if (&dst == args[0] || &dst == args[1] || args[0] == args[1] ||
-        exe.m < kPipelineChunks * 256)
+        exe.m < 1024)
       return false;
     *upload_a = host_upload(*args[0], o);
     *upload_w = host_upload(*args[1], o) && exe.k >= kPieceMinK;
@@ -856,7 +867,7 @@ struct Vm {
     const uint64_t row_c = N * 8;
     uint64_t r0[kPipelineChunks], rows[kPipelineChunks];
     for (uint32_t i = 0; i < kPipelineChunks; ++i)
-      hexir_shard_rows(exe.m, kPipelineChunks, i, &r0[i], &rows[i]);
+      pipeline_chunk(exe.m, i, &r0[i], &rows[i]);
     auto host_bytes = [&](Slot &s, uint64_t off, uint64_t bytes) {
       return s.rodata ? rodata_source(s, off, bytes)
                       : reinterpret_cast<const uint8_t *>(s.host.data()) + off;
