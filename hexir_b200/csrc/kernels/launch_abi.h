@@ -93,10 +93,6 @@ typedef struct {
   uint32_t sk_dp_tiles;
   uint32_t sk_units;
   double *sk_partials;   /* [2 G][BM][BN] */
-  /* Data-parallel launches over a range of the tile raster: CTA x computes
-   * tile tile_base + x (the launch's grid covers the range). */
-  uint32_t tile_base;
-  uint32_t reserved2;
 } hexir_linear_args_t;
 
 typedef struct {

@@ -270,8 +270,7 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   const bool issuer = threadIdx.x == 0;
 
   uint32_t tm, tn;
-  tile_of(args.tile_base + blockIdx.x, args.tiles_m, args.tiles_n, args.group_m,
-          tm, tn);
+  tile_of(blockIdx.x, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
   const uint32_t split = blockIdx.y;
   const uint32_t kt_begin = split * args.k_tiles_per_split;
   const uint32_t kt_end = min(args.k_tiles, kt_begin + args.k_tiles_per_split);
@@ -670,8 +669,7 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
   const uint32_t wm = warp >> 1, wn = warp & 1;  // warp tile 32 x 32
 
   uint32_t tm, tn;
-  tile_of(args.tile_base + blockIdx.x, args.tiles_m, args.tiles_n, args.group_m,
-          tm, tn);
+  tile_of(blockIdx.x, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
   const uint32_t split = blockIdx.y;
   const uint32_t k_tiles = (args.k + BK - 1) / BK;
   const uint32_t kt_begin = split * args.k_tiles_per_split;

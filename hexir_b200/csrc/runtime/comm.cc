@@ -81,8 +81,7 @@ struct hexir_comm_t {
   int nranks = 0;
   int rank = 0;
   int ordinal = 0;
-  CUstream gather_stream = nullptr;  // weight pieces, row sends / receives
-  CUstream copy_stream = nullptr;    // copy-engine transfers of finished tiles
+  CUstream gather_stream = nullptr;  // row sends / receives
   CUevent chunk_done[kGatherChunks] = {};
   CUevent gather_done = nullptr;
   // The weight broadcast on the side stream: its start (after the caller's
@@ -203,69 +202,6 @@ hexir_status_t probe_direct(hexir_comm_t *comm) {
   return HEXIR_OK;
 }
 
-// Copies the output tiles [t0, t1) of a launch's raster (128 x 128 tiles,
-// grouped rasters of group_m tile rows, column by column inside a group) from
-// `src` to `dst`, both [m][n] row-major, as 2-D copies on `stream`: per group
-// the partial first column, the whole columns, the partial last column.
-hexir_status_t copy_tiles(CUdeviceptr src, CUdeviceptr dst, uint32_t m,
-                          uint32_t n, uint32_t tiles_m, uint32_t tiles_n,
-                          uint32_t group_m, uint64_t t0, uint64_t t1,
-                          CUstream stream) {
-  const Driver &d = driver();
-  const uint64_t per_group = static_cast<uint64_t>(group_m) * tiles_n;
-  auto block = [&](uint32_t tm0, uint32_t tm1, uint32_t tn0,
-                   uint32_t tn1) -> bool {
-    const uint64_t r0 = static_cast<uint64_t>(tm0) * 128;
-    const uint64_t r1 = std::min<uint64_t>(static_cast<uint64_t>(tm1) * 128, m);
-    const uint64_t c0 = static_cast<uint64_t>(tn0) * 128;
-    const uint64_t c1 = std::min<uint64_t>(static_cast<uint64_t>(tn1) * 128, n);
-    if (r0 >= r1 || c0 >= c1)
-      return true;
-    CUDA_MEMCPY2D cp;
-    std::memset(&cp, 0, sizeof(cp));
-    cp.srcMemoryType = CU_MEMORYTYPE_DEVICE;
-    cp.srcDevice = src + (r0 * n + c0) * 8;
-    cp.srcPitch = static_cast<size_t>(n) * 8;
-    cp.dstMemoryType = CU_MEMORYTYPE_DEVICE;
-    cp.dstDevice = dst + (r0 * n + c0) * 8;
-    cp.dstPitch = static_cast<size_t>(n) * 8;
-    cp.WidthInBytes = (c1 - c0) * 8;
-    cp.Height = r1 - r0;
-    return d.Memcpy2DAsync(&cp, stream) == CUDA_SUCCESS;
-  };
-  for (uint64_t t = t0; t < t1;) {
-    const uint64_t g = t / per_group;
-    const uint32_t first_m = static_cast<uint32_t>(g * group_m);
-    const uint32_t rows = std::min(group_m, tiles_m - first_m);
-    const uint64_t g_begin = g * per_group;
-    const uint64_t g_end = g_begin + static_cast<uint64_t>(rows) * tiles_n;
-    const uint64_t i0 = t - g_begin, i1 = std::min(t1, g_end) - g_begin;
-    // tile i of the group: row first_m + i % rows, column i / rows
-    uint64_t i = i0;
-    bool ok = true;
-    if (i % rows) {  // partial first column
-      const uint64_t stop = std::min<uint64_t>(i1, (i / rows + 1) * rows);
-      ok &= block(first_m + static_cast<uint32_t>(i % rows),
-                  first_m + static_cast<uint32_t>((stop - 1) % rows) + 1,
-                  static_cast<uint32_t>(i / rows), static_cast<uint32_t>(i / rows) + 1);
-      i = stop;
-    }
-    if (i < i1 && i1 - i >= rows) {  // whole columns
-      const uint64_t cols = (i1 - i) / rows;
-      ok &= block(first_m, first_m + rows, static_cast<uint32_t>(i / rows),
-                  static_cast<uint32_t>(i / rows + cols));
-      i += cols * rows;
-    }
-    if (i < i1)  // partial last column
-      ok &= block(first_m, first_m + static_cast<uint32_t>(i1 - i),
-                  static_cast<uint32_t>(i / rows), static_cast<uint32_t>(i / rows) + 1);
-    if (!ok)
-      return comm_fail("copying finished tiles to the root failed");
-    t = g_begin + i1;
-  }
-  return HEXIR_OK;
-}
-
 // The weight's k pieces for a broadcast that peers compute behind: a short
 // first piece (512 of k) whose transfer is the only exposed one, then the
 // rest, which lands long before the first piece's GEMM ends (8192 x 8192 on
@@ -358,8 +294,6 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   if (cr == CUDA_SUCCESS)
     cr = d.StreamCreateWithPriority(&comm->gather_stream, CU_STREAM_NON_BLOCKING,
                                     greatest);
-  if (cr == CUDA_SUCCESS)
-    cr = d.StreamCreate(&comm->copy_stream, CU_STREAM_NON_BLOCKING);
   for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kGatherChunks; ++i)
     cr = d.EventCreate(&comm->chunk_done[i], CU_EVENT_DISABLE_TIMING);
   if (cr == CUDA_SUCCESS)
@@ -399,11 +333,10 @@ void hexir_comm_release(hexir_comm_t *comm) {
   if (dev) {
     ContextGuard guard(dev->context);
     const Driver &d = driver();
-    for (CUstream st : {comm->gather_stream, comm->copy_stream})
-      if (st) {
-        d.StreamSynchronize(st);
-        d.StreamDestroy(st);
-      }
+    if (comm->gather_stream) {
+      d.StreamSynchronize(comm->gather_stream);
+      d.StreamDestroy(comm->gather_stream);
+    }
     for (CUevent ev : comm->chunk_done)
       if (ev)
         d.EventDestroy(ev);
@@ -563,72 +496,14 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
 
   // The rest of a row range [cb, cb + cr) of this rank: the remaining k
   // pieces continuing the first one's sums, or the one-shot plan.
-  // The last launch of a peer's rows when they go to the root: with more
-  // than three waves of tiles and no k split, the tiles run in chunks of
-  // whole waves into the staging rows, each chunk's tiles leaving for the
-  // root on the copy engines while the next chunk computes, and only the
-  // last 1-2 waves store into the root's c directly.  (Stores from every
-  // GPU's epilogue reaching GPU 0 together, once per wave, are what the
-  // copy engines take off the SMs.)
-  auto last_launch = [&](const double *ap, const double *wp, uint32_t mm,
-                         uint32_t kk, const double *c_in, double *out,
-                         uint32_t lflags) -> hexir_status_t {
-    const bool tiled = !root && direct && out != c;
-    const MatmulPlan lp = plan_matmul(dev, ap, wp, out, mm, n, kk, lflags, k, c_in);
-    const uint64_t tiles = static_cast<uint64_t>(lp.tiles_m) * lp.tiles_n;
-    const uint64_t g = static_cast<uint64_t>(std::max(dev->sm_count, 1));
-    if (!tiled || lp.split_k != 1 || lp.stream_k() || lp.variant != kTma128 ||
-        tiles <= 3 * g)
-      return launch_matmul(dev, lib, ap, wp, out, mm, n, kk,
-                           lflags | HEXIR_MATMUL_REMOTE_OUTPUT, s, &error, k,
-                           c_in);
-    const uint64_t last = g + tiles % g;  // one to two waves, stored remotely
-    const uint64_t front_waves = (tiles - last) / g;
-    const uint64_t chunks = std::min<uint64_t>(3, front_waves);
-    const uint32_t group_m = std::min<uint32_t>(8, lp.tiles_m);
-    const CUdeviceptr staging = reinterpret_cast<CUdeviceptr>(c);
-    const CUdeviceptr remote = reinterpret_cast<CUdeviceptr>(out);
-    uint64_t t0 = 0;
-    hexir_status_t st = HEXIR_OK;
-    for (uint64_t j = 0; j < chunks && st == HEXIR_OK; ++j) {
-      const uint64_t waves = front_waves / chunks + (j < front_waves % chunks);
-      const uint64_t t1 = t0 + waves * g;
-      st = launch_matmul(dev, lib, ap, wp, c, mm, n, kk,
-                         lflags | HEXIR_MATMUL_SPLIT_K(1), s, &error, k, c_in,
-                         nullptr, static_cast<uint32_t>(t0),
-                         static_cast<uint32_t>(t1 - t0));
-      if (st != HEXIR_OK)
-        return st;
-      d.EventRecord(comm->chunk_done[j], s);
-      d.StreamWaitEvent(comm->copy_stream, comm->chunk_done[j], 0);
-      st = copy_tiles(staging, remote, mm, n, lp.tiles_m, lp.tiles_n, group_m, t0,
-                      t1, comm->copy_stream);
-      t0 = t1;
-    }
-    if (st == HEXIR_OK)
-      st = launch_matmul(dev, lib, ap, wp, out, mm, n, kk,
-                         lflags | HEXIR_MATMUL_SPLIT_K(1) |
-                             HEXIR_MATMUL_REMOTE_OUTPUT,
-                         s, &error, k, c_in, nullptr, static_cast<uint32_t>(t0),
-                         static_cast<uint32_t>(tiles - t0));
-    // The caller's stream (and so the closing all-reduce) waits for the
-    // copies.
-    d.EventRecord(comm->gather_done, comm->copy_stream);
-    d.StreamWaitEvent(s, comm->gather_done, 0);
-    return st;
-  };
-
   auto finish_rows = [&](uint64_t cb, uint64_t count, double *out,
                          uint32_t out_flags) -> hexir_status_t {
     if (!count)
       return HEXIR_OK;
     const uint32_t mm = static_cast<uint32_t>(count);
-    const bool to_root = (out_flags & HEXIR_MATMUL_REMOTE_OUTPUT) != 0;
     if (!chain) {
       if (!root)
         d.StreamWaitEvent(s, comm->w_done, 0);
-      if (to_root)
-        return last_launch(a_rows + cb * k, w, mm, k, nullptr, out, relu);
       return launch_matmul(dev, lib, a_rows + cb * k, w, out, mm, n, k,
                            relu | out_flags, s, &error);
     }
@@ -637,14 +512,9 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       const bool last = j + 1 == pieces;
       if (!root)
         d.StreamWaitEvent(s, comm->w_piece[j], 0);
-      const double *ap = a_rows + cb * k + bounds[j];
-      const double *wp = w + static_cast<size_t>(bounds[j]) * n;
-      const uint32_t kk = bounds[j + 1] - bounds[j];
-      if (last && to_root) {
-        st = last_launch(ap, wp, mm, kk, c + cb * n, out, relu);
-        continue;
-      }
-      st = launch_matmul(dev, lib, ap, wp, last ? out : c + cb * n, mm, n, kk,
+      st = launch_matmul(dev, lib, a_rows + cb * k + bounds[j],
+                         w + static_cast<size_t>(bounds[j]) * n,
+                         last ? out : c + cb * n, mm, n, bounds[j + 1] - bounds[j],
                          (last ? relu | out_flags : 0u) | HEXIR_MATMUL_SPLIT_K(1),
                          s, &error, k, c + cb * n);
     }

@@ -378,8 +378,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              const double *b, double *c, uint32_t m, uint32_t n,
                              uint32_t k, uint32_t flags, CUstream stream,
                              std::string *error, uint32_t lda,
-                             const double *c_in, const double *addend,
-                             uint32_t tile_begin, uint32_t tile_count) {
+                             const double *c_in, const double *addend) {
   const Driver &d = driver();
   if (m == 0 || n == 0)
     return HEXIR_OK;
@@ -436,16 +435,9 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              : fail(error, cuda_message("empty matmul", r));
   }
   MatmulPlan p = plan_matmul(dev, a, b, c, m, n, k, flags, lda, c_in, addend);
-  if (p.stream_k() && (!lib->linear_tma_sk || tile_count))
+  if (p.stream_k() && !lib->linear_tma_sk)  // an image without stream-K
     p = plan_matmul(dev, a, b, c, m, n, k, flags | HEXIR_MATMUL_NO_STREAM_K, lda,
                     c_in, addend);
-  if (tile_count &&
-      (p.split_k != 1 ||
-       static_cast<uint64_t>(tile_begin) + tile_count >
-           static_cast<uint64_t>(p.tiles_m) * p.tiles_n))
-    return fail(error, "matmul: a tile range needs an unsplit plan and must lie "
-                       "inside the raster",
-                HEXIR_ERROR_INVALID_ARGUMENT);
 
   hexir_linear_args_t args;
   std::memset(&args, 0, sizeof(args));
@@ -506,8 +498,7 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   if (rows32 && (reinterpret_cast<uintptr_t>(args.c) & 31u) == 0)
     args.epilogue |= HEXIR_EPILOGUE_VEC4;
 
-  const unsigned grid_x = tile_count ? tile_count : p.tiles_m * p.tiles_n;
-  args.tile_base = tile_count ? tile_begin : 0u;
+  const unsigned grid_x = p.tiles_m * p.tiles_n;
   hexir_status_t status;
   if (p.variant != kGuarded) {
     CUtensorMap map_a, map_b;

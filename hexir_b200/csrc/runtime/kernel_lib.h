@@ -93,15 +93,12 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
                        const double *addend = nullptr);
 
 // Launchers.  The caller has made dev->context current.  All asynchronous.
-// tile_begin / tile_count: compute only that range of the plan's tile
-// raster (tile_count 0: all); only for plans without a k split.
 hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
                              const double *b, double *c, uint32_t m, uint32_t n,
                              uint32_t k, uint32_t flags, CUstream stream,
                              std::string *error, uint32_t lda = 0,
                              const double *c_in = nullptr,
-                             const double *addend = nullptr,
-                             uint32_t tile_begin = 0, uint32_t tile_count = 0);
+                             const double *addend = nullptr);
 hexir_status_t launch_relu(DeviceState *dev, KernelLib *lib, const double *x,
                            double *y, size_t n, CUstream stream,
                            std::string *error);
