@@ -618,6 +618,37 @@ def run_suite(args):
     hbm, hbm_src = hbm_peak_gbs()
     out = []
 
+    # C1 parity graph: 256x256 linear -> relu (seed 0, a then w) through the
+    # VM on the GPU and on the host cores (the reference's CPU arithmetic);
+    # latency of one hexir_execute_capture, median of 20 after warm-up.
+    r = hx.Rng(0)
+    a_h, w_h = r.uniform((256, 256)), r.uniform((256, 256))
+    prog = hx.Program()
+    prog.relu(prog.linear(prog.constant(a_h), prog.constant(w_h)))
+    want = oracle.relu(oracle.matmul(a_h, w_h))
+    line = {"suite": "parity_graph_256"}
+    for name, placement, spec in (("cuda", "hexir.linear=cuda,hexir.relu=cuda", "cuda"),
+                                  ("cpu", "", "cpu")):
+        module = hx.Module(prog.emit(placement))
+        dev = hx.Device(spec)
+        got = hx.execute(module, dev, out_shape=(256, 256))
+        wall, kms = [], []
+        for _ in range(20):
+            t0 = time.perf_counter()
+            hx.execute(module, dev, out_shape=(256, 256))
+            wall.append((time.perf_counter() - t0) * 1e3)
+            kms.append(hx.last_kernel_ms())
+        line[name + "_execute_ms"] = round(statistics.median(wall), 4)
+        if name == "cuda":
+            line["cuda_kernel_ms"] = round(statistics.median(kms), 4)
+            line["cuda_normwise_err"] = oracle.normwise_error(got, want)
+        else:
+            line["cpu_bit_exact"] = bool(np.array_equal(got.view(np.uint64),
+                                                        want.view(np.uint64)))
+        module.close()
+        dev.close()
+    out.append(line)
+
     # GEMM sweep, square, relu fused (uniform[-1,1], seed 1, a then w).
     for size in (1024, 2048, 4096, 8192):
         r = hx.Rng(1)
@@ -703,6 +734,62 @@ def run_suite(args):
                     "e2e_tflops": round(flops / (statistics.median(wall) * 1e-3)
                                         / 1e12, 3)})
         module.close()
+    # linear -> add -> relu at 8192^3: one fused kernel against three.
+    r = hx.Rng(3)
+    a_h, w_h, b_h = (r.uniform((8192, 8192)) for _ in range(3))
+    a, w, b = (torch.from_numpy(t).cuda() for t in (a_h, w_h, b_h))
+    del a_h, w_h
+    c1, c2 = torch.empty_like(a), torch.empty_like(a)
+    n_el = 8192 * 8192
+    fused_ms = timed_ms(lambda: hx.cuda_matmul_add(
+        ordinal, a.data_ptr(), w.data_ptr(), b.data_ptr(), c1.data_ptr(), 8192,
+        8192, 8192, _ffi.MATMUL_RELU, stream), 5)
+
+    def three():
+        hx.cuda_matmul(ordinal, a.data_ptr(), w.data_ptr(), c2.data_ptr(), 8192,
+                       8192, 8192, 0, stream)
+        hx.cuda_add(ordinal, c2.data_ptr(), b.data_ptr(), c2.data_ptr(), n_el,
+                    stream)
+        hx.cuda_relu(ordinal, c2.data_ptr(), c2.data_ptr(), n_el, stream)
+    three_ms = timed_ms(three, 5)
+    out.append({"suite": "linear_add_relu_8192", "fused_ms": round(fused_ms, 4),
+                "three_kernels_ms": round(three_ms, 4),
+                "fused_tflops": round(2.0 * 8192 ** 3 / (fused_ms * 1e-3) / 1e12, 3),
+                "bit_identical": bool(torch.equal(c1.view(torch.int64),
+                                                  c2.view(torch.int64)))})
+    del a, w, b, c1, c2
+
+    # The 8192^3 module executed repeatedly with its constants kept on the
+    # GPU (hexir_module_keep_constants): a serving loop's per-call time.
+    r = hx.Rng(1)
+    a_h, w_h = r.uniform((8192, 8192)), r.uniform((8192, 8192))
+    kept = hx.Program()
+    kept.relu(kept.linear(kept.constant(a_h), kept.constant(w_h)))
+    module = hx.Module(kept.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    del kept, a_h, w_h
+    module.keep_constants(True)
+    dev = hx.Device("cuda")
+    res = torch.empty((8192, 8192), dtype=torch.float64).pin_memory().numpy()
+
+    def once():
+        _ffi.check(hx.lib().hexir_execute_capture(
+            module.handle, dev.handle, b"main", res.ctypes.data, res.nbytes),
+            "hexir_execute_capture")
+    once()
+    wall = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        once()
+        wall.append((time.perf_counter() - t0) * 1e3)
+    out.append({"suite": "kept_constants_8192", "execute_ms": round(statistics.median(wall), 3),
+                "tflops": round(2.0 * 8192 ** 3 / (statistics.median(wall) * 1e-3) / 1e12, 3),
+                "kept_bytes": module.kept_bytes,
+                "note": "hexir_execute_capture with a and w kept on the GPU; "
+                        "the 512 MiB result still copied to pinned host memory"})
+    module.close()
+    dev.close()
+    del res
+
     rows = np.linspace(0, 8191, 8).astype(int)
     want = oracle.matmul(oracle.relu(oracle.matmul(
         oracle.relu(oracle.matmul(x[rows], w1)), w2)), w3)
