@@ -47,9 +47,12 @@ hexir_status_t hexir_execute_devices(const hexir_module_t *module,
                                      unsigned device_count, const char *entry,
                                      void *out_result, size_t out_size);
 
-/* extension: device time of the kernels of the last execute on this thread,
- * in milliseconds, summed over dispatches (CUDA events around each DISPATCH
- * on the launching stream).  0 when nothing ran on a GPU. */
+/* extension: device time of the dispatches of the last execute on this
+ * thread, in milliseconds, summed (CUDA events around each DISPATCH on the
+ * launching stream).  A pipelined dispatch's span includes its waits on the
+ * uploads it overlaps; with the constants kept on the GPU
+ * (hexir_module_keep_constants) the spans are the kernels alone.  0 when
+ * nothing ran on a GPU. */
 double hexir_last_execute_kernel_ms(void);
 
 /* extension: keep the module's constants on the device between executes.
