@@ -541,16 +541,13 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       return comm_fail(nccl_message("ncclAllReduce (row stores done)", nr));
     return status;
   }
-  if (status != HEXIR_OK) {
-    set_last_error(error);
-    return status;
-  }
-
   // 4'. Rows by NCCL: this rank's rows in up to kGatherChunks pieces of
   //     shrinking size; the root writes straight into its part of c, and
   //     each finished piece of a peer goes to the root on the side stream
   //     while the next piece computes.  Every rank splits its rows by the
-  //     same rule, so the root knows each peer's pieces.
+  //     same rule, so the root knows each peer's pieces.  After a failed
+  //     launch the rank stops computing but still takes every send/receive
+  //     step, so no rank waits for ever, and reports the failure.
   uint64_t ignore_b = 0, ignore_c = 0;
   const uint32_t my_chunks = rows ? gather_piece(rows, 0, &ignore_b, &ignore_c) : 0;
   uint32_t max_chunks = 0;
@@ -562,14 +559,10 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   }
   cudaStream_t gs = reinterpret_cast<cudaStream_t>(comm->gather_stream);
   for (uint32_t i = 0; i < max_chunks; ++i) {
-    if (i < my_chunks) {
+    if (i < my_chunks && status == HEXIR_OK) {
       uint64_t cb = 0, cnt = 0;
       gather_piece(rows, i, &cb, &cnt);
-      hexir_status_t st = finish_rows(cb, cnt, c + cb * n, 0u);
-      if (st != HEXIR_OK) {
-        set_last_error(error);
-        return st;
-      }
+      status = finish_rows(cb, cnt, c + cb * n, 0u);
     }
     if (ranks == 1)
       continue;
@@ -603,7 +596,9 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   // The caller's stream completes only after the broadcast and the gather.
   d.EventRecord(comm->gather_done, comm->gather_stream);
   d.StreamWaitEvent(s, comm->gather_done, 0);
-  return HEXIR_OK;
+  if (status != HEXIR_OK)
+    set_last_error(error.empty() ? hexir_status_string(status) : error);
+  return status;
 }
 
 }  // extern "C"
