@@ -455,3 +455,49 @@ def test_row_sharded_fused_linear_add_relu():
                          devs, out_shape=(1001, 132))
     want = oracle.relu(oracle.add(oracle.matmul(a, w), b))
     assert oracle.normwise_error(sharded, want) <= TOL
+
+
+def test_kept_constants_with_fused_add_and_second_use():
+    """Kept constants feeding a fused linear -> add -> relu and a second,
+    unfused use of the same constant: three executes, the same bits."""
+    r = hx.Rng(47)
+    a, w, b = r.uniform((300, 256)), r.uniform((256, 200)), r.uniform((300, 200))
+    p = hx.Program()
+    bc = p.constant(b)
+    s = p.relu(p.add(p.linear(p.constant(a), p.constant(w)), bc))
+    p.print(p.add(s, bc))
+    mod = hx.Module(p.emit("hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda"))
+    assert [e.kind for e in hx.read_executables(p.emit(
+        "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda"))] == [6, 2]
+    dev = hx.Device("cuda")
+    plain = hx.execute(mod, dev, out_shape=(300, 200))
+    mod.keep_constants(True)
+    outs = [hx.execute(mod, dev, out_shape=(300, 200)) for _ in range(3)]
+    for out in outs:
+        assert np.array_equal(bits(out), bits(plain))
+    assert mod.kept_bytes == a.nbytes + w.nbytes + b.nbytes
+    want = oracle.add(oracle.relu(oracle.add(oracle.matmul(a, w), b)), b)
+    assert oracle.normwise_error(plain, want) <= TOL
+    mod.close()
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+def test_kept_constants_with_row_sharding():
+    """A row-sharded linear on cuda:0-1 with its constants kept: the weight's
+    kept copy on GPU 0 is broadcast every execute (the rows of a still go
+    to each GPU from the module); repeated executes equal the first bit for
+    bit."""
+    r = hx.Rng(53)
+    a, w = r.uniform((777, 320)), r.uniform((320, 256))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    mod = hx.Module(p.emit("hexir.linear=cuda:0-1,hexir.relu=cuda:0-1"))
+    devs = [hx.Device("cuda:0"), hx.Device("cuda:1")]
+    first = hx.execute(mod, devs, out_shape=(777, 256))
+    mod.keep_constants(True)
+    for _ in range(3):
+        again = hx.execute(mod, devs, out_shape=(777, 256))
+        assert np.array_equal(bits(again), bits(first))
+    assert mod.kept_bytes == w.nbytes
+    assert oracle.normwise_error(first, oracle.relu(oracle.matmul(a, w))) <= TOL
+    mod.close()
