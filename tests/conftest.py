@@ -46,3 +46,26 @@ def gpu():
 
 def bin_path(name: str) -> str:
     return os.path.join(ROOT, "hexir_b200", "bin", name)
+
+
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that was free a moment ago."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def spawn_ranks(fn, nprocs: int, args: tuple, attempts: int = 3) -> None:
+    """torch.multiprocessing spawn of `nprocs` ranks of fn(rank, nprocs, port,
+    *args), joined.  The rendezvous port is picked free but can be taken
+    before rank 0 binds it; that (EADDRINUSE) is retried with a new port."""
+    import torch.multiprocessing as mp
+    for attempt in range(attempts):
+        try:
+            mp.start_processes(fn, args=(nprocs, free_port()) + tuple(args),
+                               nprocs=nprocs, join=True, start_method="spawn")
+            return
+        except mp.ProcessRaisedException as err:
+            if "EADDRINUSE" not in str(err) or attempt + 1 == attempts:
+                raise

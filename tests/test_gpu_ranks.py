@@ -16,22 +16,16 @@ differ, so it is held to the tolerance only.
 import ctypes as C
 import datetime
 import os
-import socket
 
 import numpy as np
 import pytest
 
 import hexir_b200 as hx
+from tests.conftest import spawn_ranks
 
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-12
-
-
-def free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def _rank(rank, world, port, m, n, k, result_path):
@@ -124,10 +118,8 @@ def two_gpus():
     # whole weight and runs that plan.
     (512, 256, 4096)])
 def test_two_processes_sharded_linear(tmp_path, m, n, k):
-    import torch.multiprocessing as mp
     path = str(tmp_path / "out.npy")
-    mp.start_processes(_rank, args=(2, free_port(), m, n, k, path), nprocs=2,
-                       join=True, start_method="spawn")
+    spawn_ranks(_rank, 2, (m, n, k, path))
     r = np.load(path, allow_pickle=True)[0]
     # Two processes on one host: the peers can map rank 0's memory.
     assert int(r["direct_flag"]) == 1

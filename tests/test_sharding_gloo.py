@@ -12,18 +12,13 @@ of waiting for ever.
 
 import datetime
 import os
-import socket
 
 import numpy as np
 import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-
-def free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+from tests.conftest import free_port, spawn_ranks
 
 
 def _init(rank, world, port, timeout_s):
@@ -66,8 +61,7 @@ def _sharded_rank(rank, world, port, m, n, k, result_path):
 @pytest.mark.parametrize("m", [37, 64])
 def test_two_rank_sharded_linear_matches_oracle(tmp_path, m):
     path = str(tmp_path / "ok.npy")
-    mp.start_processes(_sharded_rank, args=(2, free_port(), m, 24, 40, path),
-                       nprocs=2, join=True, start_method="spawn")
+    spawn_ranks(_sharded_rank, 2, (m, 24, 40, path))
     assert bool(np.load(path)[0])
 
 
