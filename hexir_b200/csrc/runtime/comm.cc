@@ -81,7 +81,7 @@ struct hexir_comm_t {
   int nranks = 0;
   int rank = 0;
   int ordinal = 0;
-  CUstream gather_stream = nullptr;  // row sends / receives
+  CUstream gather_stream = nullptr;  // weight pieces, row sends / receives
   CUevent chunk_done[kGatherChunks] = {};
   CUevent gather_done = nullptr;
   // The weight broadcast on the side stream: its start (after the caller's

@@ -1,8 +1,10 @@
 // nccl_shim.h -- NCCL resolved at run time from libnccl.so.2.
 //
-// Only row-sharded dispatches need it (weight broadcast and output row
-// gather over NVLink), so it is loaded on first use and a single-GPU or CPU
-// program never touches it.  Types come from nccl.h at build time.
+// Only row-sharded dispatches need it (the weight broadcast, the root's
+// output descriptor and the one-word completion all-reduce, and the row
+// gather where peer stores are unavailable), so it is loaded on first use
+// and a single-GPU or CPU program never touches it.  Types come from nccl.h
+// at build time.
 #pragma once
 
 #include <nccl.h>
