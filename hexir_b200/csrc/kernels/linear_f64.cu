@@ -505,60 +505,70 @@ __device__ __forceinline__ void linear_tma_sk_body(
   double acc[MI][2 * NP][4];
   const uint32_t sa_addr = smem_addr(sa), sb_addr = smem_addr(sb);
   bool ok = true;
-  uint32_t seg_kt0 = 0;  // first k-tile of the current segment
-  SkSteps::Cursor cur = steps.begin();
-  for (int32_t i = 0; i < nk; ++i, steps.next(cur)) {
-    const uint32_t tile = cur.tile, kt = cur.kt;
-    if (kt == 0 || (uint32_t)i == steps.dp_steps) {
-      seg_kt0 = kt;
+  // Segments: a whole data-parallel tile, or the part of a stream-K tile in
+  // this CTA's run.  The inner loop over a segment's k-tiles is the
+  // data-parallel kernel's loop; the epilogue follows it.
+  int32_t i = 0;
+  uint32_t tile = steps.dp_steps ? steps.c : steps.first_sk_tile();
+  uint32_t kt0 = steps.dp_steps ? 0u : steps.u0 % steps.k_tiles;
+  while (i < nk) {
+    const int32_t seg_len = min((int32_t)(args.k_tiles - kt0), nk - i);
 #pragma unroll
-      for (int a = 0; a < MI; ++a)
+    for (int a = 0; a < MI; ++a)
 #pragma unroll
-        for (int b = 0; b < 2 * NP; ++b)
+      for (int b = 0; b < 2 * NP; ++b)
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            acc[a][b][q] = 0.0;
-    }
-    const int s = i % STAGES;
-    const uint32_t use = (uint32_t)i / STAGES;
-    if (!mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns)) {
-      ok = false;
-      break;
-    }
-    const uint32_t a_stage = sa_addr + s * T::A_STAGE * 8;
-    const uint32_t b_stage =
-        sb_addr + s * T::B_STAGE * 8 + (wn * NP) * T::B_SLAB * 8;
-#pragma unroll
-    for (int kk = 0; kk < BK / 8; ++kk)
-      dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
-                           b_stage, T::B_SLAB * 8, kk * 8, g, t);
-    __syncwarp();
-    if (lane == 0)
-      mbar_arrive(&empty[s]);
-    if (issuer && issued < nk) {
-      if (!mbar_wait_bounded(&empty[s], use & 1u, args.timeout_ns)) {
+        for (int q = 0; q < 4; ++q)
+          acc[a][b][q] = 0.0;
+    for (int32_t j = 0; j < seg_len; ++j, ++i) {
+      const int s = i % STAGES;
+      const uint32_t use = (uint32_t)i / STAGES;
+      if (!mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns)) {
         ok = false;
         break;
       }
-      issue(issued++);
-    }
-    __syncwarp();
-    // Segment end: the tile's last k-tile or this CTA's last step.
-    if (kt + 1 == args.k_tiles || i + 1 == nk) {
-      uint32_t tm, tn;
-      tile_of(tile, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
-      if (seg_kt0 == 0 && kt + 1 == args.k_tiles) {
-        store_warp_tile<MI, NP, true>(acc, args.c, args.m, args.n,
-                                      tm * BM + wm * T::WTM,
-                                      tn * BN + wn * T::WTN, relu, g, t, vec4,
-                                      addend);
-      } else {
-        const uint32_t slot =
-            2 * steps.c + (tile == steps.first_sk_tile() ? 0u : 1u);
-        store_warp_tile<MI, NP, true>(acc, args.sk_partials + (size_t)slot * BM * BN,
-                                      BM, BN, wm * T::WTM, wn * T::WTN, false, g,
-                                      t, true, nullptr);
+      const uint32_t a_stage = sa_addr + s * T::A_STAGE * 8;
+      const uint32_t b_stage =
+          sb_addr + s * T::B_STAGE * 8 + (wn * NP) * T::B_SLAB * 8;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk)
+        dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
+                             b_stage, T::B_SLAB * 8, kk * 8, g, t);
+      __syncwarp();
+      if (lane == 0)
+        mbar_arrive(&empty[s]);
+      if (issuer && issued < nk) {
+        if (!mbar_wait_bounded(&empty[s], use & 1u, args.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        issue(issued++);
       }
+      __syncwarp();
+    }
+    if (!ok)
+      break;
+    uint32_t tm, tn;
+    tile_of(tile, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+    if (kt0 == 0 && (uint32_t)seg_len == args.k_tiles) {
+      store_warp_tile<MI, NP, true>(acc, args.c, args.m, args.n,
+                                    tm * BM + wm * T::WTM, tn * BN + wn * T::WTN,
+                                    relu, g, t, vec4, addend);
+    } else {
+      const uint32_t slot =
+          2 * steps.c + (tile == steps.first_sk_tile() ? 0u : 1u);
+      store_warp_tile<MI, NP, true>(acc, args.sk_partials + (size_t)slot * BM * BN,
+                                    BM, BN, wm * T::WTM, wn * T::WTN, false, g,
+                                    t, true, nullptr);
+    }
+    // The next segment: the next data-parallel tile, the start of the
+    // stream-K run, or the next stream-K tile.
+    if ((uint32_t)i == steps.dp_steps) {
+      tile = steps.first_sk_tile();
+      kt0 = steps.u0 % steps.k_tiles;
+    } else {
+      tile += (uint32_t)i < steps.dp_steps ? steps.grid : 1u;
+      kt0 = 0;
     }
   }
 

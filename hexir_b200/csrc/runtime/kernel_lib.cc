@@ -353,7 +353,7 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   // stay data-parallel except the last one or two, whose k-tile units are
   // dealt out evenly over one CTA per SM (runs of >= 4 units).  Measured on
   // B200 it loses to the data-parallel and split-k schedules at every shape
-  // tried (2048^3: 29.9 against 31.6 TFLOP/s; 8192^3: 34.4 against 35.2),
+  // tried (2048^3: 30.8 against 31.6 TFLOP/s; 8192^3: 34.9 against 35.2),
   // so the planner never picks it by itself.
   if ((flags & HEXIR_MATMUL_FORCE_STREAM_K) && p.variant == kTma128 && !c_in &&
       ((flags >> 16) & 0xFFu) == 0 && !(flags & HEXIR_MATMUL_NO_STREAM_K) &&
