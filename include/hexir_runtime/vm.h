@@ -63,7 +63,8 @@ double hexir_last_execute_kernel_ms(void);
  * on every execute (runtime/src/vm/interpreter.c:300-315).  A dispatch
  * whose destination is a CONST slot writes a private buffer, never the kept
  * copy.  `enable` = 0 frees the kept copies (after the GPUs finish with
- * them), as does hexir_module_release.  Off by default. */
+ * them), as does hexir_module_release; neither may overlap an execute of the
+ * module on another thread.  Off by default. */
 hexir_status_t hexir_module_keep_constants(hexir_module_t *module, int enable);
 
 /* extension: bytes of constants currently kept on GPUs for `module`. */
