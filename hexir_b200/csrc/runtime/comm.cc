@@ -494,8 +494,8 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
     }
   }
 
-  // The rest of a row range [cb, cb + cr) of this rank: the remaining k
-  // pieces continuing the first one's sums, or the one-shot plan.
+  // The rest of this rank's rows [cb, cb + count): the remaining k pieces
+  // continuing the first one's sums, or the one-shot plan.
   auto finish_rows = [&](uint64_t cb, uint64_t count, double *out,
                          uint32_t out_flags) -> hexir_status_t {
     if (!count)
