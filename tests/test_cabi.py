@@ -107,3 +107,30 @@ def test_no_cpu_fallback_without_a_gpu():
     assert err.value.status == _ffi.ERROR_DEVICE
     with pytest.raises(_ffi.HexirError):
         hx.Device("cuda:3")
+    # Kernel-level calls refuse too: no host fallback behind them.
+    lib = hx.lib()
+    assert lib.hexir_cuda_matmul_f64(0, None, None, None, 4, 4, 4, 0, None) == \
+        _ffi.ERROR_DEVICE
+    assert lib.hexir_cuda_relu_f64(0, None, None, 16, None) == _ffi.ERROR_DEVICE
+    assert lib.hexir_cuda_matmul_add_f64(0, None, None, None, None, 4, 4, 4, 0,
+                                         None) == _ffi.ERROR_DEVICE
+
+
+def test_comm_arguments_are_checked_without_a_gpu():
+    """The multi-process entry points check their arguments before touching
+    NCCL or a GPU, and never crash on bad ones."""
+    import ctypes as C
+    lib = hx.lib()
+    assert lib.hexir_sharded_linear_f64(None, None, None, None, 8, 8, 8, 0,
+                                        None) == _ffi.ERROR_INVALID_ARGUMENT
+    small = C.create_string_buffer(16)
+    assert lib.hexir_comm_unique_id(small, 16) == _ffi.ERROR_INVALID_ARGUMENT
+    out = C.c_void_p()
+    uid = C.create_string_buffer(128)
+    assert lib.hexir_comm_init_rank(uid, 128, 2, 5, 0, C.byref(out)) == \
+        _ffi.ERROR_INVALID_ARGUMENT                     # rank >= nranks
+    assert lib.hexir_comm_init_rank(None, 128, 2, 0, 0, C.byref(out)) == \
+        _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_comm_rank(None) == -1 and lib.hexir_comm_size(None) == 0
+    assert lib.hexir_comm_direct_stores(None) == 0
+    lib.hexir_comm_release(None)  # a no-op
