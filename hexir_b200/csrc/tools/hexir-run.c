@@ -9,11 +9,18 @@
  *
  * Additions: --device=cuda:N picks a GPU; --devices=N opens cuda:0..N-1 for
  * programs placed on several GPUs or row-sharded over them; --time prints the
- * device time of the dispatches on stderr.
+ * device time of the dispatches on stderr; --repeat=N runs the entry N times
+ * (PRINT output from the first run only; with --time, the median wall and
+ * dispatch times of the runs); --keep-constants keeps the module's constants
+ * on the GPU between those runs.
  */
+#define _POSIX_C_SOURCE 200809L
+#include <fcntl.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
+#include <unistd.h>
 
 #include "hexir_runtime/runtime.h"
 
@@ -21,9 +28,15 @@ static int usage(void) {
   fprintf(stderr,
           "usage: hexir-run <module.hxb> [--device=cpu|cuda|cuda:N] "
           "[--devices=N]\n"
-          "                 [--entry=name] [--quiet] [--time]\n"
+          "                 [--entry=name] [--quiet] [--time] [--repeat=N]\n"
+          "                 [--keep-constants]\n"
           "       hexir-run --selftest [--device=cpu|cuda|cuda:N]\n");
   return 2;
+}
+
+static int compare_doubles(const void *x, const void *y) {
+  const double a = *(const double *)x, b = *(const double *)y;
+  return (a > b) - (a < b);
 }
 
 static hexir_status_t open_device(hexir_device_kind_t kind, int ordinal,
@@ -75,7 +88,8 @@ int main(int argc, char **argv) {
   hexir_device_kind_t kind = HEXIR_DEVICE_CPU;
   int ordinal = 0;
   int device_count = 0; /* --devices=N */
-  int want_selftest = 0, quiet = 0, show_time = 0;
+  int want_selftest = 0, quiet = 0, show_time = 0, keep = 0;
+  long repeat = 1;
 
   for (int i = 1; i < argc; ++i) {
     if (strcmp(argv[i], "--quiet") == 0 || strcmp(argv[i], "-q") == 0) {
@@ -84,6 +98,13 @@ int main(int argc, char **argv) {
       want_selftest = 1;
     } else if (strcmp(argv[i], "--time") == 0) {
       show_time = 1;
+    } else if (strcmp(argv[i], "--keep-constants") == 0) {
+      keep = 1;
+    } else if (strncmp(argv[i], "--repeat=", 9) == 0) {
+      char *end = NULL;
+      repeat = strtol(argv[i] + 9, &end, 10);
+      if (!end || *end || repeat < 1 || repeat > 100000)
+        return usage();
     } else if (strncmp(argv[i], "--entry=", 8) == 0) {
       entry = argv[i] + 8;
     } else if (strncmp(argv[i], "--devices=", 10) == 0) {
@@ -173,17 +194,58 @@ int main(int argc, char **argv) {
   }
   fflush(stdout);
 
-  if (device_count > 0)
-    status = hexir_execute_devices(module, devices, (unsigned)device_count,
-                                   entry, NULL, 0);
-  else
-    status = hexir_execute(module, devices[0], entry);
-  fflush(stdout);
-  if (status != HEXIR_OK)
+  if (keep && (status = hexir_module_keep_constants(module, 1)) != HEXIR_OK)
+    fprintf(stderr, "hexir-run: cannot keep constants: %s\n",
+            hexir_status_string(status));
+  double *wall_ms = calloc((size_t)repeat, sizeof(double));
+  double *kernel_ms = calloc((size_t)repeat, sizeof(double));
+  int saved_stdout = -1;
+  for (long run = 0; status == HEXIR_OK && run < repeat; ++run) {
+    if (run == 1) {
+      /* PRINT output of the first run only. */
+      fflush(stdout);
+      saved_stdout = dup(STDOUT_FILENO);
+      int null_fd = open("/dev/null", O_WRONLY);
+      if (null_fd >= 0) {
+        dup2(null_fd, STDOUT_FILENO);
+        close(null_fd);
+      }
+    }
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    if (device_count > 0)
+      status = hexir_execute_devices(module, devices, (unsigned)device_count,
+                                     entry, NULL, 0);
+    else
+      status = hexir_execute(module, devices[0], entry);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    fflush(stdout);
+    if (wall_ms && kernel_ms) {
+      wall_ms[run] = (double)(t1.tv_sec - t0.tv_sec) * 1e3 +
+                     (double)(t1.tv_nsec - t0.tv_nsec) * 1e-6;
+      kernel_ms[run] = hexir_last_execute_kernel_ms();
+    }
+  }
+  if (saved_stdout >= 0) {
+    dup2(saved_stdout, STDOUT_FILENO);
+    close(saved_stdout);
+  }
+  if (status != HEXIR_OK) {
     fprintf(stderr, "hexir-run: %s failed: %s\n", entry,
             hexir_status_string(status));
-  else if (show_time)
+  } else if (show_time && repeat == 1) {
     fprintf(stderr, "kernel time   : %.3f ms\n", hexir_last_execute_kernel_ms());
+  } else if (show_time && wall_ms && kernel_ms) {
+    /* Medians of the runs after the first (warm-up) one. */
+    qsort(wall_ms + 1, (size_t)(repeat - 1), sizeof(double), compare_doubles);
+    qsort(kernel_ms + 1, (size_t)(repeat - 1), sizeof(double), compare_doubles);
+    const long mid = 1 + (repeat - 1) / 2;
+    fprintf(stderr, "runs          : %ld (first one not counted)\n", repeat);
+    fprintf(stderr, "execute time  : %.3f ms median\n", wall_ms[mid]);
+    fprintf(stderr, "kernel time   : %.3f ms median\n", kernel_ms[mid]);
+  }
+  free(wall_ms);
+  free(kernel_ms);
 
   for (int i = 0; i < opened; ++i)
     hexir_device_release(devices[i]);

@@ -501,3 +501,18 @@ def test_kept_constants_with_row_sharding():
     assert mod.kept_bytes == w.nbytes
     assert oracle.normwise_error(first, oracle.relu(oracle.matmul(a, w))) <= TOL
     mod.close()
+
+
+def test_hexir_run_repeat_with_kept_constants_on_cuda(tmp_path):
+    """hexir-run --device=cuda --repeat=3 --keep-constants: the printed
+    result once, equal to the cpu run's digits; medians on stderr."""
+    case = GOLDEN["known_answers"][1]
+    p = known_program(case)
+    path = tmp_path / "m.hxb"
+    p.emit_file(str(path), "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda")
+    res = subprocess.run([RUN, "--device=cuda", "--quiet", "--repeat=3",
+                          "--time", "--keep-constants", str(path)],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    assert res.stdout == case["stdout_quiet"]
+    assert "kernel time   :" in res.stderr and "median" in res.stderr

@@ -279,3 +279,20 @@ def test_fused_matmul_add_kinds_run_on_the_host(relu):
     if relu:
         want = oracle.relu(want)
     assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
+
+
+def test_hexir_run_repeat_prints_once(tmp_path):
+    """hexir-run --repeat=N runs the entry N times, PRINT output from the
+    first run only; --time then reports medians; N < 1 is a usage error."""
+    p = known_program(GOLDEN["known_answers"][0])
+    path = tmp_path / "m.hxb"
+    p.emit_file(str(path))
+    res = subprocess.run([bin_path("hexir-run"), "--quiet", "--repeat=4",
+                          "--time", "--keep-constants", str(path)],
+                         capture_output=True, text=True)
+    assert res.returncode == 0
+    assert res.stdout == GOLDEN["known_answers"][0]["stdout_quiet"]
+    assert "runs          : 4" in res.stderr and "median" in res.stderr
+    bad = subprocess.run([bin_path("hexir-run"), "--repeat=0", str(path)],
+                         capture_output=True, text=True)
+    assert bad.returncode == 2
