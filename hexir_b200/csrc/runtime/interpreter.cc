@@ -268,7 +268,10 @@ struct Vm {
   // ---- binding -----------------------------------------------------------
 
   hexir_status_t bind(uint64_t index, uint64_t bytes) {
-    if (index >= kMaxSlots)
+    // A slot larger than any memory (1 TiB) is a malformed module; the cap
+    // also keeps every size computation below from wrapping.
+    constexpr uint64_t kMaxSlotBytes = 1ull << 40;
+    if (index >= kMaxSlots || bytes > kMaxSlotBytes)
       return HEXIR_ERROR_INVALID_MODULE;
     Slot &s = slots[index];
     for (auto &kv : s.dev)

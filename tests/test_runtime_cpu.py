@@ -198,7 +198,9 @@ def test_bad_section_bounds_are_invalid(tmp_path):
 
 @pytest.mark.parametrize("field,value", [
     ("const_slot", 300), ("const_offset", 1 << 40), ("const_bytes", 1 << 40),
-    ("dispatch_index", 99), ("dispatch_argc", 9), ("dispatch_slot", 255)])
+    ("dispatch_index", 99), ("dispatch_argc", 9), ("dispatch_slot", 255),
+    # ALLOC sizes that would wrap a byte count or exceed any memory
+    ("alloc_bytes", (1 << 64) - 1), ("alloc_bytes", (1 << 40) + 8)])
 def test_bad_operands_are_invalid(tmp_path, field, value):
     blob = valid_module()
     base = program_offset(blob)
@@ -208,7 +210,8 @@ def test_bad_operands_are_invalid(tmp_path, field, value):
     dispatch = alloc + 8 + 16
     where = {"const_slot": const0, "const_offset": const0 + 8,
              "const_bytes": const0 + 16, "dispatch_index": dispatch + 8,
-             "dispatch_argc": dispatch + 16, "dispatch_slot": dispatch + 24}[field]
+             "dispatch_argc": dispatch + 16, "dispatch_slot": dispatch + 24,
+             "alloc_bytes": alloc + 16}[field]
     patch_u64(blob, where, value)
     res = run_blob(blob, tmp_path)
     assert res.returncode == 1
