@@ -519,9 +519,16 @@ struct Vm {
 
   // Make slot s valid on the host and return its bytes.
   hexir_status_t on_host(Slot &s, const uint8_t **out) {
-    if (s.rodata) {
+    if (s.rodata && (reinterpret_cast<uintptr_t>(s.rodata) & 7u) == 0) {
       *out = s.rodata;
       return HEXIR_OK;
+    }
+    if (s.rodata && !s.host_valid) {
+      // A CONST at an offset that is not a multiple of 8 (the serializer
+      // never writes one): the host kernels read an aligned copy.
+      s.host.assign((s.bytes + 7) / 8, 0.0);
+      std::memcpy(s.host.data(), s.rodata, static_cast<size_t>(s.bytes));
+      s.host_valid = true;
     }
     if (!s.host_valid) {
       s.host.assign((s.bytes + 7) / 8, 0.0);

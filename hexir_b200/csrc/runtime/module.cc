@@ -68,10 +68,12 @@ hexir_status_t validate(hexir_module_t *m) {
     return HEXIR_ERROR_INVALID_MODULE;
   m->sections = reinterpret_cast<const hexir_section_entry_t *>(
       m->base + sizeof(hexir_module_header_t));
-  // Offsets come off disk: bound every payload before trusting it.
+  // Offsets come off disk: bound every payload before trusting it.  The
+  // format puts every section on an 8-byte boundary (the serializer pads)
+  // and the tables are read in place, so an unaligned section is refused.
   for (uint32_t i = 0; i < m->header.section_count; ++i) {
     const hexir_section_entry_t &s = m->sections[i];
-    if (s.offset > m->size || s.size > m->size - s.offset)
+    if (s.offset > m->size || s.size > m->size - s.offset || s.offset % 8 != 0)
       return HEXIR_ERROR_INVALID_MODULE;
   }
   return HEXIR_OK;

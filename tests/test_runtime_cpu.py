@@ -299,3 +299,38 @@ def test_hexir_run_repeat_prints_once(tmp_path):
     bad = subprocess.run([bin_path("hexir-run"), "--repeat=0", str(path)],
                          capture_output=True, text=True)
     assert bad.returncode == 2
+
+
+def test_unaligned_section_is_invalid(tmp_path):
+    """Sections sit on 8-byte boundaries; a table moved off one is refused."""
+    blob = bytearray(valid_module())
+    # first section entry: kind u32, flags u32, offset u64 at 24 + 8
+    off = struct.unpack_from("<Q", blob, 24 + 8)[0]
+    struct.pack_into("<Q", blob, 24 + 8, off + 4)
+    res = run_blob(blob, tmp_path)
+    assert res.returncode == 1 and "invalid module" in res.stderr
+
+
+def test_misaligned_const_runs_on_the_host(tmp_path):
+    """A CONST at an offset that is not a multiple of 8 (never written by the
+    serializer) still computes the reference's answer on the host: the
+    kernels read an aligned copy."""
+    a = np.array([[3.0, 1.0], [2.0, 2.0]])
+    b = np.array([[1.0, 5.0], [5.0, 2.0]])
+    # 40 bytes holding b's 32 bytes at byte offset 4.
+    raw = np.frombuffer(bytes(4) + b.tobytes() + bytes(4), dtype=np.float64)
+    p = hx.Program()
+    p.relu(p.constant(raw.reshape(1, 5)))    # keeps the 40 bytes in RODATA
+    p.linear(p.constant(a), p.constant(b))   # the captured dispatch
+    blob = bytearray(p.emit())
+    poff, _ = hx.read_sections(bytes(blob))[2]
+    pc, consts = 0, []
+    for kind, ops in hx.read_program(bytes(blob)):
+        if kind == 2:
+            consts.append((pc, ops))
+        pc += 8 + 8 * len(ops)
+    (_, raw_ops), _, (b_pc, b_ops) = consts
+    assert raw_ops[2] == 40 and b_ops[2] == 32
+    struct.pack_into("<Q", blob, poff + b_pc + 16, raw_ops[1] + 4)
+    out = hx.execute(hx.Module(bytes(blob)), hx.Device("cpu"), out_shape=(2, 2))
+    assert np.array_equal(out, [[8.0, 17.0], [12.0, 14.0]])
