@@ -35,21 +35,113 @@ static double gflops(uint32_t m, uint32_t n, uint32_t k, double seconds) {
   return seconds > 0.0 ? 2.0 * m * n * k / seconds / 1e9 : 0.0;
 }
 
-static int first_executable(const hexir_module_t *module,
-                            hexir_executable_entry_t *out) {
+static int executable_at(const hexir_module_t *module, uint64_t index,
+                         hexir_executable_entry_t *out) {
   const void *data = NULL;
   uint64_t size = 0;
   if (hexir_module_section(module, HEXIR_SECTION_EXECUTABLES, &data, &size) !=
       HEXIR_OK)
     return 0;
-  if (size < sizeof(hexir_executable_header_t) + sizeof(*out))
-    return 0;
   hexir_executable_header_t header;
-  memcpy(&header, data, sizeof(header));
-  if (header.count == 0)
+  if (size < sizeof(header))
     return 0;
-  memcpy(out, (const uint8_t *)data + sizeof(header), sizeof(*out));
+  memcpy(&header, data, sizeof(header));
+  if (index >= header.count ||
+      sizeof(header) + (index + 1) * sizeof(*out) > size)
+    return 0;
+  memcpy(out, (const uint8_t *)data + sizeof(header) + index * sizeof(*out),
+         sizeof(*out));
   return 1;
+}
+
+static int first_executable(const hexir_module_t *module,
+                            hexir_executable_entry_t *out) {
+  return executable_at(module, 0, out);
+}
+
+/* The last DISPATCH of "main" (whose destination hexir_execute_capture
+ * returns): its executable index, and for each input that a CONST defines, a
+ * pointer to the constant in RODATA (NULL for computed inputs).  When its
+ * first input was computed by an earlier DISPATCH, *producer receives that
+ * dispatch's executable index and producer_in its constant inputs (a relu
+ * over an unfused linear).  -1 when the program cannot be read. */
+static int64_t last_dispatch_inputs(const hexir_module_t *module,
+                                    const double *in[3], int64_t *producer,
+                                    const double *producer_in[3]) {
+  const void *sym = NULL, *prog = NULL, *ro = NULL;
+  uint64_t sym_size = 0, prog_size = 0, ro_size = 0;
+  if (hexir_module_section(module, HEXIR_SECTION_SYMBOLS, &sym, &sym_size) !=
+          HEXIR_OK ||
+      hexir_module_section(module, HEXIR_SECTION_PROGRAM, &prog, &prog_size) !=
+          HEXIR_OK)
+    return -1;
+  if (hexir_module_section(module, HEXIR_SECTION_RODATA, &ro, &ro_size) !=
+      HEXIR_OK)
+    ro_size = 0;
+  uint64_t pc = UINT64_MAX;
+  for (uint64_t i = 0; (i + 1) * sizeof(hexir_symbol_entry_t) <= sym_size; ++i) {
+    hexir_symbol_entry_t e;
+    memcpy(&e, (const uint8_t *)sym + i * sizeof(e), sizeof(e));
+    if (strncmp(e.name, "main", HEXIR_NAME_SIZE) == 0) {
+      pc = e.program_offset;
+      break;
+    }
+  }
+  if (pc == UINT64_MAX)
+    return -1;
+  enum { kSlots = 256 };
+  const double *slot_const[kSlots] = {0};
+  int64_t slot_exe[kSlots];  /* the dispatch that wrote a slot, or -1 */
+  const double *slot_in[kSlots][3];
+  for (int i = 0; i < kSlots; ++i)
+    slot_exe[i] = -1;
+  int64_t last = -1;
+  *producer = -1;
+  while (pc + sizeof(hexir_command_header_t) <= prog_size) {
+    hexir_command_header_t h;
+    memcpy(&h, (const uint8_t *)prog + pc, sizeof(h));
+    pc += sizeof(h);
+    if (h.operand_count > 16 || pc + 8ull * h.operand_count > prog_size)
+      return -1;
+    uint64_t ops[16];
+    memcpy(ops, (const uint8_t *)prog + pc, 8ull * h.operand_count);
+    pc += 8ull * h.operand_count;
+    if (h.kind == HEXIR_CMD_END)
+      break;
+    if (h.kind == HEXIR_CMD_CONST && h.operand_count == 3 && ops[0] < kSlots) {
+      slot_const[ops[0]] = (ops[1] % 8 == 0 && ops[1] <= ro_size &&
+                            ops[2] <= ro_size - ops[1])
+                               ? (const double *)((const uint8_t *)ro + ops[1])
+                               : NULL;
+      slot_exe[ops[0]] = -1;
+    }
+    if (h.kind == HEXIR_CMD_ALLOC && h.operand_count == 2 && ops[0] < kSlots) {
+      slot_const[ops[0]] = NULL;
+      slot_exe[ops[0]] = -1;
+    }
+    if (h.kind == HEXIR_CMD_DISPATCH && h.operand_count >= 3) {
+      const uint64_t argc = ops[1];
+      if (argc + 2 != h.operand_count || argc > 4)
+        return -1;
+      last = (int64_t)ops[0];
+      for (uint64_t a = 0; a < 3; ++a)
+        in[a] = a + 1 < argc && ops[2 + a] < kSlots ? slot_const[ops[2 + a]]
+                                                    : NULL;
+      const uint64_t first = ops[2];
+      *producer = first < kSlots ? slot_exe[first] : -1;
+      if (first < kSlots && slot_exe[first] >= 0)
+        for (int a = 0; a < 3; ++a)
+          producer_in[a] = slot_in[first][a];
+      const uint64_t dst = ops[2 + argc - 1];
+      if (dst < kSlots) {
+        slot_const[dst] = NULL;
+        slot_exe[dst] = last;
+        for (int a = 0; a < 3; ++a)
+          slot_in[dst][a] = in[a];
+      }
+    }
+  }
+  return last;
 }
 
 /* ---- cuBLAS, loaded at run time -------------------------------------- */
@@ -78,9 +170,11 @@ static int cublas_load(void) {
 }
 
 /* Sampled check against the first two RODATA constants (a, then w). */
-static int verify_sampled(const double *a, const double *b, const double *got,
-                          uint32_t m, uint32_t n, uint32_t k, int relu,
-                          int samples, double *worst_out) {
+/* Sampled check of got = epilogue(a . b [+ d]) in the reference's order:
+ * the sum over k, rounded, then the add, then the relu. */
+static int verify_sampled(const double *a, const double *b, const double *d,
+                          const double *got, uint32_t m, uint32_t n, uint32_t k,
+                          int relu, int samples, double *worst_out) {
   size_t total = (size_t)m * n, stride = total / (size_t)samples;
   if (stride == 0)
     stride = 1;
@@ -90,6 +184,8 @@ static int verify_sampled(const double *a, const double *b, const double *got,
     double expected = 0.0;
     for (uint32_t p = 0; p < k; ++p)
       expected += a[(size_t)i * k + p] * b[(size_t)p * n + j];
+    if (d)
+      expected += d[index];
     if (relu)
       expected = expected > 0.0 ? expected : 0.0;
     double scale = fabs(expected) > 1.0 ? fabs(expected) : 1.0;
@@ -163,9 +259,6 @@ int main(int argc, char **argv) {
                       entry.kind == HEXIR_KERNEL_MATMUL_RELU ||
                       entry.kind == HEXIR_KERNEL_MATMUL_ADD ||
                       entry.kind == HEXIR_KERNEL_MATMUL_ADD_RELU;
-  /* The sampled check recomputes a . w from RODATA (a then w). */
-  const int checkable = entry.kind == HEXIR_KERNEL_MATMUL ||
-                        entry.kind == HEXIR_KERNEL_MATMUL_RELU;
   if (!json) {
     printf("module   : %s\n", path);
     printf("kernel   : %.32s  %s  built for %s  %ux%ux%u  elem=%uB\n",
@@ -216,17 +309,38 @@ int main(int argc, char **argv) {
   }
   double err = -1.0;
   int correct = 1;
-  if (result && checkable) {
-    const void *rodata = NULL;
-    uint64_t rodata_bytes = 0;
-    size_t a_n = (size_t)entry.m * entry.k, b_n = (size_t)entry.k * entry.n;
-    if (hexir_module_section(module, HEXIR_SECTION_RODATA, &rodata,
-                             &rodata_bytes) == HEXIR_OK &&
-        rodata_bytes >= (a_n + b_n) * sizeof(double)) {
-      const double *ra = (const double *)rodata;
-      correct = verify_sampled(ra, ra + a_n, result, entry.m, entry.n, entry.k,
-                               entry.kind == HEXIR_KERNEL_MATMUL_RELU, 512,
-                               &err);
+  /* The captured result is the last DISPATCH's: check it when that is a
+   * linear (fused or not) whose inputs are all constants. */
+  const double *inputs[3] = {NULL, NULL, NULL}, *prod_in[3] = {NULL, NULL, NULL};
+  hexir_executable_entry_t last, prod;
+  int64_t prod_index = -1;
+  const int64_t last_index =
+      last_dispatch_inputs(module, inputs, &prod_index, prod_in);
+  int over_linear = 0;  /* a relu of an unfused linear's result */
+  if (result && last_index >= 0 &&
+      executable_at(module, (uint64_t)last_index, &last) &&
+      last.kind == HEXIR_KERNEL_RELU && prod_index >= 0 &&
+      executable_at(module, (uint64_t)prod_index, &prod) &&
+      prod.kind == HEXIR_KERNEL_MATMUL && prod.m == last.m && prod.n == last.n) {
+    over_linear = 1;
+    last = prod;
+    last.kind = HEXIR_KERNEL_MATMUL_RELU;
+    for (int a = 0; a < 3; ++a)
+      inputs[a] = prod_in[a];
+  }
+  if (result && last_index >= 0 &&
+      (over_linear || executable_at(module, (uint64_t)last_index, &last)) &&
+      last.m == entry.m && last.n == entry.n) {
+    const int add = last.kind == HEXIR_KERNEL_MATMUL_ADD ||
+                    last.kind == HEXIR_KERNEL_MATMUL_ADD_RELU;
+    const int gemm = add || last.kind == HEXIR_KERNEL_MATMUL ||
+                     last.kind == HEXIR_KERNEL_MATMUL_RELU;
+    if (gemm && inputs[0] && inputs[1] && (!add || inputs[2])) {
+      correct = verify_sampled(inputs[0], inputs[1], add ? inputs[2] : NULL,
+                               result, last.m, last.n, last.k,
+                               last.kind == HEXIR_KERNEL_MATMUL_RELU ||
+                                   last.kind == HEXIR_KERNEL_MATMUL_ADD_RELU,
+                               512, &err);
       if (!json)
         printf("verify   : hexir max relative error %.3g over 512 sampled "
                "elements (%s)\n",

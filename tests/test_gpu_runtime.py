@@ -348,6 +348,18 @@ def test_hexir_bench_tool_verifies_and_times(tmp_path):
     assert line["kernel"] == "matmul_relu" and line["m"] == 512
     assert line["e2e_ms"] > 0 and line["kernel_ms"] > 0
     assert line["cublas_ms"] > 0
+    # A fused linear -> add -> relu module is verified too (addend included).
+    d = r.uniform((512, 512))
+    p2 = hx.Program()
+    p2.relu(p2.add(p2.linear(p2.constant(a), p2.constant(w)), p2.constant(d)))
+    path2 = tmp_path / "fused.hxb"
+    p2.emit_file(str(path2), "hexir.linear=cuda,hexir.add=cuda,hexir.relu=cuda")
+    res = subprocess.run([bin_path("hexir-bench"), str(path2), "--iters=2",
+                          "--json", "--no-baseline"], capture_output=True,
+                         text=True, check=True)
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["verify_ok"] is True and line["verify_max_rel_err"] < 1e-12
+    assert line["kernel"] == "matmul_add_relu"
 
 
 

@@ -334,3 +334,19 @@ def test_misaligned_const_runs_on_the_host(tmp_path):
     struct.pack_into("<Q", blob, poff + b_pc + 16, raw_ops[1] + 4)
     out = hx.execute(hx.Module(bytes(blob)), hx.Device("cpu"), out_shape=(2, 2))
     assert np.array_equal(out, [[8.0, 17.0], [12.0, 14.0]])
+
+
+def test_hexir_bench_verifies_cpu_modules(tmp_path):
+    """hexir-bench --device=cpu checks the captured result: a relu over an
+    unfused linear (the cpu form) against the reference arithmetic."""
+    r = hx.Rng(5)
+    a, w = r.uniform((64, 48)), r.uniform((48, 40))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    path = tmp_path / "m.hxb"
+    p.emit_file(str(path))
+    res = subprocess.run([bin_path("hexir-bench"), "--device=cpu", "--iters=2",
+                          "--no-baseline", "--json", str(path)],
+                         capture_output=True, text=True, check=True)
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["verify_ok"] is True and line["verify_max_rel_err"] == 0
