@@ -448,7 +448,9 @@ def run_hexir(args):
         line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg,
                               shard_flags)
 
-    if rank == 0 and not args.no_cpu_baseline:
+    # The CPU baseline is measured at N = 1 only (the other ranks would wait
+    # on it at the closing barrier).
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         rows = max(2 * threads, 16)
         gflops, used, kind, sample, _ = cpu_reference_rate(rows, steps=1)
