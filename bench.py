@@ -24,7 +24,7 @@ One JSON line on rank 0:
              peak measured on this GPU by a register-only DMMA probe
   cpu_baseline  the reference's own CPU kernel (hexir_ref_matmul_f64, built
              from the reference sources into oracle/_ref) on a bounded row
-             sample with all host threads
+             sample with all host threads (N = 1 only)
 --impl reference times that CPU implementation alone, as the reference arm.
 """
 
