@@ -441,7 +441,7 @@ def run_hexir(args):
         line["vendor"] = {"cublas_dgemm_tflops": round(
             cublas_dgemm_tflops(a, w), 3)}
 
-    if rank == 0 and not args.no_relu:
+    if rank == 0 and world == 1 and not args.no_relu:
         line["relu"] = relu_stream(ordinal)
 
     if not args.no_e2e:
