@@ -39,6 +39,10 @@ MATMUL_NO_STREAM_K = 0x800
 MATMUL_FORCE_STREAM_K = 0x2000
 SHARD_GATHER_NCCL = 0x1000
 
+# Activation codes = kernel kinds 7-14 (include/hexir_runtime/program.h).
+ACTIVATIONS = {"leaky_relu": 7, "elu": 8, "sigmoid": 9, "tanh": 10,
+               "softmax": 11, "gelu": 12, "swish": 13, "mish": 14}
+
 
 def MATMUL_SPLIT_K(s: int) -> int:
     return (s & 0xFF) << 16
@@ -47,6 +51,7 @@ def MATMUL_SPLIT_K(s: int) -> int:
 # include/hexir_b200/hxb_writer.h
 EMIT_NO_FUSE = 0x1
 EMIT_NO_IMAGE = 0x2
+EMIT_ACTIVATIONS = 0x4
 
 
 class Rng(C.Structure):
@@ -111,6 +116,7 @@ _SIGNATURES = [
                                          _u32, _u32, _vp]),
     ("hexir_cuda_add_f64", _int, [_int, _vp, _vp, _vp, _sz, _vp]),
     ("hexir_cuda_relu_f64", _int, [_int, _vp, _vp, _sz, _vp]),
+    ("hexir_cuda_activation_f64", _int, [_int, _u32, _vp, _vp, _u64, _u32, _vp]),
     ("hexir_cuda_matmul_f64_noalloc", _int, [_int, _vp, _vp, _vp, _u32, _u32,
                                              _u32, _u32, _vp]),
     ("hexir_cuda_synchronize", _int, [_int, _vp]),
@@ -145,6 +151,7 @@ _SIGNATURES = [
     ("hexir_program_linear", _i32, [_vp, _i32, _i32]),
     ("hexir_program_add", _i32, [_vp, _i32, _i32]),
     ("hexir_program_relu", _i32, [_vp, _i32]),
+    ("hexir_program_activation", _i32, [_vp, C.c_char_p, _i32]),
     ("hexir_program_print", _int, [_vp, _i32]),
     ("hexir_program_emit_file", _int, [_vp, C.c_char_p, _u32, C.c_char_p]),
     ("hexir_program_emit_memory", _int, [_vp, C.c_char_p, _u32,

@@ -74,6 +74,13 @@ class Program:
     def relu(self, x: int) -> int:
         return self._value(lib().hexir_program_relu(self._h, x), "relu")
 
+    def activation(self, op: str, x: int) -> int:
+        """One of the dialect's declared activations (leaky_relu, elu,
+        sigmoid, tanh, softmax, gelu, swish, mish); emit() serializes it only
+        with flags including EMIT_ACTIVATIONS."""
+        return self._value(
+            lib().hexir_program_activation(self._h, op.encode(), x), op)
+
     def print(self, x: int) -> None:
         check(lib().hexir_program_print(self._h, x), "print")
 
@@ -435,6 +442,16 @@ def cuda_add(ordinal: int, a: int, b: int, c: int, n: int,
              stream: int = 0) -> None:
     check(lib().hexir_cuda_add_f64(ordinal, a, b, c, n, stream or None),
           "hexir_cuda_add_f64")
+
+
+def cuda_activation(ordinal: int, op, x: int, y: int, rows: int, cols: int,
+                    stream: int = 0) -> None:
+    """y = op(x) over a [rows x cols] f64 tensor (hexir_cuda_activation_f64);
+    op is a name of _ffi.ACTIVATIONS or its code."""
+    code = _ffi.ACTIVATIONS[op] if isinstance(op, str) else int(op)
+    check(lib().hexir_cuda_activation_f64(ordinal, code, x, y, rows, cols,
+                                          stream or None),
+          "hexir_cuda_activation_f64")
 
 
 def cuda_synchronize(ordinal: int, stream: int = 0) -> None:

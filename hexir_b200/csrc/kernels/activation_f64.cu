@@ -1,0 +1,264 @@
+// activation_f64.cu -- the hexir dialect's declared activations
+// (include/hexir/Dialect/Hexir/IR/HexirOps.td:189-308) over f64 tensors:
+//
+//   leaky_relu  x > 0 ? x : 0.01 x          ("max(x, alpha * x)", alpha fixed)
+//   elu         x > 0 ? x : 1.0 expm1(x)    ("alpha * (exp(x) - 1)", alpha fixed)
+//   sigmoid     1 / (1 + exp(-x))
+//   tanh        tanh(x)
+//   softmax     exp(x - max) / sum exp(x - max) along each row
+//   gelu        0.5 x erfc(-x / sqrt 2)     (= x 0.5 (1 + erf(x / sqrt 2)),
+//                                            without the cancellation of 1 + erf
+//                                            for negative x)
+//   swish       x / (1 + exp(-x))           (= x sigmoid(x), one rounding)
+//   mish        x tanh(softplus(x)),        softplus(x) = x > 0 ? x + log1p(exp(-x))
+//                                                               : log1p(exp(x))
+//
+// The reference declares these ops but lowers none of them; the formulas
+// above are its op descriptions written in forms that keep their relative
+// accuracy over the whole f64 range.  The host backend (cpu_kernels.cc)
+// evaluates the same formulas with the C library's functions, so the two
+// agree to the functions' last-place differences.  Every add, multiply and
+// divide here is an explicit round-to-nearest intrinsic so that no fused
+// multiply-add is formed across the inlined math functions.
+//
+// Elementwise ops run on the relu/add stream loop (16-byte streaming loads and
+// stores, four vectors in flight per thread).  Softmax keeps each row in
+// registers: a warp per row up to 1024 columns, one 256- or 512-thread block
+// per row up to 8192 / 16384 columns (one read and one write of the row), and
+// a three-pass block per row beyond that.
+
+namespace {
+
+__device__ __forceinline__ double neg_inf() {
+  return __longlong_as_double(static_cast<long long>(0xfff0000000000000ull));
+}
+
+struct LeakyReluOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return x > 0.0 ? x : __dmul_rn(HEXIR_LEAKY_RELU_ALPHA, x);
+  }
+};
+struct EluOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return x > 0.0 ? x : __dmul_rn(HEXIR_ELU_ALPHA, expm1(x));
+  }
+};
+struct SigmoidOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
+  }
+};
+struct TanhOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return tanh(x);
+  }
+};
+struct GeluOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return __dmul_rn(__dmul_rn(0.5, x),
+                     erfc(__dmul_rn(-x, 0.70710678118654752440)));
+  }
+};
+struct SwishOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return __ddiv_rn(x, __dadd_rn(1.0, exp(-x)));
+  }
+};
+__device__ __forceinline__ double softplus(double x) {
+  return x > 0.0 ? __dadd_rn(x, log1p(exp(-x))) : log1p(exp(x));
+}
+struct MishOp {
+  __device__ __forceinline__ double operator()(double x, double) const {
+    return __dmul_rn(x, tanh(softplus(x)));
+  }
+};
+
+template <typename Op>
+__device__ __forceinline__ void activation_stream(
+    const hexir_activation_args_t &a, Op op) {
+  const hexir_elementwise_args_t e{a.x, nullptr, a.out, a.count};
+  stream_f64<false>(e, op);
+}
+
+// ---------------------------------------------------------------- softmax
+
+struct MaxOp {
+  __device__ __forceinline__ double operator()(double a, double b) const {
+    return b > a ? b : a;
+  }
+};
+struct SumOp {
+  __device__ __forceinline__ double operator()(double a, double b) const {
+    return __dadd_rn(a, b);
+  }
+};
+
+// Butterfly over the warp: IEEE add and the compare-select max are
+// commutative, so every lane ends with the same value.
+template <typename Op>
+__device__ __forceinline__ double warp_reduce(double v, Op op) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// The block's reduction, the same value in every thread: warps reduce, then
+// every thread folds the per-warp values in warp order.
+template <int THREADS, typename Op>
+__device__ __forceinline__ double block_reduce(double v, double *red, Op op) {
+  v = warp_reduce(v, op);
+  if ((threadIdx.x & 31) == 0)
+    red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double r = red[0];
+#pragma unroll
+  for (int w = 1; w < THREADS / 32; ++w)
+    r = op(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+// One row per block, PER elements per thread kept in registers: one read and
+// one write of the row.  The maximum skips NaN (x > m is false); a NaN or an
+// infinity in the row makes the whole row NaN through exp(x - m), as in the
+// host formula.
+template <int THREADS, int PER>
+__device__ __forceinline__ void softmax_rows_block(
+    const hexir_activation_args_t &p) {
+  __shared__ double red[THREADS / 32];
+  const uint32_t cols = p.cols;
+  for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const double *xr = p.x + row * cols;
+    double *yr = p.out + row * cols;
+    double v[PER];
+    double m = neg_inf();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      v[i] = j < cols ? __ldcs(xr + j) : neg_inf();
+      m = v[i] > m ? v[i] : m;
+    }
+    m = block_reduce<THREADS>(m, red, MaxOp{});
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      if (j < cols) {
+        v[i] = exp(__dsub_rn(v[i], m));
+        s = __dadd_rn(s, v[i]);
+      }
+    }
+    s = block_reduce<THREADS>(s, red, SumOp{});
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      if (j < cols)
+        __stcs(yr + j, __ddiv_rn(v[i], s));
+    }
+  }
+}
+
+// One row per warp, PER elements per lane.
+template <int PER>
+__device__ __forceinline__ void softmax_rows_warp(
+    const hexir_activation_args_t &p) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
+  const uint32_t cols = p.cols;
+  for (uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x +
+                       threadIdx.x) >> 5;
+       row < p.rows; row += warps) {
+    const double *xr = p.x + row * cols;
+    double *yr = p.out + row * cols;
+    double v[PER];
+    double m = neg_inf();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = lane + i * 32;
+      v[i] = j < cols ? __ldcs(xr + j) : neg_inf();
+      m = v[i] > m ? v[i] : m;
+    }
+    m = warp_reduce(m, MaxOp{});
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = lane + i * 32;
+      if (j < cols) {
+        v[i] = exp(__dsub_rn(v[i], m));
+        s = __dadd_rn(s, v[i]);
+      }
+    }
+    s = warp_reduce(s, SumOp{});
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = lane + i * 32;
+      if (j < cols)
+        __stcs(yr + j, __ddiv_rn(v[i], s));
+    }
+  }
+}
+
+// Rows too long for registers: maximum, sum and output each read the row
+// (the second and third reads mostly from L2).
+template <int THREADS>
+__device__ __forceinline__ void softmax_rows_wide(
+    const hexir_activation_args_t &p) {
+  __shared__ double red[THREADS / 32];
+  const uint32_t cols = p.cols;
+  for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const double *xr = p.x + row * cols;
+    double *yr = p.out + row * cols;
+    double m = neg_inf();
+    for (uint32_t j = threadIdx.x; j < cols; j += THREADS) {
+      const double x = xr[j];
+      m = x > m ? x : m;
+    }
+    m = block_reduce<THREADS>(m, red, MaxOp{});
+    double s = 0.0;
+    for (uint32_t j = threadIdx.x; j < cols; j += THREADS)
+      s = __dadd_rn(s, exp(__dsub_rn(xr[j], m)));
+    s = block_reduce<THREADS>(s, red, SumOp{});
+    for (uint32_t j = threadIdx.x; j < cols; j += THREADS)
+      __stcs(yr + j, __ddiv_rn(exp(__dsub_rn(__ldcs(xr + j), m)), s));
+  }
+}
+
+}  // namespace
+
+#define HEXIR_ACTIVATION_KERNEL(name, Op)                              \
+  extern "C" __global__ void __launch_bounds__(256)                    \
+      name(const hexir_activation_args_t args) {                       \
+    activation_stream(args, Op{});                                     \
+  }
+
+HEXIR_ACTIVATION_KERNEL(hexir_leaky_relu_f64, LeakyReluOp)
+HEXIR_ACTIVATION_KERNEL(hexir_elu_f64, EluOp)
+HEXIR_ACTIVATION_KERNEL(hexir_sigmoid_f64, SigmoidOp)
+HEXIR_ACTIVATION_KERNEL(hexir_tanh_f64, TanhOp)
+HEXIR_ACTIVATION_KERNEL(hexir_gelu_f64, GeluOp)
+HEXIR_ACTIVATION_KERNEL(hexir_swish_f64, SwishOp)
+HEXIR_ACTIVATION_KERNEL(hexir_mish_f64, MishOp)
+
+#undef HEXIR_ACTIVATION_KERNEL
+
+// 256 threads = 8 rows per block.
+extern "C" __global__ void __launch_bounds__(256)
+    hexir_softmax_warp_f64(const hexir_activation_args_t args) {
+  softmax_rows_warp<HEXIR_SOFTMAX_WARP_COLS / 32>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(256, 2)
+    hexir_softmax_b256_f64(const hexir_activation_args_t args) {
+  softmax_rows_block<256, HEXIR_SOFTMAX_B256_COLS / 256>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(512, 1)
+    hexir_softmax_b512_f64(const hexir_activation_args_t args) {
+  softmax_rows_block<512, HEXIR_SOFTMAX_B512_COLS / 512>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(512)
+    hexir_softmax_wide_f64(const hexir_activation_args_t args) {
+  softmax_rows_wide<512>(args);
+}

@@ -111,6 +111,36 @@ typedef struct {
   uint64_t count;
 } hexir_elementwise_args_t;
 
+/* Activation codes: the kernel kind numbers of program.h (7-14). */
+#define HEXIR_ACT_LEAKY_RELU 7u
+#define HEXIR_ACT_ELU 8u
+#define HEXIR_ACT_SIGMOID 9u
+#define HEXIR_ACT_TANH 10u
+#define HEXIR_ACT_SOFTMAX 11u
+#define HEXIR_ACT_GELU 12u
+#define HEXIR_ACT_SWISH 13u
+#define HEXIR_ACT_MISH 14u
+/* The fixed slopes of leaky_relu and elu (the ops carry no attribute). */
+#define HEXIR_LEAKY_RELU_ALPHA 0.01
+#define HEXIR_ELU_ALPHA 1.0
+
+/* Softmax launch shapes: a warp per row up to 32 x 32 columns, a 256-thread
+ * block per row up to 256 x 32, a 512-thread block per row up to 512 x 32
+ * (each thread holding up to 32 elements in registers), and above that a
+ * 512-thread block per row that reads the row three times. */
+#define HEXIR_SOFTMAX_WARP_COLS 1024u
+#define HEXIR_SOFTMAX_B256_COLS 8192u
+#define HEXIR_SOFTMAX_B512_COLS 16384u
+
+typedef struct {
+  const double *x;
+  double *out;
+  uint64_t count; /* elementwise: elements; softmax: rows * cols */
+  uint64_t rows;  /* softmax rows */
+  uint32_t cols;  /* softmax row length */
+  uint32_t op;    /* HEXIR_ACT_* */
+} hexir_activation_args_t;
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,12 +11,14 @@
 // cuda-placed dispatches never come here: the VM refuses them on a CPU device.
 
 #include <algorithm>
+#include <cmath>
 #include <cstddef>
 #include <cstdint>
 #include <thread>
 #include <vector>
 
 #include "hal_internal.h"
+#include "hexir_runtime/program.h"
 
 namespace hexir {
 
@@ -69,6 +71,65 @@ void cpu_add_f64(const double *a, const double *b, double *c, size_t n) {
 void cpu_relu_f64(const double *x, double *y, size_t n) {
   for (size_t i = 0; i < n; ++i)
     y[i] = x[i] > 0.0 ? x[i] : 0.0;
+}
+
+// The activations the reference dialect declares without lowering
+// (include/hexir/Dialect/Hexir/IR/HexirOps.td:189-308), as the GPU kernels
+// evaluate them: each op description written in a form that keeps its
+// relative accuracy (gelu through erfc, softplus split at 0), leaky_relu's
+// alpha 0.01 and elu's alpha 1.0 fixed because the ops carry no attribute.
+// Softmax subtracts the row maximum (NaN skipped by the compare) and sums the
+// row left to right.
+namespace {
+
+double softplus(double x) {
+  return x > 0.0 ? x + std::log1p(std::exp(-x)) : std::log1p(std::exp(x));
+}
+
+double activation(uint32_t kind, double x) {
+  switch (kind) {
+  case HEXIR_KERNEL_LEAKY_RELU: return x > 0.0 ? x : 0.01 * x;
+  case HEXIR_KERNEL_ELU: return x > 0.0 ? x : 1.0 * std::expm1(x);
+  case HEXIR_KERNEL_SIGMOID: return 1.0 / (1.0 + std::exp(-x));
+  case HEXIR_KERNEL_TANH: return std::tanh(x);
+  case HEXIR_KERNEL_GELU:
+    return (0.5 * x) * std::erfc(-x * 0.70710678118654752440);
+  case HEXIR_KERNEL_SWISH: return x / (1.0 + std::exp(-x));
+  case HEXIR_KERNEL_MISH: return x * std::tanh(softplus(x));
+  }
+  return x;
+}
+
+}  // namespace
+
+void cpu_activation_f64(uint32_t kind, const double *x, double *y,
+                        uint64_t rows, uint64_t cols) {
+  if (kind == HEXIR_KERNEL_SOFTMAX) {
+    parallel_rows(rows, cols * 8, [=](uint64_t r0, uint64_t r1) {
+      for (uint64_t r = r0; r < r1; ++r) {
+        const double *xr = x + r * cols;
+        double *yr = y + r * cols;
+        double m = -HUGE_VAL;
+        for (uint64_t j = 0; j < cols; ++j)
+          m = xr[j] > m ? xr[j] : m;
+        double s = 0.0;
+        for (uint64_t j = 0; j < cols; ++j) {
+          yr[j] = std::exp(xr[j] - m);
+          s += yr[j];
+        }
+        for (uint64_t j = 0; j < cols; ++j)
+          yr[j] = yr[j] / s;
+      }
+    });
+    return;
+  }
+  const uint64_t n = rows * cols;
+  const uint64_t chunk = 1u << 16;
+  parallel_rows((n + chunk - 1) / chunk, chunk * 8, [=](uint64_t c0, uint64_t c1) {
+    const uint64_t end = std::min(n, c1 * chunk);
+    for (uint64_t i = c0 * chunk; i < end; ++i)
+      y[i] = activation(kind, x[i]);
+  });
 }
 
 }  // namespace hexir

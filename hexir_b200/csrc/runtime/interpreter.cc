@@ -607,7 +607,12 @@ struct Vm {
 
   // Buffer sizes against the kernel's extents.
   // Operands before the destination, by kernel kind.
+  static bool is_activation(uint32_t kind) {
+    return kind >= HEXIR_KERNEL_LEAKY_RELU && kind <= HEXIR_KERNEL_MISH;
+  }
   static int inputs_of(uint32_t kind) {
+    if (is_activation(kind))
+      return 1;
     switch (kind) {
     case HEXIR_KERNEL_RELU: return 1;
     case HEXIR_KERNEL_MATMUL_ADD:
@@ -659,6 +664,14 @@ struct Vm {
         return HEXIR_ERROR_INVALID_MODULE;
       return HEXIR_OK;
     case HEXIR_KERNEL_RELU:
+    case HEXIR_KERNEL_LEAKY_RELU:
+    case HEXIR_KERNEL_ELU:
+    case HEXIR_KERNEL_SIGMOID:
+    case HEXIR_KERNEL_TANH:
+    case HEXIR_KERNEL_SOFTMAX:
+    case HEXIR_KERNEL_GELU:
+    case HEXIR_KERNEL_SWISH:
+    case HEXIR_KERNEL_MISH:
       if (argc != 2)
         return HEXIR_ERROR_INVALID_MODULE;
       if (args[0]->bytes < mn || args[1]->bytes < mn)
@@ -711,6 +724,9 @@ struct Vm {
       break;
     case HEXIR_KERNEL_RELU:
       cpu_relu_f64(a, c, elems(exe));
+      break;
+    default:
+      cpu_activation_f64(exe.kind, a, c, exe.m, exe.n);
       break;
     }
     return HEXIR_OK;
@@ -1083,6 +1099,10 @@ struct Vm {
     case HEXIR_KERNEL_RELU:
       st = launch_relu(dev->state, lib, a, c, elems(exe), dev->stream, &error);
       break;
+    default:
+      st = launch_activation(dev->state, lib, exe.kind, a, c, exe.m, exe.n,
+                             dev->stream, &error);
+      break;
     }
     end_span(span);
     if (st != HEXIR_OK) {
@@ -1243,6 +1263,12 @@ struct Vm {
         st = launch_relu(dev->state, lib, reinterpret_cast<const double *>(x),
                          reinterpret_cast<double *>(out), count_elems,
                          dev->stream, &error);
+        break;
+      default:
+        st = launch_activation(dev->state, lib, exe.kind,
+                               reinterpret_cast<const double *>(x),
+                               reinterpret_cast<double *>(out), rows[r], exe.n,
+                               dev->stream, &error);
         break;
       }
       if (st != HEXIR_OK) {
@@ -1656,6 +1682,14 @@ const char *hexir_kernel_kind_string(uint32_t kind) {
   case HEXIR_KERNEL_MATMUL_RELU: return "matmul_relu";
   case HEXIR_KERNEL_MATMUL_ADD: return "matmul_add";
   case HEXIR_KERNEL_MATMUL_ADD_RELU: return "matmul_add_relu";
+  case HEXIR_KERNEL_LEAKY_RELU: return "leaky_relu";
+  case HEXIR_KERNEL_ELU: return "elu";
+  case HEXIR_KERNEL_SIGMOID: return "sigmoid";
+  case HEXIR_KERNEL_TANH: return "tanh";
+  case HEXIR_KERNEL_SOFTMAX: return "softmax";
+  case HEXIR_KERNEL_GELU: return "gelu";
+  case HEXIR_KERNEL_SWISH: return "swish";
+  case HEXIR_KERNEL_MISH: return "mish";
   }
   return "unknown";
 }

@@ -225,6 +225,32 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
       d.ModuleGetFunction(&lib->sk_fixup, lib->module,
                           "hexir_linear_f64_sk_fixup") != CUDA_SUCCESS)
     lib->linear_tma_sk = lib->sk_fixup = nullptr;
+  // Optional: the activation kernels, all or none.
+  {
+    struct Opt {
+      CUfunction *slot;
+      const char *name;
+    } acts[] = {
+        {&lib->activation[HEXIR_ACT_LEAKY_RELU - 7], "hexir_leaky_relu_f64"},
+        {&lib->activation[HEXIR_ACT_ELU - 7], "hexir_elu_f64"},
+        {&lib->activation[HEXIR_ACT_SIGMOID - 7], "hexir_sigmoid_f64"},
+        {&lib->activation[HEXIR_ACT_TANH - 7], "hexir_tanh_f64"},
+        {&lib->activation[HEXIR_ACT_GELU - 7], "hexir_gelu_f64"},
+        {&lib->activation[HEXIR_ACT_SWISH - 7], "hexir_swish_f64"},
+        {&lib->activation[HEXIR_ACT_MISH - 7], "hexir_mish_f64"},
+        {&lib->softmax_warp, "hexir_softmax_warp_f64"},
+        {&lib->softmax_b256, "hexir_softmax_b256_f64"},
+        {&lib->softmax_b512, "hexir_softmax_b512_f64"},
+        {&lib->softmax_wide, "hexir_softmax_wide_f64"},
+    };
+    bool all = true;
+    for (const Opt &o : acts)
+      all = all && d.ModuleGetFunction(o.slot, lib->module, o.name) == CUDA_SUCCESS;
+    if (!all) {
+      for (const Opt &o : acts)
+        *o.slot = nullptr;
+    }
+  }
   size_t word_bytes = 0;
   r = d.ModuleGetGlobal(&lib->error_word, &word_bytes, lib->module,
                         "hexir_device_error_word");
@@ -601,6 +627,48 @@ hexir_status_t launch_add(DeviceState *dev, KernelLib *lib, const double *a,
                 "launch hexir_add_f64", error);
 }
 
+hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
+                                 const double *x, double *y, uint64_t rows,
+                                 uint32_t cols, CUstream stream,
+                                 std::string *error) {
+  if (op < HEXIR_ACT_LEAKY_RELU || op > HEXIR_ACT_MISH)
+    return fail(error, "activation: unknown op " + std::to_string(op),
+                HEXIR_ERROR_INVALID_ARGUMENT);
+  const uint64_t count = rows * cols;
+  if (cols && count / cols != rows)
+    return fail(error, "activation: rows x cols overflows",
+                HEXIR_ERROR_INVALID_ARGUMENT);
+  if (count == 0)
+    return HEXIR_OK;
+  if (!x || !y)
+    return fail(error, "activation: null pointer", HEXIR_ERROR_INVALID_ARGUMENT);
+  if (!lib->softmax_warp)
+    return fail(error, "kernel library image lacks the activation kernels",
+                HEXIR_ERROR_UNIMPLEMENTED);
+  hexir_activation_args_t args{x, y, count, rows, cols, op};
+  void *params[] = {&args};
+  if (op != HEXIR_ACT_SOFTMAX)
+    return launch(lib->activation[op - 7], stream_grid(dev, count / 2), 1, 256,
+                  0, stream, params, "launch activation kernel", error);
+  // Softmax: one row per warp or per block; blocks beyond the resident ones
+  // queue, which balances rows of uneven cost.
+  const uint64_t cap = 1u << 20;
+  if (cols <= HEXIR_SOFTMAX_WARP_COLS) {
+    const uint64_t blocks = std::min<uint64_t>((rows + 7) / 8, cap);
+    return launch(lib->softmax_warp, static_cast<unsigned>(blocks), 1, 256, 0,
+                  stream, params, "launch hexir_softmax_warp_f64", error);
+  }
+  const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>(rows, cap));
+  if (cols <= HEXIR_SOFTMAX_B256_COLS)
+    return launch(lib->softmax_b256, blocks, 1, 256, 0, stream, params,
+                  "launch hexir_softmax_b256_f64", error);
+  if (cols <= HEXIR_SOFTMAX_B512_COLS)
+    return launch(lib->softmax_b512, blocks, 1, 512, 0, stream, params,
+                  "launch hexir_softmax_b512_f64", error);
+  return launch(lib->softmax_wide, blocks, 1, 512, 0, stream, params,
+                "launch hexir_softmax_wide_f64", error);
+}
+
 hexir_status_t check_device(DeviceState *dev, CUstream stream,
                             std::string *error) {
   const Driver &d = driver();
@@ -731,6 +799,19 @@ extern "C" hexir_status_t hexir_cuda_relu_f64(int ordinal, const double *x,
   ContextGuard guard(call.dev->context);
   return call.finish(launch_relu(call.dev, call.lib, x, y, n,
                                  static_cast<CUstream>(stream), &call.error));
+}
+
+extern "C" hexir_status_t hexir_cuda_activation_f64(int ordinal, uint32_t op,
+                                                    const double *x, double *y,
+                                                    uint64_t rows, uint32_t cols,
+                                                    void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  ContextGuard guard(call.dev->context);
+  return call.finish(launch_activation(call.dev, call.lib, op, x, y, rows, cols,
+                                       static_cast<CUstream>(stream),
+                                       &call.error));
 }
 
 extern "C" hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream) {

@@ -30,6 +30,12 @@ struct KernelLib {
   CUfunction splitk_reduce = nullptr;
   CUfunction relu = nullptr;
   CUfunction add = nullptr;
+  // Activations (absent in images written before they existed): the
+  // elementwise kernels by HEXIR_ACT_* code - 7 (the softmax slot stays
+  // empty), then the four softmax launch shapes.
+  CUfunction activation[8] = {};
+  CUfunction softmax_warp = nullptr, softmax_b256 = nullptr,
+             softmax_b512 = nullptr, softmax_wide = nullptr;
   CUfunction dmma_probe = nullptr;
   CUfunction wait_probe = nullptr;
   CUdeviceptr error_word = 0;
@@ -105,6 +111,12 @@ hexir_status_t launch_relu(DeviceState *dev, KernelLib *lib, const double *x,
 hexir_status_t launch_add(DeviceState *dev, KernelLib *lib, const double *a,
                           const double *b, double *c, size_t n, CUstream stream,
                           std::string *error);
+// y = op(x) over rows x cols (HEXIR_ACT_* op; softmax along each row, the
+// others elementwise over rows * cols).
+hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
+                                 const double *x, double *y, uint64_t rows,
+                                 uint32_t cols, CUstream stream,
+                                 std::string *error);
 
 // Synchronise `stream` and collect (and clear) the device error word of
 // every module loaded on this device.

@@ -9,8 +9,10 @@
 // With no input it writes the built-in program of the reference compiler
 // (compiler/Support/Builder.cpp:264-327: [[3,1],[2,2]] . [[1,5],[5,2]],
 // printed).  Additions: --no-fuse keeps linear and relu as two executables;
-// --no-image writes cuda-placed executables as descriptors only; placement
-// devices cuda:N and cuda:F-L.
+// --no-image writes cuda-placed executables as descriptors only;
+// --activations writes the dialect's activations (leaky_relu ... mish) as
+// kernel kinds 7-14 instead of refusing them; placement devices cuda:N and
+// cuda:F-L.
 
 #include <cstdio>
 #include <cstring>
@@ -25,10 +27,15 @@ static int usage() {
   std::fprintf(stderr,
                "usage: hexir-mkhxb [-emit=hxb] [-o <file>] "
                "[-placement=<op>=<device>[,...]]\n"
-               "                   [--no-fuse] [--no-image] [input.mlir]\n"
+               "                   [--no-fuse] [--no-image] [--activations] "
+               "[input.mlir]\n"
                "devices: cpu, cuda, gpu, cuda:N, cuda:F-L (rows split over "
                "GPUs F..L)\n"
-               "placeable ops: hexir.add, hexir.linear, hexir.relu\n");
+               "placeable ops: hexir.add, hexir.linear, hexir.relu; with "
+               "--activations also\n"
+               "  hexir.leaky_relu, hexir.elu, hexir.sigmoid, hexir.tanh, "
+               "hexir.softmax,\n"
+               "  hexir.gelu, hexir.swish, hexir.mish\n");
   return 2;
 }
 
@@ -66,6 +73,8 @@ int main(int argc, char **argv) {
       flags |= HEXIR_EMIT_NO_FUSE;
     } else if (arg == "--no-image") {
       flags |= HEXIR_EMIT_NO_IMAGE;
+    } else if (arg == "--activations") {
+      flags |= HEXIR_EMIT_ACTIVATIONS;
     } else if (arg == "-h" || arg == "--help") {
       return usage();
     } else if (!arg.empty() && arg[0] == '-' && arg != "-") {

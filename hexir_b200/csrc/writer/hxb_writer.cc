@@ -26,7 +26,27 @@
 
 namespace {
 
-enum class OpKind { Constant, Linear, Add, Relu, Print };
+enum class OpKind { Constant, Linear, Add, Relu, Activation, Print };
+
+// The activations the dialect declares (HexirOps.td:189-308), by the kernel
+// kind that runs them.
+struct ActivationName {
+  const char *name;
+  uint32_t kind;
+};
+const ActivationName kActivations[] = {
+    {"leaky_relu", HEXIR_KERNEL_LEAKY_RELU}, {"elu", HEXIR_KERNEL_ELU},
+    {"sigmoid", HEXIR_KERNEL_SIGMOID},       {"tanh", HEXIR_KERNEL_TANH},
+    {"softmax", HEXIR_KERNEL_SOFTMAX},       {"gelu", HEXIR_KERNEL_GELU},
+    {"swish", HEXIR_KERNEL_SWISH},           {"mish", HEXIR_KERNEL_MISH},
+};
+
+const char *activation_name(uint32_t kind) {
+  for (const ActivationName &a : kActivations)
+    if (a.kind == kind)
+      return a.name;
+  return "";
+}
 
 struct Value {
   uint32_t rows = 0, cols = 0;
@@ -42,6 +62,7 @@ struct Op {
   std::vector<double> data;  // constants
   bool splat = false;
   double splat_value = 0.0;
+  uint32_t act = 0;  // Activation: its kernel kind
 };
 
 struct Function {
@@ -73,17 +94,19 @@ struct Bytes {
   size_t size() const { return b.size(); }
 };
 
-const char *op_name(OpKind k) {
-  switch (k) {
+const char *op_name(const Op &op) {
+  switch (op.kind) {
   case OpKind::Linear: return "linear";
   case OpKind::Add: return "add";
   case OpKind::Relu: return "relu";
+  case OpKind::Activation: return activation_name(op.act);
   default: return "";
   }
 }
 
 bool is_compute(OpKind k) {
-  return k == OpKind::Linear || k == OpKind::Add || k == OpKind::Relu;
+  return k == OpKind::Linear || k == OpKind::Add || k == OpKind::Relu ||
+         k == OpKind::Activation;
 }
 
 void write_name(char (&dst)[HEXIR_NAME_SIZE], const std::string &name) {
@@ -179,12 +202,17 @@ struct hexir_program_t {
 
 namespace {
 
+// The placeable ops are the reference's three (compiler/Target/
+// TargetInfo.cpp:21-23), plus the activations when they are being written.
 hexir_status_t parse_placement(const char *text,
                                std::map<std::string, DeviceSpec> *spec,
-                               std::string *error) {
+                               std::string *error, bool activations) {
   (*spec)["hexir.linear"] = DeviceSpec{};
   (*spec)["hexir.add"] = DeviceSpec{};
   (*spec)["hexir.relu"] = DeviceSpec{};
+  if (activations)
+    for (const ActivationName &a : kActivations)
+      (*spec)[std::string("hexir.") + a.name] = DeviceSpec{};
   if (!text || !*text)
     return HEXIR_OK;
   std::string all(text);
@@ -218,13 +246,8 @@ hexir_status_t parse_placement(const char *text,
   return HEXIR_OK;
 }
 
-const char *op_key(OpKind k) {
-  switch (k) {
-  case OpKind::Linear: return "hexir.linear";
-  case OpKind::Add: return "hexir.add";
-  case OpKind::Relu: return "hexir.relu";
-  default: return "";
-  }
+std::string op_key(const Op &op) {
+  return std::string("hexir.") + op_name(op);
 }
 
 }  // namespace
@@ -232,9 +255,19 @@ const char *op_key(OpKind k) {
 hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
                                      Bytes *out) {
   std::map<std::string, DeviceSpec> spec;
-  hexir_status_t st = parse_placement(placement, &spec, &error);
+  hexir_status_t st = parse_placement(placement, &spec, &error,
+                                      (flags & HEXIR_EMIT_ACTIVATIONS) != 0);
   if (st != HEXIR_OK)
     return st;
+  // The reference serializer has no kernel for the activations and refuses
+  // them (ModuleSerializer.cpp:368); they are written only on request.
+  if (!(flags & HEXIR_EMIT_ACTIVATIONS))
+    for (const Op &op : ops)
+      if (op.kind == OpKind::Activation) {
+        error = "'" + op_key(op) +
+                "' op cannot serialize this op into a host program";
+        return HEXIR_ERROR_UNIMPLEMENTED;
+      }
 
   // Kernel names in walk order (functions in order, ops in order), every
   // compute op taking a number even if fusion later folds it away.
@@ -244,9 +277,10 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
   for (const Function &f : funcs)
     for (int oi : f.ops)
       if (is_compute(ops[oi].kind)) {
-        kernel_name[oi] = std::string(op_name(ops[oi].kind)) + "_" +
+        kernel_name[oi] = std::string(op_name(ops[oi])) + "_" +
                           std::to_string(counter++);
-        where[oi] = spec[op_key(ops[oi].kind)];
+        where[oi] = spec.count(op_key(ops[oi])) ? spec[op_key(ops[oi])]
+                                                : DeviceSpec{};
       }
 
   // Fusions on a GPU, each where the intermediate value has no other user and
@@ -334,6 +368,8 @@ hexir_status_t hexir_program_t::emit(const char *placement, uint32_t flags,
       if (op.kind == OpKind::Linear)
         e.kind = fused[oi] ? fused_kind[oi]
                            : static_cast<uint32_t>(HEXIR_KERNEL_MATMUL);
+      else if (op.kind == OpKind::Activation)
+        e.kind = op.act;
       else
         e.kind = op.kind == OpKind::Add ? HEXIR_KERNEL_ADD : HEXIR_KERNEL_RELU;
       e.device = where[oi].cuda ? 1u : 0u;
@@ -601,6 +637,31 @@ int32_t hexir_program_relu(hexir_program_t *p, int32_t input) {
   const Value &a = p->values[input];
   return p->add_op(Op{OpKind::Relu, {input}, -1, {}, false, 0.0}, a.rows,
                    a.cols);
+}
+
+int32_t hexir_program_activation(hexir_program_t *p, const char *op,
+                                 int32_t input) {
+  if (!p)
+    return -1;
+  std::string name = op ? op : "";
+  if (name.rfind("hexir.", 0) == 0)
+    name = name.substr(6);
+  uint32_t kind = 0;
+  for (const ActivationName &a : kActivations)
+    if (name == a.name)
+      kind = a.kind;
+  if (!kind) {
+    p->error = "'" + name + "' is not an activation";
+    return -1;
+  }
+  if (!p->valid(input)) {
+    p->error = "hexir." + name + ": unknown operand";
+    return -1;
+  }
+  const Value &a = p->values[input];
+  Op o{OpKind::Activation, {input}, -1, {}, false, 0.0};
+  o.act = kind;
+  return p->add_op(o, a.rows, a.cols);
 }
 
 hexir_status_t hexir_program_print(hexir_program_t *p, int32_t value) {

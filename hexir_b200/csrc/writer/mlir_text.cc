@@ -8,14 +8,19 @@
 //     %n = hexir.linear %x, %w : (tensor<8x16xf64>, tensor<16x4xf64>) -> tensor<8x4xf64>
 //     %s = hexir.add %m, %b : tensor<2x2xf64>
 //     %r = hexir.relu %s : tensor<2x2xf64>
+//     %g = hexir.gelu %r : tensor<2x2xf64>
 //     hexir.print %r : tensor<2x2xf64>
 //     return
 //   }
 //
 // Binary ops accept `: T` or the functional form `(T1, T2) -> T3`, as the
 // reference parser does (compiler/Dialect/Hexir/IR/HexirDialect.cpp:238-264).
-// Any other hexir op is refused with the reference serializer's message
-// "cannot serialize this op into a host program" (ModuleSerializer.cpp:368).
+// The unary activations the dialect declares (leaky_relu, elu, sigmoid, tanh,
+// softmax, gelu, swish, mish; printed like relu, HexirDialect.cpp:377-390)
+// parse into the program; the writer serializes them only on request, else
+// it refuses them as the reference serializer does.  Any other hexir op is
+// refused here with that serializer's message "cannot serialize this op into
+// a host program" (ModuleSerializer.cpp:368).
 
 #include <cctype>
 #include <cstdio>
@@ -28,6 +33,16 @@
 #include "hexir_b200/hxb_writer.h"
 
 namespace {
+
+bool is_activation(const std::string &op) {
+  static const char *const names[] = {
+      "hexir.leaky_relu", "hexir.elu",     "hexir.sigmoid", "hexir.tanh",
+      "hexir.softmax",    "hexir.gelu",    "hexir.swish",   "hexir.mish"};
+  for (const char *n : names)
+    if (op == n)
+      return true;
+  return false;
+}
 
 struct Parser {
   const char *s;
@@ -245,6 +260,11 @@ struct Parser {
       if (!operand(&a) || !op_type(1, &rows, &cols))
         return false;
       id = hexir_program_relu(prog, a);
+    } else if (is_activation(op)) {
+      int32_t a;
+      if (!operand(&a) || !op_type(1, &rows, &cols))
+        return false;
+      id = hexir_program_activation(prog, op.c_str(), a);
     } else if (op.rfind("hexir.", 0) == 0) {
       return fail("'" + op + "': cannot serialize this op into a host program");
     } else {

@@ -17,7 +17,9 @@ from . import api
 SECTION_NAMES = {1: "SYMBOLS", 2: "PROGRAM", 3: "RODATA", 4: "EXECUTABLES",
                  5: "LAUNCH"}
 KERNEL_KINDS = {1: "matmul", 2: "add", 3: "relu", 4: "matmul_relu",
-                5: "matmul_add", 6: "matmul_add_relu"}
+                5: "matmul_add", 6: "matmul_add_relu", 7: "leaky_relu",
+                8: "elu", 9: "sigmoid", 10: "tanh", 11: "softmax", 12: "gelu",
+                13: "swish", 14: "mish"}
 COMMANDS = {0: "END", 1: "ALLOC", 2: "CONST", 3: "DISPATCH", 4: "PRINT"}
 
 

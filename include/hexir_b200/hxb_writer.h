@@ -58,6 +58,13 @@ int32_t hexir_program_linear(hexir_program_t *program, int32_t input,
                              int32_t weight);
 int32_t hexir_program_add(hexir_program_t *program, int32_t lhs, int32_t rhs);
 int32_t hexir_program_relu(hexir_program_t *program, int32_t input);
+/* One of the activations the dialect declares without lowering
+ * (include/hexir/Dialect/Hexir/IR/HexirOps.td:189-308): op is "leaky_relu",
+ * "elu", "sigmoid", "tanh", "softmax", "gelu", "swish" or "mish" (a "hexir."
+ * prefix is accepted).  Same shape as the input.  Serialized only with
+ * HEXIR_EMIT_ACTIVATIONS. */
+int32_t hexir_program_activation(hexir_program_t *program, const char *op,
+                                 int32_t input);
 hexir_status_t hexir_program_print(hexir_program_t *program, int32_t value);
 
 /* Do not fuse linear -> relu into one matmul_relu executable. */
@@ -65,6 +72,11 @@ hexir_status_t hexir_program_print(hexir_program_t *program, int32_t value);
 /* cuda-placed executables carry descriptors only (no image, no LAUNCH), as
  * the reference serializer does when it cannot compile device code. */
 #define HEXIR_EMIT_NO_IMAGE 0x2u
+/* Serialize the activations (kernel kinds 7-14 of hexir_runtime/program.h).
+ * Without it an activation fails the emit with the reference serializer's
+ * "cannot serialize this op into a host program", as the reference has no
+ * kernel for them. */
+#define HEXIR_EMIT_ACTIVATIONS 0x4u
 
 /* Serialize with a -placement= string ("hexir.linear=cuda,hexir.relu=cpu";
  * NULL or "" = all cpu).  Placement errors return INVALID_ARGUMENT with the

@@ -102,6 +102,28 @@ hexir_status_t hexir_cuda_add_f64(int ordinal, const double *a,
 hexir_status_t hexir_cuda_relu_f64(int ordinal, const double *x, double *y,
                                    size_t n, void *stream);
 
+/* Activation codes: the kernel kind numbers of hexir_runtime/program.h. */
+#define HEXIR_ACTIVATION_LEAKY_RELU 7u /* x > 0 ? x : 0.01 x */
+#define HEXIR_ACTIVATION_ELU 8u        /* x > 0 ? x : expm1(x) (alpha 1) */
+#define HEXIR_ACTIVATION_SIGMOID 9u    /* 1 / (1 + exp(-x)) */
+#define HEXIR_ACTIVATION_TANH 10u      /* tanh(x) */
+#define HEXIR_ACTIVATION_SOFTMAX 11u   /* exp(x - max) / sum, along each row */
+#define HEXIR_ACTIVATION_GELU 12u      /* 0.5 x erfc(-x / sqrt 2) */
+#define HEXIR_ACTIVATION_SWISH 13u     /* x / (1 + exp(-x)) */
+#define HEXIR_ACTIVATION_MISH 14u      /* x tanh(softplus(x)) */
+
+/* y = op(x) for a row-major [rows x cols] f64 tensor: softmax along each
+ * row, every other op elementwise over rows * cols.  No reference kernel
+ * exists: the reference declares these ops
+ * (include/hexir/Dialect/Hexir/IR/HexirOps.td:189-308) without lowering
+ * them.  The formulas above are its op descriptions; results agree with the
+ * host backend's (C library functions) to a few units in the last place,
+ * softmax to its row sum's rounding.  x and y may be the same buffer. */
+hexir_status_t hexir_cuda_activation_f64(int ordinal, uint32_t op,
+                                         const double *x, double *y,
+                                         uint64_t rows, uint32_t cols,
+                                         void *stream);
+
 /* Wait for `stream` and report any error a kernel of this library recorded
  * on the device since the last check (the error word is then cleared). */
 hexir_status_t hexir_cuda_synchronize(int ordinal, void *stream);

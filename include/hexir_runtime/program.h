@@ -14,6 +14,12 @@
  *   - kernel kinds 5 and 6, HEXIR_KERNEL_MATMUL_ADD(_RELU): a . b + d (then
  *     the relu), a linear whose only user is an add (whose only user is a
  *     relu) on the same device.  DISPATCH operands: a, b, d, destination.
+ *   - kernel kinds 7-14, the activations the reference dialect declares
+ *     without lowering (leaky_relu, elu, sigmoid, tanh, softmax, gelu, swish,
+ *     mish): y = op(x) over [m x n], softmax along each row.  DISPATCH
+ *     operands: x, destination.  Written only on request
+ *     (HEXIR_EMIT_ACTIVATIONS); by default the writer refuses these ops as
+ *     the reference serializer does.
  *   - the LAUNCH section (module.h kind 5), one hexir_launch_entry_t per
  *     executable, in executable order.
  */
@@ -48,6 +54,14 @@ typedef enum {
   HEXIR_KERNEL_MATMUL_RELU = 4, /* extension: c = relu(a . b) */
   HEXIR_KERNEL_MATMUL_ADD = 5,  /* extension: c = a . b + d */
   HEXIR_KERNEL_MATMUL_ADD_RELU = 6, /* extension: c = relu(a . b + d) */
+  HEXIR_KERNEL_LEAKY_RELU = 7,  /* extension: x > 0 ? x : 0.01 x */
+  HEXIR_KERNEL_ELU = 8,         /* extension: x > 0 ? x : expm1(x) */
+  HEXIR_KERNEL_SIGMOID = 9,     /* extension: 1 / (1 + exp(-x)) */
+  HEXIR_KERNEL_TANH = 10,       /* extension: tanh(x) */
+  HEXIR_KERNEL_SOFTMAX = 11,    /* extension: softmax along each row */
+  HEXIR_KERNEL_GELU = 12,       /* extension: 0.5 x erfc(-x / sqrt 2) */
+  HEXIR_KERNEL_SWISH = 13,      /* extension: x / (1 + exp(-x)) */
+  HEXIR_KERNEL_MISH = 14,       /* extension: x tanh(softplus(x)) */
 } hexir_kernel_kind_t;
 
 #define HEXIR_NAME_SIZE 32

@@ -13,11 +13,35 @@
  *   oracle_add_f64      <- hexir_ref_add_f64, lines 15-18: c = a + b.
  *   oracle_relu_f64     <- hexir_ref_relu_f64, lines 20-23: x > 0 ? x : 0.
  *
+ * and the activations the reference dialect declares but never lowers
+ * (include/hexir/Dialect/Hexir/IR/HexirOps.td:189-308), from their op
+ * descriptions, so parity for them is unpinned (no reference kernel, test or
+ * golden value exists):
+ *
+ *   oracle_activation_f64(kind, ...)   kind = program.h kernel kind 7-14
+ *     7  leaky_relu  "max(x, alpha * x)":          x > 0 ? x : 0.01 * x
+ *     8  elu         "x if x > 0, else alpha * (exp(x) - 1)":
+ *                                                  x > 0 ? x : 1.0 * expm1(x)
+ *     9  sigmoid     "1 / (1 + exp(-x))"
+ *     10 tanh        "tanh(x)"
+ *     11 softmax     "normalizes values along the last dimension so that they
+ *                    sum to 1": exp(x - rowmax) / sum, summed left to right
+ *     12 gelu        "x * 0.5 * (1 + erf(x / sqrt(2)))", as
+ *                    (0.5 * x) * erfc(-x * (1 / sqrt 2))
+ *     13 swish       "x * sigmoid(x)", as x / (1 + exp(-x))
+ *     14 mish        "x * tanh(softplus(x))", softplus(x) = x > 0 ?
+ *                    x + log1p(exp(-x)) : log1p(exp(x))
+ *
+ * The ops carry no alpha, so leaky_relu and elu use the fixed 0.01 and 1.0.
+ * The rewritten forms are equal in exact arithmetic and keep the relative
+ * accuracy the literal ones lose (1 + erf(x) for negative x, log(1 + e^x)).
+ *
  * The matmul may split ROWS over threads; every element keeps the reference's
  * sequential p order, so the result is bit-identical to the single-threaded
  * reference (pinned by tests/test_oracle.py against the reference library
  * built from its sources, oracle/_ref, and against tests/golden fixtures).
  */
+#include <math.h>
 #include <pthread.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -90,4 +114,61 @@ void oracle_add_f64(const double *a, const double *b, double *c, size_t n) {
 void oracle_relu_f64(const double *x, double *y, size_t n) {
   for (size_t i = 0; i < n; ++i)
     y[i] = x[i] > 0.0 ? x[i] : 0.0;
+}
+
+static double oracle_softplus(double x) {
+  return x > 0.0 ? x + log1p(exp(-x)) : log1p(exp(x));
+}
+
+/* Returns 0, or -1 for a kind that is not an activation. */
+int oracle_activation_f64(uint32_t kind, const double *x, double *y,
+                          uint64_t rows, uint64_t cols) {
+  const uint64_t n = rows * cols;
+  switch (kind) {
+  case 7:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = x[i] > 0.0 ? x[i] : 0.01 * x[i];
+    return 0;
+  case 8:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = x[i] > 0.0 ? x[i] : 1.0 * expm1(x[i]);
+    return 0;
+  case 9:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = 1.0 / (1.0 + exp(-x[i]));
+    return 0;
+  case 10:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = tanh(x[i]);
+    return 0;
+  case 11:
+    for (uint64_t r = 0; r < rows; ++r) {
+      const double *xr = x + r * cols;
+      double *yr = y + r * cols;
+      double m = -HUGE_VAL, s = 0.0;
+      for (uint64_t j = 0; j < cols; ++j)
+        if (xr[j] > m)
+          m = xr[j];
+      for (uint64_t j = 0; j < cols; ++j) {
+        yr[j] = exp(xr[j] - m);
+        s += yr[j];
+      }
+      for (uint64_t j = 0; j < cols; ++j)
+        yr[j] /= s;
+    }
+    return 0;
+  case 12:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = (0.5 * x[i]) * erfc(-x[i] * 0.70710678118654752440);
+    return 0;
+  case 13:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = x[i] / (1.0 + exp(-x[i]));
+    return 0;
+  case 14:
+    for (uint64_t i = 0; i < n; ++i)
+      y[i] = x[i] * tanh(oracle_softplus(x[i]));
+    return 0;
+  }
+  return -1;
 }

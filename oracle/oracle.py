@@ -47,6 +47,9 @@ def _load_oracle():
         for f in ("oracle_matmul_f64", "oracle_matmul_rows_f64",
                   "oracle_add_f64", "oracle_relu_f64"):
             getattr(lib, f).restype = None
+        lib.oracle_activation_f64.argtypes = [C.c_uint32, _dp, _dp, C.c_uint64,
+                                              C.c_uint64]
+        lib.oracle_activation_f64.restype = C.c_int
         _oracle = lib
     return _oracle
 
@@ -113,6 +116,33 @@ def add(a, b) -> np.ndarray:
     c = np.empty_like(a)
     _load_oracle().oracle_add_f64(_p(a), _p(b), _p(c), a.size)
     return c
+
+
+ACTIVATION_KINDS = {"leaky_relu": 7, "elu": 8, "sigmoid": 9, "tanh": 10,
+                    "softmax": 11, "gelu": 12, "swish": 13, "mish": 14}
+
+
+def activation(op: str, x) -> np.ndarray:
+    """op(x) for a rank-2 x (softmax along each row), by the op descriptions
+    of HexirOps.td:189-308 as restated in hexir_oracle.c."""
+    x = _f64(x)
+    assert x.ndim == 2
+    y = np.empty_like(x)
+    rc = _load_oracle().oracle_activation_f64(ACTIVATION_KINDS[op], _p(x), _p(y),
+                                              x.shape[0], x.shape[1])
+    assert rc == 0
+    return y
+
+
+def ulp_error_ok(got, want, ulps: float, floor: float = 2.0 ** -1000) -> np.ndarray:
+    """Elementwise: |got - want| <= ulps * 2^-52 * |want| + floor, NaN exactly
+    where want is NaN, equal infinities where want is infinite."""
+    got, want = np.asarray(got), np.asarray(want)
+    nan = np.isnan(want)
+    inf = np.isinf(want)
+    with np.errstate(invalid="ignore", over="ignore"):
+        close = np.abs(got - want) <= ulps * 2.0 ** -52 * np.abs(want) + floor
+    return np.where(nan, np.isnan(got), np.where(inf, got == want, close))
 
 
 def ref_matmul(a, b) -> np.ndarray:

@@ -114,6 +114,9 @@ def test_no_cpu_fallback_without_a_gpu():
     assert lib.hexir_cuda_relu_f64(0, None, None, 16, None) == _ffi.ERROR_DEVICE
     assert lib.hexir_cuda_matmul_add_f64(0, None, None, None, None, 4, 4, 4, 0,
                                          None) == _ffi.ERROR_DEVICE
+    for code in _ffi.ACTIVATIONS.values():
+        assert lib.hexir_cuda_activation_f64(0, code, None, None, 4, 4,
+                                             None) == _ffi.ERROR_DEVICE
 
 
 def test_comm_arguments_are_checked_without_a_gpu():

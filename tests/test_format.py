@@ -190,14 +190,65 @@ def test_text_functional_type_and_splat():
 
 
 def test_text_unlowered_op_is_refused_like_the_reference():
+    """The reference serializer refuses hexir.sigmoid (runtime/test/
+    hxb-errors.mlir:6-10); so does the writer unless activations are asked
+    for."""
     text = """func.func @main() {
       %a = hexir.constant dense<[[3.0, 1.0], [2.0, 2.0]]> : tensor<2x2xf64>
       %s = hexir.sigmoid %a : tensor<2x2xf64>
       hexir.print %s : tensor<2x2xf64>
       return
     }"""
+    prog = hx.parse(text)
     with pytest.raises(ValueError, match="cannot serialize this op into a host program"):
-        hx.parse(text)
+        prog.emit()
+    with pytest.raises(ValueError, match="'hexir.sigmoid' is not a placeable op"):
+        prog.emit("hexir.sigmoid=cuda", _ffi.EMIT_NO_FUSE)
+    exe = hx.read_executables(prog.emit(flags=_ffi.EMIT_ACTIVATIONS))
+    assert [(e.name, e.kind, e.m, e.n, e.k) for e in exe] == [("sigmoid_0", 9, 2, 2, 0)]
+    # Ops the dialect does not declare stay refused at parse time.
+    with pytest.raises(ValueError, match="cannot serialize this op into a host program"):
+        hx.parse(text.replace("hexir.sigmoid", "hexir.softplus"))
+
+
+@pytest.mark.parametrize("op,kind", sorted(_ffi.ACTIVATIONS.items()))
+def test_activation_executables(op, kind):
+    """Each activation: parsed from text and built through the API, named
+    <op>_<n> in walk order, placeable on cpu or cuda, never fused into the
+    linear that feeds it."""
+    text = f"""func.func @main() {{
+      %x = hexir.constant dense<1.5> : tensor<3x4xf64>
+      %w = hexir.constant dense<0.5> : tensor<4x5xf64>
+      %m = hexir.linear %x, %w : (tensor<3x4xf64>, tensor<4x5xf64>) -> tensor<3x5xf64>
+      %a = hexir.{op} %m : tensor<3x5xf64>
+      hexir.print %a : tensor<3x5xf64>
+      return
+    }}"""
+    for placement, device in (("", 0), (f"hexir.linear=cuda,hexir.{op}=cuda", 1)):
+        blob = hx.parse(text).emit(placement, _ffi.EMIT_ACTIVATIONS)
+        exes = hx.read_executables(blob)
+        assert [(e.name, e.kind, e.device) for e in exes] == [
+            ("linear_0", 1, device), (f"{op}_1", kind, device)]
+        assert (exes[1].m, exes[1].n, exes[1].k) == (3, 5, 0)
+        assert [c[0] for c in hx.read_program(blob)].count(3) == 2
+    p = hx.Program()
+    x = p.constant(np.ones((2, 3)))
+    y = p.activation(op, x)
+    p.print(y)
+    exes = hx.read_executables(p.emit(f"hexir.{op}=cuda:0-1", _ffi.EMIT_ACTIVATIONS))
+    assert [(e.name, e.kind, e.device) for e in exes] == [(f"{op}_0", kind, 1)]
+    launch = hx.read_launch(p.emit(f"hexir.{op}=cuda:0-1", _ffi.EMIT_ACTIVATIONS))
+    assert (launch[0].device_first, launch[0].device_count) == (0, 2)
+
+
+def test_activation_api_errors():
+    p = hx.Program()
+    x = p.constant(np.ones((2, 3)))
+    with pytest.raises(Exception, match="not an activation"):
+        p.activation("softplus", x)
+    with pytest.raises(Exception, match="unknown operand"):
+        p.activation("gelu", 99)
+    assert p.activation("hexir.gelu", x) >= 0
 
 
 def test_shape_mismatch_is_refused():

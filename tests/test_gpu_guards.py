@@ -115,3 +115,17 @@ def test_elementwise_write_only_their_output(gpu, count):
     hx.cuda_add(0, x.ptr, y.ptr, out2, count, gpu.stream)
     hx.cuda_synchronize(0, gpu.stream)
     check(buf2, count, shift=8)
+
+
+@pytest.mark.parametrize("op", sorted(_ffi.ACTIVATIONS))
+@pytest.mark.parametrize("rows,cols,shift", [
+    (1, 1, 0), (3, 7, 8), (33, 1025, 0), (9, 8193, 8), (5, 16385, 0),
+    (2, 40001, 8)])
+def test_activations_write_only_their_output(gpu, op, rows, cols, shift):
+    """Each activation kernel (and every softmax launch shape) on ragged
+    rows and columns, aligned and 8 bytes off."""
+    x = gpu.upload(np.random.default_rng(rows + cols).normal(size=rows * cols + 1))
+    buf, out = guarded(gpu, rows * cols, shift=shift)
+    hx.cuda_activation(0, op, x.ptr + shift, out, rows, cols, gpu.stream)
+    hx.cuda_synchronize(0, gpu.stream)
+    check(buf, rows * cols, shift=shift)

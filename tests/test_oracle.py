@@ -104,3 +104,72 @@ def test_normwise_error_definition():
     got = want + np.array([[0.0, 4e-12], [0.0, 0.0]])
     assert oracle.normwise_error(got, want) == pytest.approx(1e-12)
     assert oracle.normwise_error(np.zeros(3), np.zeros(3)) == 0.0
+
+
+# ---- activations: the oracle against the op descriptions ------------------
+#
+# No reference kernel, test or golden value exists for the activations
+# (HexirOps.td:189-308 declares them without a lowering), so the oracle is
+# checked against the descriptions themselves, evaluated independently with
+# numpy / scipy where the literal formula is well conditioned.
+
+def _activation_inputs():
+    rng = np.random.default_rng(11)
+    x = np.concatenate([np.linspace(-8, 8, 401), rng.normal(0, 3, 599)])
+    return x.reshape(10, 100)
+
+
+def test_oracle_activations_follow_the_op_descriptions():
+    import scipy.special as sp
+    x = _activation_inputs()
+    lit = {
+        "leaky_relu": np.maximum(x, 0.01 * x),
+        "elu": np.where(x > 0, x, 1.0 * (np.exp(x) - 1)),
+        "sigmoid": 1 / (1 + np.exp(-x)),
+        "tanh": np.tanh(x),
+        "softmax": sp.softmax(x, axis=1),
+        "gelu": x * 0.5 * (1 + sp.erf(x / np.sqrt(2))),
+        "swish": x * sp.expit(x),
+        "mish": x * np.tanh(np.log1p(np.exp(x))),
+    }
+    for op, want in lit.items():
+        got = oracle.activation(op, x)
+        if op == "leaky_relu":
+            assert np.array_equal(got, want)
+            continue
+        # The literal forms lose relative accuracy where they cancel
+        # (exp(x) - 1 near 0, 1 + erf for x < 0): compare those against the
+        # result's scale instead.
+        scale = np.maximum(np.abs(want), 1.0 if op in ("elu", "gelu") else 0)
+        err = np.abs(got - want) / np.where(scale > 0, scale, 1)
+        assert err.max() < 1e-13, op
+
+
+def test_oracle_activation_stable_forms_keep_relative_accuracy():
+    """Where the literal forms cancel, the oracle's rewritten forms stay
+    accurate: gelu's left tail against x/2 erfc(-x/sqrt 2) evaluated with
+    scipy's erfc, and mish at large |x|."""
+    import scipy.special as sp
+    x = np.linspace(-30, -5, 251).reshape(1, -1)
+    # The same rounded argument: erfc's condition number 2 z^2 would turn a
+    # last-place difference in z into ~1e-13 at x = -30.
+    want = 0.5 * x * sp.erfc(-x * 0.70710678118654752440)
+    got = oracle.activation("gelu", x)
+    assert np.all(np.abs(got - want) <= 1e-13 * np.abs(want))
+    assert oracle.activation("mish", np.array([[800.0]]))[0, 0] == 800.0
+    assert oracle.activation("sigmoid", np.array([[-800.0, 800.0]])).tolist() == [[0.0, 1.0]]
+
+
+def test_oracle_softmax_rows_sum_to_one_and_specials():
+    x = _activation_inputs()
+    y = oracle.activation("softmax", x)
+    assert np.all(np.abs(y.sum(axis=1) - 1) < 1e-14)
+    # A NaN, +inf, or an all -inf row turns that row to NaN; other rows keep
+    # their values.
+    z = x.copy()
+    z[1, 5] = np.nan
+    z[2, 7] = np.inf
+    z[3, :] = -np.inf
+    w = oracle.activation("softmax", z)
+    assert np.all(np.isnan(w[1:4]))
+    assert np.array_equal(w[0], y[0]) and np.array_equal(w[4:], y[4:])

@@ -154,6 +154,60 @@ def test_mlp_chain_on_cpu_matches_oracle():
     assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
 
 
+def activation_input(rows=37, cols=53, seed=21):
+    """Normal values at scale 4 plus the special ones: signed zeros,
+    infinities, NaN, huge magnitudes and the exp overflow edges."""
+    x = np.random.default_rng(seed).normal(0, 4, (rows, cols))
+    specials = [0.0, -0.0, np.inf, -np.inf, np.nan, 1e300, -1e300, 709.8,
+                -709.8, 745.2, -745.2, 5e-324, -5e-324, 40.0, -40.0]
+    x[0, :len(specials)] = specials
+    return x
+
+
+@pytest.mark.parametrize("op", sorted(_ffi.ACTIVATIONS))
+def test_activations_on_cpu_match_oracle_bit_for_bit(op):
+    """cpu-placed activations run the host backend: the oracle's formulas
+    with the same C library, so the bits agree (softmax rows included, a
+    row of specials among them)."""
+    x = activation_input()
+    p = hx.Program()
+    p.activation(op, p.constant(x))
+    out = hx.execute(hx.Module(p.emit(flags=_ffi.EMIT_ACTIVATIONS)),
+                     hx.Device("cpu"), out_shape=x.shape)
+    want = oracle.activation(op, x)
+    assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
+
+
+def test_activation_chain_through_hexir_run(tmp_path):
+    """linear -> gelu -> softmax written by hexir-mkhxb --activations and
+    printed by hexir-run on the CPU; without the flag the writer refuses."""
+    src = tmp_path / "act.mlir"
+    src.write_text("""func.func @main() {
+  %a = hexir.constant dense<[[3.0, -1.0], [2.0, 2.0]]> : tensor<2x2xf64>
+  %b = hexir.constant dense<[[1.0, 5.0], [5.0, -2.0]]> : tensor<2x2xf64>
+  %m = hexir.linear %a, %b : tensor<2x2xf64>
+  %g = hexir.gelu %m : tensor<2x2xf64>
+  %s = hexir.softmax %g : tensor<2x2xf64>
+  hexir.print %s : tensor<2x2xf64>
+  return
+}
+""")
+    out = tmp_path / "act.hxb"
+    res = subprocess.run([MK, "-o", str(out), str(src)], capture_output=True,
+                         text=True)
+    assert res.returncode == 1
+    assert "cannot serialize this op into a host program" in res.stderr
+    subprocess.run([MK, "--activations", "-o", str(out), str(src)], check=True)
+    m = oracle.matmul(np.array([[3.0, -1.0], [2.0, 2.0]]),
+                      np.array([[1.0, 5.0], [5.0, -2.0]]))
+    want = oracle.activation("softmax", oracle.activation("gelu", m))
+    text = "".join("".join(f"{v:f} " for v in row) + "\n" for row in want)
+    assert run("--quiet", str(out), check=True).stdout == text
+    exes = hx.read_executables(out.read_bytes())
+    assert [(e.name, e.kind) for e in exes] == [
+        ("linear_0", 1), ("gelu_1", 12), ("softmax_2", 11)]
+
+
 def test_execute_devices_with_no_gpu_runs_cpu_programs():
     p = known_program(GOLDEN["known_answers"][1])
     out = hx.execute(hx.Module(p.emit()), [], out_shape=(2, 2))
