@@ -66,15 +66,21 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-relu", action="store_true")
-    p.add_argument("--profile", choices=["relu", "skinny", "linear"],
+    p.add_argument("--profile", choices=["relu", "skinny", "linear",
+                                         "activation"],
                    help="run only one kernel a few times (the small cases the "
                         "committed ncu summaries capture)")
+    p.add_argument("--op", default="gelu",
+                   help="--profile activation: which activation")
+    p.add_argument("--cols", type=int, default=8192,
+                   help="--profile activation: row length (2^log2n elements)")
     p.add_argument("--log2n", type=int, default=26,
                    help="--profile relu: 2^log2n elements")
     p.add_argument("--suite", action="store_true",
                    help="instead of the bench line, one JSON line per "
                         "configuration: GEMM sweep 1024-8192, relu 2^28, "
-                        "skinny linear M=1/16/128, 3-layer MLP chain")
+                        "the activations over 2^28, skinny linear "
+                        "M=1/16/128, 3-layer MLP chain")
     return p.parse_args()
 
 
@@ -606,6 +612,40 @@ def relu_stream(ordinal: int, log2n: int = 28) -> dict:
             "kernel": "hexir_relu_f64", "checked": ok}
 
 
+def activation_stream(ordinal: int, op: str, rows: int = 16384,
+                      cols: int = 16384) -> dict:
+    """One activation over a rows x cols f64 tensor ~ N(0,1) (seed 4; 2^28
+    elements, in + out 4 GiB, past L2 every launch): HBM GB/s at 16 B per
+    element, sampled rows checked against the oracle."""
+    import numpy as np
+    import torch
+    import hexir_b200 as hx
+    from oracle import oracle
+    n = rows * cols
+    x = torch.from_numpy(hx.Rng(4).normal(n)).cuda()
+    y = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = timed_ms(lambda: hx.cuda_activation(ordinal, op, x.data_ptr(),
+                                             y.data_ptr(), rows, cols, stream),
+                  steps=20)
+    hx.cuda_synchronize(ordinal, stream)
+    pick = [0, rows // 3, rows - 1]
+    xs = x.view(rows, cols)[pick].cpu().numpy()
+    ys = y.view(rows, cols)[pick].cpu().numpy()
+    ulps = {"leaky_relu": 0, "gelu": 32, "softmax": cols + 16}.get(op, 16)
+    want = oracle.activation(op, xs)
+    ok = bool(np.array_equal(ys, want) if ulps == 0 else
+              oracle.ulp_error_ok(ys, want, ulps).all())
+    gbs = 16.0 * n / (ms * 1e-3) / 1e9
+    peak, src = hbm_peak_gbs()
+    return {"op": op, "value": round(gbs, 1), "unit": "GB/s", "rows": rows,
+            "cols": cols, "bytes_per_launch": 16 * n,
+            "ms_per_launch": round(ms, 4), "frac": round(gbs / peak, 4),
+            "peak_gbs": peak, "peak_source": src,
+            "checked_rows": len(pick), "within_tolerance_ulps": ulps,
+            "checked": ok}
+
+
 def run_suite(args):
     """One JSON line per configuration of the benchmark plan (1 GPU)."""
     import numpy as np
@@ -675,6 +715,11 @@ def run_suite(args):
 
     # relu stream.
     out.append({"suite": "relu_2^28", **relu_stream(ordinal)})
+
+    # The activations, each over 16384 x 16384 (softmax along the rows).
+    for op in sorted(_ffi.ACTIVATIONS):
+        out.append({"suite": "activation_2^28", **activation_stream(ordinal, op)})
+        torch.cuda.empty_cache()
 
     # Skinny linear: weight-read bandwidth.
     r = hx.Rng(5)
@@ -832,6 +877,14 @@ def run_profile(args):
         y = torch.empty_like(x)
         run = lambda: hx.cuda_relu(0, x.data_ptr(), y.data_ptr(), n, stream)
         what = f"relu 2^{args.log2n} f64"
+    elif args.profile == "activation":
+        n = 1 << args.log2n
+        rows = n // args.cols
+        x = torch.from_numpy(hx.Rng(4).normal(n)).cuda()
+        y = torch.empty_like(x)
+        run = lambda: hx.cuda_activation(0, args.op, x.data_ptr(), y.data_ptr(),
+                                         rows, args.cols, stream)
+        what = f"{args.op} {rows}x{args.cols} f64"
     else:
         m = args.m
         r = hx.Rng(5 if args.profile == "skinny" else 1)

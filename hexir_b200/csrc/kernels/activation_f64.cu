@@ -10,14 +10,20 @@
 //                                            without the cancellation of 1 + erf
 //                                            for negative x)
 //   swish       x / (1 + exp(-x))           (= x sigmoid(x), one rounding)
-//   mish        x tanh(softplus(x)),        softplus(x) = x > 0 ? x + log1p(exp(-x))
-//                                                               : log1p(exp(x))
+//   mish        x tanh(softplus(x)), evaluated with one exp and one divide:
+//               tanh(log(1 + e^x)) = ((1 + e^x)^2 - 1) / ((1 + e^x)^2 + 1), so
+//               with u = e^x for x <= 0:   q = u (u + 2) / (u (u + 2) + 2)
+//               and  u = e^-x for x > 0:   q = (1 + 2u) / (1 + 2u + 2u^2)
+//               (every term positive, nothing overflows), mish = x q.  Within
+//               4 ulp of the exact value, as the exp / log1p / tanh chain is
+//               within 3; the chain costs about six times as much here.
 //
 // The reference declares these ops but lowers none of them; the formulas
 // above are its op descriptions written in forms that keep their relative
 // accuracy over the whole f64 range.  The host backend (cpu_kernels.cc)
-// evaluates the same formulas with the C library's functions, so the two
-// agree to the functions' last-place differences.  Every add, multiply and
+// evaluates them with the C library's functions (mish as the literal
+// x tanh(softplus(x)), softmax dividing by the sum), so the two agree to a
+// few units in the last place.  Every add, multiply and
 // divide here is an explicit round-to-nearest intrinsic so that no fused
 // multiply-add is formed across the inlined math functions.
 //
@@ -25,7 +31,11 @@
 // stores, four vectors in flight per thread).  Softmax keeps each row in
 // registers: a warp per row up to 1024 columns, one 256- or 512-thread block
 // per row up to 8192 / 16384 columns (one read and one write of the row), and
-// a three-pass block per row beyond that.
+// a three-pass block per row beyond that; it scales by one correctly rounded
+// reciprocal of the row sum instead of dividing every element.
+//
+// FP64 arithmetic, not HBM, bounds the transcendental ones on B200 (gelu's
+// erfc, tanh, softmax's exp): each element costs tens of FP64 instructions.
 
 namespace {
 
@@ -64,12 +74,15 @@ struct SwishOp {
     return __ddiv_rn(x, __dadd_rn(1.0, exp(-x)));
   }
 };
-__device__ __forceinline__ double softplus(double x) {
-  return x > 0.0 ? __dadd_rn(x, log1p(exp(-x))) : log1p(exp(x));
-}
 struct MishOp {
   __device__ __forceinline__ double operator()(double x, double) const {
-    return __dmul_rn(x, tanh(softplus(x)));
+    const bool neg = x <= 0.0;
+    const double u = exp(neg ? x : -x);
+    const double num = neg ? __dmul_rn(u, __dadd_rn(u, 2.0))
+                           : __dadd_rn(1.0, __dmul_rn(2.0, u));
+    const double den =
+        __dadd_rn(num, neg ? 2.0 : __dmul_rn(__dmul_rn(2.0, u), u));
+    return __dmul_rn(x, __ddiv_rn(num, den));
   }
 };
 
@@ -149,12 +162,12 @@ __device__ __forceinline__ void softmax_rows_block(
         s = __dadd_rn(s, v[i]);
       }
     }
-    s = block_reduce<THREADS>(s, red, SumOp{});
+    const double rs = __drcp_rn(block_reduce<THREADS>(s, red, SumOp{}));
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const uint32_t j = threadIdx.x + i * THREADS;
       if (j < cols)
-        __stcs(yr + j, __ddiv_rn(v[i], s));
+        __stcs(yr + j, __dmul_rn(v[i], rs));
     }
   }
 }
@@ -189,12 +202,12 @@ __device__ __forceinline__ void softmax_rows_warp(
         s = __dadd_rn(s, v[i]);
       }
     }
-    s = warp_reduce(s, SumOp{});
+    const double rs = __drcp_rn(warp_reduce(s, SumOp{}));
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const uint32_t j = lane + i * 32;
       if (j < cols)
-        __stcs(yr + j, __ddiv_rn(v[i], s));
+        __stcs(yr + j, __dmul_rn(v[i], rs));
     }
   }
 }
@@ -218,9 +231,9 @@ __device__ __forceinline__ void softmax_rows_wide(
     double s = 0.0;
     for (uint32_t j = threadIdx.x; j < cols; j += THREADS)
       s = __dadd_rn(s, exp(__dsub_rn(xr[j], m)));
-    s = block_reduce<THREADS>(s, red, SumOp{});
+    const double rs = __drcp_rn(block_reduce<THREADS>(s, red, SumOp{}));
     for (uint32_t j = threadIdx.x; j < cols; j += THREADS)
-      __stcs(yr + j, __ddiv_rn(exp(__dsub_rn(__ldcs(xr + j), m)), s));
+      __stcs(yr + j, __dmul_rn(exp(__dsub_rn(__ldcs(xr + j), m)), rs));
   }
 }
 
