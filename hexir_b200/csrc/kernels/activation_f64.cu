@@ -212,6 +212,77 @@ __device__ __forceinline__ void softmax_rows_warp(
   }
 }
 
+// Persistent blocks (rows blockIdx.x, + gridDim.x, ...), PER elements per
+// thread in registers, and one row-sized shared buffer that the bulk-copy
+// engine fills with the block's next row while the current one computes:
+//   wait for row r in smem -> registers, maximum (block reduction; after it
+//   no thread reads the buffer) -> one thread starts the copy of the next
+//   row -> exp, sum, reciprocal, scaled stores of row r.
+// The host runs it only for an even row length and a 16-byte aligned x, so
+// every row starts 16-byte aligned and is a multiple of 16 bytes long.  A
+// wait that runs out (timeout_ns) sets the error word and the whole block
+// returns; the only copy in flight is the one that did not arrive.
+template <int THREADS, int PER>
+__device__ __forceinline__ void softmax_rows_bulk(
+    const hexir_activation_args_t &p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ double red[THREADS / 32];
+  __shared__ __align__(8) uint64_t bar;
+  double *buf = reinterpret_cast<double *>(smem_raw);
+  const uint32_t cols = p.cols;
+  const uint32_t bytes = cols * 8u;
+  uint64_t row = blockIdx.x;
+  if (row >= p.rows)
+    return;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_load(buf, p.x + row * cols, bytes, &bar);
+  }
+  uint32_t phase = 0;
+  for (; row < p.rows; row += gridDim.x) {
+    const bool arrived = mbar_wait_bounded(&bar, phase, p.timeout_ns);
+    if (!__syncthreads_and(arrived))
+      return;
+    phase ^= 1u;
+    double *yr = p.out + row * cols;
+    double v[PER];
+    double m = neg_inf();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      v[i] = j < cols ? buf[j] : neg_inf();
+      m = v[i] > m ? v[i] : m;
+    }
+    m = block_reduce<THREADS>(m, red, MaxOp{});
+    const uint64_t next = row + gridDim.x;
+    if (threadIdx.x == 0 && next < p.rows) {
+      mbar_arrive_expect_tx(&bar, bytes);
+      bulk_load(buf, p.x + next * cols, bytes, &bar);
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      if (j < cols) {
+        v[i] = exp(__dsub_rn(v[i], m));
+        s = __dadd_rn(s, v[i]);
+      }
+    }
+    const double rs = __drcp_rn(block_reduce<THREADS>(s, red, SumOp{}));
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      if (j < cols)
+        __stcs(yr + j, __dmul_rn(v[i], rs));
+    }
+  }
+}
+
 // Rows too long for registers: maximum, sum and output each read the row
 // (the second and third reads mostly from L2).
 template <int THREADS>
@@ -274,4 +345,14 @@ extern "C" __global__ void __launch_bounds__(512, 1)
 extern "C" __global__ void __launch_bounds__(512)
     hexir_softmax_wide_f64(const hexir_activation_args_t args) {
   softmax_rows_wide<512>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(256, 2)
+    hexir_softmax_bulk256_f64(const hexir_activation_args_t args) {
+  softmax_rows_bulk<256, HEXIR_SOFTMAX_B256_COLS / 256>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(512, 1)
+    hexir_softmax_bulk512_f64(const hexir_activation_args_t args) {
+  softmax_rows_bulk<512, HEXIR_SOFTMAX_B512_COLS / 512>(args);
 }

@@ -92,6 +92,18 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
       : "memory");
 }
 
+// 1-D bulk copy of `bytes` from global to this CTA's shared memory,
+// completing on `bar`.  Both addresses 16-byte aligned, bytes a multiple of
+// 16 (the caller checks).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src,
+                                          uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(map))

@@ -127,7 +127,10 @@ typedef struct {
 /* Softmax launch shapes: a warp per row up to 32 x 32 columns, a 256-thread
  * block per row up to 256 x 32, a 512-thread block per row up to 512 x 32
  * (each thread holding up to 32 elements in registers), and above that a
- * 512-thread block per row that reads the row three times. */
+ * 512-thread block per row that reads the row three times.  Rows of an even
+ * length starting 16-byte aligned, above the warp shape, run the persistent
+ * "bulk" blocks instead: the next row is copied into shared memory
+ * (cp.async.bulk) while the current one computes. */
 #define HEXIR_SOFTMAX_WARP_COLS 1024u
 #define HEXIR_SOFTMAX_B256_COLS 8192u
 #define HEXIR_SOFTMAX_B512_COLS 16384u
@@ -139,6 +142,7 @@ typedef struct {
   uint64_t rows;  /* softmax rows */
   uint32_t cols;  /* softmax row length */
   uint32_t op;    /* HEXIR_ACT_* */
+  uint64_t timeout_ns; /* bound on every wait (the bulk softmax) */
 } hexir_activation_args_t;
 
 #ifdef __cplusplus

@@ -242,6 +242,8 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
         {&lib->softmax_b256, "hexir_softmax_b256_f64"},
         {&lib->softmax_b512, "hexir_softmax_b512_f64"},
         {&lib->softmax_wide, "hexir_softmax_wide_f64"},
+        {&lib->softmax_bulk256, "hexir_softmax_bulk256_f64"},
+        {&lib->softmax_bulk512, "hexir_softmax_bulk512_f64"},
     };
     bool all = true;
     for (const Opt &o : acts)
@@ -274,6 +276,15 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
     r = d.FuncSetAttribute(lib->linear_tma_sk,
                            CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
                            HEXIR_LINEAR_SMEM_BYTES);
+  // The bulk softmax blocks hold one row of up to 8192 / 16384 f64.
+  if (r == CUDA_SUCCESS && lib->softmax_bulk256)
+    r = d.FuncSetAttribute(lib->softmax_bulk256,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_SOFTMAX_B256_COLS * 8);
+  if (r == CUDA_SUCCESS && lib->softmax_bulk512)
+    r = d.FuncSetAttribute(lib->softmax_bulk512,
+                           CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                           HEXIR_SOFTMAX_B512_COLS * 8);
   if (r != CUDA_SUCCESS) {
     d.ModuleUnload(lib->module);
     fail(error, cuda_message("kernel library setup", r));
@@ -645,7 +656,7 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
   if (!lib->softmax_warp)
     return fail(error, "kernel library image lacks the activation kernels",
                 HEXIR_ERROR_UNIMPLEMENTED);
-  hexir_activation_args_t args{x, y, count, rows, cols, op};
+  hexir_activation_args_t args{x, y, count, rows, cols, op, kWaitTimeoutNs};
   void *params[] = {&args};
   if (op != HEXIR_ACT_SOFTMAX)
     return launch(lib->activation[op - 7], stream_grid(dev, count / 2), 1, 256,
@@ -658,6 +669,23 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
     return launch(lib->softmax_warp, static_cast<unsigned>(blocks), 1, 256, 0,
                   stream, params, "launch hexir_softmax_warp_f64", error);
   }
+  // Even rows from a 16-byte aligned x start 16-byte aligned: the persistent
+  // blocks that prefetch each next row with a bulk copy (two per SM for
+  // rows up to 8192, one above).
+  const bool bulk = cols % 2 == 0 && cols <= HEXIR_SOFTMAX_B512_COLS &&
+                    (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                    lib->softmax_bulk256 && lib->softmax_bulk512;
+  const uint64_t sms = static_cast<uint64_t>(std::max(dev->sm_count, 1));
+  if (bulk && cols <= HEXIR_SOFTMAX_B256_COLS)
+    return launch(lib->softmax_bulk256,
+                  static_cast<unsigned>(std::min<uint64_t>(rows, 2 * sms)), 1,
+                  256, cols * 8u, stream, params,
+                  "launch hexir_softmax_bulk256_f64", error);
+  if (bulk)
+    return launch(lib->softmax_bulk512,
+                  static_cast<unsigned>(std::min<uint64_t>(rows, sms)), 1, 512,
+                  cols * 8u, stream, params, "launch hexir_softmax_bulk512_f64",
+                  error);
   const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>(rows, cap));
   if (cols <= HEXIR_SOFTMAX_B256_COLS)
     return launch(lib->softmax_b256, blocks, 1, 256, 0, stream, params,

@@ -35,7 +35,8 @@ struct KernelLib {
   // empty), then the four softmax launch shapes.
   CUfunction activation[8] = {};
   CUfunction softmax_warp = nullptr, softmax_b256 = nullptr,
-             softmax_b512 = nullptr, softmax_wide = nullptr;
+             softmax_b512 = nullptr, softmax_wide = nullptr,
+             softmax_bulk256 = nullptr, softmax_bulk512 = nullptr;
   CUfunction dmma_probe = nullptr;
   CUfunction wait_probe = nullptr;
   CUdeviceptr error_word = 0;

@@ -93,10 +93,13 @@ def test_elementwise_activation_over_the_whole_range(gpu, op):
 
 @pytest.mark.parametrize("rows,cols", [
     (1, 1), (5, 2), (300, 31), (300, 33), (64, 1000), (64, 1024), (64, 1025),
-    (40, 4097), (17, 8192), (9, 8193), (9, 16384), (5, 16385), (3, 40000)])
+    (64, 1026), (1000, 2048), (40, 4097), (17, 8192), (700, 8192), (9, 8193),
+    (9, 16384), (300, 12000), (5, 16385), (3, 40000)])
 def test_softmax_matches_oracle(gpu, rows, cols):
-    """Every launch shape (warp per row, 256- and 512-thread blocks, the
-    three-pass block) at and around its column limit."""
+    """Every launch shape at and around its column limit: warp per row; the
+    persistent bulk-prefetch blocks for even rows (more rows than blocks, so
+    each block walks several); the 256- and 512-thread blocks for odd rows;
+    the three-pass block."""
     x = np.random.default_rng(rows * cols).normal(0, 3, (rows, cols))
     got = run_gpu(gpu, "softmax", x)
     want = oracle.activation("softmax", x)
@@ -215,3 +218,15 @@ def test_sharded_activation_across_gpus(gpu):
             d.close()
     assert np.array_equal(one.view(np.uint64), two.view(np.uint64))
     assert_close("softmax", one, oracle.activation("softmax", x))
+
+
+@pytest.mark.parametrize("rows,cols", [(40, 2048), (9, 16384)])
+def test_softmax_misaligned_rows_take_the_register_blocks(gpu, rows, cols):
+    """x 8 bytes off its 16-byte alignment: the bulk copy cannot start there,
+    so the per-row register blocks run; same results within the bar."""
+    x = np.random.default_rng(cols).normal(0, 3, (rows, cols))
+    aligned = run_gpu(gpu, "softmax", x)
+    shifted = run_gpu(gpu, "softmax", x, shift=8)
+    want = oracle.activation("softmax", x)
+    assert_close("softmax", aligned, want)
+    assert_close("softmax", shifted, want)

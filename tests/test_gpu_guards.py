@@ -120,7 +120,7 @@ def test_elementwise_write_only_their_output(gpu, count):
 @pytest.mark.parametrize("op", sorted(_ffi.ACTIVATIONS))
 @pytest.mark.parametrize("rows,cols,shift", [
     (1, 1, 0), (3, 7, 8), (33, 1025, 0), (9, 8193, 8), (5, 16385, 0),
-    (2, 40001, 8)])
+    (2, 40001, 8), (333, 2050, 0), (151, 16384, 0), (5, 4096, 8)])
 def test_activations_write_only_their_output(gpu, op, rows, cols, shift):
     """Each activation kernel (and every softmax launch shape) on ragged
     rows and columns, aligned and 8 bytes off."""
