@@ -12,7 +12,8 @@ this package is a thin Python face over it.
 from ._ffi import HexirError, lib  # noqa: F401
 from .api import (Buffer, Device, Module, Program, Rng, cuda_activation,  # noqa: F401
                   cuda_add, cuda_matmul, cuda_matmul_acc, cuda_matmul_add, cuda_relu,
-                  cuda_synchronize, device_count,
+                  cuda_synchronize, device_count, fault_calls,
+                  fault_configure,
                   execute, kernel_image, last_kernel_ms, launch_count,
                   matmul_plan, parse, read_executables, read_launch,
                   read_program,

@@ -140,6 +140,9 @@ _SIGNATURES = [
     ("hexir_comm_rank", _int, [_vp]),
     ("hexir_comm_size", _int, [_vp]),
     ("hexir_comm_direct_stores", _int, [_vp]),
+    # fault.h
+    ("hexir_fault_configure", _int, [C.c_char_p]),
+    ("hexir_fault_calls", _u64, [C.c_char_p]),
     ("hexir_sharded_linear_f64", _int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32,
                                         _u32, _vp]),
     # hexir_b200/hxb_writer.h

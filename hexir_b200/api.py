@@ -470,6 +470,17 @@ def matmul_plan(m: int, n: int, k: int, flags: int = 0, ordinal: int = 0,
     return v.value, s.value
 
 
+def fault_configure(spec: str = "") -> None:
+    """Host-side fault injection rules (hexir_fault_configure): e.g.
+    "alloc:3", "launch:1+", "alloc:2,nccl:1"; "" turns injection off."""
+    check(lib().hexir_fault_configure(spec.encode()), "hexir_fault_configure")
+
+
+def fault_calls(site: str) -> int:
+    """Calls counted at "alloc", "launch" or "nccl" since the rules were set."""
+    return lib().hexir_fault_calls(site.encode())
+
+
 def launch_count() -> int:
     return lib().hexir_cuda_launch_count()
 

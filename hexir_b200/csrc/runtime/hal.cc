@@ -16,6 +16,7 @@
 #include <mutex>
 
 #include "cuda_driver.h"
+#include "fault.h"
 #include "hal_internal.h"
 #include "kernel_lib.h"
 
@@ -36,6 +37,8 @@ struct CpuDevice : hexir_device_t {
   }
   hexir_status_t buffer_allocate(size_t size, hexir_memory_kind_t,
                                  hexir_buffer_t **out) override {
+    if (fault_hit(FaultSite::Alloc))
+      return HEXIR_ERROR_OUT_OF_MEMORY;
     auto *buffer = new (std::nothrow) hexir_buffer_t;
     if (!buffer)
       return HEXIR_ERROR_OUT_OF_MEMORY;
@@ -145,6 +148,10 @@ hexir_status_t CudaDevice::allocate_pooled(size_t size, hexir_buffer_t **out) {
 
 hexir_status_t CudaDevice::allocate_raw(size_t size, hexir_buffer_t **out) {
   const Driver &d = driver();
+  if (fault_hit(FaultSite::Alloc)) {
+    report("cuMemAlloc(" + std::to_string(size) + "): injected fault (HEXIR_FAULT)");
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  }
   auto *buffer = new (std::nothrow) hexir_buffer_t;
   if (!buffer)
     return HEXIR_ERROR_OUT_OF_MEMORY;
@@ -296,6 +303,10 @@ hexir_status_t CudaDevice::launch(const void *image, size_t image_size,
   for (unsigned i = 0; i < arg_count; ++i) {
     addresses[i] = reinterpret_cast<CUdeviceptr>(args[i]->impl);
     params[i] = &addresses[i];
+  }
+  if (fault_hit(FaultSite::Launch)) {
+    report(std::string("launch of '") + entry + "': injected fault (HEXIR_FAULT)");
+    return HEXIR_ERROR_DEVICE;
   }
   r = d.LaunchKernel(function, grid_x, grid_y, 1, block_x, block_y, 1, 0, stream,
                      params, nullptr);

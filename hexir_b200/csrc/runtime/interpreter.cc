@@ -37,6 +37,7 @@
 #include <vector>
 
 #include "cuda_driver.h"
+#include "fault.h"
 #include "hal_internal.h"
 #include "hexir_b200/comm.h"
 #include "hexir_b200/kernels.h"
@@ -438,7 +439,8 @@ struct Vm {
       fresh.device = dev->state;
       fresh.offset = offset;
       fresh.bytes = s.bytes;
-      if (d.MemAlloc(&fresh.ptr, s.bytes) != CUDA_SUCCESS) {
+      if (fault_hit(FaultSite::Alloc) ||
+          d.MemAlloc(&fresh.ptr, s.bytes) != CUDA_SUCCESS) {
         delete b;  // no room to keep it: upload per execute as usual
         return HEXIR_OK;
       }
@@ -523,6 +525,8 @@ struct Vm {
       *out = s.rodata;
       return HEXIR_OK;
     }
+    if (!s.host_valid && fault_hit(FaultSite::Alloc))
+      return HEXIR_ERROR_OUT_OF_MEMORY;
     if (s.rodata && !s.host_valid) {
       // A CONST at an offset that is not a multiple of 8 (the serializer
       // never writes one): the host kernels read an aligned copy.
@@ -554,7 +558,11 @@ struct Vm {
     s.dev_valid.clear();
     s.dev_valid.insert(o);
   }
+  // nullptr when the storage cannot be had (an injected fault; a real
+  // shortage throws std::bad_alloc, caught at the C ABI).
   double *written_on_host(Slot &s) {
+    if (fault_hit(FaultSite::Alloc))
+      return nullptr;
     drop_borrowed(s);
     s.host.resize((s.bytes + 7) / 8);
     s.zero = false;
@@ -704,6 +712,8 @@ struct Vm {
     const double *b = reinterpret_cast<const double *>(in[1]);
     const double *d = reinterpret_cast<const double *>(in[2]);
     double *c = written_on_host(dst);
+    if (!c)
+      return HEXIR_ERROR_OUT_OF_MEMORY;
     switch (exe.kind) {
     case HEXIR_KERNEL_MATMUL:
       cpu_matmul_f64(a, b, c, exe.m, exe.n, exe.k);
@@ -1167,6 +1177,10 @@ struct Vm {
           return st;
       if (!everywhere) {
         const size_t elemsw = static_cast<size_t>(exe.k) * exe.n;
+        if (fault_hit(FaultSite::Nccl)) {
+          report("ncclBroadcast (weight): injected fault (HEXIR_FAULT)");
+          return HEXIR_ERROR_DEVICE;
+        }
         nc.GroupStart();
         for (int r = 0; r < count; ++r)
           nc.Broadcast(reinterpret_cast<void *>(w[r]), reinterpret_cast<void *>(w[r]),
@@ -1291,6 +1305,10 @@ struct Vm {
       }
     }
     if (any_gather) {
+      if (fault_hit(FaultSite::Nccl)) {
+        report("ncclSend/ncclRecv (rows): injected fault (HEXIR_FAULT)");
+        return HEXIR_ERROR_DEVICE;
+      }
       nc.GroupStart();
       for (int r = 1; r < count; ++r) {
         if (!rows[r] || direct[r])

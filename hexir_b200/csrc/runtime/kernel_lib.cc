@@ -10,6 +10,7 @@
 
 #include "../kernels/launch_abi.h"
 #include "cuda_driver.h"
+#include "fault.h"
 #include "hexir_b200/kernels.h"
 
 extern "C" {
@@ -57,7 +58,8 @@ hexir_status_t ensure_workspace(DeviceState *dev, size_t bytes,
     dev->workspace = 0;
     dev->workspace_bytes = 0;
   }
-  CUresult r = d.MemAlloc(&dev->workspace, bytes);
+  CUresult r = fault_hit(FaultSite::Alloc) ? CUDA_ERROR_OUT_OF_MEMORY
+                                           : d.MemAlloc(&dev->workspace, bytes);
   if (r != CUDA_SUCCESS)
     return fail(error, cuda_message("cuMemAlloc(split-K workspace)", r),
                 HEXIR_ERROR_OUT_OF_MEMORY);
@@ -68,6 +70,8 @@ hexir_status_t ensure_workspace(DeviceState *dev, size_t bytes,
 hexir_status_t launch(CUfunction fn, unsigned gx, unsigned gy, unsigned bx,
                       unsigned smem, CUstream stream, void **params,
                       const char *what, std::string *error) {
+  if (fault_hit(FaultSite::Launch))
+    return fail(error, std::string(what) + ": injected fault (HEXIR_FAULT)");
   CUresult r =
       driver().LaunchKernel(fn, gx, gy, 1, bx, 1, 1, smem, stream, params, nullptr);
   if (r != CUDA_SUCCESS)
