@@ -18,8 +18,8 @@ It records
     reference's own hexir_ref_*_f64 kernels, stored as sha256 of the output
     bytes plus a few sampled values.
 
-The tests then need neither the reference tree nor the reference library:
-the GPU box has neither.
+The tests then need neither the reference tree nor the reference library,
+so they also run on machines that have neither.
 """
 
 import argparse
