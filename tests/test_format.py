@@ -310,6 +310,28 @@ def test_reference_runtime_runs_our_cpu_modules(tmp_path):
         assert res.stdout == case["stdout_quiet"]
 
 
+@pytest.mark.parametrize("op", sorted(_ffi.ACTIVATIONS))
+def test_reference_runtime_refuses_activation_kinds(tmp_path, op):
+    """Kinds 7-14 are additive: the reference runtime, which has no kernel
+    for them, refuses such a module ("unimplemented") instead of running
+    something else, while this runtime prints the oracle's values."""
+    if not oracle.have_reference():
+        pytest.skip("reference runtime not built here")
+    x = np.array([[1.0, -2.0], [0.5, 3.0]])
+    p = hx.Program()
+    p.print(p.activation(op, p.constant(x)))
+    path = tmp_path / f"{op}.hxb"
+    p.emit_file(str(path), "", _ffi.EMIT_ACTIVATIONS)
+    res = subprocess.run([oracle.REF_RUN, "--quiet", str(path)],
+                         capture_output=True, text=True)
+    assert res.returncode != 0 and "unimplemented" in res.stderr
+    ours = subprocess.run([bin_path("hexir-run"), "--quiet", str(path)],
+                          capture_output=True, text=True, check=True)
+    want = oracle.activation(op, x)
+    assert ours.stdout == "".join("".join(f"{v:f} " for v in row) + "\n"
+                                  for row in want)
+
+
 def test_linear_add_relu_fuses_at_the_add():
     """linear -> add -> relu on one GPU spec: one matmul_add_relu executable
     named after the linear (kind 6), dispatched where the add stands with
