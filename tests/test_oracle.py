@@ -173,3 +173,48 @@ def test_oracle_softmax_rows_sum_to_one_and_specials():
     w = oracle.activation("softmax", z)
     assert np.all(np.isnan(w[1:4]))
     assert np.array_equal(w[0], y[0]) and np.array_equal(w[4:], y[4:])
+
+
+def test_oracle_activations_within_a_few_ulp_of_exact():
+    """Against 200-bit values from mpmath of the op descriptions themselves:
+    every elementwise activation of the oracle is within 4 ulp, except gelu,
+    and softmax within (cols + 4) ulp (its row sum is a left-to-right f64
+    sum).  gelu evaluates erfc at the rounded argument z = fl(-x * (1/sqrt 2)),
+    whose error of up to 2 ulp erfc's condition number 2 z^2 multiplies: the
+    bound there is 4 + 4 z^2 ulp (about 3e-13 relative at the underflow edge,
+    x = -37), as in the GPU kernel, which rounds the same argument.  Results
+    below 2^-1000 are compared absolutely."""
+    mpmath = pytest.importorskip("mpmath")
+    mpmath.mp.prec = 200
+    rng = np.random.default_rng(17)
+    x = np.concatenate([rng.normal(0, 4, 300), rng.uniform(-40, 40, 200),
+                        np.ldexp(rng.uniform(1, 2, 100),
+                                 rng.integers(-60, 9, 100)) *
+                        rng.choice([-1, 1], 100)]).reshape(6, 100)
+    mp = mpmath.mpf
+    exact = {
+        "leaky_relu": lambda v: v if v > 0 else mp("0.01") * v,
+        "elu": lambda v: v if v > 0 else mpmath.expm1(v),
+        "sigmoid": lambda v: 1 / (1 + mpmath.exp(-v)),
+        "tanh": mpmath.tanh,
+        # 1 + erf(z) = erfc(-z) exactly; mpmath's erfc keeps the left tail
+        # that 1 + erf would cancel even at 200 bits.
+        "gelu": lambda v: v / 2 * mpmath.erfc(-v / mpmath.sqrt(2)),
+        "swish": lambda v: v / (1 + mpmath.exp(-v)),
+        "mish": lambda v: v * mpmath.tanh(mpmath.log1p(mpmath.exp(v))),
+    }
+    for op, f in exact.items():
+        got = oracle.activation(op, x)
+        want = np.array([[float(f(mp(float(v)))) for v in row] for row in x])
+        tiny = np.abs(want) < 2.0 ** -1000
+        ulp = np.abs(got - want) / np.spacing(np.abs(want))
+        bound = 4 + 4 * (x / np.sqrt(2)) ** 2 if op == "gelu" else 4
+        assert np.all(np.where(tiny, np.abs(got - want) <= 2.0 ** -1000,
+                               ulp <= bound)), (op, ulp[~tiny].max())
+    got = oracle.activation("softmax", x)
+    for r, row in enumerate(x):
+        es = [mpmath.exp(mp(float(v))) for v in row]
+        total = mpmath.fsum(es)
+        want = np.array([float(e / total) for e in es])
+        ulp = np.abs(got[r] - want) / np.spacing(np.abs(want))
+        assert ulp.max() <= x.shape[1] + 4, ulp.max()
