@@ -419,3 +419,21 @@ def test_dump_tool_decodes_fused_kinds_and_launch(tmp_path):
                          capture_output=True, text=True,
                          cwd=os.path.dirname(os.path.dirname(__file__)))
     assert res.returncode == 1 and "not a version 3 hexir module" in res.stderr
+
+
+def test_dump_tool_names_the_activation_kinds(tmp_path):
+    import sys
+    p = hx.Program()
+    a, _ = two_by_two(p)
+    v = a
+    for op in sorted(_ffi.ACTIVATIONS):
+        v = p.activation(op, v)
+    p.print(v)
+    path = tmp_path / "act.hxb"
+    p.emit_file(str(path), "hexir.gelu=cuda", _ffi.EMIT_ACTIVATIONS)
+    res = subprocess.run([sys.executable, "-m", "hexir_b200.dump", str(path)],
+                         capture_output=True, text=True, check=True,
+                         cwd=os.path.dirname(os.path.dirname(__file__)))
+    for i, op in enumerate(sorted(_ffi.ACTIVATIONS)):
+        assert f"{op}_{i}" in res.stdout
+    assert "kind " not in res.stdout  # every kind has a name
