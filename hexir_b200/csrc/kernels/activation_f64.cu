@@ -29,10 +29,13 @@
 //
 // Elementwise ops run on the relu/add stream loop (16-byte streaming loads and
 // stores, four vectors in flight per thread).  Softmax keeps each row in
-// registers: a warp per row up to 1024 columns, one 256- or 512-thread block
-// per row up to 8192 / 16384 columns (one read and one write of the row), and
-// a three-pass block per row beyond that; it scales by one correctly rounded
-// reciprocal of the row sum instead of dividing every element.
+// registers (one read and one write of the row): a warp per row up to 1024
+// columns; above that, for even rows starting 16-byte aligned, persistent
+// blocks that bulk-copy their next row into shared memory while the current
+// one computes (up to 8192 / 16384 columns with 256 / 512 threads); for other
+// rows one 256- or 512-thread block per row; and a three-pass block per row
+// beyond 16384 columns.  It scales by one correctly rounded reciprocal of the
+// row sum instead of dividing every element.
 //
 // FP64 arithmetic, not HBM, bounds the transcendental ones on B200 (gelu's
 // erfc, tanh, softmax's exp): each element costs tens of FP64 instructions.
