@@ -61,6 +61,14 @@ def test_library_exports_every_declared_function():
     assert not missing, sorted(missing)
 
 
+def test_library_exports_nothing_but_its_c_abi():
+    """The C++ and CUDA runtimes linked statically into the library stay
+    private (no operator new, __cxa_* or cuda* symbols leak into a program
+    that links it)."""
+    foreign = {s for s in exported_symbols() if not s.startswith("hexir_")}
+    assert not foreign, sorted(foreign)[:20]
+
+
 def test_python_bindings_cover_every_declared_function():
     missing = declared_functions() - set(_ffi.EXPORTED)
     assert not missing, sorted(missing)
