@@ -404,3 +404,33 @@ def test_hexir_bench_verifies_cpu_modules(tmp_path):
                          capture_output=True, text=True, check=True)
     line = json.loads(res.stdout.strip().splitlines()[-1])
     assert line["verify_ok"] is True and line["verify_max_rel_err"] == 0
+
+
+def test_one_module_executes_concurrently_from_many_threads():
+    """One loaded module, executed at once from 8 threads (ctypes releases
+    the GIL for the call), each on its own CPU device and on one shared
+    device: every result has the oracle's bits."""
+    import threading
+    r = hx.Rng(41)
+    a, w = r.uniform((96, 64)), r.uniform((64, 48))
+    p = hx.Program()
+    p.activation("softmax", p.relu(p.linear(p.constant(a), p.constant(w))))
+    module = hx.Module(p.emit(flags=_ffi.EMIT_ACTIVATIONS))
+    want = oracle.activation("softmax", oracle.relu(oracle.matmul(a, w)))
+    shared = hx.Device("cpu")
+    bad = []
+
+    def worker(own):
+        dev = hx.Device("cpu") if own else shared
+        for _ in range(25):
+            out = hx.execute(module, dev, out_shape=want.shape)
+            if not np.array_equal(out.view(np.uint64), want.view(np.uint64)):
+                bad.append(own)
+
+    threads = [threading.Thread(target=worker, args=(i % 2 == 0,))
+               for i in range(8)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not bad
