@@ -26,6 +26,13 @@ One JSON line on rank 0:
              from the reference sources into oracle/_ref) on a bounded row
              sample with all host threads (N = 1 only)
 --impl reference times that CPU implementation alone, as the reference arm.
+
+--suite prints one JSON line per configuration instead (1 GPU): the 256 x 256
+parity graph's latency, the GEMM sweep 1024-8192, relu over 2^28, each
+activation over 16384 x 16384 (softmax along the rows), the skinny linear
+M = 1 / 16 / 128, the three-layer MLP chain, the fused linear -> add -> relu
+and constants kept on the GPU.  --profile runs one kernel a few times: the
+command line the committed ncu summaries capture.
 """
 
 from __future__ import annotations
