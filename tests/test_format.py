@@ -437,3 +437,19 @@ def test_dump_tool_names_the_activation_kinds(tmp_path):
     for i, op in enumerate(sorted(_ffi.ACTIVATIONS)):
         assert f"{op}_{i}" in res.stdout
     assert "kind " not in res.stdout  # every kind has a name
+
+
+def test_linear_relu_fusion_next_to_an_activation():
+    """linear -> relu -> gelu on one GPU: linear and relu fuse (kind 4, the
+    relu's number taken but folded), the gelu stays its own executable and
+    reads the fused result."""
+    p = hx.Program()
+    a, b = two_by_two(p)
+    p.print(p.activation("gelu", p.relu(p.linear(a, b))))
+    blob = p.emit("hexir.linear=cuda,hexir.relu=cuda,hexir.gelu=cuda",
+                  _ffi.EMIT_ACTIVATIONS)
+    exes = hx.read_executables(blob)
+    assert [(e.name, e.kind) for e in exes] == [("linear_0", 4), ("gelu_2", 12)]
+    dispatches = [ops for kind, ops in hx.read_program(blob) if kind == 3]
+    # gelu reads the slot the fused kernel writes.
+    assert dispatches[1][2] == dispatches[0][-1]

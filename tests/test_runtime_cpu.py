@@ -434,3 +434,15 @@ def test_one_module_executes_concurrently_from_many_threads():
     for t in threads:
         t.join()
     assert not bad
+
+
+def test_cuda_placed_activation_is_refused_on_cpu(tmp_path):
+    """A cuda-placed activation on a CPU device gets the reference's
+    misplacement message, like a cuda-placed linear."""
+    p = hx.Program()
+    p.print(p.activation("tanh", p.constant(np.ones((2, 2)))))
+    path = tmp_path / "t.hxb"
+    p.emit_file(str(path), "hexir.tanh=cuda", _ffi.EMIT_ACTIVATIONS)
+    res = run("--quiet", str(path))
+    assert res.returncode != 0
+    assert "placed on cuda but the active device is cpu" in res.stderr
