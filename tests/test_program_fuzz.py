@@ -21,15 +21,30 @@ from oracle import oracle
 OPS = ["linear", "add", "relu", "activation"]
 
 
-def build(seed):
+def ty(shape):
+    return f"tensor<{shape[0]}x{shape[1]}xf64>"
+
+
+def build(seed, text=None):
+    """(program, expected result); with `text` a list, the same graph is
+    also rendered there as hexir text, one statement per entry."""
     rnd = random.Random(seed)
     rng = np.random.default_rng(seed)
     p = hx.Program()
     values = []  # (program value, numpy value)
+    names = {}
+    lines = text if text is not None else []
+
+    def emit_line(value, line):
+        names[value] = f"%v{value}"
+        lines.append(f"%v{value} = {line}")
 
     def constant(r, c):
         a = rng.uniform(-2, 2, (r, c))
         values.append((p.constant(a), a))
+        rows = ", ".join("[" + ", ".join(repr(float(e)) for e in row) + "]"
+                         for row in a)
+        emit_line(values[-1][0], f"hexir.constant dense<[{rows}]> : {ty(a.shape)}")
         return values[-1]
 
     for _ in range(rnd.randint(1, 3)):
@@ -44,20 +59,26 @@ def build(seed):
             wv, w = rnd.choice(ws) if ws and rnd.random() < 0.5 else \
                 constant(k, rnd.randint(1, 9))
             out = (p.linear(v, wv), oracle.matmul(x, w))
+            emit_line(out[0], f"hexir.linear {names[v]}, {names[wv]} : "
+                              f"({ty(x.shape)}, {ty(w.shape)}) -> {ty(out[1].shape)}")
         elif op == "add":
             same = [(ov, o) for ov, o in values if o.shape == x.shape]
             ov, o = rnd.choice(same)
             out = (p.add(v, ov), oracle.add(x, o))
+            emit_line(out[0], f"hexir.add {names[v]}, {names[ov]} : {ty(x.shape)}")
         elif op == "relu":
             out = (p.relu(v), oracle.relu(x))
+            emit_line(out[0], f"hexir.relu {names[v]} : {ty(x.shape)}")
         else:
             name = rnd.choice(sorted(_ffi.ACTIVATIONS))
             out = (p.activation(name, v), oracle.activation(name, x))
+            emit_line(out[0], f"hexir.{name} {names[v]} : {ty(x.shape)}")
         values.append(out)
         last = out
     if last is None:  # every graph ends in at least one dispatch
         v, x = values[0]
         last = (p.relu(v), oracle.relu(x))
+        emit_line(last[0], f"hexir.relu {names[v]} : {ty(x.shape)}")
     return p, last[1]
 
 
@@ -67,3 +88,17 @@ def test_random_program_matches_oracle(seed):
     out = hx.execute(hx.Module(p.emit(flags=_ffi.EMIT_ACTIVATIONS)),
                      hx.Device("cpu"), out_shape=want.shape)
     assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
+
+
+@pytest.mark.parametrize("seed", range(0, 120, 3))
+def test_random_program_text_writes_the_same_module(seed):
+    """The same graph written as hexir text and parsed gives a module
+    byte-identical to the one built through the API (placements and the
+    fusion rules included)."""
+    lines = []
+    p, _ = build(seed, lines)
+    text = "func.func @main() {\n  " + "\n  ".join(lines) + "\n  return\n}\n"
+    q = hx.parse(text)
+    for placement in ("", "hexir.linear=cuda,hexir.relu=cuda,hexir.add=cuda"):
+        flags = _ffi.EMIT_ACTIVATIONS | _ffi.EMIT_NO_IMAGE
+        assert q.emit(placement, flags) == p.emit(placement, flags)
