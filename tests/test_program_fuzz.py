@@ -25,9 +25,10 @@ def ty(shape):
     return f"tensor<{shape[0]}x{shape[1]}xf64>"
 
 
-def build(seed, text=None):
-    """(program, expected result); with `text` a list, the same graph is
-    also rendered there as hexir text, one statement per entry."""
+def build(seed, text=None, ops=OPS):
+    """(program, expected result, its program value); with `text` a list,
+    the same graph is also rendered there as hexir text, one statement per
+    entry."""
     rnd = random.Random(seed)
     rng = np.random.default_rng(seed)
     p = hx.Program()
@@ -51,7 +52,7 @@ def build(seed, text=None):
         constant(rnd.randint(1, 9), rnd.randint(1, 9))
     last = None
     for _ in range(rnd.randint(1, 8)):
-        op = rnd.choice(OPS)
+        op = rnd.choice(ops)
         v, x = rnd.choice(values)
         if op == "linear":
             k = x.shape[1]
@@ -79,12 +80,12 @@ def build(seed, text=None):
         v, x = values[0]
         last = (p.relu(v), oracle.relu(x))
         emit_line(last[0], f"hexir.relu {names[v]} : {ty(x.shape)}")
-    return p, last[1]
+    return p, last[1], last[0]
 
 
 @pytest.mark.parametrize("seed", range(120))
 def test_random_program_matches_oracle(seed):
-    p, want = build(seed)
+    p, want, _ = build(seed)
     out = hx.execute(hx.Module(p.emit(flags=_ffi.EMIT_ACTIVATIONS)),
                      hx.Device("cpu"), out_shape=want.shape)
     assert np.array_equal(out.view(np.uint64), want.view(np.uint64))
@@ -96,9 +97,29 @@ def test_random_program_text_writes_the_same_module(seed):
     byte-identical to the one built through the API (placements and the
     fusion rules included)."""
     lines = []
-    p, _ = build(seed, lines)
+    p, _, _ = build(seed, lines)
     text = "func.func @main() {\n  " + "\n  ".join(lines) + "\n  return\n}\n"
     q = hx.parse(text)
     for placement in ("", "hexir.linear=cuda,hexir.relu=cuda,hexir.add=cuda"):
         flags = _ffi.EMIT_ACTIVATIONS | _ffi.EMIT_NO_IMAGE
         assert q.emit(placement, flags) == p.emit(placement, flags)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_reference_runtime_prints_random_programs_like_this_one(tmp_path, seed):
+    """Graphs of the reference's own ops (linear, add, relu) with a PRINT:
+    the reference runtime, built from its sources, and this runtime print
+    the same text for the same module."""
+    import subprocess
+    from tests.conftest import bin_path
+    if not oracle.have_reference():
+        pytest.skip("reference runtime not built here")
+    p, _, v = build(seed, ops=["linear", "add", "relu"])
+    p.print(v)
+    path = tmp_path / "r.hxb"
+    p.emit_file(str(path))
+    ref = subprocess.run([oracle.REF_RUN, "--quiet", str(path)],
+                         capture_output=True, text=True, check=True)
+    ours = subprocess.run([bin_path("hexir-run"), "--quiet", str(path)],
+                          capture_output=True, text=True, check=True)
+    assert ours.stdout == ref.stdout and ref.stdout
