@@ -368,9 +368,16 @@ def run_hexir(args):
                 comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
                 K_DIM, shard_flags, stream), "sharded linear")
 
+    def synchronize():
+        hx.cuda_synchronize(ordinal, stream)
+        if comm is not None:
+            # Every rank: a failure on any rank's part of the step.
+            _ffi.check(hx.lib().hexir_comm_synchronize(comm, stream),
+                       "hexir_comm_synchronize")
+
     for _ in range(args.warmup):
         step()
-    hx.cuda_synchronize(ordinal, stream)
+    synchronize()
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
@@ -388,7 +395,7 @@ def run_hexir(args):
     torch.cuda.synchronize()
     launches = hx.launch_count() - launches0
     clock_info = clocks.stop()
-    hx.cuda_synchronize(ordinal, stream)
+    synchronize()
     ms = start.elapsed_time(stop) / args.steps
     if pg:
         t = torch.tensor([ms], device="cuda")
@@ -543,7 +550,8 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg, shard_flags):
                 K_DIM, shard_flags, stream), "sharded linear")
             if rank == 0:
                 out.copy_(c, non_blocking=True)
-            torch.cuda.synchronize()
+            _ffi.check(hx.lib().hexir_comm_synchronize(comm, stream),
+                       "hexir_comm_synchronize")
 
         for _ in range(warm):
             once()

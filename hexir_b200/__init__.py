@@ -17,4 +17,5 @@ from .api import (Buffer, Device, Module, Program, Rng, cuda_activation,  # noqa
                   execute, kernel_image, last_kernel_ms, launch_count,
                   matmul_plan, parse, read_executables, read_launch,
                   read_program,
-                  read_sections, shard_rows)
+                  read_sections, shard_gather_pieces, shard_rows,
+                  shard_weight_pieces)

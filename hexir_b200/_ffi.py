@@ -140,6 +140,11 @@ _SIGNATURES = [
     ("hexir_comm_rank", _int, [_vp]),
     ("hexir_comm_size", _int, [_vp]),
     ("hexir_comm_direct_stores", _int, [_vp]),
+    ("hexir_comm_synchronize", _int, [_vp, _vp]),
+    ("hexir_shard_gather_pieces", _int, [_u64, _u32, C.POINTER(_u64),
+                                         C.POINTER(_u64), C.POINTER(_u32)]),
+    ("hexir_shard_weight_pieces", _int, [_u32, _u32, C.POINTER(_u32),
+                                         C.POINTER(_u32)]),
     # fault.h
     ("hexir_fault_configure", _int, [C.c_char_p]),
     ("hexir_fault_calls", _u64, [C.c_char_p]),

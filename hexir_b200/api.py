@@ -492,6 +492,32 @@ def shard_rows(rows: int, shards: int, index: int) -> tuple:
     return b.value, c.value
 
 
+def shard_gather_pieces(rows: int) -> List[tuple]:
+    """[(begin, count), ...]: the pieces a rank's `rows` output rows are
+    gathered to the root in (hexir_shard_gather_pieces)."""
+    out = []
+    i = 0
+    while True:
+        b, c, n = C.c_uint64(), C.c_uint64(), C.c_uint32()
+        check(lib().hexir_shard_gather_pieces(rows, i, C.byref(b), C.byref(c),
+                                              C.byref(n)),
+              "hexir_shard_gather_pieces")
+        if i >= n.value:
+            return out
+        out.append((b.value, c.value))
+        i += 1
+
+
+def shard_weight_pieces(k: int, ranks: int) -> List[int]:
+    """[0, ..., k]: the k bounds the weight is broadcast in
+    (hexir_shard_weight_pieces)."""
+    bounds = (C.c_uint32 * 3)()
+    n = C.c_uint32()
+    check(lib().hexir_shard_weight_pieces(k, ranks, bounds, C.byref(n)),
+          "hexir_shard_weight_pieces")
+    return [bounds[i] for i in range(n.value + 1)]
+
+
 def kernel_image() -> bytes:
     p, n = C.c_void_p(), C.c_size_t()
     check(lib().hexir_cuda_kernel_image(C.byref(p), C.byref(n)),

@@ -19,7 +19,7 @@ namespace {
 // geometrically shrinking size (1/2, 1/4, 1/8, 1/16, 1/16 of its rows), so
 // every transfer but the last hides behind the GEMM of the next piece and the
 // exposed last one is small.  Pieces keep >= kMinChunkRows rows.
-constexpr uint32_t kGatherChunks = 5;
+constexpr uint32_t kGatherChunks = HEXIR_SHARD_MAX_GATHER_PIECES;
 constexpr uint64_t kMinChunkRows = 256;
 
 // Piece `i` of `rows` rows: [*begin, *begin + *count).  Returns the number of
@@ -89,7 +89,10 @@ struct hexir_comm_t {
   CUevent w_start = nullptr, w_piece[2] = {}, w_done = nullptr;
   // Direct row stores into the root's c (all ranks on one host, IPC works).
   bool direct = false;
-  CUdeviceptr scratch = 0;  // descriptor [kDescBytes] + completion word
+  // Device scratch: the root's output descriptor [kDescBytes], then the
+  // failure word -- nonzero once any rank's part of a sharded call failed
+  // since the last hexir_comm_synchronize (every call max-reduces it).
+  CUdeviceptr scratch = 0;
   RootOutput *desc_host = nullptr;  // pinned [kDescSlots]
   CUevent desc_done[kDescSlots] = {};
   uint32_t desc_next = 0;
@@ -208,17 +211,43 @@ hexir_status_t probe_direct(hexir_comm_t *comm) {
 // B200: the 480 MiB rest crosses NVLink in ~0.8 ms, the first piece takes
 // ~2 ms of DMMA time on 8192 rows).  Each extra piece costs ~0.2 ms there
 // (every CTA stores and reloads its partial sums, one more tail wave), so
-// there are two.  Multiples of the 32-wide k tile.  Returns the count.
+// there are two.  Multiples of the 32-wide k tile.  One piece for a single
+// rank (nothing to broadcast).  Returns the count.
 constexpr uint32_t kBroadcastPieceMinK = 2048;
-uint32_t broadcast_pieces(uint32_t k, uint32_t bounds[3]) {
+uint32_t broadcast_pieces(uint32_t k, uint32_t ranks, uint32_t bounds[3]) {
   bounds[0] = 0;
-  if (k < kBroadcastPieceMinK) {
+  if (ranks < 2 || k < kBroadcastPieceMinK) {
     bounds[1] = k;
+    bounds[2] = k;
     return 1;
   }
   bounds[1] = 512;
   bounds[2] = k;
   return 2;
+}
+
+CUdeviceptr failure_word(const hexir_comm_t *comm) {
+  return comm->scratch + kDescBytes;
+}
+
+// Every rank, at the end of every sharded call, in the same order: a rank
+// whose part failed marks the failure word, and a max all-reduce hands the
+// mark to every rank on the caller's stream (where hexir_comm_synchronize
+// reads it).  A rank that failed still takes this step, so no rank waits
+// for ever on it.
+hexir_status_t reduce_failure(hexir_comm_t *comm, CUstream s, bool failed) {
+  const Driver &d = driver();
+  CUresult r = CUDA_SUCCESS;
+  if (failed)
+    r = d.MemsetD32Async(failure_word(comm), 1u, 1, s);
+  void *w = reinterpret_cast<void *>(failure_word(comm));
+  const ncclResult_t nr = nccl().AllReduce(
+      w, w, 1, ncclInt32, ncclMax, comm->comm, reinterpret_cast<cudaStream_t>(s));
+  if (nr != ncclSuccess)
+    return comm_fail(nccl_message("ncclAllReduce (failure word)", nr));
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("marking the failure word", r));
+  return HEXIR_OK;
 }
 
 }  // namespace
@@ -232,6 +261,35 @@ hexir_status_t hexir_shard_rows(uint64_t rows, uint32_t shards, uint32_t index,
   const uint64_t base = rows / shards, extra = rows % shards;
   *begin = index * base + (index < extra ? index : extra);
   *count = base + (index < extra ? 1 : 0);
+  return HEXIR_OK;
+}
+
+hexir_status_t hexir_shard_gather_pieces(uint64_t rows, uint32_t index,
+                                         uint64_t *begin, uint64_t *count,
+                                         uint32_t *pieces) {
+  if (!begin || !count)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  if (!rows) {
+    *begin = 0;
+    *count = 0;
+    if (pieces)
+      *pieces = 0;
+    return HEXIR_OK;
+  }
+  const uint32_t n = gather_piece(rows, index, begin, count);
+  if (pieces)
+    *pieces = n;
+  return HEXIR_OK;
+}
+
+hexir_status_t hexir_shard_weight_pieces(uint32_t k, uint32_t ranks,
+                                         uint32_t *bounds, uint32_t *pieces) {
+  if (!bounds || !pieces || ranks == 0)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  uint32_t b[3];
+  *pieces = broadcast_pieces(k, ranks, b);
+  for (uint32_t i = 0; i <= *pieces; ++i)
+    bounds[i] = b[i];
   return HEXIR_OK;
 }
 
@@ -321,6 +379,15 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
       return st;
     }
   }
+  // The probe used the failure word for its vote; no call has failed yet.
+  cr = d.MemsetD32Async(failure_word(comm), 0u, 1, comm->gather_stream);
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamSynchronize(comm->gather_stream);
+  if (cr != CUDA_SUCCESS) {
+    set_last_error(cuda_message("clearing the failure word", cr));
+    hexir_comm_release(comm);
+    return HEXIR_ERROR_DEVICE;
+  }
   *out = comm;
   return HEXIR_OK;
 }
@@ -408,7 +475,7 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   // its one-shot plan has no k split; otherwise it runs that plan once the
   // whole weight has landed.
   uint32_t bounds[3] = {0, k, k};
-  const uint32_t pieces = ranks > 1 ? broadcast_pieces(k, bounds) : 1;
+  const uint32_t pieces = broadcast_pieces(k, ranks, bounds);
   const MatmulPlan one = plan_matmul(dev, a_rows, w, c, my_rows, n, k, relu);
   const bool chain = pieces > 1 && one.split_k == 1 && !one.stream_k();
 
@@ -523,8 +590,8 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
 
   if (direct) {
     // 4. Every rank's kernel stores its output tiles into the root's c over
-    //    NVLink (system-scope fence before each CTA retires); a one-word
-    //    all-reduce then orders the root's stream after every peer's
+    //    NVLink (system-scope fence before each CTA retires); the failure
+    //    word's all-reduce then orders the root's stream after every peer's
     //    kernels.  A rank whose launch failed still takes every collective
     //    step, so no rank waits for ever.
     if (status == HEXIR_OK) {
@@ -534,12 +601,8 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
     if (status != HEXIR_OK)
       set_last_error(error.empty() ? hexir_status_string(status) : error);
     d.StreamWaitEvent(s, comm->w_done, 0);
-    void *word = reinterpret_cast<void *>(comm->scratch + kDescBytes);
-    ncclResult_t nr =
-        nc.AllReduce(word, word, 1, ncclInt32, ncclMin, comm->comm, cs);
-    if (nr != ncclSuccess)
-      return comm_fail(nccl_message("ncclAllReduce (row stores done)", nr));
-    return status;
+    const hexir_status_t rs = reduce_failure(comm, s, status != HEXIR_OK);
+    return status != HEXIR_OK ? status : rs;
   }
   // 4'. Rows by NCCL: this rank's rows in up to kGatherChunks pieces of
   //     shrinking size; the root writes straight into its part of c, and
@@ -598,7 +661,50 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   d.StreamWaitEvent(s, comm->gather_done, 0);
   if (status != HEXIR_OK)
     set_last_error(error.empty() ? hexir_status_string(status) : error);
+  if (ranks > 1) {
+    const hexir_status_t rs = reduce_failure(comm, s, status != HEXIR_OK);
+    if (status == HEXIR_OK)
+      status = rs;
+  }
   return status;
+}
+
+hexir_status_t hexir_comm_synchronize(hexir_comm_t *comm, void *stream) {
+  if (!comm)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  std::string error;
+  DeviceState *dev = device_state(comm->ordinal, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  CUstream s = static_cast<CUstream>(stream);
+  // The stream's work, and the error words of this GPU's kernels.
+  hexir_status_t st = check_device(dev, s, &error);
+  if (st != HEXIR_OK) {
+    set_last_error(error);
+    return st;
+  }
+  if (comm->nranks < 2)
+    return HEXIR_OK;
+  ContextGuard guard(dev->context);
+  const Driver &d = driver();
+  int32_t failed = 0;
+  CUresult r = d.MemcpyDtoHAsync(&failed, failure_word(comm), sizeof(failed), s);
+  if (r == CUDA_SUCCESS)
+    r = d.StreamSynchronize(s);
+  if (r == CUDA_SUCCESS && failed) {
+    r = d.MemsetD32Async(failure_word(comm), 0u, 1, s);
+    if (r == CUDA_SUCCESS)
+      r = d.StreamSynchronize(s);
+  }
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("reading the failure word", r));
+  if (failed)
+    return comm_fail("a rank's part of a sharded linear failed since the last "
+                     "hexir_comm_synchronize (that rank's own call returned "
+                     "the error); the root's output rows are not valid");
+  return HEXIR_OK;
 }
 
 }  // extern "C"

@@ -71,6 +71,7 @@ void load() {
             bind(lib, d.Memcpy2DAsync, "cuMemcpy2DAsync_v2", e) &&
             bind(lib, d.MemcpyPeerAsync, "cuMemcpyPeerAsync", e) &&
             bind(lib, d.MemsetD8Async, "cuMemsetD8Async", e) &&
+            bind(lib, d.MemsetD32Async, "cuMemsetD32Async", e) &&
             bind(lib, d.PointerGetAttribute, "cuPointerGetAttribute", e) &&
             bind(lib, d.MemGetAddressRange, "cuMemGetAddressRange_v2", e) &&
             bind(lib, d.IpcGetMemHandle, "cuIpcGetMemHandle", e) &&

@@ -53,6 +53,8 @@ struct Driver {
                               size_t, CUstream) = nullptr;
   CUresult (*MemsetD8Async)(CUdeviceptr, unsigned char, size_t, CUstream) =
       nullptr;
+  CUresult (*MemsetD32Async)(CUdeviceptr, unsigned int, size_t, CUstream) =
+      nullptr;
   CUresult (*PointerGetAttribute)(void *, CUpointer_attribute,
                                   CUdeviceptr) = nullptr;
   CUresult (*MemGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr) = nullptr;

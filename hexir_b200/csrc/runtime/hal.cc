@@ -107,6 +107,7 @@ CudaDevice::~CudaDevice() {
   if (stream) {
     ContextGuard guard(state->context);
     driver().StreamSynchronize(stream);
+    std::lock_guard<std::mutex> lock(pool_mu);
     for (auto &kv : pool)
       driver().MemFree(kv.second);
     pool.clear();
@@ -115,6 +116,7 @@ CudaDevice::~CudaDevice() {
 }
 
 hexir_status_t CudaDevice::allocate_pooled(size_t size, hexir_buffer_t **out) {
+  std::lock_guard<std::mutex> lock(pool_mu);
   auto it = pool.find(size);
   if (it == pool.end()) {
     hexir_status_t st = allocate_raw(size, out);
@@ -199,11 +201,14 @@ void CudaDevice::buffer_release(hexir_buffer_t *buffer) {
   }
   // The pool keeps at most kPoolCapBytes; beyond that blocks are freed.
   constexpr size_t kPoolCapBytes = 32ull << 30;
-  if (buffer->pooled && buffer->impl && pool_bytes + buffer->size <= kPoolCapBytes) {
-    pool.emplace(buffer->size, reinterpret_cast<CUdeviceptr>(buffer->impl));
-    pool_bytes += buffer->size;
-    delete buffer;
-    return;
+  if (buffer->pooled && buffer->impl) {
+    std::lock_guard<std::mutex> lock(pool_mu);
+    if (pool_bytes + buffer->size <= kPoolCapBytes) {
+      pool.emplace(buffer->size, reinterpret_cast<CUdeviceptr>(buffer->impl));
+      pool_bytes += buffer->size;
+      delete buffer;
+      return;
+    }
   }
   if (buffer->impl) {
     ContextGuard guard(state->context);

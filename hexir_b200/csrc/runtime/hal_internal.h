@@ -9,6 +9,7 @@
 
 #include <cstddef>
 #include <map>
+#include <mutex>
 #include <string>
 
 #include "hexir_runtime/hal.h"
@@ -83,10 +84,11 @@ struct CudaDevice : hexir_device_t {
   // Same, from the device's pool of released VM buffers when one of exactly
   // this size is free.  Pooled blocks are reused in stream order (every VM
   // use is on this device's stream), capped at 32 GiB per device, and freed
-  // with the device.  A device object serves one thread at a time, as in the
-  // reference runtime.
+  // with the device.  `pool_mu` guards the pool itself; the VM still runs
+  // one execute per device object at a time (its streams are the object's).
   hexir_status_t allocate_pooled(size_t size, hexir_buffer_t **out);
 
+  std::mutex pool_mu;
   std::multimap<size_t, CUdeviceptr> pool;
   size_t pool_bytes = 0;
 

@@ -1288,6 +1288,12 @@ struct Vm {
       if (st != HEXIR_OK) {
         report(std::string("kernel '") + exe.name + "' shard " +
                std::to_string(r) + ": " + error);
+        // Shards already launched may still be storing into the root's
+        // result: the root's stream (and the release of its buffers back to
+        // the pool) must come after them.
+        for (int j = 1; j < r; ++j)
+          if (rows[j] && direct[j])
+            order_after(cuda[first + j], root);
         return st;
       }
     }

@@ -35,6 +35,30 @@ extern "C" {
 hexir_status_t hexir_shard_rows(uint64_t rows, uint32_t shards, uint32_t index,
                                 uint64_t *begin, uint64_t *count);
 
+/* Most pieces a rank's output rows are gathered in (the NCCL path of
+ * hexir_sharded_linear_f64) and most k pieces the weight is broadcast in. */
+#define HEXIR_SHARD_MAX_GATHER_PIECES 5
+#define HEXIR_SHARD_MAX_WEIGHT_PIECES 2
+
+/* Piece `index` of a rank's `rows` output rows as hexir_sharded_linear_f64
+ * sends them to the root when it gathers with NCCL: rows [*begin, *begin +
+ * *count) of that rank's block, *pieces the number of pieces (at most
+ * HEXIR_SHARD_MAX_GATHER_PIECES; 0 for no rows).  The pieces halve in size
+ * down to whole 128-row tiles of at least 256 rows, so every send but the
+ * last hides behind the next piece's GEMM; an index past the last piece
+ * gives *count 0.  Every rank computes every peer's pieces with this rule. */
+hexir_status_t hexir_shard_gather_pieces(uint64_t rows, uint32_t index,
+                                         uint64_t *begin, uint64_t *count,
+                                         uint32_t *pieces);
+
+/* The k pieces in which hexir_sharded_linear_f64 broadcasts the weight over
+ * `ranks` ranks and the peers compute behind it: bounds[0] = 0 <
+ * bounds[1] < ... < bounds[*pieces] = k.  `bounds` holds
+ * HEXIR_SHARD_MAX_WEIGHT_PIECES + 1 entries.  One piece for one rank or
+ * k < 2048; else [0, 512) and [512, k). */
+hexir_status_t hexir_shard_weight_pieces(uint32_t k, uint32_t ranks,
+                                         uint32_t *bounds, uint32_t *pieces);
+
 typedef struct hexir_comm_t hexir_comm_t;
 
 #define HEXIR_COMM_ID_BYTES 128
@@ -80,11 +104,25 @@ int hexir_comm_direct_stores(const hexir_comm_t *comm);
  * returns only once the root's stream has reached the same call (the root
  * sends the location of c every call).  Peers write the root's c only after
  * the root's `stream` reaches the call, so the root orders its own use of c
- * on that stream. */
+ * on that stream.
+ *
+ * Errors.  The return value reports this rank's own failures (a launch, a
+ * driver or NCCL call).  A rank that fails still takes every collective step
+ * of the call, so its peers never wait for ever, and marks a failure word
+ * that every call max-reduces over all ranks on `stream`.  So the root's call
+ * can return HEXIR_OK while a peer's rows were never written: before using
+ * c, call hexir_comm_synchronize, which reports a failure on any rank. */
 hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows,
                                         double *w, double *c, uint32_t m,
                                         uint32_t n, uint32_t k, uint32_t flags,
                                         void *stream);
+
+/* Waits for `stream` and returns HEXIR_ERROR_DEVICE on every rank if any
+ * rank's part of any hexir_sharded_linear_f64 call on `comm` failed since
+ * the last hexir_comm_synchronize (or a kernel on this GPU reported a device
+ * error); HEXIR_OK otherwise.  Clears the failure.  Call it on every rank at
+ * the same point of the call sequence, on the stream the calls used. */
+hexir_status_t hexir_comm_synchronize(hexir_comm_t *comm, void *stream);
 
 #ifdef __cplusplus
 }

@@ -21,6 +21,7 @@ import numpy as np
 import pytest
 
 import hexir_b200 as hx
+from hexir_b200 import _ffi
 from tests.conftest import spawn_ranks
 
 pytestmark = pytest.mark.gpu
@@ -68,7 +69,8 @@ def _rank(rank, world, port, m, n, k, result_path):
         _ffi.check(lib.hexir_sharded_linear_f64(comm, ba.ptr, bw.ptr, buf.ptr,
                                                 m, n, k, flags, dev.stream),
                    "sharded linear " + name)
-        hx.cuda_synchronize(rank, dev.stream)
+        _ffi.check(lib.hexir_comm_synchronize(comm, dev.stream),
+                   "comm synchronize " + name)
         if rank == 0:
             results[name] = buf.read((m, n))
     lib.hexir_comm_release(comm)
@@ -128,3 +130,78 @@ def test_two_processes_sharded_linear(tmp_path, m, n, k):
         assert r["err_" + name] <= TOL, name
     assert r["direct_is_single"]
     assert r["direct_is_again"]
+
+
+def _failing_peer_rank(rank, world, port, m, n, k, flags, result_path):
+    """Rank 1's first kernel launch fails (host-side fault injection, before
+    the driver call); rank 0 must learn of it from hexir_comm_synchronize,
+    and the next call, with no fault, must be right again."""
+    import torch.distributed as dist
+    from hexir_b200 import _ffi
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    lib = hx.lib()
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        _ffi.check(lib.hexir_comm_unique_id(uid, 128), "unique id")
+    obj = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    uid = C.create_string_buffer(obj[0], 128)
+    comm = C.c_void_p()
+    _ffi.check(lib.hexir_comm_init_rank(uid, 128, world, rank, rank,
+                                        C.byref(comm)), "comm init")
+    comm = comm.value
+    rng = hx.Rng(37)
+    a = rng.uniform((m, k))
+    w = rng.uniform((k, n))
+    begin, rows = hx.shard_rows(m, world, rank)
+    dev = hx.Device(f"cuda:{rank}")
+    ba = dev.upload(a[begin:begin + rows])
+    bw = dev.upload(w if rank == 0 else np.zeros_like(w))
+    c = dev.buffer((m if rank == 0 else rows) * n * 8)
+    out = {}
+    for name, fault in (("faulted", rank == 1), ("clean", False)):
+        if fault:
+            hx.fault_configure("launch:1")
+        dist.barrier()
+        out["call_" + name] = lib.hexir_sharded_linear_f64(
+            comm, ba.ptr, bw.ptr, c.ptr, m, n, k, flags, dev.stream)
+        hx.fault_configure("")
+        out["sync_" + name] = lib.hexir_comm_synchronize(comm, dev.stream)
+        if rank == 0 and name == "clean":
+            from oracle import oracle
+            got = c.read((m, n))
+            sample = np.unique(np.linspace(0, m - 1, 24).astype(int))
+            out["err"] = oracle.normwise_error(
+                got[sample], oracle.relu(oracle.matmul(a[sample], w)))
+    lib.hexir_comm_release(comm)
+    np.save(result_path.replace(".npy", f"_{rank}.npy"),
+            np.array([out], dtype=object))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+@pytest.mark.parametrize("gather", ["direct", "nccl"])
+@pytest.mark.parametrize("k", [512, 2048])
+def test_peer_failure_reaches_every_rank(tmp_path, gather, k):
+    m, n = 1000, 256
+    flags = _ffi.MATMUL_RELU | (_ffi.SHARD_GATHER_NCCL if gather == "nccl"
+                                else 0)
+    path = str(tmp_path / "out.npy")
+    spawn_ranks(_failing_peer_rank, 2, (m, n, k, flags, path))
+    r0 = np.load(path.replace(".npy", "_0.npy"), allow_pickle=True)[0]
+    r1 = np.load(path.replace(".npy", "_1.npy"), allow_pickle=True)[0]
+    # The failing rank's own call reports its launch failure ...
+    assert r1["call_faulted"] == _ffi.ERROR_DEVICE
+    # ... the root's call itself cannot know yet, but its synchronize does,
+    # and so does the failing rank's.
+    assert r0["call_faulted"] == _ffi.OK
+    assert r0["sync_faulted"] == _ffi.ERROR_DEVICE
+    assert r1["sync_faulted"] == _ffi.ERROR_DEVICE
+    # The failure is cleared: the next call is whole and right.
+    for r in (r0, r1):
+        assert r["call_clean"] == _ffi.OK and r["sync_clean"] == _ffi.OK
+    assert r0["err"] <= TOL
