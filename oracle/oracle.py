@@ -58,6 +58,20 @@ def have_reference() -> bool:
     return os.path.exists(REF_SO)
 
 
+REF_ROOT_RECORD = os.path.join(HERE, "_ref", "REFERENCE_ROOT")
+
+
+def reference_root():
+    """The reference checkout's root, or None where it is absent: the
+    environment variable HEXIR_REFERENCE, else the checkout `make ref` last
+    compiled _ref from (recorded in _ref/REFERENCE_ROOT)."""
+    root = os.environ.get("HEXIR_REFERENCE")
+    if not root and os.path.exists(REF_ROOT_RECORD):
+        with open(REF_ROOT_RECORD) as f:
+            root = f.read().strip()
+    return root if root and os.path.isdir(root) else None
+
+
 def _load_ref():
     global _ref
     if _ref is None:

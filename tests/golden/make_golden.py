@@ -4,9 +4,9 @@
 Run in a container that has the reference tree and the reference runtime
 built from its own sources (`make -C oracle ref`):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference checkout>]
 
-It records
+It records (golden.json)
   - the reference's checked-in CPU fixture (runtime/test/fixtures/mlp-cpu.hxb):
     size, sha256 and what the reference hexir-run prints for it;
   - known-answer programs from the reference's runtime tests, written here as
@@ -17,6 +17,12 @@ It records
     stream (small shapes and the 256x256 seed-0 parity graph), outputs of the
     reference's own hexir_ref_*_f64 kernels, stored as sha256 of the output
     bytes plus a few sampled values.
+
+With --lit it writes lit_cases.json instead: for each of the reference's
+runtime lit tests that need no fixture files (runtime/test/*.mlir), its
+REQUIRES features, RUN lines, check directives and program, so that
+tests/test_reference_lit.py runs them where the reference tree is absent
+(a GPU machine, for the files that require cuda).
 
 The tests then need neither the reference tree nor the reference library,
 so they also run on machines that have neither.
@@ -90,10 +96,74 @@ def seeded_inputs(m, n, k, seed):
     return rng.uniform((m, k)), rng.uniform((k, n))
 
 
+LIT_FILES = ["hxb-roundtrip.mlir", "hxb-errors.mlir", "hxb-cuda.mlir",
+             "hxb-cpu-vs-gpu.mlir"]
+
+
+def lit_case(path: str) -> dict:
+    """What a lit run of one reference runtime test needs, read from the
+    file: its REQUIRES features, its RUN lines (continuations joined), its
+    check directives by prefix, and the program (the lines that are not
+    comments)."""
+    import re
+    requires, run, checks, program = [], [], {}, []
+    current = ""
+    directive = re.compile(r"^//\s*([A-Z][A-Z0-9_]*)(-NEXT)?:(.*)$")
+    for raw in open(path, encoding="utf-8"):
+        line = raw.rstrip("\n")
+        m = re.search(r"REQUIRES:(.*)$", line)
+        if m:
+            requires += [f.strip() for f in m.group(1).split(",") if f.strip()]
+            continue
+        m = re.search(r"RUN:(.*)$", line)
+        if m:
+            part = m.group(1).strip()
+            if part.endswith("\\"):
+                current += part[:-1] + " "
+            else:
+                run.append(current + part)
+                current = ""
+            continue
+        m = directive.match(line.strip())
+        if m and m.group(1) not in ("REQUIRES", "RUN"):
+            checks.setdefault(m.group(1), []).append(
+                [bool(m.group(2)), m.group(3).strip()])
+            continue
+        if not line.lstrip().startswith("//"):
+            program.append(line)
+    while program and not program[0].strip():
+        program.pop(0)
+    while program and not program[-1].strip():
+        program.pop()
+    return {"file": "runtime/test/" + os.path.basename(path),
+            "requires": requires, "run": run, "checks": checks,
+            "program": program}
+
+
+def write_lit_cases(reference: str) -> None:
+    cases = [lit_case(os.path.join(reference, "runtime/test", name))
+             for name in LIT_FILES]
+    dest = os.path.join(HERE, "lit_cases.json")
+    with open(dest, "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py --lit",
+                   "cases": cases}, f, indent=1)
+    print("wrote", dest)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=oracle.reference_root(),
+                    help="the reference checkout (default: HEXIR_REFERENCE, "
+                         "else the one oracle/_ref was built from)")
+    ap.add_argument("--lit", action="store_true",
+                    help="only write lit_cases.json: the reference runtime "
+                         "tests' RUN lines, checks and programs")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("set HEXIR_REFERENCE or pass --reference")
+    if args.lit:
+        write_lit_cases(args.reference)
+        return
     if not oracle.have_reference():
         raise SystemExit("build the reference runtime first: make -C oracle ref")
     ref_run = oracle.REF_RUN

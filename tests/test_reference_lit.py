@@ -15,8 +15,13 @@ The features lit would gate on are `runtime` and `compiler` (both present
 here) and `cuda`, which this runner grants only when a CUDA GPU is visible;
 a RUN line that needs one (`--device=cuda`) is skipped without a GPU.
 
-The test files are read in place from the reference tree (nothing of them is
-copied here); without that tree the tests skip.
+The test files are read in place from the reference tree where it is
+present (HEXIR_REFERENCE, else the checkout oracle/_ref was compiled from).
+Without the tree -- on a GPU machine, where the files that require cuda
+matter most -- the four .mlir files are rebuilt from tests/golden/
+lit_cases.json (their RUN lines, check directives and programs, extracted
+by tests/golden/make_golden.py --lit and pinned to the tree below); the two
+.test files, which need the reference's fixture directory, then skip.
 """
 
 import os
@@ -25,11 +30,22 @@ import stat
 import subprocess
 import sys
 
+import json
+
 import pytest
 
+from oracle import oracle
 from tests.conftest import bin_path
 
-REF_TESTS = "/root/reference/runtime/test"
+LIT_CASES = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                         "lit_cases.json")
+
+
+def ref_tests_dir():
+    root = oracle.reference_root()
+    return os.path.join(root, "runtime", "test") if root else None
+
+
 FILES = ["fixture-cpu.test", "builtin-program.test", "hxb-roundtrip.mlir",
          "hxb-errors.mlir", "hxb-cuda.mlir", "hxb-cpu-vs-gpu.mlir"]
 
@@ -127,11 +143,67 @@ def requires(path):
     return feats
 
 
+def fixture_cases():
+    with open(LIT_CASES) as f:
+        return {os.path.basename(c["file"]): c for c in json.load(f)["cases"]}
+
+
+def materialize(cases, dest):
+    """Write each fixture case back as a lit file: its program, then its
+    REQUIRES, RUN and check lines as comments."""
+    for name, case in cases.items():
+        lines = list(case["program"]) + [""]
+        if case["requires"]:
+            lines.append("// REQUIRES: " + ", ".join(case["requires"]))
+        lines += ["// RUN: " + r for r in case["run"]]
+        for prefix, checks in case["checks"].items():
+            lines += [f"// {prefix}{'-NEXT' if nxt else ''}: {pat}"
+                      for nxt, pat in checks]
+        (dest / name).write_text("\n".join(lines) + "\n")
+
+
+def lit_path(tmp_path, name):
+    """The lit file `name`: in place in the reference tree, else rebuilt
+    from the fixture; None when neither has it."""
+    tree = ref_tests_dir()
+    if tree and os.path.exists(os.path.join(tree, name)):
+        return os.path.join(tree, name)
+    cases = fixture_cases()
+    if name not in cases:
+        return None
+    d = tmp_path / "lit"
+    d.mkdir()
+    materialize(cases, d)
+    return str(d / name)
+
+
+def test_lit_fixture_matches_the_reference_tree():
+    tree = ref_tests_dir()
+    if not tree:
+        pytest.skip("the reference tree is not present here")
+    sys.path.insert(0, os.path.dirname(LIT_CASES))
+    import make_golden
+    for name, case in fixture_cases().items():
+        assert make_golden.lit_case(os.path.join(tree, name)) == case, name
+
+
+def test_rebuilt_lit_file_reads_back_the_same(tmp_path):
+    """The rebuilt files give the runner the same RUN lines and checks."""
+    sys.path.insert(0, os.path.dirname(LIT_CASES))
+    import make_golden
+    cases = fixture_cases()
+    materialize(cases, tmp_path)
+    for name, case in cases.items():
+        got = make_golden.lit_case(str(tmp_path / name))
+        assert {k: v for k, v in got.items() if k != "file"} == \
+            {k: v for k, v in case.items() if k != "file"}, name
+
+
 @pytest.mark.parametrize("name", FILES)
 def test_reference_runtime_lit_file(tmp_path, name):
-    path = os.path.join(REF_TESTS, name)
-    if not os.path.exists(path):
-        pytest.skip("the reference's runtime tests are not present here")
+    path = lit_path(tmp_path, name)
+    if path is None:
+        pytest.skip("needs the reference tree (its fixture directory)")
     gpu = have_gpu()
     missing = requires(path) - {"runtime", "compiler"} - ({"cuda"} if gpu else set())
     if missing:
