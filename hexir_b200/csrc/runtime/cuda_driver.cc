@@ -63,6 +63,7 @@ void load() {
             bind(lib, d.MemFree, "cuMemFree_v2", e) &&
             bind(lib, d.MemAllocHost, "cuMemAllocHost_v2", e) &&
             bind(lib, d.MemFreeHost, "cuMemFreeHost", e) &&
+            bind(lib, d.MemHostAlloc, "cuMemHostAlloc", e) &&
             bind(lib, d.MemHostRegister, "cuMemHostRegister_v2", e) &&
             bind(lib, d.MemHostUnregister, "cuMemHostUnregister", e) &&
             bind(lib, d.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2", e) &&

@@ -41,6 +41,7 @@ struct Driver {
   CUresult (*MemFree)(CUdeviceptr) = nullptr;
   CUresult (*MemAllocHost)(void **, size_t) = nullptr;
   CUresult (*MemFreeHost)(void *) = nullptr;
+  CUresult (*MemHostAlloc)(void **, size_t, unsigned int) = nullptr;
   CUresult (*MemHostRegister)(void *, size_t, unsigned int) = nullptr;
   CUresult (*MemHostUnregister)(void *) = nullptr;
   CUresult (*MemcpyHtoDAsync)(CUdeviceptr, const void *, size_t, CUstream) =

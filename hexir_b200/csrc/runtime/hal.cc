@@ -83,6 +83,50 @@ std::map<std::pair<CUcontext, uint64_t>, CUmodule> g_named_modules;
 
 }  // namespace
 
+namespace {
+std::mutex g_pinned_mu;
+std::multimap<size_t, void *> g_pinned;  // free blocks by size
+size_t g_pinned_bytes = 0;
+constexpr size_t kPinnedCapBytes = 8ull << 30;
+}  // namespace
+
+void *pinned_take(size_t bytes, CUcontext context) {
+  if (!bytes)
+    return nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_pinned_mu);
+    auto it = g_pinned.find(bytes);
+    if (it != g_pinned.end()) {
+      void *p = it->second;
+      g_pinned.erase(it);
+      g_pinned_bytes -= bytes;
+      return p;
+    }
+  }
+  const Driver &d = driver();
+  if (!d.ok)
+    return nullptr;
+  ContextGuard guard(context);
+  void *p = nullptr;
+  if (d.MemHostAlloc(&p, bytes, CU_MEMHOSTALLOC_PORTABLE) != CUDA_SUCCESS)
+    return nullptr;
+  return p;
+}
+
+void pinned_give(void *block, size_t bytes) {
+  if (!block)
+    return;
+  {
+    std::lock_guard<std::mutex> lock(g_pinned_mu);
+    if (g_pinned_bytes + bytes <= kPinnedCapBytes) {
+      g_pinned.emplace(bytes, block);
+      g_pinned_bytes += bytes;
+      return;
+    }
+  }
+  driver().MemFreeHost(block);
+}
+
 CudaDevice *as_cuda(hexir_device_t *device) {
   return device && device->kind == HEXIR_DEVICE_CUDA
              ? static_cast<CudaDevice *>(device)

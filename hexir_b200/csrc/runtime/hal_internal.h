@@ -100,6 +100,17 @@ struct CudaDevice : hexir_device_t {
 
 CudaDevice *as_cuda(hexir_device_t *device);
 
+// Page-locked host blocks, kept across executes and shared by every device
+// of the process: a module whose ops alternate between host and GPU copies
+// whole tensors both ways every execute, and page-locked memory moves them
+// at copy-engine speed without the driver's pageable staging.  take returns
+// a block of exactly `bytes` (from the pool, else newly page-locked with
+// `context` current; portable to every context), or nullptr when none can
+// be had; give returns it once no copy can still use it.  At most 8 GiB
+// stay pooled.
+void *pinned_take(size_t bytes, CUcontext context);
+void pinned_give(void *block, size_t bytes);
+
 // Reports a backend failure the way the reference does: "hexir: <message>"
 // on stderr.
 void report(const std::string &message);

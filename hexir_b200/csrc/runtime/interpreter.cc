@@ -29,6 +29,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <new>
 #include <set>
@@ -203,7 +204,10 @@ struct Slot {
   bool defined = false;
   uint64_t bytes = 0;
   const uint8_t *rodata = nullptr;  // CONST: bytes in the module mapping
-  std::vector<double> host;         // host copy
+  // Host copy: a page-locked block the Vm owns (when the execute has GPUs)
+  // or host_own's storage; never zero-filled unless the slot is zero.
+  double *host = nullptr;
+  std::unique_ptr<double[]> host_own;
   bool host_valid = false;
   bool zero = false;                // ALLOC'd and not written yet
   std::map<int, hexir_buffer_t *> dev;  // program ordinal -> buffer
@@ -232,6 +236,23 @@ struct Vm {
   Slot slots[kMaxSlots];
   std::vector<std::pair<CudaDevice *, hexir_buffer_t *>> temps;
   std::vector<Span> spans;
+  // Page-locked host blocks of this execute: they go back to the process
+  // pool at release, after settle() has drained every stream that could
+  // still copy from them (a pinned host-to-device copy is asynchronous).
+  std::vector<std::pair<void *, size_t>> pinned;
+  // Constants uploaded ahead of the dispatch that reads them, by (RODATA
+  // offset, program ordinal): the buffer and the event its upload records
+  // on the device's copy stream.  A CONST that binds the offset adopts the
+  // buffer (see prefetch_ahead).
+  struct Prefetched {
+    uint64_t bytes = 0;
+    hexir_buffer_t *buffer = nullptr;
+    CUevent ready = nullptr;
+  };
+  std::map<std::pair<uint64_t, int>, Prefetched> prefetched;
+  uint64_t prefetched_bytes = 0;
+  const uint8_t *program = nullptr;
+  uint64_t program_size = 0;
   bool trace = false;
 
   // Capture target of hexir_execute_capture and the program offset of the
@@ -254,6 +275,19 @@ struct Vm {
     for (auto &t : temps)
       hexir_buffer_release(t.second);
     temps.clear();
+    for (auto &b : pinned)
+      pinned_give(b.first, b.second);
+    pinned.clear();
+    for (auto &kv : prefetched) {
+      CudaDevice *dev = cuda[kv.first.second];
+      ContextGuard guard(dev->state->context);
+      // An upload nobody adopted (an execute that failed first).
+      driver().EventSynchronize(kv.second.ready);
+      driver().EventDestroy(kv.second.ready);
+      hexir_buffer_release(kv.second.buffer);
+    }
+    prefetched.clear();
+    prefetched_bytes = 0;
     for (Span &sp : spans) {
       ContextGuard guard(sp.device->state->context);
       driver().EventDestroy(sp.start);
@@ -386,7 +420,7 @@ struct Vm {
       return to->write_async(dst, rodata_source(s, offset, bytes), bytes);
     } else if (s.host_valid) {
       return to->write_async(
-          dst, reinterpret_cast<const uint8_t *>(s.host.data()) + offset, bytes);
+          dst, reinterpret_cast<const uint8_t *>(s.host) + offset, bytes);
     } else if (s.dev_valid.count(o)) {
       r = d.MemcpyDtoDAsync(
           dst, reinterpret_cast<CUdeviceptr>(s.dev[o]->impl) + offset, bytes,
@@ -530,23 +564,43 @@ struct Vm {
     if (s.rodata && !s.host_valid) {
       // A CONST at an offset that is not a multiple of 8 (the serializer
       // never writes one): the host kernels read an aligned copy.
-      s.host.assign((s.bytes + 7) / 8, 0.0);
-      std::memcpy(s.host.data(), s.rodata, static_cast<size_t>(s.bytes));
+      double *h = host_storage(s);
+      std::memcpy(h, s.rodata, static_cast<size_t>(s.bytes));
       s.host_valid = true;
     }
     if (!s.host_valid) {
-      s.host.assign((s.bytes + 7) / 8, 0.0);
+      double *h = host_storage(s);
       if (!s.zero && !s.dev_valid.empty()) {
+        // Every byte comes from the device copy.
         const int p = *s.dev_valid.begin();
-        hexir_status_t st = hexir_buffer_read(
-            s.dev[p], s.host.data(), static_cast<size_t>(s.bytes));
+        hexir_status_t st =
+            hexir_buffer_read(s.dev[p], h, static_cast<size_t>(s.bytes));
         if (st != HEXIR_OK)
           return st;
+      } else {
+        std::memset(h, 0, static_cast<size_t>((s.bytes + 7) / 8 * 8));
       }
       s.host_valid = true;
     }
-    *out = reinterpret_cast<const uint8_t *>(s.host.data());
+    *out = reinterpret_cast<const uint8_t *>(s.host);
     return HEXIR_OK;
+  }
+
+  // Storage for slot s's host copy, contents undefined: a page-locked block
+  // when the execute has a GPU to copy to or from, else ordinary memory.
+  double *host_storage(Slot &s) {
+    const size_t bytes = static_cast<size_t>((s.bytes + 7) / 8 * 8);
+    if (s.host)
+      return s.host;
+    void *p = cuda.empty() ? nullptr : pinned_take(bytes, cuda.front()->state->context);
+    if (p) {
+      pinned.emplace_back(p, bytes);
+      s.host = static_cast<double *>(p);
+    } else {
+      s.host_own.reset(new double[bytes / 8]);
+      s.host = s.host_own.get();
+    }
+    return s.host;
   }
 
   // The destination of a dispatch becomes valid only where it is written.
@@ -564,12 +618,12 @@ struct Vm {
     if (fault_hit(FaultSite::Alloc))
       return nullptr;
     drop_borrowed(s);
-    s.host.resize((s.bytes + 7) / 8);
+    double *h = host_storage(s);
     s.zero = false;
     s.rodata = nullptr;
     s.host_valid = true;
     s.dev_valid.clear();
-    return s.host.data();
+    return h;
   }
 
   // ---- dispatch ----------------------------------------------------------
@@ -906,7 +960,7 @@ struct Vm {
       pipeline_chunk(exe.m, i, &r0[i], &rows[i]);
     auto host_bytes = [&](Slot &s, uint64_t off, uint64_t bytes) {
       return s.rodata ? rodata_source(s, off, bytes)
-                      : reinterpret_cast<const uint8_t *>(s.host.data()) + off;
+                      : reinterpret_cast<const uint8_t *>(s.host) + off;
     };
     // Uploads of w's rows [k0, k1) and of a's columns [k0, k1) for rows
     // [ra, ra + nr), on the copy stream.
@@ -1054,6 +1108,146 @@ struct Vm {
     if (upload_w)
       ws.dev_valid.insert(o);
     written_on_device(dst, o);
+    return HEXIR_OK;
+  }
+
+  // ---- constants uploaded ahead ---------------------------------------------
+
+  // A later dispatch's constant starts uploading only once it is at least
+  // this large (smaller ones cost less than the bookkeeping), and at most
+  // kPrefetchCapBytes are in flight or waiting to be adopted.
+  static constexpr uint64_t kPrefetchMinBytes = 4ull << 20;
+  static constexpr uint64_t kPrefetchCapBytes = 8ull << 30;
+
+  // The single GPU (program ordinal) an executable runs on through the
+  // kernel library, or -1 (host, reference-convention image, row-sharded).
+  int single_gpu(uint64_t index) const {
+    if (index >= exe_count || exes[index].device != HEXIR_DEVICE_CUDA ||
+        !launches || index >= launch_count)
+      return -1;
+    const hexir_launch_entry_t &L = launches[index];
+    if (L.abi != HEXIR_LAUNCH_ABI_V1 || !(L.flags & HEXIR_LAUNCH_FLAG_LIBRARY) ||
+        L.device_count > 1 || L.device_first >= cuda.size())
+      return -1;
+    return static_cast<int>(L.device_first);
+  }
+
+  // After a dispatch is queued: the constants that later single-GPU
+  // dispatches of this entry read start uploading on their GPU's copy
+  // stream, behind the uploads the queued dispatch makes there, so they
+  // cross PCIe while its kernel runs instead of in front of the kernel
+  // that needs them.  A program binds a constant (CONST) just before its
+  // first use, so the scan records CONSTs as it meets them and matches
+  // DISPATCH operands against them; it stops at END.
+  hexir_status_t prefetch_ahead(uint64_t pc) {
+    if (cuda.empty() || !program)
+      return HEXIR_OK;
+    ModuleState *ms = module_state(module);
+    if (ms && ms->keep_constants.load())
+      return HEXIR_OK;  // kept constants are uploaded once, whole
+    std::map<uint64_t, std::pair<uint64_t, uint64_t>> const_of;  // slot -> (offset, bytes)
+    while (pc + sizeof(hexir_command_header_t) <= program_size) {
+      hexir_command_header_t h;
+      std::memcpy(&h, program + pc, sizeof(h));
+      const uint64_t at = pc + sizeof(h);
+      const uint64_t next = at + static_cast<uint64_t>(h.operand_count) * 8;
+      if (next > program_size || h.kind == HEXIR_CMD_END)
+        break;
+      auto operand = [&](uint32_t i) {
+        uint64_t v;
+        std::memcpy(&v, program + at + 8ull * i, 8);
+        return v;
+      };
+      if (h.kind == HEXIR_CMD_CONST && h.operand_count == 3) {
+        const uint64_t offset = operand(1), bytes = operand(2);
+        if (offset <= rodata_size && bytes <= rodata_size - offset)
+          const_of[operand(0)] = {offset, bytes};
+      } else if (h.kind == HEXIR_CMD_ALLOC && h.operand_count >= 1) {
+        const_of.erase(operand(0));
+      } else if (h.kind == HEXIR_CMD_DISPATCH && h.operand_count >= 3) {
+        const int o = single_gpu(operand(0));
+        // Inputs only: the last operand is the destination.
+        for (uint32_t i = 2; o >= 0 && i + 1 < h.operand_count; ++i) {
+          auto it = const_of.find(operand(i));
+          if (it == const_of.end())
+            continue;
+          const uint64_t offset = it->second.first, bytes = it->second.second;
+          if (bytes < kPrefetchMinBytes ||
+              prefetched.count({offset, o}) ||
+              prefetched_bytes + bytes > kPrefetchCapBytes)
+            continue;
+          hexir_status_t st = start_prefetch(offset, bytes, o);
+          if (st != HEXIR_OK)
+            return st;
+        }
+      }
+      pc = next;
+    }
+    return HEXIR_OK;
+  }
+
+  hexir_status_t start_prefetch(uint64_t offset, uint64_t bytes, int o) {
+    CudaDevice *dev = cuda[o];
+    CUstream cs = dev->copy_stream();
+    if (!cs)
+      return HEXIR_OK;  // no copy stream: the dispatch uploads as usual
+    hexir_buffer_t *b = nullptr;
+    if (dev->allocate_pooled(bytes, &b) != HEXIR_OK)
+      return HEXIR_OK;  // no room ahead of time: the dispatch uploads it
+    const Driver &d = driver();
+    ContextGuard guard(dev->state->context);
+    Slot view;
+    view.rodata = rodata + offset;
+    CUevent ready = nullptr;
+    CUresult r = d.MemcpyHtoDAsync(reinterpret_cast<CUdeviceptr>(b->impl),
+                                   rodata_source(view, 0, bytes), bytes, cs);
+    if (r == CUDA_SUCCESS)
+      r = d.EventCreate(&ready, CU_EVENT_DISABLE_TIMING);
+    if (r == CUDA_SUCCESS)
+      r = d.EventRecord(ready, cs);
+    if (r != CUDA_SUCCESS) {
+      d.StreamSynchronize(cs);
+      if (ready)
+        d.EventDestroy(ready);
+      hexir_buffer_release(b);
+      report(cuda_message("constant upload ahead of its dispatch", r));
+      return HEXIR_ERROR_DEVICE;
+    }
+    prefetched[{offset, o}] = Prefetched{bytes, b, ready};
+    prefetched_bytes += bytes;
+    if (trace)
+      std::fprintf(stderr, "hexir: constant at %llu (%llu bytes) uploading "
+                   "ahead to cuda:%d\n", static_cast<unsigned long long>(offset),
+                   static_cast<unsigned long long>(bytes), o);
+    return HEXIR_OK;
+  }
+
+  // A CONST just bound slot s to RODATA at `offset`: where that constant was
+  // uploaded ahead, the slot takes the buffer, and the GPU's stream waits
+  // for the upload before anything that reads it.
+  hexir_status_t adopt_prefetched(Slot &s, uint64_t offset) {
+    for (auto it = prefetched.begin(); it != prefetched.end();) {
+      if (it->first.first != offset || it->second.bytes != s.bytes) {
+        ++it;
+        continue;
+      }
+      const int o = it->first.second;
+      CudaDevice *dev = cuda[o];
+      ContextGuard guard(dev->state->context);
+      const CUresult r = driver().StreamWaitEvent(dev->stream, it->second.ready, 0);
+      driver().EventDestroy(it->second.ready);
+      if (r != CUDA_SUCCESS) {
+        hexir_buffer_release(it->second.buffer);
+        prefetched_bytes -= it->second.bytes;
+        prefetched.erase(it);
+        report(cuda_message("waiting for a constant uploaded ahead", r));
+        return HEXIR_ERROR_DEVICE;
+      }
+      s.dev[o] = it->second.buffer;
+      s.dev_valid.insert(o);
+      prefetched_bytes -= it->second.bytes;
+      it = prefetched.erase(it);
+    }
     return HEXIR_OK;
   }
 
@@ -1595,6 +1789,8 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
     return HEXIR_ERROR_NOT_FOUND;
 
   const uint8_t *program = static_cast<const uint8_t *>(program_data);
+  vm->program = program;
+  vm->program_size = program_size;
   // Find the entry's last DISPATCH: its destination is what a capture copies
   // out, so that dispatch may stream its result straight to out_result.
   if (out_result && out_size) {
@@ -1666,14 +1862,18 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
         break;
       }
       status = vm->bind(ops[0], bytes);
-      if (status == HEXIR_OK)
+      if (status == HEXIR_OK) {
         vm->slots[ops[0]].rodata = vm->rodata + offset;
+        status = vm->adopt_prefetched(vm->slots[ops[0]], offset);
+      }
       break;
     }
     case HEXIR_CMD_DISPATCH:
       status = vm->dispatch(ops.data(), header.operand_count);
       if (status == HEXIR_OK && header.operand_count >= 3)
         result_slot = static_cast<int64_t>(ops[header.operand_count - 1]);
+      if (status == HEXIR_OK)
+        status = vm->prefetch_ahead(pc);
       break;
     case HEXIR_CMD_PRINT:
       if (header.operand_count != 3)
