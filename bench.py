@@ -222,13 +222,25 @@ def cublas_dgemm_tflops(a, w, steps: int = 3) -> float:
     return 2.0 * a.shape[0] * a.shape[1] * w.shape[1] / (ms * 1e-3) / 1e12
 
 
-def cpu_reference_rate(rows: int, steps: int = 1, warmup: int = 0):
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_reference_rate(rows: int, steps: int = 1, warmup: int = 0,
+                       threads: int = 0):
     """GFLOP/s of the reference CPU kernel on `rows` rows of the workload
-    (all host threads, each on its own row slice).  Returns (gflops, threads,
-    kind, sample description, step seconds list)."""
+    (`threads` host threads, default all, each on its own row slice).
+    Returns (gflops, threads, kind, sample description, step seconds)."""
     import numpy as np
     from oracle import oracle
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     kind = "reference" if oracle.have_reference() else "port"
     rng = np.random.default_rng(SEED)
     a = rng.uniform(-1, 1, (rows, K_DIM))
@@ -263,8 +275,43 @@ def cpu_reference_rate(rows: int, steps: int = 1, warmup: int = 0):
     used = min(threads, rows)
     sample = (f"{rows} rows of the {M_PER_GPU}x{N_DIM}x{K_DIM} linear per step "
               f"(cost is linear in rows), hexir_ref_matmul_f64 on row slices, "
-              f"{used} threads")
+              f"{used} thread{'s' if used > 1 else ''} of {os.cpu_count()} "
+              f"host cores ({cpu_model()})")
     return gflops, used, kind, sample, times
+
+
+def reference_schedule_gpu(ordinal, a, w, peak, steps: int = 2) -> dict:
+    """The reference's own GPU schedule for the linear (thread per output,
+    serial k; hexir_cuda_baseline_reference_schedule_f64, a CUDA-C
+    restatement, since the reference's compiler cannot be built here) on
+    the same GPU and operands: a reported baseline."""
+    import numpy as np
+    import torch
+    import hexir_b200 as hx
+    from hexir_b200 import _ffi
+    from oracle import oracle
+    m, k = a.shape
+    n = w.shape[1]
+    c = torch.empty((m, n), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    run = lambda: _ffi.check(hx.lib().hexir_cuda_baseline_reference_schedule_f64(
+        ordinal, a.data_ptr(), w.data_ptr(), c.data_ptr(), m, n, k, stream),
+        "reference schedule")
+    ms = timed_ms(run, steps=steps, warmup=1)
+    rows = np.linspace(0, m - 1, 3).astype(int)
+    err = oracle.normwise_error(
+        c[torch.from_numpy(rows).cuda()].cpu().numpy(),
+        oracle.matmul(a[torch.from_numpy(rows).cuda()].cpu().numpy(),
+                      w.cpu().numpy()))
+    tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    return {"value": round(tf * 1e3, 3), "unit": "GFLOP/s",
+            "ms_per_launch": round(ms, 3), "frac_of_dmma_peak": round(tf / peak, 4),
+            "kernel": "hexir_baseline_reference_schedule_f64",
+            "kind": "CUDA-C restatement of the reference's generated schedule "
+                    "(thread per output, grid (n/bs, m), serial k, FMA); the "
+                    "reference compiler (MLIR, LLVM 24.0git) is not buildable "
+                    "here",
+            "normwise_err_sampled": err, "steps": steps}
 
 
 # ------------------------------------------------------------------ arms
@@ -463,6 +510,9 @@ def run_hexir(args):
 
     if rank == 0 and world == 1 and not args.no_relu:
         line["relu"] = relu_stream(ordinal)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["reference_schedule_gpu"] = reference_schedule_gpu(
+            ordinal, a, w, line["roofline"]["peak"])
 
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg,
@@ -476,6 +526,12 @@ def run_hexir(args):
         gflops, used, kind, sample, _ = cpu_reference_rate(rows, steps=1)
         line["cpu_baseline"] = {"value": round(gflops, 3), "unit": "GFLOP/s",
                                 "cores": used, "kind": kind, "sample": sample}
+        # The stock reference path is single-threaded by construction.
+        g1, _, kind1, sample1, _ = cpu_reference_rate(4, steps=1, threads=1)
+        line["cpu_baseline"]["single_thread"] = {
+            "value": round(g1, 4), "unit": "GFLOP/s", "cores": 1,
+            "kind": kind1, "sample": sample1,
+            "note": "the reference's CPU path as it ships: one thread"}
 
     if comm:
         hx.lib().hexir_comm_release(comm)

@@ -123,6 +123,8 @@ _SIGNATURES = [
     ("hexir_cuda_matmul_plan", _int, [_int, _vp, _vp, _vp, _u32, _u32, _u32,
                                       _u32, C.POINTER(_int),
                                       C.POINTER(_u32)]),
+    ("hexir_cuda_baseline_reference_schedule_f64", _int,
+     [_int, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     ("hexir_cuda_dmma_probe", _int, [_int, _vp, _u32, _u32, _vp,
                                      C.POINTER(C.c_double)]),
     ("hexir_cuda_wait_probe", _int, [_int, _u64, _vp]),

@@ -223,6 +223,11 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
       return nullptr;
     }
   }
+  // Optional: the baseline restating the reference's generated schedule.
+  if (d.ModuleGetFunction(&lib->baseline_schedule, lib->module,
+                          "hexir_baseline_reference_schedule_f64") !=
+      CUDA_SUCCESS)
+    lib->baseline_schedule = nullptr;
   // Optional: images written before the stream-K kernels existed lack them.
   if (d.ModuleGetFunction(&lib->linear_tma_sk, lib->module,
                           "hexir_linear_f64_tma_sk") != CUDA_SUCCESS ||
@@ -869,6 +874,39 @@ extern "C" hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
   if (split_k)
     *split_k = p.stream_k() ? p.sk_grid : p.split_k;
   return HEXIR_OK;
+}
+
+extern "C" hexir_status_t hexir_cuda_baseline_reference_schedule_f64(
+    int ordinal, const double *a, const double *b, double *c, uint32_t m,
+    uint32_t n, uint32_t k, void *stream) {
+  Call call;
+  if (!call.open(ordinal))
+    return call.finish(HEXIR_ERROR_DEVICE);
+  if (!call.lib->baseline_schedule) {
+    call.error = "kernel image lacks hexir_baseline_reference_schedule_f64";
+    return call.finish(HEXIR_ERROR_NOT_FOUND);
+  }
+  // The generated kernel's grid puts the rows on grid.y, which stops at
+  // 65535: larger m cannot launch in the reference either.
+  if (m > 65535u) {
+    call.error = "reference schedule: m > 65535 rows does not fit grid.y";
+    return call.finish(HEXIR_ERROR_INVALID_ARGUMENT);
+  }
+  if (!m || !n)
+    return HEXIR_OK;
+  if (!a || !b || !c) {
+    call.error = "reference schedule: null operand";
+    return call.finish(HEXIR_ERROR_INVALID_ARGUMENT);
+  }
+  uint32_t bs = 256;
+  while (bs > 1 && n % bs)
+    bs /= 2;
+  ContextGuard guard(call.dev->context);
+  void *params[] = {&a, &b, &c, &n, &k};
+  return call.finish(launch(call.lib->baseline_schedule, n / bs, m, bs, 0,
+                            static_cast<CUstream>(stream), params,
+                            "launch hexir_baseline_reference_schedule_f64",
+                            &call.error));
 }
 
 extern "C" hexir_status_t hexir_cuda_dmma_probe(int ordinal, double *out,

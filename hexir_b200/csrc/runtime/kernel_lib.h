@@ -38,6 +38,9 @@ struct KernelLib {
              softmax_b512 = nullptr, softmax_wide = nullptr,
              softmax_bulk256 = nullptr, softmax_bulk512 = nullptr;
   CUfunction dmma_probe = nullptr;
+  // The reference's generated schedule, a measurement baseline only
+  // (absent in images written before it existed).
+  CUfunction baseline_schedule = nullptr;
   CUfunction wait_probe = nullptr;
   CUdeviceptr error_word = 0;
 };

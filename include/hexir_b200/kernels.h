@@ -138,6 +138,18 @@ hexir_status_t hexir_cuda_matmul_plan(int ordinal, const double *a,
                                       uint32_t n, uint32_t k, uint32_t flags,
                                       int *variant, uint32_t *split_k);
 
+/* MEASUREMENT BASELINE, not a product path: c = a . b with the schedule the
+ * reference's compiler generates for a cuda-placed hexir.linear
+ * (compiler/Conversion/HexirToTIR/HexirToTIR.cpp:82-170), restated in CUDA
+ * C: one thread per output, grid (n / bs, m), block bs = the largest power
+ * of two <= 256 dividing n, serial k with one fused multiply-add per step,
+ * operands read from global memory.  m > 65535 is refused
+ * (INVALID_ARGUMENT), as the reference's grid.y cannot launch it.
+ * Asynchronous on `stream`. */
+hexir_status_t hexir_cuda_baseline_reference_schedule_f64(
+    int ordinal, const double *a, const double *b, double *c, uint32_t m,
+    uint32_t n, uint32_t k, void *stream);
+
 /* FP64 tensor-core throughput probe: one launch of `blocks` CTAs x 256
  * threads, each warp running `iters` rounds of 8 dependent-free DMMAs.
  * *flops receives the launch's FLOP count.  `out` must hold blocks*256 f64. */

@@ -357,3 +357,26 @@ def test_stream_k_schedule(gpu, m, n, k, flags, add):
         want = oracle.relu(want)
     assert oracle.normwise_error(outs[0][rows], want) <= TOL
     assert oracle.normwise_error(outs[0], outs[2]) <= TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 7, 9), (37, 96, 64), (128, 130, 40),
+                                   (256, 256, 256), (3, 1024, 300), (1, 1, 1)])
+def test_reference_schedule_baseline_matches_oracle(gpu, m, n, k):
+    """The measurement baseline restating the reference's generated GPU
+    schedule (thread per output, serial k, FMA-contracted) computes the
+    same product: within the linear's normwise bar (its contraction differs
+    from the CPU's separate multiply and add in the last bits)."""
+    rng = hx.Rng(71)
+    a, b = rng.uniform((m, k)), rng.uniform((k, n))
+    ba, bb, bc = gpu.upload(a), gpu.upload(b), gpu.buffer(m * n * 8)
+    _ffi.check(hx.lib().hexir_cuda_baseline_reference_schedule_f64(
+        0, ba.ptr, bb.ptr, bc.ptr, m, n, k, gpu.stream), "baseline")
+    hx.cuda_synchronize(0, gpu.stream)
+    got = bc.read((m, n))
+    assert oracle.normwise_error(got, oracle.matmul(a, b)) <= TOL
+
+
+def test_reference_schedule_baseline_refuses_what_the_reference_cannot_launch(gpu):
+    st = hx.lib().hexir_cuda_baseline_reference_schedule_f64(
+        0, 0, 0, 0, 65536, 8, 8, gpu.stream)
+    assert st == _ffi.ERROR_INVALID_ARGUMENT
