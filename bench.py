@@ -17,9 +17,10 @@ One JSON line on rank 0:
              (CUDA events on the launching stream, max over ranks)
   e2e        the same through the public API with host buffers: a .hxb module
              run by hexir_execute_capture (constants copied host->device,
-             result copied back) at N = 1; host->device copies of each rank's
-             rows, the sharded linear, result copied from GPU 0 to the host,
-             at N > 1
+             result copied back) at N = 1; hexir_sharded_linear_host_f64 at
+             N > 1 (each rank's rows of a up and of c down over its own host
+             link, the weight in per-rank slices gathered over NVLink, the
+             result rows in one shared host mapping)
   roofline   the GEMM kernel's FLOP rate against the FP64 tensor-core (DMMA)
              peak measured on this GPU by a register-only DMMA probe
   cpu_baseline  the reference's own CPU kernel (hexir_ref_matmul_f64, built
@@ -167,7 +168,7 @@ def make_w(world: int, m_rows: int):
     return rng.uniform((K_DIM, N_DIM))
 
 
-def a_rows(rows):
+def a_rows_global(rows):
     """Rows `rows` (global indices) of the synthetic a."""
     import numpy as np
     import hexir_b200 as hx
@@ -456,7 +457,7 @@ def run_hexir(args):
         rows = np.concatenate([p * m_rows + np.linspace(0, m_rows - 1, 3)
                                .astype(int) for p in range(world)])
         got = c[torch.from_numpy(rows).cuda()].cpu().numpy()
-        want = oracle.relu(oracle.matmul(a_rows(rows), w_host))
+        want = oracle.relu(oracle.matmul(a_rows_global(rows), w_host))
         err = oracle.normwise_error(got, want)
         if not err <= 1e-12:
             raise SystemExit(f"bench output wrong: normwise error {err}")
@@ -587,27 +588,49 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg, shard_flags):
         h2d = a_host.nbytes + w_host.nbytes
         d2h = m_rows * N_DIM * 8
     else:
-        a_pin = torch.from_numpy(a_host).pin_memory()
-        w_pin = torch.from_numpy(w_host).pin_memory()
-        a = torch.empty_like(a_pin, device="cuda")
-        w = torch.empty_like(w_pin, device="cuda")
-        c = torch.empty((m_total if rank == 0 else m_rows, N_DIM),
-                        dtype=torch.float64, device="cuda")
-        out = torch.empty((m_total, N_DIM), dtype=torch.float64).pin_memory() \
-            if rank == 0 else None
+        # Through hexir_sharded_linear_host_f64: every rank moves its own rows
+        # of a up and of c down over its own host link, the weight is
+        # uploaded in per-rank slices that meet over NVLink, and the rows
+        # land in one shared host mapping, so rank 0's process holds the
+        # whole result.  Inputs and result are page-locked once, outside
+        # the timed region.
+        import ctypes as C
+        lib = hx.lib()
+        begin, rows = hx.shard_rows(m_total, world, rank)
+        c_bytes = m_total * N_DIM * 8
+        obj = [None]
+        if rank == 0:
+            path = None
+            st = os.statvfs("/dev/shm") if os.path.isdir("/dev/shm") else None
+            if st and st.f_bavail * st.f_frsize > c_bytes + (1 << 30):
+                path = f"/dev/shm/hexir_bench_{os.getpid()}.f64"
+                np.memmap(path, dtype=np.float64, mode="w+",
+                          shape=(m_total, N_DIM)).flush()
+            obj = [path]
+        pg.broadcast_object_list(obj, src=0)
+        shared = obj[0]
+        if shared:
+            c_all = np.memmap(shared, dtype=np.float64, mode="r+",
+                              shape=(m_total, N_DIM))
+            c_rows = c_all[begin:begin + rows]
+        else:
+            c_all = None
+            c_rows = np.empty((rows, N_DIM))
+        a_rows = np.ascontiguousarray(a_host)
+        w_all = np.ascontiguousarray(w_host)
+        registered = []
+        for arr in (a_rows, w_all, c_rows):
+            ptr = arr.ctypes.data
+            _ffi.check(lib.hexir_host_register(ptr, arr.nbytes), "host register")
+            registered.append(ptr)
         stream = torch.cuda.current_stream().cuda_stream
+        flags = _ffi.MATMUL_RELU | _ffi.SHARD_W_ON_ALL
 
         def once():
-            a.copy_(a_pin, non_blocking=True)
-            if rank == 0:
-                w.copy_(w_pin, non_blocking=True)
-            _ffi.check(hx.lib().hexir_sharded_linear_f64(
-                comm, a.data_ptr(), w.data_ptr(), c.data_ptr(), m_total, N_DIM,
-                K_DIM, shard_flags, stream), "sharded linear")
-            if rank == 0:
-                out.copy_(c, non_blocking=True)
-            _ffi.check(hx.lib().hexir_comm_synchronize(comm, stream),
-                       "hexir_comm_synchronize")
+            _ffi.check(lib.hexir_sharded_linear_host_f64(
+                comm, a_rows.ctypes.data, w_all.ctypes.data, c_rows.ctypes.data,
+                m_total, N_DIM, K_DIM, flags, stream),
+                "hexir_sharded_linear_host_f64")
 
         for _ in range(warm):
             once()
@@ -619,16 +642,39 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg, shard_flags):
         t = torch.tensor([sec], device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         sec = float(t.item())
+        pg.barrier()
+        checked = None
+        if rank == 0 and c_all is not None:
+            # Every rank's rows as they landed in the shared result.
+            from oracle import oracle
+            sample = np.concatenate([
+                hx.shard_rows(m_total, world, r)[0] + np.array([0, m_rows // 2,
+                                                                m_rows - 1])
+                for r in range(world)])
+            want = oracle.relu(oracle.matmul(a_rows_global(sample), w_host))
+            checked = oracle.normwise_error(np.asarray(c_all[sample]), want)
+            if not checked <= 1e-12:
+                raise SystemExit(f"e2e result wrong: normwise error {checked}")
+        for ptr in registered:
+            lib.hexir_host_unregister(ptr)
+        pg.barrier()
+        if rank == 0 and shared:
+            del c_all, c_rows
+            os.unlink(shared)
         h2d = a_host.nbytes * world + w_host.nbytes
         d2h = m_total * N_DIM * 8
+        path_desc = ("hexir_sharded_linear_host_f64: each rank's host rows "
+                     "of a up and of c down over its own host link, w in "
+                     "per-rank slices all-gathered over NVLink, result rows "
+                     "in one shared host mapping" + (
+                         "" if shared else " (per-rank host rows: /dev/shm "
+                                           "too small for a shared one)"))
     value = 2.0 * m_total * N_DIM * K_DIM / sec / 1e9
     return {"value": round(value, 3), "unit": "GFLOP/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(sec * 1e3, 3),
             "path": ("hexir_execute_capture of a .hxb (linear=cuda, relu=cuda)"
-                     if world == 1 else
-                     "pinned host rows -> hexir_sharded_linear_f64 -> pinned "
-                     "host result on rank 0"),
+                     if world == 1 else path_desc),
             "timing": "host wall clock around synchronous calls, max over ranks"}
 
 

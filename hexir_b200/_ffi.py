@@ -38,6 +38,7 @@ MATMUL_REMOTE_OUTPUT = 0x400
 MATMUL_NO_STREAM_K = 0x800
 MATMUL_FORCE_STREAM_K = 0x2000
 SHARD_GATHER_NCCL = 0x1000
+SHARD_W_ON_ALL = 0x4000
 
 # Activation codes = kernel kinds 7-14 (include/hexir_runtime/program.h).
 ACTIVATIONS = {"leaky_relu": 7, "elu": 8, "sigmoid": 9, "tanh": 10,
@@ -143,6 +144,10 @@ _SIGNATURES = [
     ("hexir_comm_size", _int, [_vp]),
     ("hexir_comm_direct_stores", _int, [_vp]),
     ("hexir_comm_synchronize", _int, [_vp, _vp]),
+    ("hexir_sharded_linear_host_f64", _int, [_vp, _vp, _vp, _vp, _u32, _u32,
+                                             _u32, _u32, _vp]),
+    ("hexir_host_register", _int, [_vp, _sz]),
+    ("hexir_host_unregister", _int, [_vp]),
     ("hexir_shard_gather_pieces", _int, [_u64, _u32, C.POINTER(_u64),
                                          C.POINTER(_u64), C.POINTER(_u32)]),
     ("hexir_shard_weight_pieces", _int, [_u32, _u32, C.POINTER(_u32),

@@ -20,6 +20,19 @@ namespace {
 // every transfer but the last hides behind the GEMM of the next piece and the
 // exposed last one is small.  Pieces keep >= kMinChunkRows rows.
 constexpr uint32_t kGatherChunks = HEXIR_SHARD_MAX_GATHER_PIECES;
+// hexir_sharded_linear_host_f64 moves a rank's rows through its host link
+// in kHostChunks row chunks: 1/8, 1/4, 1/4, 1/4, 1/8 of the rows (whole
+// 128-row tiles), so the first upload that compute waits for and the last
+// download left after it are each an eighth.
+constexpr uint32_t kHostChunks = 5;
+void host_chunk(uint64_t rows, uint32_t i, uint64_t *begin, uint64_t *count) {
+  static const uint32_t eighths[kHostChunks + 1] = {0, 1, 3, 5, 7, 8};
+  auto bound = [&](uint32_t j) {
+    return j == kHostChunks ? rows : (rows * eighths[j] / 8) / 128 * 128;
+  };
+  *begin = bound(i);
+  *count = bound(i + 1) - *begin;
+}
 constexpr uint64_t kMinChunkRows = 256;
 
 // Piece `i` of `rows` rows: [*begin, *begin + *count).  Returns the number of
@@ -99,6 +112,13 @@ struct hexir_comm_t {
   MappedOutput mapped[kMaxMapped] = {};
   size_t mapped_count = 0;
   uint64_t calls = 0;
+  // hexir_sharded_linear_host_f64: streams for this GPU's host link (one
+  // each way), its events, and device workspace kept between calls.
+  CUstream up_stream = nullptr, down_stream = nullptr;
+  CUevent w_uploaded = nullptr, w_ready = nullptr, down_done = nullptr;
+  CUevent a_ready[kHostChunks] = {}, c_ready[kHostChunks] = {};
+  CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
+  size_t a_bytes = 0, w_bytes = 0, c_bytes = 0;
 };
 
 namespace {
@@ -224,6 +244,26 @@ uint32_t broadcast_pieces(uint32_t k, uint32_t ranks, uint32_t bounds[3]) {
   bounds[1] = 512;
   bounds[2] = k;
   return 2;
+}
+
+// Device workspace `*p` of at least `bytes` (kept between calls, grown as
+// needed once the streams that used it are idle).
+CUresult ensure_buffer(CUdeviceptr *p, size_t *have, size_t bytes) {
+  if (*have >= bytes)
+    return CUDA_SUCCESS;
+  const Driver &d = driver();
+  if (*p) {
+    CUresult r = d.CtxSynchronize();
+    if (r != CUDA_SUCCESS)
+      return r;
+    d.MemFree(*p);
+    *p = 0;
+    *have = 0;
+  }
+  CUresult r = d.MemAlloc(p, bytes ? bytes : 16);
+  if (r == CUDA_SUCCESS)
+    *have = bytes;
+  return r;
 }
 
 CUdeviceptr failure_word(const hexir_comm_t *comm) {
@@ -359,9 +399,19 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kDescSlots; ++i)
     cr = d.EventCreate(&comm->desc_done[i], CU_EVENT_DISABLE_TIMING);
   for (CUevent *ev : {&comm->w_start, &comm->w_piece[0], &comm->w_piece[1],
-                      &comm->w_done})
+                      &comm->w_done, &comm->w_uploaded, &comm->w_ready,
+                      &comm->down_done})
     if (cr == CUDA_SUCCESS)
       cr = d.EventCreate(ev, CU_EVENT_DISABLE_TIMING);
+  for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kHostChunks; ++i) {
+    cr = d.EventCreate(&comm->a_ready[i], CU_EVENT_DISABLE_TIMING);
+    if (cr == CUDA_SUCCESS)
+      cr = d.EventCreate(&comm->c_ready[i], CU_EVENT_DISABLE_TIMING);
+  }
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamCreate(&comm->up_stream, CU_STREAM_NON_BLOCKING);
+  if (cr == CUDA_SUCCESS)
+    cr = d.StreamCreate(&comm->down_stream, CU_STREAM_NON_BLOCKING);
   if (cr == CUDA_SUCCESS)
     cr = d.MemAlloc(&comm->scratch, kDescBytes + 16);
   if (cr == CUDA_SUCCESS)
@@ -426,6 +476,21 @@ void hexir_comm_release(hexir_comm_t *comm) {
       d.MemFreeHost(comm->desc_host);
     if (comm->scratch)
       d.MemFree(comm->scratch);
+    for (CUstream st : {comm->up_stream, comm->down_stream})
+      if (st) {
+        d.StreamSynchronize(st);
+        d.StreamDestroy(st);
+      }
+    for (CUevent ev : {comm->w_uploaded, comm->w_ready, comm->down_done})
+      if (ev)
+        d.EventDestroy(ev);
+    for (uint32_t i = 0; i < kHostChunks; ++i)
+      for (CUevent ev : {comm->a_ready[i], comm->c_ready[i]})
+        if (ev)
+          d.EventDestroy(ev);
+    for (CUdeviceptr p : {comm->a_dev, comm->w_dev, comm->c_dev})
+      if (p)
+        d.MemFree(p);
   }
   if (comm->comm && nccl().ok)
     nccl().CommDestroy(comm->comm);
@@ -667,6 +732,219 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       status = rs;
   }
   return status;
+}
+
+hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
+                                             const double *a_rows,
+                                             const double *w, double *c_rows,
+                                             uint32_t m, uint32_t n, uint32_t k,
+                                             uint32_t flags, void *stream) {
+  if (!comm)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  const uint32_t ranks = static_cast<uint32_t>(comm->nranks);
+  const uint32_t rank = static_cast<uint32_t>(comm->rank);
+  const bool w_everywhere = (flags & HEXIR_SHARD_W_ON_ALL) != 0;
+  uint64_t begin = 0, rows = 0;
+  hexir_shard_rows(m, ranks, rank, &begin, &rows);
+  // Argument errors are the caller's on every rank alike (same m, n, k,
+  // flags), so returning before any collective leaves no rank waiting.
+  if ((rows && (!a_rows || !c_rows)) ||
+      ((rank == 0 || w_everywhere) && !w && k && n))
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  std::string error;
+  DeviceState *dev = device_state(comm->ordinal, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  KernelLib *lib = embedded_library(dev, &error);
+  if (!lib) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ContextGuard guard(dev->context);
+  const Driver &d = driver();
+  const Nccl &nc = nccl();
+  CUstream s = static_cast<CUstream>(stream);
+  CUstream up = comm->up_stream, down = comm->down_stream;
+  CUstream gs = comm->gather_stream;
+  const size_t row_a = static_cast<size_t>(k) * 8, row_c = static_cast<size_t>(n) * 8;
+  const size_t w_size = static_cast<size_t>(k) * row_c;
+  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
+
+  bool failed = false;
+  auto note = [&](CUresult r, const char *what) {
+    if (r != CUDA_SUCCESS && !failed) {
+      failed = true;
+      error = cuda_message(what, r);
+    }
+    return r == CUDA_SUCCESS;
+  };
+  // 0. Workspace, agreed on: the weight gather below needs a buffer on
+  //    every rank, so every rank learns whether any rank could not get its
+  //    own (one word max-reduced and read back) and all return together.
+  note(ensure_buffer(&comm->a_dev, &comm->a_bytes, rows * row_a), "cuMemAlloc (rows of a)");
+  if (!failed)
+    note(ensure_buffer(&comm->w_dev, &comm->w_bytes, w_size), "cuMemAlloc (weight)");
+  if (!failed)
+    note(ensure_buffer(&comm->c_dev, &comm->c_bytes, rows * row_c), "cuMemAlloc (rows of c)");
+  if (ranks > 1) {
+    hexir_status_t st = reduce_failure(comm, s, failed);
+    if (st == HEXIR_OK)
+      st = hexir_comm_synchronize(comm, stream);
+    if (failed || st != HEXIR_OK) {
+      if (failed)
+        set_last_error(error);
+      return failed ? HEXIR_ERROR_OUT_OF_MEMORY : st;
+    }
+  } else if (failed) {
+    set_last_error(error);
+    return HEXIR_ERROR_OUT_OF_MEMORY;
+  }
+  // From here a failure skips this rank's own work but still takes every
+  // collective step: the weight gather and the failure word's reduction.
+
+  // 1. The weight.  Every rank holding it uploads its own k slice over its
+  //    own host link and the slices meet over NVLink (one broadcast per
+  //    slice, grouped: an all-gather of unequal slices); otherwise the root
+  //    uploads it whole and broadcasts it.  It is the first thing on the
+  //    upload stream: every chunk's GEMM waits for it.
+  //    Every copy waits for the caller's queued work (it may still read the
+  //    workspace a previous call left).
+  CUevent start = comm->w_start;
+  if (!failed)
+    note(d.EventRecord(start, s), "cuEventRecord");
+  if (!failed)
+    note(d.StreamWaitEvent(up, start, 0), "cuStreamWaitEvent");
+  if (!failed)
+    note(d.StreamWaitEvent(down, start, 0), "cuStreamWaitEvent");
+  uint64_t kb = 0, kc = k;
+  if (w_everywhere)
+    hexir_shard_rows(k, ranks, rank, &kb, &kc);
+  const bool uploads_w = w_everywhere || rank == 0;
+  if (!failed && uploads_w && kc)
+    note(d.MemcpyHtoDAsync(comm->w_dev + kb * row_c, w + kb * n, kc * row_c, up),
+         "weight upload");
+  if (!failed)
+    note(d.EventRecord(comm->w_uploaded, up), "cuEventRecord");
+  if (!failed)
+    note(d.StreamWaitEvent(gs, comm->w_uploaded, 0), "cuStreamWaitEvent");
+  if (ranks > 1) {
+    void *wd = reinterpret_cast<void *>(comm->w_dev);
+    cudaStream_t g = reinterpret_cast<cudaStream_t>(gs);
+    ncclResult_t nr = ncclSuccess;
+    if (w_everywhere) {
+      nc.GroupStart();
+      for (uint32_t r = 0; r < ranks; ++r) {
+        uint64_t rb = 0, rc = 0;
+        hexir_shard_rows(k, ranks, r, &rb, &rc);
+        if (!rc)
+          continue;
+        void *piece = static_cast<char *>(wd) + rb * row_c;
+        nc.Broadcast(piece, piece, rc * n, ncclDouble, static_cast<int>(r),
+                     comm->comm, g);
+      }
+      nr = nc.GroupEnd();
+    } else {
+      nr = nc.Broadcast(wd, wd, w_size / 8, ncclDouble, 0, comm->comm, g);
+    }
+    if (nr != ncclSuccess && !failed) {
+      failed = true;
+      error = nccl_message("weight gather", nr);
+    }
+  }
+  d.EventRecord(comm->w_ready, gs);
+
+  // 2. This rank's rows in chunks: each chunk uploads behind the weight and
+  //    the chunks before it, computes once both are in, and downloads into
+  //    c_rows while the next computes.  Every chunk runs the k split of one
+  //    launch over all the rank's rows, so the bits are that launch's.
+  const MatmulPlan plan = plan_matmul(
+      dev, reinterpret_cast<const double *>(comm->a_dev),
+      reinterpret_cast<const double *>(comm->w_dev),
+      reinterpret_cast<const double *>(comm->c_dev), static_cast<uint32_t>(rows),
+      n, k, relu);
+  const uint32_t chunk_flags = relu | HEXIR_MATMUL_SPLIT_K(plan.split_k);
+  if (!failed)
+    note(d.StreamWaitEvent(s, comm->w_ready, 0), "cuStreamWaitEvent");
+  for (uint32_t i = 0; i < kHostChunks && !failed; ++i) {
+    uint64_t cb = 0, cnt = 0;
+    host_chunk(rows, i, &cb, &cnt);
+    if (!cnt)
+      continue;
+    if (!note(d.MemcpyHtoDAsync(comm->a_dev + cb * row_a, a_rows + cb * k,
+                                cnt * row_a, up),
+              "row upload") ||
+        !note(d.EventRecord(comm->a_ready[i], up), "cuEventRecord") ||
+        !note(d.StreamWaitEvent(s, comm->a_ready[i], 0), "cuStreamWaitEvent"))
+      break;
+    hexir_status_t st = launch_matmul(
+        dev, lib, reinterpret_cast<const double *>(comm->a_dev + cb * row_a),
+        reinterpret_cast<const double *>(comm->w_dev),
+        reinterpret_cast<double *>(comm->c_dev + cb * row_c),
+        static_cast<uint32_t>(cnt), n, k, chunk_flags, s, &error);
+    if (st != HEXIR_OK) {
+      failed = true;
+      break;
+    }
+    if (!note(d.EventRecord(comm->c_ready[i], s), "cuEventRecord") ||
+        !note(d.StreamWaitEvent(down, comm->c_ready[i], 0), "cuStreamWaitEvent") ||
+        !note(d.MemcpyDtoHAsync(c_rows + cb * n, comm->c_dev + cb * row_c,
+                                cnt * row_c, down),
+              "row download"))
+      break;
+  }
+  // The caller's stream ends after the downloads (and the weight gather).
+  d.EventRecord(comm->down_done, down);
+  d.StreamWaitEvent(s, comm->down_done, 0);
+  if (failed)
+    set_last_error(error.empty() ? "sharded linear (host buffers) failed" : error);
+  hexir_status_t rs = HEXIR_OK;
+  if (ranks > 1)
+    rs = reduce_failure(comm, s, failed);
+  // 3. Synchronous: the rows are in c_rows on return, and a failure on any
+  //    rank is reported on every rank.
+  hexir_status_t ss = hexir_comm_synchronize(comm, stream);
+  if (failed)
+    return HEXIR_ERROR_DEVICE;
+  return rs != HEXIR_OK ? rs : ss;
+}
+
+hexir_status_t hexir_host_register(void *ptr, size_t bytes) {
+  if (!ptr || !bytes)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  const Driver &d = driver();
+  if (!d.ok) {
+    set_last_error(d.error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  std::string error;
+  DeviceState *dev = device_state(0, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ContextGuard guard(dev->context);
+  const CUresult r = d.MemHostRegister(ptr, bytes, CU_MEMHOSTREGISTER_PORTABLE);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("cuMemHostRegister", r));
+  return HEXIR_OK;
+}
+
+hexir_status_t hexir_host_unregister(void *ptr) {
+  if (!ptr)
+    return HEXIR_ERROR_INVALID_ARGUMENT;
+  std::string error;
+  DeviceState *dev = device_state(0, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ContextGuard guard(dev->context);
+  const CUresult r = driver().MemHostUnregister(ptr);
+  if (r != CUDA_SUCCESS)
+    return comm_fail(cuda_message("cuMemHostUnregister", r));
+  return HEXIR_OK;
 }
 
 hexir_status_t hexir_comm_synchronize(hexir_comm_t *comm, void *stream) {

@@ -117,6 +117,50 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
                                         uint32_t n, uint32_t k, uint32_t flags,
                                         void *stream);
 
+/* hexir_sharded_linear_host_f64 flag: every rank passes the whole weight
+ * (the same values) and uploads only its share of its rows. */
+#define HEXIR_SHARD_W_ON_ALL 0x4000u
+
+/* The row-sharded linear with HOST buffers, for one process per GPU: the
+ * call a program makes when its operands and result live in host memory.
+ * Collective over all ranks of `comm`:
+ *   a_rows  this rank's rows of a [rows x k], rows = hexir_shard_rows(m,
+ *           size, rank);
+ *   w       [k x n] on the root; with HEXIR_SHARD_W_ON_ALL on every rank
+ *           (NULL elsewhere is allowed);
+ *   c_rows  where this rank's rows of c [rows x n] go.
+ * flags: HEXIR_MATMUL_RELU, HEXIR_SHARD_W_ON_ALL.
+ *
+ * Each rank moves its own rows over its own host link, so the copies of
+ * all ranks run side by side: its rows of a upload in chunks, each chunk
+ * computing as soon as it and the weight are in and downloading into
+ * c_rows while the next computes.  The weight crosses a host link once:
+ * the root uploads it and broadcasts it over NVLink, or, with
+ * HEXIR_SHARD_W_ON_ALL, every rank uploads rows hexir_shard_rows(k, size,
+ * rank) of it and the slices meet over NVLink.  To hold the whole result in
+ * one process, pass each rank a pointer into one shared mapping (rank r at
+ * row hexir_shard_rows(m, size, r)).  Host memory that is page-locked
+ * (hexir_host_register, or cuMemHostAlloc) moves at copy-engine speed;
+ * pageable memory works, slower.  Each chunk runs the k split of one launch
+ * over the rank's rows, so c_rows holds that launch's bits.  Device
+ * workspace is kept in `comm` between calls.
+ *
+ * Synchronous: returns once this rank's rows are in c_rows, with
+ * HEXIR_ERROR_DEVICE on every rank if any rank's part failed (as
+ * hexir_comm_synchronize reports), HEXIR_ERROR_OUT_OF_MEMORY on every rank
+ * if any rank could not get its workspace.  `stream` orders the call after
+ * the caller's work on it. */
+hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
+                                             const double *a_rows,
+                                             const double *w, double *c_rows,
+                                             uint32_t m, uint32_t n, uint32_t k,
+                                             uint32_t flags, void *stream);
+
+/* Page-lock (and unlock) an existing host range for fast copies to and from
+ * every GPU of the process (cuMemHostRegister, portable). */
+hexir_status_t hexir_host_register(void *ptr, size_t bytes);
+hexir_status_t hexir_host_unregister(void *ptr);
+
 /* Waits for `stream` and returns HEXIR_ERROR_DEVICE on every rank if any
  * rank's part of any hexir_sharded_linear_f64 call on `comm` failed since
  * the last hexir_comm_synchronize (or a kernel on this GPU reported a device

@@ -205,3 +205,113 @@ def test_peer_failure_reaches_every_rank(tmp_path, gather, k):
     for r in (r0, r1):
         assert r["call_clean"] == _ffi.OK and r["sync_clean"] == _ffi.OK
     assert r0["err"] <= TOL
+
+
+def _host_rank(rank, world, port, m, n, k, flags, result_path):
+    """hexir_sharded_linear_host_f64: every rank hands in host rows of a
+    (page-locked), the weight (root only, or every rank with
+    SHARD_W_ON_ALL) and gets its rows of c back in host memory."""
+    import torch.distributed as dist
+    from hexir_b200 import _ffi
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = _comm(rank, world, dist)
+    lib = hx.lib()
+    rng = hx.Rng(43)
+    a = rng.uniform((m, k))
+    w = rng.uniform((k, n))
+    begin, rows = hx.shard_rows(m, world, rank)
+    a_rows = np.ascontiguousarray(a[begin:begin + rows])
+    c_rows = np.full((max(rows, 1), n), np.nan)
+    for arr in (a_rows, c_rows):
+        _ffi.check(lib.hexir_host_register(arr.ctypes.data, arr.nbytes),
+                   "host register")
+    w_arg = w.ctypes.data if (rank == 0 or flags & _ffi.SHARD_W_ON_ALL) else None
+    dev = hx.Device(f"cuda:{rank}")
+    statuses = []
+    for _ in range(2):  # twice: the workspace kept in comm is reused
+        c_rows[:] = np.nan
+        statuses.append(lib.hexir_sharded_linear_host_f64(
+            comm, a_rows.ctypes.data, w_arg, c_rows.ctypes.data, m, n, k,
+            flags, dev.stream))
+    for arr in (a_rows, c_rows):
+        lib.hexir_host_unregister(arr.ctypes.data)
+    lib.hexir_comm_release(comm)
+    # Rank 0 assembles every rank's rows (gloo) and checks them.
+    got = [None] * world
+    dist.all_gather_object(got, (begin, rows, c_rows[:rows].copy(), statuses))
+    if rank == 0:
+        from oracle import oracle
+        c = np.full((m, n), np.nan)
+        all_ok = True
+        for b, r, block, st in got:
+            c[b:b + r] = block
+            all_ok &= all(s == _ffi.OK for s in st)
+        # One launch per rank's block on this GPU alone: the bits to match.
+        single = np.empty((m, n))
+        bw = dev.upload(w)
+        for b, r, _, _ in got:
+            if not r:
+                continue
+            xa = dev.upload(a[b:b + r])
+            xc = dev.buffer(r * n * 8)
+            hx.cuda_matmul(0, xa.ptr, bw.ptr, xc.ptr, r, n, k,
+                           flags & _ffi.MATMUL_RELU, dev.stream)
+            hx.cuda_synchronize(0, dev.stream)
+            single[b:b + r] = xc.read((r, n))
+        sample = np.unique(np.linspace(0, m - 1, min(m, 48)).astype(int))
+        want = oracle.matmul(a[sample], w)
+        if flags & _ffi.MATMUL_RELU:
+            want = oracle.relu(want)
+        np.save(result_path, np.array([{
+            "ok": bool(all_ok), "nan": bool(np.isnan(c).any()),
+            "bits": bool(np.array_equal(c.view(np.uint64), single.view(np.uint64))),
+            "err": oracle.normwise_error(c[sample], want)}], dtype=object))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _comm(rank, world, dist):
+    from hexir_b200 import _ffi
+    lib = hx.lib()
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        _ffi.check(lib.hexir_comm_unique_id(uid, 128), "unique id")
+    obj = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    uid = C.create_string_buffer(obj[0], 128)
+    comm = C.c_void_p()
+    _ffi.check(lib.hexir_comm_init_rank(uid, 128, world, rank, rank,
+                                        C.byref(comm)), "comm init")
+    return comm.value
+
+
+def _check_host_result(path):
+    r = np.load(path, allow_pickle=True)[0]
+    assert r["ok"]
+    assert not r["nan"]
+    assert r["bits"]
+    assert r["err"] <= TOL
+
+
+@pytest.mark.parametrize("m,n,k,flags", [
+    (1000, 384, 512, _ffi.MATMUL_RELU),
+    (2048 + 130, 256, 1024, 0),
+    (3, 130, 96, _ffi.MATMUL_RELU)])
+def test_host_buffer_sharded_linear_one_rank(tmp_path, m, n, k, flags):
+    """One rank (one GPU): the chunked upload / compute / download path."""
+    path = str(tmp_path / "out.npy")
+    spawn_ranks(_host_rank, 1, (m, n, k, flags, path))
+    _check_host_result(path)
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+@pytest.mark.parametrize("m,n,k", [(1000, 384, 512), (4096 + 7, 1024, 2048),
+                                   (3, 130, 96)])
+@pytest.mark.parametrize("w_mode", [0, _ffi.SHARD_W_ON_ALL])
+def test_host_buffer_sharded_linear_two_ranks(tmp_path, m, n, k, w_mode):
+    path = str(tmp_path / "out.npy")
+    spawn_ranks(_host_rank, 2, (m, n, k, _ffi.MATMUL_RELU | w_mode, path))
+    _check_host_result(path)
