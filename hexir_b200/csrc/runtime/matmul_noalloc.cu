@@ -28,6 +28,12 @@
 #include "kernel_lib.h"
 
 // The device code this path launches: its own copy of the linear kernels.
+// The error word below is this copy's own, and nothing reads it: only the
+// TMA kernels' bounded mbarrier waits ever set it, and this path launches
+// just the guarded kernel (double-buffered through __syncthreads) and the
+// split-K reduction, neither of which waits on anything.  A variant of this
+// path that launched a kernel with a bounded wait would have to read it
+// back (cudaMemcpyFromSymbol) to report a timeout.
 extern "C" {
 __device__ unsigned int hexir_device_error_word = 0u;
 }
@@ -136,7 +142,7 @@ extern "C" hexir_status_t hexir_cuda_matmul_f64_noalloc(
   args.k_tiles = p.k_tiles;
   args.split_k = p.split_k;
   args.k_tiles_per_split = p.k_tiles_per_split;
-  args.timeout_ns = 4000000000ull;
+  args.timeout_ns = 4000000000ull;  // unused: the guarded kernel has no waits
 
   cudaError_t e = cudaSuccess;
   if (k == 0) {
