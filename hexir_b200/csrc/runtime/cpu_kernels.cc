@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstddef>
 #include <cstdint>
+#include <cstring>
 #include <thread>
 #include <vector>
 
@@ -75,6 +76,18 @@ void cpu_add_f64(const double *a, const double *b, double *c, size_t n) {
     const size_t end = std::min<size_t>(n, r1 * kElementsPerRange);
     for (size_t i = r0 * kElementsPerRange; i < end; ++i)
       c[i] = a[i] + b[i];
+  });
+}
+
+void parallel_copy(void *dst, const void *src, size_t bytes) {
+  constexpr uint64_t kBytesPerRange = 1u << 20;
+  const uint64_t ranges = (bytes + kBytesPerRange - 1) / kBytesPerRange;
+  // 2^22 "work" per thread at least: a range counts its bytes / 64.
+  parallel_rows(ranges, kBytesPerRange / 64, [=](uint64_t r0, uint64_t r1) {
+    const size_t b0 = r0 * kBytesPerRange;
+    const size_t b1 = std::min<size_t>(bytes, r1 * kBytesPerRange);
+    std::memcpy(static_cast<char *>(dst) + b0,
+                static_cast<const char *>(src) + b0, b1 - b0);
   });
 }
 

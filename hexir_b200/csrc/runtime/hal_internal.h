@@ -123,6 +123,9 @@ void cpu_matmul_f64(const double *a, const double *b, double *c, uint32_t m,
                     uint32_t n, uint32_t k);
 void cpu_add_f64(const double *a, const double *b, double *c, size_t n);
 void cpu_relu_f64(const double *x, double *y, size_t n);
+// memcpy over the host threads (large copies between host buffers, e.g.
+// out of page-locked staging into a caller's pageable memory).
+void parallel_copy(void *dst, const void *src, size_t bytes);
 // y = op(x) over a row-major [rows x cols] tensor for the activation kernel
 // kinds 7-14 of program.h (softmax along each row).
 void cpu_activation_f64(uint32_t kind, const double *x, double *y,

@@ -35,6 +35,7 @@
 #include <set>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "cuda_driver.h"
@@ -260,6 +261,13 @@ struct Vm {
   // last dispatch copies its rows out as they finish (see run_pipelined).
   void *capture_out = nullptr;
   size_t capture_size = 0;
+  // A capture buffer that is not page-locked: results land in a pooled
+  // page-locked block (capture_out) and reach the caller's memory
+  // (capture_user) by host-thread copies, chunk by chunk as each finished
+  // chunk's download completes (staged_chunks: offset, bytes, event).
+  void *capture_user = nullptr;
+  std::vector<std::tuple<uint64_t, uint64_t, CUevent>> staged_chunks;
+  size_t staged_copied = 0;
   uint64_t last_dispatch_pc = UINT64_MAX;
   uint64_t current_pc = 0;
   bool capture_done = false;
@@ -275,6 +283,12 @@ struct Vm {
     for (auto &t : temps)
       hexir_buffer_release(t.second);
     temps.clear();
+    for (auto &chunk : staged_chunks) {
+      ContextGuard guard(cuda.front()->state->context);
+      driver().EventSynchronize(std::get<2>(chunk));
+      driver().EventDestroy(std::get<2>(chunk));
+    }
+    staged_chunks.clear();
     for (auto &b : pinned)
       pinned_give(b.first, b.second);
     pinned.clear();
@@ -1095,6 +1109,18 @@ struct Vm {
           release_events();
           return HEXIR_ERROR_DEVICE;
         }
+        if (capture_user) {
+          // Outlives this dispatch: the chunk's host copy waits on it.
+          CUevent landed = nullptr;
+          if (d.EventCreate(&landed, CU_EVENT_DISABLE_TIMING) != CUDA_SUCCESS ||
+              d.EventRecord(landed, cs) != CUDA_SUCCESS) {
+            if (landed)
+              d.EventDestroy(landed);
+            release_events();
+            return HEXIR_ERROR_DEVICE;
+          }
+          staged_chunks.emplace_back(begin, bytes, landed);
+        }
       }
       capture_done = true;
     }
@@ -1656,6 +1682,54 @@ struct Vm {
   }
 
   // Wait for every GPU, collect kernel error words and span timings.
+  // Page-locked host memory (registered or allocated by the driver)?
+  bool page_locked(const void *p) {
+    if (cuda.empty())
+      return false;
+    ContextGuard guard(cuda.front()->state->context);
+    unsigned int type = 0;
+    return driver().PointerGetAttribute(
+               &type, CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
+               reinterpret_cast<CUdeviceptr>(p)) == CUDA_SUCCESS &&
+           type == CU_MEMORYTYPE_HOST;
+  }
+
+  // Large captures into pageable memory go through a page-locked block.
+  void stage_capture(void *out, size_t size) {
+    capture_out = out;
+    capture_size = size;
+    constexpr size_t kStageMinBytes = 1u << 20;
+    if (cuda.empty() || size < kStageMinBytes || page_locked(out))
+      return;
+    void *stage = pinned_take(size, cuda.front()->state->context);
+    if (!stage)
+      return;  // the downloads go to `out` directly, at pageable speed
+    pinned.emplace_back(stage, size);
+    capture_user = out;
+    capture_out = stage;
+  }
+
+  // Streamed chunks of the capture, each copied to the caller's memory once
+  // its download has landed (the later ones may still be computing).
+  hexir_status_t drain_staged() {
+    const Driver &d = driver();
+    hexir_status_t st = HEXIR_OK;
+    for (auto &chunk : staged_chunks) {
+      const uint64_t off = std::get<0>(chunk), bytes = std::get<1>(chunk);
+      CUevent ev = std::get<2>(chunk);
+      ContextGuard guard(cuda.front()->state->context);
+      if (d.EventSynchronize(ev) != CUDA_SUCCESS)
+        st = HEXIR_ERROR_DEVICE;
+      else if (st == HEXIR_OK)
+        parallel_copy(static_cast<uint8_t *>(capture_user) + off,
+                      static_cast<const uint8_t *>(capture_out) + off, bytes);
+      d.EventDestroy(ev);
+      staged_copied += bytes;
+    }
+    staged_chunks.clear();
+    return st;
+  }
+
   hexir_status_t settle() {
     hexir_status_t result = HEXIR_OK;
     for (CudaDevice *dev : cuda) {
@@ -1807,8 +1881,7 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
         break;
       scan = next;
     }
-    vm->capture_out = out_result;
-    vm->capture_size = out_size;
+    vm->stage_capture(out_result, out_size);
   }
   hexir_status_t status = HEXIR_OK;
   int64_t result_slot = -1;
@@ -1834,12 +1907,18 @@ hexir_status_t execute_unguarded(const hexir_module_t *module,
 
     switch (header.kind) {
     case HEXIR_CMD_END: {
+      hexir_status_t drained = vm->drain_staged();
       hexir_status_t settled = vm->settle();
       if (settled != HEXIR_OK)
         return settled;
-      if (out_result && out_size && result_slot >= 0 && !vm->capture_done)
-        status = vm->capture(static_cast<uint64_t>(result_slot), out_result,
-                             out_size);
+      if (drained != HEXIR_OK)
+        return drained;
+      if (out_result && out_size && result_slot >= 0 && !vm->capture_done) {
+        status = vm->capture(static_cast<uint64_t>(result_slot),
+                             vm->capture_out, out_size);
+        if (status == HEXIR_OK && vm->capture_user)
+          parallel_copy(vm->capture_user, vm->capture_out, out_size);
+      }
       return status;
     }
     case HEXIR_CMD_ALLOC:

@@ -194,17 +194,68 @@ def test_weight_streamed_pipeline_is_bit_identical(gpu, m, n, k, capture_rows):
 
 def test_relu_stream_2_28_bit_exact():
     """relu on 2^28 f64 ~ N(0,1) seed 4 as tensor<16384x16384xf64>: bit-exact
-    against the CPU relu (compared in place, no second big host copy)."""
+    against the oracle's relu of the same bytes."""
     n = 1 << 28
     x = hx.Rng(4).normal(n)
     dev = hx.Device("cuda")
     bx, by = dev.upload(x), dev.buffer(n * 8)
     hx.cuda_relu(0, bx.ptr, by.ptr, n, dev.stream)
     hx.cuda_synchronize(0, dev.stream)
+    del bx
     got = by.read(n)
-    np.maximum(x, 0.0, out=x)  # x > 0 ? x : 0 for finite non-NaN inputs
-    x[x == 0] = 0.0            # -0.0 -> +0.0 as the reference relu
-    assert np.array_equal(bits(got), bits(x))
+    del by
+    want = oracle.relu(x)
+    del x
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_linear_8192_every_tile_against_oracle():
+    """The headline shape, 8192^3 with relu (seed 1, a then w): one row of
+    every 128-row tile, at a different offset inside each tile, against the
+    oracle over all 8192 columns -- every output tile of the launch is
+    sampled."""
+    size = 8192
+    r = hx.Rng(1)
+    a, w = r.uniform((size, size)), r.uniform((size, size))
+    dev = hx.Device("cuda")
+    ba, bw, bc = dev.upload(a), dev.upload(w), dev.buffer(size * size * 8)
+    hx.cuda_matmul(0, ba.ptr, bw.ptr, bc.ptr, size, size, size,
+                   _ffi.MATMUL_RELU, dev.stream)
+    hx.cuda_synchronize(0, dev.stream)
+    del ba, bw
+    got = bc.read((size, size))
+    rows = np.array([t * 128 + (t * 37) % 128 for t in range(size // 128)])
+    want = oracle.relu(oracle.matmul(a[rows], w))
+    assert oracle.normwise_error(got[rows], want) <= TOL
+    # and column-wise: the sampled rows' per-column maxima stay in bar too
+    per_col = np.abs(got[rows] - want).max(axis=0) / np.abs(want).max()
+    assert per_col.max() <= TOL
+
+
+def test_launch_fault_reports_and_next_execute_is_exact():
+    """HEXIR_FAULT's launch site on the GPU: the injected failure comes back
+    as HEXIR_ERROR_DEVICE before the driver is called, and the next
+    execute, with no fault, gives the same bits as one before it."""
+    r = hx.Rng(9)
+    a, w = r.uniform((256, 192)), r.uniform((192, 320))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    module = hx.Module(p.emit("hexir.linear=cuda,hexir.relu=cuda"))
+    dev = hx.Device("cuda")
+    before = hx.execute(module, dev, out_shape=(256, 320))
+    hx.fault_configure("launch:1")
+    try:
+        with pytest.raises(hx.HexirError) as err:
+            hx.execute(module, dev, out_shape=(256, 320))
+        assert err.value.status == _ffi.ERROR_DEVICE
+        assert hx.fault_calls("launch") >= 1
+    finally:
+        hx.fault_configure("")
+    after = hx.execute(module, dev, out_shape=(256, 320))
+    assert np.array_equal(bits(after), bits(before))
+    assert oracle.normwise_error(after, oracle.relu(oracle.matmul(a, w))) <= TOL
+    module.close()
+    dev.close()
 
 
 @pytest.mark.parametrize("m", [1, 16, 128])
@@ -528,3 +579,29 @@ def test_hexir_run_repeat_with_kept_constants_on_cuda(tmp_path):
     assert res.returncode == 0, res.stderr
     assert res.stdout == case["stdout_quiet"]
     assert "kernel time   :" in res.stderr and "median" in res.stderr
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
+def test_nccl_fault_in_sharded_dispatch_reports_and_recovers():
+    """HEXIR_FAULT's NCCL site: a row-sharded dispatch whose weight
+    broadcast is made to fail returns HEXIR_ERROR_DEVICE with no rank left
+    waiting, and the next execute is whole."""
+    r = hx.Rng(10)
+    a, w = r.uniform((600, 256)), r.uniform((256, 384))
+    p = hx.Program()
+    p.relu(p.linear(p.constant(a), p.constant(w)))
+    module = hx.Module(p.emit("hexir.linear=cuda:0-1,hexir.relu=cuda:0-1"))
+    devs = [hx.Device("cuda:0"), hx.Device("cuda:1")]
+    before = hx.execute(module, devs, out_shape=(600, 384))
+    hx.fault_configure("nccl:1")
+    try:
+        with pytest.raises(hx.HexirError) as err:
+            hx.execute(module, devs, out_shape=(600, 384))
+        assert err.value.status == _ffi.ERROR_DEVICE
+    finally:
+        hx.fault_configure("")
+    after = hx.execute(module, devs, out_shape=(600, 384))
+    assert np.array_equal(bits(after), bits(before))
+    module.close()
+    for d in devs:
+        d.close()
