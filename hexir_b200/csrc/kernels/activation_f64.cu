@@ -4,7 +4,7 @@
 //   leaky_relu  x > 0 ? x : 0.01 x          ("max(x, alpha * x)", alpha fixed)
 //   elu         x > 0 ? x : 1.0 expm1(x)    ("alpha * (exp(x) - 1)", alpha fixed)
 //   sigmoid     1 / (1 + exp(-x))
-//   tanh        tanh(x)
+//   tanh        tanh(x), as expm1(2x) / (expm1(2x) + 2) (see TanhOp)
 //   softmax     exp(x - max) / sum exp(x - max) along each row
 //   gelu        0.5 x erfc(-x / sqrt 2)     (= x 0.5 (1 + erf(x / sqrt 2)),
 //                                            without the cancellation of 1 + erf
@@ -61,9 +61,19 @@ struct SigmoidOp {
     return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
   }
 };
+// tanh(x) = (e^{2x} - 1) / (e^{2x} + 1) = t / (t + 2) with t = expm1(2x):
+// expm1 keeps the relative accuracy of small |x| (t ~ 2x, so the quotient
+// ~ x), the two roundings after it add ~1 ulp, and it costs one
+// exponential and one divide -- sigmoid's cost -- instead of a general
+// tanh.  Beyond |x| = 20, 1 - tanh|x| < 2^-57 and the result rounds to
+// +-1 (the clamp also covers infinities); NaN propagates through expm1;
+// -0.0 gives -0.0.
 struct TanhOp {
   __device__ __forceinline__ double operator()(double x, double) const {
-    return tanh(x);
+    if (fabs(x) > 20.0)
+      return copysign(1.0, x);
+    const double t = expm1(__dmul_rn(2.0, x));
+    return __ddiv_rn(t, __dadd_rn(t, 2.0));
   }
 };
 struct GeluOp {

@@ -230,3 +230,20 @@ def test_softmax_misaligned_rows_take_the_register_blocks(gpu, rows, cols):
     want = oracle.activation("softmax", x)
     assert_close("softmax", aligned, want)
     assert_close("softmax", shifted, want)
+
+
+def test_tanh_expm1_form_is_within_4_ulp(gpu):
+    """tanh is evaluated as expm1(2x) / (expm1(2x) + 2), clamped to +-1
+    beyond |x| = 20: within 4 ulp of the oracle's C-library tanh over a
+    dense grid through the clamp, tiny magnitudes (where the relative
+    accuracy of expm1 is what keeps it), and the sign of zero."""
+    grid = np.linspace(-25.0, 25.0, 1 << 18)
+    tiny = np.geomspace(1e-300, 1e-2, 4096)
+    x = np.concatenate([grid, tiny, -tiny, [0.0, -0.0, 20.0, -20.0,
+                                            np.nextafter(20.0, 21.0)]])
+    x = x.reshape(1, -1)
+    got = run_gpu(gpu, "tanh", x)
+    want = oracle.activation("tanh", x)
+    assert oracle.ulp_error_ok(got, want, 4, floor=0.0).all()
+    assert np.signbit(got[0, -4]) and not np.signbit(got[0, -5])
+    assert got[0, -1] == 1.0
