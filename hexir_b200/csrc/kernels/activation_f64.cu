@@ -365,6 +365,18 @@ extern "C" __global__ void __launch_bounds__(256, 2)
   softmax_rows_bulk<256, HEXIR_SOFTMAX_B256_COLS / 256>(args);
 }
 
+// Short rows: the same persistent bulk-prefetch blocks with fewer elements
+// per thread, so more blocks (and so more row copies in flight) fit an SM.
+extern "C" __global__ void __launch_bounds__(256, 4)
+    hexir_softmax_bulk_s2k_f64(const hexir_activation_args_t args) {
+  softmax_rows_bulk<256, HEXIR_SOFTMAX_S2K_COLS / 256>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(256, 3)
+    hexir_softmax_bulk_s4k_f64(const hexir_activation_args_t args) {
+  softmax_rows_bulk<256, HEXIR_SOFTMAX_S4K_COLS / 256>(args);
+}
+
 extern "C" __global__ void __launch_bounds__(512, 1)
     hexir_softmax_bulk512_f64(const hexir_activation_args_t args) {
   softmax_rows_bulk<512, HEXIR_SOFTMAX_B512_COLS / 512>(args);

@@ -134,6 +134,10 @@ typedef struct {
 #define HEXIR_SOFTMAX_WARP_COLS 1024u
 #define HEXIR_SOFTMAX_B256_COLS 8192u
 #define HEXIR_SOFTMAX_B512_COLS 16384u
+// Short rows through the bulk-prefetch blocks: fewer elements per thread,
+// more blocks per SM (4 up to 2048 columns, 3 up to 4096).
+#define HEXIR_SOFTMAX_S2K_COLS 2048u
+#define HEXIR_SOFTMAX_S4K_COLS 4096u
 
 typedef struct {
   const double *x;

@@ -262,6 +262,14 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
         *o.slot = nullptr;
     }
   }
+  // Optional: the short-row softmax blocks (rows in at most 16 / 32 KiB of
+  // shared memory, under the default dynamic limit), both or neither.
+  if (lib->softmax_bulk256 &&
+      (d.ModuleGetFunction(&lib->softmax_bulk_s2k, lib->module,
+                           "hexir_softmax_bulk_s2k_f64") != CUDA_SUCCESS ||
+       d.ModuleGetFunction(&lib->softmax_bulk_s4k, lib->module,
+                           "hexir_softmax_bulk_s4k_f64") != CUDA_SUCCESS))
+    lib->softmax_bulk_s2k = lib->softmax_bulk_s4k = nullptr;
   size_t word_bytes = 0;
   r = d.ModuleGetGlobal(&lib->error_word, &word_bytes, lib->module,
                         "hexir_device_error_word");
@@ -685,6 +693,16 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
                     (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                     lib->softmax_bulk256 && lib->softmax_bulk512;
   const uint64_t sms = static_cast<uint64_t>(std::max(dev->sm_count, 1));
+  if (bulk && cols <= HEXIR_SOFTMAX_S2K_COLS && lib->softmax_bulk_s2k)
+    return launch(lib->softmax_bulk_s2k,
+                  static_cast<unsigned>(std::min<uint64_t>(rows, 4 * sms)), 1,
+                  256, cols * 8u, stream, params,
+                  "launch hexir_softmax_bulk_s2k_f64", error);
+  if (bulk && cols <= HEXIR_SOFTMAX_S4K_COLS && lib->softmax_bulk_s4k)
+    return launch(lib->softmax_bulk_s4k,
+                  static_cast<unsigned>(std::min<uint64_t>(rows, 3 * sms)), 1,
+                  256, cols * 8u, stream, params,
+                  "launch hexir_softmax_bulk_s4k_f64", error);
   if (bulk && cols <= HEXIR_SOFTMAX_B256_COLS)
     return launch(lib->softmax_bulk256,
                   static_cast<unsigned>(std::min<uint64_t>(rows, 2 * sms)), 1,

@@ -36,7 +36,8 @@ struct KernelLib {
   CUfunction activation[8] = {};
   CUfunction softmax_warp = nullptr, softmax_b256 = nullptr,
              softmax_b512 = nullptr, softmax_wide = nullptr,
-             softmax_bulk256 = nullptr, softmax_bulk512 = nullptr;
+             softmax_bulk256 = nullptr, softmax_bulk512 = nullptr,
+             softmax_bulk_s2k = nullptr, softmax_bulk_s4k = nullptr;
   CUfunction dmma_probe = nullptr;
   // The reference's generated schedule, a measurement baseline only
   // (absent in images written before it existed).

@@ -93,13 +93,15 @@ def test_elementwise_activation_over_the_whole_range(gpu, op):
 
 @pytest.mark.parametrize("rows,cols", [
     (1, 1), (5, 2), (300, 31), (300, 33), (64, 1000), (64, 1024), (64, 1025),
-    (64, 1026), (1000, 2048), (40, 4097), (17, 8192), (700, 8192), (9, 8193),
+    (64, 1026), (1000, 2048), (1200, 1026), (700, 2050), (450, 3000),
+    (700, 4096), (40, 4097), (17, 8192), (700, 8192), (9, 8193),
     (9, 16384), (300, 12000), (5, 16385), (3, 40000)])
 def test_softmax_matches_oracle(gpu, rows, cols):
     """Every launch shape at and around its column limit: warp per row; the
-    persistent bulk-prefetch blocks for even rows (more rows than blocks, so
-    each block walks several); the 256- and 512-thread blocks for odd rows;
-    the three-pass block."""
+    persistent bulk-prefetch blocks for even rows, short-row (<= 2048, <=
+    4096 columns) and long (more rows than blocks, so each block walks
+    several); the 256- and 512-thread blocks for odd rows; the three-pass
+    block."""
     x = np.random.default_rng(rows * cols).normal(0, 3, (rows, cols))
     got = run_gpu(gpu, "softmax", x)
     want = oracle.activation("softmax", x)
