@@ -75,7 +75,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-relu", action="store_true")
     p.add_argument("--profile", choices=["relu", "skinny", "linear",
-                                         "activation"],
+                                         "activation", "square"],
                    help="run only one kernel a few times (the small cases the "
                         "committed ncu summaries capture)")
     p.add_argument("--op", default="gelu",
@@ -84,6 +84,9 @@ def parse_args():
                    help="--profile activation: row length (2^log2n elements)")
     p.add_argument("--log2n", type=int, default=26,
                    help="--profile relu: 2^log2n elements")
+    p.add_argument("--size", type=int, default=1024,
+                   help="--profile square: size^3 linear + relu (seed 1), "
+                        "the planner's plan")
     p.add_argument("--suite", action="store_true",
                    help="instead of the bench line, one JSON line per "
                         "configuration: GEMM sweep 1024-8192, relu 2^28, "
@@ -1000,6 +1003,16 @@ def run_profile(args):
         y = torch.empty_like(x)
         run = lambda: hx.cuda_relu(0, x.data_ptr(), y.data_ptr(), n, stream)
         what = f"relu 2^{args.log2n} f64"
+    elif args.profile == "square":
+        size = args.size
+        r = hx.Rng(1)
+        a = torch.from_numpy(r.uniform((size, size))).cuda()
+        w = torch.from_numpy(r.uniform((size, size))).cuda()
+        c = torch.empty_like(a)
+        run = lambda: hx.cuda_matmul(0, a.data_ptr(), w.data_ptr(), c.data_ptr(),
+                                     size, size, size, _ffi.MATMUL_RELU, stream)
+        what = (f"linear+relu {size}^3 plan "
+                f"{hx.matmul_plan(size, size, size, _ffi.MATMUL_RELU)}")
     elif args.profile == "activation":
         n = 1 << args.log2n
         rows = n // args.cols
