@@ -393,6 +393,11 @@ def run_hexir(args):
         _ffi.check(hx.lib().hexir_comm_init_rank(uid, 128, world, rank, ordinal,
                                                  C.byref(h)), "comm init")
         comm = h.value
+        # One line per rank about its communicator (stderr).
+        print(f"hexir comm: rank {hx.lib().hexir_comm_rank(comm)} of "
+              f"{hx.lib().hexir_comm_size(comm)} on cuda:{ordinal}, direct "
+              f"row stores {hx.lib().hexir_comm_direct_stores(comm)}, "
+              f"NCCL {torch.cuda.nccl.version()}", file=sys.stderr, flush=True)
     shard_flags = _ffi.MATMUL_RELU | (_ffi.SHARD_GATHER_NCCL
                                       if args.gather == "nccl" else 0)
     direct = bool(comm) and args.gather != "nccl" and bool(
@@ -483,6 +488,9 @@ def run_hexir(args):
             "gpu_launches": launches,
             "clocks": clock_info}
     if world > 1:
+        line["comm"] = {"nranks": hx.lib().hexir_comm_size(comm),
+                        "direct_row_stores": bool(direct),
+                        "nccl": ".".join(map(str, torch.cuda.nccl.version()))}
         line["rows_to_gpu0"] = ("kernel stores over NVLink into GPU 0's output "
                                 "(CUDA IPC mapping)" if direct else
                                 "NCCL send/receive in pieces behind the GEMM")
