@@ -3,6 +3,7 @@ the headers in include/ declare.  No compute calls: without a GPU the CUDA
 entry points must refuse (no CPU fallback), which is checked through device
 creation only."""
 
+import ctypes as C
 import os
 import re
 
@@ -145,3 +146,24 @@ def test_comm_arguments_are_checked_without_a_gpu():
     assert lib.hexir_comm_rank(None) == -1 and lib.hexir_comm_size(None) == 0
     assert lib.hexir_comm_direct_stores(None) == 0
     lib.hexir_comm_release(None)  # a no-op
+
+
+def test_sharded_entry_points_check_arguments_without_a_gpu():
+    """The multi-GPU entry points refuse what they are not given before
+    they touch a device or a collective."""
+    lib = hx.lib()
+    assert lib.hexir_comm_synchronize(None, None) == _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_sharded_linear_host_f64(
+        None, None, None, None, 8, 8, 8, 0, None) == _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_sharded_linear_f64(
+        None, None, None, None, 8, 8, 8, 0, None) == _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_host_register(None, 64) == _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_host_unregister(None) == _ffi.ERROR_INVALID_ARGUMENT
+    b, c, n = C.c_uint64(), C.c_uint64(), C.c_uint32()
+    assert lib.hexir_shard_gather_pieces(10, 0, None, C.byref(c), None) == \
+        _ffi.ERROR_INVALID_ARGUMENT
+    bounds = (C.c_uint32 * 3)()
+    assert lib.hexir_shard_weight_pieces(64, 0, bounds, C.byref(n)) == \
+        _ffi.ERROR_INVALID_ARGUMENT
+    assert lib.hexir_shard_weight_pieces(64, 2, None, C.byref(n)) == \
+        _ffi.ERROR_INVALID_ARGUMENT
