@@ -37,7 +37,6 @@ MATMUL_FORCE_GUARDED = 0x200
 MATMUL_REMOTE_OUTPUT = 0x400
 MATMUL_NO_STREAM_K = 0x800
 MATMUL_FORCE_STREAM_K = 0x2000
-MATMUL_REDUCE_KERNEL = 0x8000
 SHARD_GATHER_NCCL = 0x1000
 SHARD_W_ON_ALL = 0x4000
 

@@ -93,14 +93,6 @@ typedef struct {
   uint32_t sk_dp_tiles;
   uint32_t sk_units;
   double *sk_partials;   /* [2 G][BM][BN] */
-  /* Split-K in one launch (TMA kernels of images exporting
-   * hexir_b200_serial_splitk_v1): non-null, every CTA stores its partial
-   * sums to c + split*m*n as usual, then counts itself in on
-   * tile_flags[tile]; the CTA that arrives last sums the tile's partials in
-   * split order (the splitk_reduce kernel's arithmetic), applies the
-   * epilogue, stores to c_final and sets the flag back to 0. */
-  unsigned int *tile_flags;
-  double *c_final;
 } hexir_linear_args_t;
 
 typedef struct {

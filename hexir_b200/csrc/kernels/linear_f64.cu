@@ -216,70 +216,9 @@ __device__ __forceinline__ void load_warp_tile(
   }
 }
 
-// The split-K sum of a warp tile, in this thread's registers: for each
-// element, 0.0 plus the partial of split 0, 1, ... in order (the
-// splitk_reduce kernel's arithmetic), where this CTA's own split comes from
-// `acc` and the others from `partials` (plane = m * n doubles apart), read
-// from L2 because other SMs wrote them.  n is even (TMA kernels), so every
-// column pair is one 16-byte load.
-template <int MI, int NP>
-__device__ __forceinline__ void sum_split_partials(
-    double (&acc)[MI][2 * NP][4], const double *__restrict__ partials,
-    size_t plane, uint32_t split, uint32_t mine, uint32_t m, uint32_t n,
-    uint32_t row0, uint32_t col0, uint32_t g, uint32_t t) {
-#pragma unroll
-  for (int mi = 0; mi < MI; ++mi) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t row = row0 + mi * 16 + g + half * 8;
-      if (row >= m)
-        continue;
-#pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        const uint32_t col = col0 + p * 16 + 4 * t;
-        double *e[4] = {&acc[mi][2 * p][2 * half], &acc[mi][2 * p + 1][2 * half],
-                        &acc[mi][2 * p][2 * half + 1],
-                        &acc[mi][2 * p + 1][2 * half + 1]};
-        double s[4] = {0.0, 0.0, 0.0, 0.0};
-        for (uint32_t sp = 0; sp < split; ++sp) {
-          double v[4] = {0.0, 0.0, 0.0, 0.0};
-          if (sp == mine) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              v[q] = *e[q];
-          } else {
-            const double *src = partials + sp * plane + (size_t)row * n + col;
-            if (col < n) {
-              const double2 x = __ldcg(reinterpret_cast<const double2 *>(src));
-              v[0] = x.x;
-              v[1] = x.y;
-            }
-            if (col + 2 < n) {
-              const double2 x =
-                  __ldcg(reinterpret_cast<const double2 *>(src + 2));
-              v[2] = x.x;
-              v[3] = x.y;
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            s[q] = __dadd_rn(s[q], v[q]);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *e[q] = s[q];
-      }
-    }
-  }
-}
-
 }  // namespace hexir
 
 using namespace hexir;
-
-// Marks an image whose TMA kernels finish split-K in one launch
-// (hexir_linear_args_t.tile_flags).
-extern "C" __global__ void hexir_b200_serial_splitk_v1() {}
 
 namespace hexir {
 
@@ -442,33 +381,6 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   }
   store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
                                 n0 + wn * T::WTN, relu, g, t, vec4, addend);
-  if (args.split_k > 1 && args.tile_flags) {
-    // Split-K finished here: the tile's last CTA to arrive sums the
-    // partials.  Release: this CTA's partial stores before its arrival.
-    __shared__ unsigned int last;
-    __threadfence();
-    __syncthreads();
-    if (issuer) {
-      unsigned int *flag = args.tile_flags + (tm * args.tiles_n + tn);
-      last = atomicAdd(flag, 1u) == args.split_k - 1;
-      if (last)
-        *flag = 0u;  // every split has arrived: ready for the next launch
-    }
-    __syncthreads();
-    if (!last)
-      return;
-    __threadfence();  // acquire: the other CTAs' partials
-    sum_split_partials<MI, NP>(acc, args.c, (size_t)args.m * args.n,
-                               args.split_k, split, args.m, args.n,
-                               m0 + wm * T::WTM, n0 + wn * T::WTN, g, t);
-    store_warp_tile<MI, NP, true>(
-        acc, args.c_final, args.m, args.n, m0 + wm * T::WTM, n0 + wn * T::WTN,
-        (args.epilogue & HEXIR_EPILOGUE_RELU) != 0, g, t, vec4,
-        (args.epilogue & HEXIR_EPILOGUE_ADD) ? args.addend : nullptr);
-    if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)
-      __threadfence_system();
-    return;
-  }
   if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
     __threadfence_system();
 }

@@ -29,9 +29,6 @@ thread_local std::string g_last_error;
 
 // Every pipeline wait in the kernels gives up after this much wall time.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
-// Tiles one one-launch split-K can count (a 32768 x 32768 output in
-// 128 x 128 tiles); larger outputs reduce in a second kernel.
-constexpr uint64_t kTileFlags = 1u << 16;
 
 bool aligned16(const void *p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
@@ -50,27 +47,6 @@ hexir_status_t fail(std::string *error, std::string message,
 
 // Workspace for split-K partials: grown on demand, never shrunk.  Growing
 // frees the old block only after the context is idle.
-// One-launch split-K's arrival counters, allocated and zeroed on first use.
-hexir_status_t ensure_tile_flags(DeviceState *dev, std::string *error) {
-  if (dev->tile_flags)
-    return HEXIR_OK;
-  const Driver &d = driver();
-  CUdeviceptr p = 0;
-  CUresult r = d.MemAlloc(&p, kTileFlags * sizeof(unsigned int));
-  if (r == CUDA_SUCCESS)
-    r = d.MemsetD8Async(p, 0, kTileFlags * sizeof(unsigned int), nullptr);
-  if (r == CUDA_SUCCESS)
-    r = d.CtxSynchronize();
-  if (r != CUDA_SUCCESS) {
-    if (p)
-      d.MemFree(p);
-    return fail(error, cuda_message("split-K tile counters", r),
-                HEXIR_ERROR_OUT_OF_MEMORY);
-  }
-  dev->tile_flags = p;
-  return HEXIR_OK;
-}
-
 hexir_status_t ensure_workspace(DeviceState *dev, size_t bytes,
                                 std::string *error) {
   const Driver &d = driver();
@@ -247,10 +223,6 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
       return nullptr;
     }
   }
-  CUfunction serial_marker = nullptr;
-  lib->serial_splitk = d.ModuleGetFunction(&serial_marker, lib->module,
-                                           "hexir_b200_serial_splitk_v1") ==
-                       CUDA_SUCCESS;
   // Optional: the baseline restating the reference's generated schedule.
   if (d.ModuleGetFunction(&lib->baseline_schedule, lib->module,
                           "hexir_baseline_reference_schedule_f64") !=
@@ -567,27 +539,15 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     args.sk_dp_tiles = p.sk_dp_tiles;
     args.sk_units = p.sk_units;
   }
-  // Split-K in one launch: the TMA kernels' last CTA per tile sums the
-  // partials (images that export the marker, tile counts that fit).
-  const bool serial = p.split_k > 1 && p.variant != kGuarded &&
-                      lib->serial_splitk &&
-                      !(flags & HEXIR_MATMUL_REDUCE_KERNEL) &&
-                      static_cast<uint64_t>(p.tiles_m) * p.tiles_n <= kTileFlags;
   if (p.split_k > 1) {
     ws_lock.lock();
     hexir_status_t s = ensure_workspace(
         dev, static_cast<size_t>(p.split_k) * out_bytes, error);
-    if (s == HEXIR_OK && serial)
-      s = ensure_tile_flags(dev, error);
     if (s != HEXIR_OK)
       return s;
     // The previous user of the workspace may be another stream.
     d.StreamWaitEvent(stream, dev->ws_ready, 0);
     args.c = reinterpret_cast<double *>(dev->workspace);
-    if (serial) {
-      args.tile_flags = reinterpret_cast<unsigned int *>(dev->tile_flags);
-      args.c_final = c;
-    }
   }
   if (rows32 && (reinterpret_cast<uintptr_t>(args.c) & 31u) == 0)
     args.epilogue |= HEXIR_EPILOGUE_VEC4;
@@ -643,10 +603,6 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
     }
     status = launch(fn, grid_x, p.split_k, HEXIR_LINEAR_THREADS, smem, stream,
                     params, what, error);
-    if (serial) {
-      d.EventRecord(dev->ws_ready, stream);
-      return status;
-    }
   } else {
     void *params[] = {&args};
     status = launch(lib->linear_guarded, grid_x, p.split_k,
@@ -790,12 +746,6 @@ hexir_status_t check_device(DeviceState *dev, CUstream stream,
       d.MemsetD8Async(lib->error_word, 0, sizeof(word), stream);
       d.StreamSynchronize(stream);
     }
-  }
-  if (bits && dev->tile_flags) {
-    // A kernel that gave up may have left a tile's split-K count short.
-    d.MemsetD8Async(dev->tile_flags, 0, kTileFlags * sizeof(unsigned int),
-                    stream);
-    d.StreamSynchronize(stream);
   }
   if (bits & HEXIR_KERR_WAIT_TIMEOUT)
     return fail(error, "a kernel pipeline wait ran out of time (device error "

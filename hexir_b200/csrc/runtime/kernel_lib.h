@@ -42,8 +42,6 @@ struct KernelLib {
   // The reference's generated schedule, a measurement baseline only
   // (absent in images written before it existed).
   CUfunction baseline_schedule = nullptr;
-  // The TMA kernels finish split-K in one launch (tile_flags).
-  bool serial_splitk = false;
   CUfunction wait_probe = nullptr;
   CUdeviceptr error_word = 0;
 };
@@ -63,10 +61,6 @@ struct DeviceState {
   CUdeviceptr workspace = 0;
   size_t workspace_bytes = 0;
   CUevent ws_ready = nullptr;
-  // Per-tile arrival counters of one-launch split-K (kTileFlags words,
-  // zeroed once; every completed tile sets its word back to 0), ordered
-  // like the workspace.
-  CUdeviceptr tile_flags = 0;
 };
 
 // Per-ordinal state; nullptr (and *error set) if the GPU cannot be opened.

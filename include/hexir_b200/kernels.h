@@ -49,11 +49,6 @@ extern "C" {
  * split is requested and no c_in is given.  NO_STREAM_K overrides. */
 #define HEXIR_MATMUL_NO_STREAM_K 0x800u
 #define HEXIR_MATMUL_FORCE_STREAM_K 0x2000u
-/* A split k range is summed in one launch: each output tile's last CTA to
- * finish adds the tile's partials in split order.  REDUCE_KERNEL sums them
- * in a second kernel instead (the same arithmetic, bit for bit; what an
- * image written before one-launch split-K does). */
-#define HEXIR_MATMUL_REDUCE_KERNEL 0x8000u
 /* tests: split the k range into S pieces (1..255; any S rules out stream-K);
  * 0 = choose automatically */
 #define HEXIR_MATMUL_SPLIT_K(S) (((uint32_t)(S) & 0xFFu) << 16)

@@ -380,36 +380,3 @@ def test_reference_schedule_baseline_refuses_what_the_reference_cannot_launch(gp
     st = hx.lib().hexir_cuda_baseline_reference_schedule_f64(
         0, 0, 0, 0, 65536, 8, 8, gpu.stream)
     assert st == _ffi.ERROR_INVALID_ARGUMENT
-
-
-@pytest.mark.parametrize("m,n,k,split", [
-    (64, 256, 4096, 4), (1000, 384, 2048, 3), (2048, 2048, 2048, 4),
-    (16, 8192, 8192, 9), (1, 4096, 4096, 7), (130, 258, 640, 5),
-    (300, 200, 1024, 2)])
-@pytest.mark.parametrize("relu", [0, _ffi.MATMUL_RELU])
-def test_one_launch_split_k_equals_reduce_kernel(gpu, m, n, k, split, relu):
-    """Split-K summed by each tile's last CTA in the GEMM launch gives the
-    bits of the separate reduce kernel (same split order), twice in a row
-    (the per-tile counters reset themselves), and with a fused addend."""
-    rng = hx.Rng(m * 131 + n + k)
-    a, b, d = rng.uniform((m, k)), rng.uniform((k, n)), rng.uniform((m, n))
-    ba, bb, bd = gpu.upload(a), gpu.upload(b), gpu.upload(d)
-    outs = []
-    for extra in (0, 0, _ffi.MATMUL_REDUCE_KERNEL):
-        bc = gpu.buffer(m * n * 8)
-        hx.cuda_matmul(0, ba.ptr, bb.ptr, bc.ptr, m, n, k,
-                       relu | _ffi.MATMUL_SPLIT_K(split) | extra, gpu.stream)
-        hx.cuda_synchronize(0, gpu.stream)
-        outs.append(bc.read((m, n)))
-    assert np.array_equal(bits(outs[0]), bits(outs[2]))
-    assert np.array_equal(bits(outs[1]), bits(outs[2]))
-    want = oracle.matmul(a, b)
-    assert oracle.normwise_error(outs[0], oracle.relu(want) if relu else want) <= TOL
-    fused = []
-    for extra in (0, _ffi.MATMUL_REDUCE_KERNEL):
-        bc = gpu.buffer(m * n * 8)
-        hx.cuda_matmul_add(0, ba.ptr, bb.ptr, bd.ptr, bc.ptr, m, n, k,
-                           relu | _ffi.MATMUL_SPLIT_K(split) | extra, gpu.stream)
-        hx.cuda_synchronize(0, gpu.stream)
-        fused.append(bc.read((m, n)))
-    assert np.array_equal(bits(fused[0]), bits(fused[1]))
