@@ -198,6 +198,13 @@ class HexirError(RuntimeError):
         super().__init__(msg)
 
 
+def loaded():
+    """The library if it has been loaded, else None; never loads it.  For
+    finalizers: at interpreter shutdown module globals may already be gone,
+    and the process's exit frees what they would release."""
+    return _LIB
+
+
 def lib() -> C.CDLL:
     """The loaded library; raises if it has not been built."""
     global _LIB

@@ -39,9 +39,10 @@ class Program:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
-            lib().hexir_program_release(h)
-            self._h = None
+        handle = _ffi.loaded()
+        if h and handle is not None:
+            handle.hexir_program_release(h)
+        self._h = None
 
     def _value(self, v: int, what: str) -> int:
         if v < 0:
@@ -250,9 +251,10 @@ class Module:
         return self._h
 
     def close(self) -> None:
-        if getattr(self, "_h", None):
-            lib().hexir_module_release(self._h)
-            self._h = None
+        handle = _ffi.loaded()
+        if getattr(self, "_h", None) and handle is not None:
+            handle.hexir_module_release(self._h)
+        self._h = None
 
     __del__ = close
 
@@ -321,11 +323,12 @@ class Device:
         check(lib().hexir_device_wait(self._h), "hexir_device_wait")
 
     def close(self) -> None:
-        if getattr(self, "_h", None):
+        handle = _ffi.loaded()
+        if getattr(self, "_h", None) and handle is not None:
             for b in list(getattr(self, "_buffers", ())):
                 b.close()
-            lib().hexir_device_release(self._h)
-            self._h = None
+            handle.hexir_device_release(self._h)
+        self._h = None
 
     __del__ = close
 
@@ -368,9 +371,10 @@ class Buffer:
         return out
 
     def close(self) -> None:
-        if getattr(self, "_h", None):
-            lib().hexir_buffer_release(self._h)
-            self._h = None
+        handle = _ffi.loaded()
+        if getattr(self, "_h", None) and handle is not None:
+            handle.hexir_buffer_release(self._h)
+        self._h = None
 
     __del__ = close
 

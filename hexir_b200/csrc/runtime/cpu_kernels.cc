@@ -82,8 +82,9 @@ void cpu_add_f64(const double *a, const double *b, double *c, size_t n) {
 void parallel_copy(void *dst, const void *src, size_t bytes) {
   constexpr uint64_t kBytesPerRange = 1u << 20;
   const uint64_t ranges = (bytes + kBytesPerRange - 1) / kBytesPerRange;
-  // 2^22 "work" per thread at least: a range counts its bytes / 64.
-  parallel_rows(ranges, kBytesPerRange / 64, [=](uint64_t r0, uint64_t r1) {
+  // Threads for copies of 4 MiB and more (parallel_rows' 2^22 threshold,
+  // counted in bytes).
+  parallel_rows(ranges, kBytesPerRange, [=](uint64_t r0, uint64_t r1) {
     const size_t b0 = r0 * kBytesPerRange;
     const size_t b1 = std::min<size_t>(bytes, r1 * kBytesPerRange);
     std::memcpy(static_cast<char *>(dst) + b0,
