@@ -367,7 +367,7 @@ extern "C" __global__ void __launch_bounds__(256, 2)
 
 // Short rows: the same persistent bulk-prefetch blocks with fewer elements
 // per thread, so more blocks (and so more row copies in flight) fit an SM.
-extern "C" __global__ void __launch_bounds__(256, 4)
+extern "C" __global__ void __launch_bounds__(256, 5)
     hexir_softmax_bulk_s2k_f64(const hexir_activation_args_t args) {
   softmax_rows_bulk<256, HEXIR_SOFTMAX_S2K_COLS / 256>(args);
 }

@@ -135,7 +135,7 @@ typedef struct {
 #define HEXIR_SOFTMAX_B256_COLS 8192u
 #define HEXIR_SOFTMAX_B512_COLS 16384u
 // Short rows through the bulk-prefetch blocks: fewer elements per thread,
-// more blocks per SM (4 up to 2048 columns, 3 up to 4096).
+// more blocks per SM (5 up to 2048 columns, 3 up to 4096).
 #define HEXIR_SOFTMAX_S2K_COLS 2048u
 #define HEXIR_SOFTMAX_S4K_COLS 4096u
 

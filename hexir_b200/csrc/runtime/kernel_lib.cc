@@ -695,7 +695,7 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
   const uint64_t sms = static_cast<uint64_t>(std::max(dev->sm_count, 1));
   if (bulk && cols <= HEXIR_SOFTMAX_S2K_COLS && lib->softmax_bulk_s2k)
     return launch(lib->softmax_bulk_s2k,
-                  static_cast<unsigned>(std::min<uint64_t>(rows, 4 * sms)), 1,
+                  static_cast<unsigned>(std::min<uint64_t>(rows, 5 * sms)), 1,
                   256, cols * 8u, stream, params,
                   "launch hexir_softmax_bulk_s2k_f64", error);
   if (bulk && cols <= HEXIR_SOFTMAX_S4K_COLS && lib->softmax_bulk_s4k)
