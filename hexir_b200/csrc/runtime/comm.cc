@@ -115,8 +115,7 @@ struct hexir_comm_t {
   // hexir_sharded_linear_host_f64: streams for this GPU's host link (one
   // each way), its events, and device workspace kept between calls.
   CUstream up_stream = nullptr, down_stream = nullptr;
-  CUevent w_uploaded = nullptr, w_ready = nullptr, down_done = nullptr;
-  CUevent a_ready[kHostChunks] = {}, c_ready[kHostChunks] = {};
+  CUevent down_done = nullptr;
   CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
   size_t a_bytes = 0, w_bytes = 0, c_bytes = 0;
 };
@@ -399,15 +398,9 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kDescSlots; ++i)
     cr = d.EventCreate(&comm->desc_done[i], CU_EVENT_DISABLE_TIMING);
   for (CUevent *ev : {&comm->w_start, &comm->w_piece[0], &comm->w_piece[1],
-                      &comm->w_done, &comm->w_uploaded, &comm->w_ready,
-                      &comm->down_done})
+                      &comm->w_done, &comm->down_done})
     if (cr == CUDA_SUCCESS)
       cr = d.EventCreate(ev, CU_EVENT_DISABLE_TIMING);
-  for (uint32_t i = 0; cr == CUDA_SUCCESS && i < kHostChunks; ++i) {
-    cr = d.EventCreate(&comm->a_ready[i], CU_EVENT_DISABLE_TIMING);
-    if (cr == CUDA_SUCCESS)
-      cr = d.EventCreate(&comm->c_ready[i], CU_EVENT_DISABLE_TIMING);
-  }
   if (cr == CUDA_SUCCESS)
     cr = d.StreamCreate(&comm->up_stream, CU_STREAM_NON_BLOCKING);
   if (cr == CUDA_SUCCESS)
@@ -481,13 +474,8 @@ void hexir_comm_release(hexir_comm_t *comm) {
         d.StreamSynchronize(st);
         d.StreamDestroy(st);
       }
-    for (CUevent ev : {comm->w_uploaded, comm->w_ready, comm->down_done})
-      if (ev)
-        d.EventDestroy(ev);
-    for (uint32_t i = 0; i < kHostChunks; ++i)
-      for (CUevent ev : {comm->a_ready[i], comm->c_ready[i]})
-        if (ev)
-          d.EventDestroy(ev);
+    if (comm->down_done)
+      d.EventDestroy(comm->down_done);
     for (CUdeviceptr p : {comm->a_dev, comm->w_dev, comm->c_dev})
       if (p)
         d.MemFree(p);
@@ -804,13 +792,25 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
   // From here a failure skips this rank's own work but still takes every
   // collective step: the weight gather and the failure word's reduction.
 
-  // 1. The weight.  Every rank holding it uploads its own k slice over its
-  //    own host link and the slices meet over NVLink (one broadcast per
-  //    slice, grouped: an all-gather of unequal slices); otherwise the root
-  //    uploads it whole and broadcasts it.  It is the first thing on the
-  //    upload stream: every chunk's GEMM waits for it.
-  //    Every copy waits for the caller's queued work (it may still read the
-  //    workspace a previous call left).
+  // 1. The weight, in k pieces: every rank holding it uploads its own share
+  //    of each piece's rows over its own host link and the shares meet over
+  //    NVLink (one broadcast per share, grouped: an all-gather of unequal
+  //    shares); otherwise the root uploads each piece and broadcasts it.
+  //    For k >= 2048 the first half of k goes in growing pieces
+  //    (weight_stream_bounds) so the GEMM starts after the first one, then
+  //    the second half in one piece; every rank takes the same pieces (they
+  //    depend on k alone).  Each copy starts after the caller's queued work
+  //    (which may still read the workspace a previous call left).
+  std::vector<uint32_t> bounds{0};
+  uint32_t k1 = k;  // the streamed first half of k ends here
+  if (k >= kBroadcastPieceMinK) {
+    k1 = (k / 2) / 32 * 32;
+    bounds = weight_stream_bounds(k1);
+  }
+  if (bounds.back() != k)
+    bounds.push_back(k);
+  const size_t pieces = bounds.size() - 1;
+  const bool uploads_w = w_everywhere || rank == 0;
   CUevent start = comm->w_start;
   if (!failed)
     note(d.EventRecord(start, s), "cuEventRecord");
@@ -818,83 +818,169 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
     note(d.StreamWaitEvent(up, start, 0), "cuStreamWaitEvent");
   if (!failed)
     note(d.StreamWaitEvent(down, start, 0), "cuStreamWaitEvent");
-  uint64_t kb = 0, kc = k;
-  if (w_everywhere)
-    hexir_shard_rows(k, ranks, rank, &kb, &kc);
-  const bool uploads_w = w_everywhere || rank == 0;
-  if (!failed && uploads_w && kc)
-    note(d.MemcpyHtoDAsync(comm->w_dev + kb * row_c, w + kb * n, kc * row_c, up),
-         "weight upload");
   if (!failed)
-    note(d.EventRecord(comm->w_uploaded, up), "cuEventRecord");
-  if (!failed)
-    note(d.StreamWaitEvent(gs, comm->w_uploaded, 0), "cuStreamWaitEvent");
-  if (ranks > 1) {
-    void *wd = reinterpret_cast<void *>(comm->w_dev);
-    cudaStream_t g = reinterpret_cast<cudaStream_t>(gs);
-    ncclResult_t nr = ncclSuccess;
-    if (w_everywhere) {
-      nc.GroupStart();
-      for (uint32_t r = 0; r < ranks; ++r) {
-        uint64_t rb = 0, rc = 0;
-        hexir_shard_rows(k, ranks, r, &rb, &rc);
-        if (!rc)
-          continue;
-        void *piece = static_cast<char *>(wd) + rb * row_c;
-        nc.Broadcast(piece, piece, rc * n, ncclDouble, static_cast<int>(r),
-                     comm->comm, g);
-      }
-      nr = nc.GroupEnd();
-    } else {
-      nr = nc.Broadcast(wd, wd, w_size / 8, ncclDouble, 0, comm->comm, g);
+    note(d.StreamWaitEvent(gs, start, 0), "cuStreamWaitEvent");
+  // Events of this call: the weight share of piece j uploaded (w_up) and
+  // gathered (w_in), piece j's column band of a uploaded (band), each row
+  // chunk's upload; destroyed once the caller's stream has passed them.
+  std::vector<CUevent> events;
+  auto event_on = [&](CUstream st) -> CUevent {
+    CUevent ev = nullptr;
+    if (!failed && note(d.EventCreate(&ev, CU_EVENT_DISABLE_TIMING), "cuEventCreate")) {
+      events.push_back(ev);
+      note(d.EventRecord(ev, st), "cuEventRecord");
     }
-    if (nr != ncclSuccess && !failed) {
-      failed = true;
-      error = nccl_message("weight gather", nr);
-    }
-  }
-  d.EventRecord(comm->w_ready, gs);
+    return ev;
+  };
+  auto wait_on = [&](CUstream st, CUevent ev) {
+    if (!failed && ev)
+      note(d.StreamWaitEvent(st, ev, 0), "cuStreamWaitEvent");
+  };
 
-  // 2. This rank's rows in chunks: each chunk uploads behind the weight and
-  //    the chunks before it, computes once both are in, and downloads into
-  //    c_rows while the next computes.  Every chunk runs the k split of one
-  //    launch over all the rank's rows, so the bits are that launch's.
+  // A rank continues its sums piece by piece over all its rows where its
+  // one-shot plan has no k split (the same operations as one launch);
+  // otherwise it runs that plan per row chunk once the whole weight is in.
   const MatmulPlan plan = plan_matmul(
       dev, reinterpret_cast<const double *>(comm->a_dev),
       reinterpret_cast<const double *>(comm->w_dev),
       reinterpret_cast<const double *>(comm->c_dev), static_cast<uint32_t>(rows),
       n, k, relu);
+  const bool chain = pieces > 1 && plan.split_k == 1 && !plan.stream_k() && rows;
   const uint32_t chunk_flags = relu | HEXIR_MATMUL_SPLIT_K(plan.split_k);
-  if (!failed)
-    note(d.StreamWaitEvent(s, comm->w_ready, 0), "cuStreamWaitEvent");
+
+  // a's columns [c0, c1) of rows [r0, r0 + nr), a 2-D copy (row pitch k).
+  auto upload_band = [&](uint64_t r0, uint64_t nr, uint32_t c0, uint32_t c1) {
+    if (failed || !nr || c1 <= c0)
+      return;
+    CUDA_MEMCPY2D cp;
+    std::memset(&cp, 0, sizeof(cp));
+    cp.srcMemoryType = CU_MEMORYTYPE_HOST;
+    cp.srcHost = a_rows + r0 * k + c0;
+    cp.srcPitch = row_a;
+    cp.dstMemoryType = CU_MEMORYTYPE_DEVICE;
+    cp.dstDevice = comm->a_dev + r0 * row_a + static_cast<size_t>(c0) * 8;
+    cp.dstPitch = row_a;
+    cp.WidthInBytes = static_cast<size_t>(c1 - c0) * 8;
+    cp.Height = nr;
+    note(d.Memcpy2DAsync(&cp, up), "row upload");
+  };
+
+  std::vector<CUevent> w_in(pieces, nullptr), band(pieces, nullptr);
+  cudaStream_t g = reinterpret_cast<cudaStream_t>(gs);
+  for (size_t j = 0; j < pieces; ++j) {
+    const uint32_t p0 = bounds[j], p1 = bounds[j + 1];
+    uint64_t sb = 0, sc = p1 - p0;
+    if (w_everywhere)
+      hexir_shard_rows(p1 - p0, ranks, rank, &sb, &sc);
+    if (!failed && uploads_w && sc)
+      note(d.MemcpyHtoDAsync(comm->w_dev + (p0 + sb) * row_c, w + (p0 + sb) * n,
+                             sc * row_c, up),
+           "weight upload");
+    wait_on(gs, event_on(up));
+    if (ranks > 1) {
+      // Posted whatever happened above: every rank takes every step.
+      ncclResult_t nr = ncclSuccess;
+      if (w_everywhere) {
+        nc.GroupStart();
+        for (uint32_t r = 0; r < ranks; ++r) {
+          uint64_t rb = 0, rc = 0;
+          hexir_shard_rows(p1 - p0, ranks, r, &rb, &rc);
+          if (!rc)
+            continue;
+          void *share = reinterpret_cast<void *>(comm->w_dev + (p0 + rb) * row_c);
+          nc.Broadcast(share, share, rc * n, ncclDouble, static_cast<int>(r),
+                       comm->comm, g);
+        }
+        nr = nc.GroupEnd();
+      } else {
+        void *piece = reinterpret_cast<void *>(comm->w_dev + static_cast<size_t>(p0) * row_c);
+        nr = nc.Broadcast(piece, piece, static_cast<size_t>(p1 - p0) * n,
+                          ncclDouble, 0, comm->comm, g);
+      }
+      if (nr != ncclSuccess && !failed) {
+        failed = true;
+        error = nccl_message("weight gather", nr);
+      }
+    }
+    w_in[j] = event_on(gs);
+    // The rows' columns of this piece, for a rank that computes behind it
+    // (the last piece's columns go with the row chunks below).
+    if (chain && j + 1 < pieces) {
+      upload_band(0, rows, p0, p1);
+      band[j] = event_on(up);
+    }
+  }
+
+  // 2. Compute.  Phase 1 (chain): each piece of the first half over all
+  //    the rank's rows, continuing the previous piece's sums in c.  Phase 2:
+  //    per row chunk, the rest of k (or all of it), the relu, and the chunk's
+  //    download into c_rows while the next chunk computes.
+  hexir_status_t st = HEXIR_OK;
+  if (chain) {
+    for (size_t j = 0; j + 1 < pieces && !failed; ++j) {
+      wait_on(s, w_in[j]);
+      wait_on(s, band[j]);
+      if (failed)
+        break;
+      st = launch_matmul(
+          dev, lib, reinterpret_cast<const double *>(comm->a_dev + static_cast<size_t>(bounds[j]) * 8),
+          reinterpret_cast<const double *>(comm->w_dev + static_cast<size_t>(bounds[j]) * row_c),
+          reinterpret_cast<double *>(comm->c_dev), static_cast<uint32_t>(rows), n,
+          bounds[j + 1] - bounds[j], HEXIR_MATMUL_SPLIT_K(1), s, &error, k,
+          j ? reinterpret_cast<const double *>(comm->c_dev) : nullptr);
+      if (st != HEXIR_OK)
+        failed = true;
+    }
+  } else {
+    for (size_t j = 0; j < pieces; ++j)
+      wait_on(s, w_in[j]);
+  }
+  if (chain)
+    wait_on(s, w_in[pieces - 1]);
   for (uint32_t i = 0; i < kHostChunks && !failed; ++i) {
     uint64_t cb = 0, cnt = 0;
     host_chunk(rows, i, &cb, &cnt);
     if (!cnt)
       continue;
-    if (!note(d.MemcpyHtoDAsync(comm->a_dev + cb * row_a, a_rows + cb * k,
-                                cnt * row_a, up),
-              "row upload") ||
-        !note(d.EventRecord(comm->a_ready[i], up), "cuEventRecord") ||
-        !note(d.StreamWaitEvent(s, comm->a_ready[i], 0), "cuStreamWaitEvent"))
+    if (chain)
+      upload_band(cb, cnt, bounds[pieces - 1], k);
+    else if (!failed)
+      note(d.MemcpyHtoDAsync(comm->a_dev + cb * row_a, a_rows + cb * k,
+                             cnt * row_a, up),
+           "row upload");
+    wait_on(s, event_on(up));
+    if (failed)
       break;
-    hexir_status_t st = launch_matmul(
-        dev, lib, reinterpret_cast<const double *>(comm->a_dev + cb * row_a),
-        reinterpret_cast<const double *>(comm->w_dev),
-        reinterpret_cast<double *>(comm->c_dev + cb * row_c),
-        static_cast<uint32_t>(cnt), n, k, chunk_flags, s, &error);
+    if (chain) {
+      const uint32_t kl = bounds[pieces - 1];
+      st = launch_matmul(
+          dev, lib,
+          reinterpret_cast<const double *>(comm->a_dev + cb * row_a + static_cast<size_t>(kl) * 8),
+          reinterpret_cast<const double *>(comm->w_dev + static_cast<size_t>(kl) * row_c),
+          reinterpret_cast<double *>(comm->c_dev + cb * row_c),
+          static_cast<uint32_t>(cnt), n, k - kl, relu | HEXIR_MATMUL_SPLIT_K(1), s,
+          &error, k, reinterpret_cast<const double *>(comm->c_dev + cb * row_c));
+    } else {
+      st = launch_matmul(
+          dev, lib, reinterpret_cast<const double *>(comm->a_dev + cb * row_a),
+          reinterpret_cast<const double *>(comm->w_dev),
+          reinterpret_cast<double *>(comm->c_dev + cb * row_c),
+          static_cast<uint32_t>(cnt), n, k, chunk_flags, s, &error);
+    }
     if (st != HEXIR_OK) {
       failed = true;
       break;
     }
-    if (!note(d.EventRecord(comm->c_ready[i], s), "cuEventRecord") ||
-        !note(d.StreamWaitEvent(down, comm->c_ready[i], 0), "cuStreamWaitEvent") ||
-        !note(d.MemcpyDtoHAsync(c_rows + cb * n, comm->c_dev + cb * row_c,
-                                cnt * row_c, down),
-              "row download"))
-      break;
+    wait_on(down, event_on(s));
+    if (!failed)
+      note(d.MemcpyDtoHAsync(c_rows + cb * n, comm->c_dev + cb * row_c,
+                             cnt * row_c, down),
+           "row download");
   }
-  // The caller's stream ends after the downloads (and the weight gather).
+  // The caller's stream waits for everything this call queued elsewhere.
+  wait_on(s, event_on(gs));
+  wait_on(s, event_on(up));
+  // ... and its downloads.
   d.EventRecord(comm->down_done, down);
   d.StreamWaitEvent(s, comm->down_done, 0);
   if (failed)
@@ -905,6 +991,15 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
   // 3. Synchronous: the rows are in c_rows on return, and a failure on any
   //    rank is reported on every rank.
   hexir_status_t ss = hexir_comm_synchronize(comm, stream);
+  if (ss != HEXIR_OK) {
+    // The stream did not reach its end: let every queued copy finish
+    // before the events go.
+    d.StreamSynchronize(up);
+    d.StreamSynchronize(down);
+    d.StreamSynchronize(gs);
+  }
+  for (CUevent ev : events)
+    d.EventDestroy(ev);
   if (failed)
     return HEXIR_ERROR_DEVICE;
   return rs != HEXIR_OK ? rs : ss;

@@ -865,24 +865,9 @@ struct Vm {
     return *upload_a || *upload_w || *stream_out;
   }
 
-  // Bounds of phase 1's k pieces over [0, k1): 256 first, then each piece at
-  // most 256 + 0.7 x the k done so far (rounded to the 32-wide k tile), so a
-  // piece's upload (a column slice plus w rows, ~2.25 ms per 1024 k at 8192
-  // rows and columns over PCIe) ends before the previous pieces' compute
-  // (~3.9 ms per 1024 k) does.
+  // Bounds of phase 1's k pieces over [0, k1): weight_stream_bounds.
   static std::vector<uint32_t> k_piece_bounds(uint32_t k1) {
-    std::vector<uint32_t> b{0};
-    const uint32_t first = std::min<uint32_t>(256, k1);
-    uint32_t done = 0;
-    while (done < k1) {
-      uint32_t len = done == 0 ? first : (first + done * 7 / 10) / 32 * 32;
-      len = std::max<uint32_t>(len, 32);
-      if (done + len >= k1 || k1 - (done + len) < len / 2)
-        len = k1 - done;
-      done += len;
-      b.push_back(done);
-    }
-    return b;
+    return weight_stream_bounds(k1);
   }
 
   hexir_status_t run_pipelined(uint32_t index, int o, Slot *const *args,

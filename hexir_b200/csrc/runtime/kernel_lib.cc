@@ -92,6 +92,21 @@ unsigned stream_grid(const DeviceState *dev, uint64_t pairs) {
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+std::vector<uint32_t> weight_stream_bounds(uint32_t k1) {
+  std::vector<uint32_t> b{0};
+  const uint32_t first = std::min<uint32_t>(256, k1);
+  uint32_t done = 0;
+  while (done < k1) {
+    uint32_t len = done == 0 ? first : (first + done * 7 / 10) / 32 * 32;
+    len = std::max<uint32_t>(len, 32);
+    if (done + len >= k1 || k1 - (done + len) < len / 2)
+      len = k1 - done;
+    done += len;
+    b.push_back(done);
+  }
+  return b;
+}
+
 void set_last_error(const std::string &message) { g_last_error = message; }
 
 uint64_t hash_bytes(const void *data, size_t size) {

@@ -14,6 +14,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "hexir_runtime/status.h"
 
@@ -127,6 +128,14 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
 // every module loaded on this device.
 hexir_status_t check_device(DeviceState *dev, CUstream stream,
                             std::string *error);
+
+// Bounds 0 = b0 < b1 < ... = k1 of the k pieces in which a weight streamed
+// from the host is used while the rest of it still arrives: 256 first, then
+// each piece at most 256 + 0.7 x the k done so far (rounded to the 32-wide k
+// tile), so a piece's upload (a column slice plus weight rows, ~2.25 ms per
+// 1024 k at 8192 rows and columns over PCIe) ends before the previous
+// pieces' compute (~3.9 ms per 1024 k) does.
+std::vector<uint32_t> weight_stream_bounds(uint32_t k1);
 
 void count_launch();
 void set_last_error(const std::string &message);

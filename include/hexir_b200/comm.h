@@ -132,12 +132,15 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
  * flags: HEXIR_MATMUL_RELU, HEXIR_SHARD_W_ON_ALL.
  *
  * Each rank moves its own rows over its own host link, so the copies of
- * all ranks run side by side: its rows of a upload in chunks, each chunk
- * computing as soon as it and the weight are in and downloading into
- * c_rows while the next computes.  The weight crosses a host link once:
- * the root uploads it and broadcasts it over NVLink, or, with
- * HEXIR_SHARD_W_ON_ALL, every rank uploads rows hexir_shard_rows(k, size,
- * rank) of it and the slices meet over NVLink.  To hold the whole result in
+ * all ranks run side by side, and the weight crosses a host link once: the
+ * root uploads it and broadcasts it over NVLink, or, with
+ * HEXIR_SHARD_W_ON_ALL, every rank uploads its share of it
+ * (hexir_shard_rows over each piece's rows) and the shares meet over
+ * NVLink.  For k >= 2048 the first half of k goes in growing pieces, and a
+ * rank whose plan does not split k computes each piece over all its rows
+ * as it lands (the rows' columns of that piece uploading beside it),
+ * continuing its sums; the rest of k then runs per row chunk, and each
+ * chunk downloads into c_rows while the next computes.  To hold the whole result in
  * one process, pass each rank a pointer into one shared mapping (rank r at
  * row hexir_shard_rows(m, size, r)).  Host memory that is page-locked
  * (hexir_host_register, or cuMemHostAlloc) moves at copy-engine speed;

@@ -299,7 +299,12 @@ def _check_host_result(path):
 @pytest.mark.parametrize("m,n,k,flags", [
     (1000, 384, 512, _ffi.MATMUL_RELU),
     (2048 + 130, 256, 1024, 0),
-    (3, 130, 96, _ffi.MATMUL_RELU)])
+    (3, 130, 96, _ffi.MATMUL_RELU),
+    # k >= 2048 and an unsplit plan: the weight streams in k pieces and the
+    # rows continue their sums piece by piece (bits of one launch).
+    (8192 + 5, 1280, 2048, _ffi.MATMUL_RELU),
+    # k >= 2048 but a plan that splits k: whole weight, then the plan.
+    (300, 256, 4096, _ffi.MATMUL_RELU)])
 def test_host_buffer_sharded_linear_one_rank(tmp_path, m, n, k, flags):
     """One rank (one GPU): the chunked upload / compute / download path."""
     path = str(tmp_path / "out.npy")
@@ -309,7 +314,7 @@ def test_host_buffer_sharded_linear_one_rank(tmp_path, m, n, k, flags):
 
 @pytest.mark.skipif(not two_gpus(), reason="needs 2 GPUs")
 @pytest.mark.parametrize("m,n,k", [(1000, 384, 512), (4096 + 7, 1024, 2048),
-                                   (3, 130, 96)])
+                                   (3, 130, 96), (16384 + 6, 1280, 2048)])
 @pytest.mark.parametrize("w_mode", [0, _ffi.SHARD_W_ON_ALL])
 def test_host_buffer_sharded_linear_two_ranks(tmp_path, m, n, k, w_mode):
     path = str(tmp_path / "out.npy")
