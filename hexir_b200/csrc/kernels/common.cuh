@@ -133,6 +133,16 @@ __device__ __forceinline__ void stg256(double *p, double a, double b, double c,
                : "memory");
 }
 
+// The same with the streaming (evict-first) cache hint: for outputs nothing
+// in the kernel reads again, so they do not push the operands' panels out of
+// L2.
+__device__ __forceinline__ void stg256_cs(double *p, double a, double b,
+                                          double c, double d) {
+  asm volatile("st.global.cs.v4.f64 [%0], {%1, %2, %3, %4};" ::"l"(p), "d"(a),
+               "d"(b), "d"(c), "d"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ void ldg256(const double *p, double (&v)[4]) {
   asm volatile("ld.global.v4.f64 {%0, %1, %2, %3}, [%4];"
                : "=d"(v[0]), "=d"(v[1]), "=d"(v[2]), "=d"(v[3])

@@ -57,6 +57,9 @@ extern "C" {
  * its only user, fused.  Same rounding as the two kernels: the sum is an f64
  * before the add. */
 #define HEXIR_EPILOGUE_ADD 0x8u
+/* The output is final (no split-K partial another kernel reads): store it
+ * with the streaming cache hint (evict first). */
+#define HEXIR_EPILOGUE_STREAM 0x10u
 
 /* Error bits a kernel ORs into the device error word. */
 #define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */

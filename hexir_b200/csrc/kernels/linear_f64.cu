@@ -98,7 +98,8 @@ template <int MI, int NP, bool VEC>
 __device__ __forceinline__ void store_warp_tile(
     const double (&acc)[MI][2 * NP][4], double *__restrict__ c, uint32_t m,
     uint32_t n, uint32_t row0, uint32_t col0, bool relu, uint32_t g,
-    uint32_t t, bool vec4 = false, const double *__restrict__ addend = nullptr) {
+    uint32_t t, bool vec4 = false, const double *__restrict__ addend = nullptr,
+    bool stream = false) {
 #pragma unroll
   for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
@@ -148,15 +149,27 @@ __device__ __forceinline__ void store_warp_tile(
         }
         if (VEC && vec4) {
           // n % 4 == 0 and rows 32-byte aligned: quads never straddle n.
-          if (col < n)
-            stg256(crow + col, v[0], v[1], v[2], v[3]);
+          if (col < n) {
+            if (stream)
+              stg256_cs(crow + col, v[0], v[1], v[2], v[3]);
+            else
+              stg256(crow + col, v[0], v[1], v[2], v[3]);
+          }
         } else if (VEC) {
           // n is even and the base 16-byte aligned: pairs never straddle n.
-          if (col < n)
-            *reinterpret_cast<double2 *>(crow + col) = make_double2(v[0], v[1]);
-          if (col + 2 < n)
-            *reinterpret_cast<double2 *>(crow + col + 2) =
-                make_double2(v[2], v[3]);
+          double2 *q = reinterpret_cast<double2 *>(crow + col);
+          if (col < n) {
+            if (stream)
+              __stcs(q, make_double2(v[0], v[1]));
+            else
+              *q = make_double2(v[0], v[1]);
+          }
+          if (col + 2 < n) {
+            if (stream)
+              __stcs(q + 1, make_double2(v[2], v[3]));
+            else
+              q[1] = make_double2(v[2], v[3]);
+          }
         } else {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -379,8 +392,10 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
     relu = false;
     addend = nullptr;
   }
-  store_warp_tile<MI, NP, true>(acc, dst, args.m, args.n, m0 + wm * T::WTM,
-                                n0 + wn * T::WTN, relu, g, t, vec4, addend);
+  store_warp_tile<MI, NP, true>(
+      acc, dst, args.m, args.n, m0 + wm * T::WTM, n0 + wn * T::WTN, relu, g, t,
+      vec4, addend,
+      args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_STREAM) != 0);
   if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
     __threadfence_system();
 }

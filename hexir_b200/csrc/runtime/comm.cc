@@ -115,6 +115,7 @@ struct hexir_comm_t {
   // hexir_sharded_linear_host_f64: streams for this GPU's host link (one
   // each way), its events, and device workspace kept between calls.
   CUstream up_stream = nullptr, down_stream = nullptr;
+  CUstream side_stream = nullptr;  // odd row chunks (their tails overlap)
   CUevent down_done = nullptr;
   CUdeviceptr a_dev = 0, w_dev = 0, c_dev = 0;
   size_t a_bytes = 0, w_bytes = 0, c_bytes = 0;
@@ -406,6 +407,8 @@ hexir_status_t hexir_comm_init_rank(const void *id, size_t size, int nranks,
   if (cr == CUDA_SUCCESS)
     cr = d.StreamCreate(&comm->down_stream, CU_STREAM_NON_BLOCKING);
   if (cr == CUDA_SUCCESS)
+    cr = d.StreamCreate(&comm->side_stream, CU_STREAM_NON_BLOCKING);
+  if (cr == CUDA_SUCCESS)
     cr = d.MemAlloc(&comm->scratch, kDescBytes + 16);
   if (cr == CUDA_SUCCESS)
     cr = d.MemAllocHost(reinterpret_cast<void **>(&comm->desc_host),
@@ -469,7 +472,7 @@ void hexir_comm_release(hexir_comm_t *comm) {
       d.MemFreeHost(comm->desc_host);
     if (comm->scratch)
       d.MemFree(comm->scratch);
-    for (CUstream st : {comm->up_stream, comm->down_stream})
+    for (CUstream st : {comm->up_stream, comm->down_stream, comm->side_stream})
       if (st) {
         d.StreamSynchronize(st);
         d.StreamDestroy(st);
@@ -937,18 +940,24 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
   }
   if (chain)
     wait_on(s, w_in[pieces - 1]);
+  // The row chunks are independent: odd ones run on the side stream, which
+  // starts after everything queued on `s` so far, so each chunk's last wave
+  // of tiles overlaps the next one's first; `s` joins it after the chunks.
+  CUstream side = comm->side_stream;
+  wait_on(side, event_on(s));
   for (uint32_t i = 0; i < kHostChunks && !failed; ++i) {
     uint64_t cb = 0, cnt = 0;
     host_chunk(rows, i, &cb, &cnt);
     if (!cnt)
       continue;
+    const CUstream on = i % 2 ? side : s;
     if (chain)
       upload_band(cb, cnt, bounds[pieces - 1], k);
     else if (!failed)
       note(d.MemcpyHtoDAsync(comm->a_dev + cb * row_a, a_rows + cb * k,
                              cnt * row_a, up),
            "row upload");
-    wait_on(s, event_on(up));
+    wait_on(on, event_on(up));
     if (failed)
       break;
     if (chain) {
@@ -958,26 +967,27 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
           reinterpret_cast<const double *>(comm->a_dev + cb * row_a + static_cast<size_t>(kl) * 8),
           reinterpret_cast<const double *>(comm->w_dev + static_cast<size_t>(kl) * row_c),
           reinterpret_cast<double *>(comm->c_dev + cb * row_c),
-          static_cast<uint32_t>(cnt), n, k - kl, relu | HEXIR_MATMUL_SPLIT_K(1), s,
+          static_cast<uint32_t>(cnt), n, k - kl, relu | HEXIR_MATMUL_SPLIT_K(1), on,
           &error, k, reinterpret_cast<const double *>(comm->c_dev + cb * row_c));
     } else {
       st = launch_matmul(
           dev, lib, reinterpret_cast<const double *>(comm->a_dev + cb * row_a),
           reinterpret_cast<const double *>(comm->w_dev),
           reinterpret_cast<double *>(comm->c_dev + cb * row_c),
-          static_cast<uint32_t>(cnt), n, k, chunk_flags, s, &error);
+          static_cast<uint32_t>(cnt), n, k, chunk_flags, on, &error);
     }
     if (st != HEXIR_OK) {
       failed = true;
       break;
     }
-    wait_on(down, event_on(s));
+    wait_on(down, event_on(on));
     if (!failed)
       note(d.MemcpyDtoHAsync(c_rows + cb * n, comm->c_dev + cb * row_c,
                              cnt * row_c, down),
            "row download");
   }
   // The caller's stream waits for everything this call queued elsewhere.
+  wait_on(s, event_on(side));
   wait_on(s, event_on(gs));
   wait_on(s, event_on(up));
   // ... and its downloads.
@@ -991,12 +1001,14 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
   // 3. Synchronous: the rows are in c_rows on return, and a failure on any
   //    rank is reported on every rank.
   hexir_status_t ss = hexir_comm_synchronize(comm, stream);
-  if (ss != HEXIR_OK) {
-    // The stream did not reach its end: let every queued copy finish
-    // before the events go.
+  if (ss != HEXIR_OK || failed) {
+    // The caller's stream may not have joined the others: let everything
+    // queued on them finish before the events go and the workspace is
+    // reused.
     d.StreamSynchronize(up);
     d.StreamSynchronize(down);
     d.StreamSynchronize(gs);
+    d.StreamSynchronize(side);
   }
   for (CUevent ev : events)
     d.EventDestroy(ev);

@@ -142,7 +142,21 @@ CUstream CudaDevice::copy_stream() {
   return copies;
 }
 
+CUstream CudaDevice::side_stream() {
+  if (!side) {
+    ContextGuard guard(state->context);
+    if (driver().StreamCreate(&side, CU_STREAM_NON_BLOCKING) != CUDA_SUCCESS)
+      side = nullptr;
+  }
+  return side;
+}
+
 CudaDevice::~CudaDevice() {
+  if (side) {
+    ContextGuard guard(state->context);
+    driver().StreamSynchronize(side);
+    driver().StreamDestroy(side);
+  }
   if (copies) {
     ContextGuard guard(state->context);
     driver().StreamSynchronize(copies);

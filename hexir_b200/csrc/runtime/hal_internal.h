@@ -96,6 +96,12 @@ struct CudaDevice : hexir_device_t {
   // pipelined upload / download of a large dispatch); created on first use.
   CUstream copy_stream();
   CUstream copies = nullptr;
+
+  // Second compute stream: independent row chunks of one dispatch alternate
+  // between `stream` and this one, so one chunk's last wave of tiles
+  // overlaps the next chunk's first; created on first use.
+  CUstream side_stream();
+  CUstream side = nullptr;
 };
 
 CudaDevice *as_cuda(hexir_device_t *device);

@@ -990,20 +990,46 @@ struct Vm {
       return HEXIR_ERROR_DEVICE;
     };
     auto launch = [&](uint64_t ra, uint64_t nr, uint64_t k0, uint64_t k1,
-                      uint32_t flags, bool cont) -> hexir_status_t {
+                      uint32_t flags, bool cont,
+                      CUstream on = nullptr) -> hexir_status_t {
       std::string error;
       double *c = reinterpret_cast<double *>(c_dev + ra * row_c);
       hexir_status_t ls = launch_matmul(
           dev->state, lib, reinterpret_cast<const double *>(a_dev + ra * row_a + k0 * 8),
           reinterpret_cast<const double *>(w_dev + k0 * row_c), c,
           static_cast<uint32_t>(nr), exe.n, static_cast<uint32_t>(k1 - k0),
-          flags | HEXIR_MATMUL_SPLIT_K(1), dev->stream, &error, exe.k,
+          flags | HEXIR_MATMUL_SPLIT_K(1), on ? on : dev->stream, &error, exe.k,
           cont ? c : nullptr);
       if (ls != HEXIR_OK)
         report(std::string("kernel '") + exe.name + "': " + error);
       return ls;
     };
     std::vector<CUevent> c_ready(kPipelineChunks, nullptr);
+    // The row chunks are independent: odd ones run on the side stream (after
+    // everything queued on the main stream so far), so each chunk's last
+    // wave of tiles overlaps the next one's first.  The main stream joins it
+    // after the chunks.
+    CUstream side = dev->side_stream();
+    bool side_started = false;
+    // Called before the first chunk is queued: the side stream starts after
+    // everything on the main stream up to here.
+    auto fork_side = [&]() {
+      if (!side)
+        return;
+      CUevent fork = event(dev->stream);
+      if (fork && d.StreamWaitEvent(side, fork, 0) == CUDA_SUCCESS)
+        side_started = true;
+    };
+    auto chunk_stream = [&](uint32_t i) -> CUstream {
+      return side_started && i % 2 == 1 ? side : dev->stream;
+    };
+    auto join_side = [&]() {
+      if (side_started) {
+        CUevent done = event(side);
+        if (done)
+          d.StreamWaitEvent(dev->stream, done, 0);
+      }
+    };
     if (pieces) {
       const uint64_t k1 = K / 2 / 32 * 32;
       const std::vector<uint32_t> b = k_piece_bounds(static_cast<uint32_t>(k1));
@@ -1030,17 +1056,21 @@ struct Vm {
           return st;
         }
       }
+      fork_side();
       for (uint32_t i = 0; i < kPipelineChunks; ++i) {
         if (!rows[i])
           continue;
-        d.StreamWaitEvent(dev->stream, chunk_ready[i], 0);
-        if ((st = launch(r0[i], rows[i], k1, K, relu, k1 > 0)) != HEXIR_OK) {
+        CUstream on = chunk_stream(i);
+        d.StreamWaitEvent(on, chunk_ready[i], 0);
+        if ((st = launch(r0[i], rows[i], k1, K, relu, k1 > 0, on)) != HEXIR_OK) {
+          join_side();
           release_events();
           return st;
         }
         if (stream_out)
-          c_ready[i] = event(dev->stream);
+          c_ready[i] = event(on);
       }
+      join_side();
     } else {
       std::vector<CUevent> a_ready(kPipelineChunks, nullptr);
       for (uint32_t i = 0; i < kPipelineChunks; ++i) {
@@ -1055,27 +1085,30 @@ struct Vm {
       // Every chunk uses the k split the whole matmul would use, so each
       // element is summed exactly as by the one-shot launch.
       const uint32_t flags = relu | HEXIR_MATMUL_SPLIT_K(whole.split_k);
+      fork_side();
       for (uint32_t i = 0; i < kPipelineChunks; ++i) {
         if (!rows[i])
           continue;
+        CUstream on = chunk_stream(i);
         if (a_ready[i])
-          d.StreamWaitEvent(dev->stream, a_ready[i], 0);
+          d.StreamWaitEvent(on, a_ready[i], 0);
         std::string error;
         st = launch_matmul(
             dev->state, lib,
             reinterpret_cast<const double *>(a_dev + r0[i] * row_a),
             reinterpret_cast<const double *>(w_dev),
             reinterpret_cast<double *>(c_dev + r0[i] * row_c),
-            static_cast<uint32_t>(rows[i]), exe.n, exe.k, flags, dev->stream,
-            &error);
+            static_cast<uint32_t>(rows[i]), exe.n, exe.k, flags, on, &error);
         if (st != HEXIR_OK) {
           report(std::string("kernel '") + exe.name + "': " + error);
+          join_side();
           release_events();
           return st;
         }
         if (stream_out)
-          c_ready[i] = event(dev->stream);
+          c_ready[i] = event(on);
       }
+      join_side();
     }
     end_span(span);
     if (stream_out) {

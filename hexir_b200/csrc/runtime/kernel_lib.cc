@@ -566,6 +566,10 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   }
   if (rows32 && (reinterpret_cast<uintptr_t>(args.c) & 31u) == 0)
     args.epilogue |= HEXIR_EPILOGUE_VEC4;
+  // A final output (not split-K partials, which the reduce reads back):
+  // evict-first stores, so c does not displace a's and b's panels in L2.
+  if (p.split_k == 1 && !p.stream_k())
+    args.epilogue |= HEXIR_EPILOGUE_STREAM;
 
   const unsigned grid_x = p.tiles_m * p.tiles_n;
   hexir_status_t status;
