@@ -625,59 +625,61 @@ def run_e2e(args, rank, world, ordinal, a_host, w_host, comm, pg, shard_flags):
                           shape=(m_total, N_DIM)).flush()
             obj = [path]
         pg.broadcast_object_list(obj, src=0)
-        shared = obj[0]
-        if shared:
-            c_all = np.memmap(shared, dtype=np.float64, mode="r+",
-                              shape=(m_total, N_DIM))
-            c_rows = c_all[begin:begin + rows]
-        else:
-            c_all = None
-            c_rows = np.empty((rows, N_DIM))
-        a_rows = np.ascontiguousarray(a_host)
-        w_all = np.ascontiguousarray(w_host)
-        registered = []
-        for arr in (a_rows, w_all, c_rows):
-            ptr = arr.ctypes.data
-            _ffi.check(lib.hexir_host_register(ptr, arr.nbytes), "host register")
-            registered.append(ptr)
-        stream = torch.cuda.current_stream().cuda_stream
-        flags = _ffi.MATMUL_RELU | _ffi.SHARD_W_ON_ALL
+        try:
+            shared = obj[0]
+            if shared:
+                c_all = np.memmap(shared, dtype=np.float64, mode="r+",
+                                  shape=(m_total, N_DIM))
+                c_rows = c_all[begin:begin + rows]
+            else:
+                c_all = None
+                c_rows = np.empty((rows, N_DIM))
+            a_rows = np.ascontiguousarray(a_host)
+            w_all = np.ascontiguousarray(w_host)
+            registered = []
+            for arr in (a_rows, w_all, c_rows):
+                ptr = arr.ctypes.data
+                _ffi.check(lib.hexir_host_register(ptr, arr.nbytes), "host register")
+                registered.append(ptr)
+            stream = torch.cuda.current_stream().cuda_stream
+            flags = _ffi.MATMUL_RELU | _ffi.SHARD_W_ON_ALL
 
-        def once():
-            _ffi.check(lib.hexir_sharded_linear_host_f64(
-                comm, a_rows.ctypes.data, w_all.ctypes.data, c_rows.ctypes.data,
-                m_total, N_DIM, K_DIM, flags, stream),
-                "hexir_sharded_linear_host_f64")
+            def once():
+                _ffi.check(lib.hexir_sharded_linear_host_f64(
+                    comm, a_rows.ctypes.data, w_all.ctypes.data, c_rows.ctypes.data,
+                    m_total, N_DIM, K_DIM, flags, stream),
+                    "hexir_sharded_linear_host_f64")
 
-        for _ in range(warm):
-            once()
-        pg.barrier()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            once()
-        sec = (time.perf_counter() - t0) / steps
-        t = torch.tensor([sec], device="cuda")
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        sec = float(t.item())
-        pg.barrier()
-        checked = None
-        if rank == 0 and c_all is not None:
-            # Every rank's rows as they landed in the shared result.
-            from oracle import oracle
-            sample = np.concatenate([
-                hx.shard_rows(m_total, world, r)[0] + np.array([0, m_rows // 2,
-                                                                m_rows - 1])
-                for r in range(world)])
-            want = oracle.relu(oracle.matmul(a_rows_global(sample), w_host))
-            checked = oracle.normwise_error(np.asarray(c_all[sample]), want)
-            if not checked <= 1e-12:
-                raise SystemExit(f"e2e result wrong: normwise error {checked}")
-        for ptr in registered:
-            lib.hexir_host_unregister(ptr)
-        pg.barrier()
-        if rank == 0 and shared:
-            del c_all, c_rows
-            os.unlink(shared)
+            for _ in range(warm):
+                once()
+            pg.barrier()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                once()
+            sec = (time.perf_counter() - t0) / steps
+            t = torch.tensor([sec], device="cuda")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            sec = float(t.item())
+            pg.barrier()
+            checked = None
+            if rank == 0 and c_all is not None:
+                # Every rank's rows as they landed in the shared result.
+                from oracle import oracle
+                sample = np.concatenate([
+                    hx.shard_rows(m_total, world, r)[0] + np.array([0, m_rows // 2,
+                                                                    m_rows - 1])
+                    for r in range(world)])
+                want = oracle.relu(oracle.matmul(a_rows_global(sample), w_host))
+                checked = oracle.normwise_error(np.asarray(c_all[sample]), want)
+                if not checked <= 1e-12:
+                    raise SystemExit(f"e2e result wrong: normwise error {checked}")
+            for ptr in registered:
+                lib.hexir_host_unregister(ptr)
+            pg.barrier()
+        finally:
+            # The shared result file goes even if the leg failed.
+            if rank == 0 and obj[0] and os.path.exists(obj[0]):
+                os.unlink(obj[0])
         h2d = a_host.nbytes * world + w_host.nbytes
         d2h = m_total * N_DIM * 8
         path_desc = ("hexir_sharded_linear_host_f64: each rank's host rows "

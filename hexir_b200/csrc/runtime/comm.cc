@@ -292,6 +292,33 @@ hexir_status_t reduce_failure(hexir_comm_t *comm, CUstream s, bool failed) {
 
 }  // namespace
 
+namespace {
+// Runs `fn` with a context current: the calling thread's own, when it has
+// one (a process driving GPU r under torch or another runtime has GPU r's
+// primary context current), else GPU 0's.  Page-locking is portable, so any
+// context serves; borrowing GPU 0's where another GPU is in use would create
+// a context on GPU 0 for nothing.
+template <typename Fn>
+hexir_status_t with_some_context(Fn fn) {
+  const Driver &d = driver();
+  if (!d.ok) {
+    set_last_error(d.error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  CUcontext current = nullptr;
+  if (d.CtxGetCurrent(&current) == CUDA_SUCCESS && current)
+    return fn();
+  std::string error;
+  DeviceState *dev = device_state(0, &error);
+  if (!dev) {
+    set_last_error(error);
+    return HEXIR_ERROR_DEVICE;
+  }
+  ContextGuard guard(dev->context);
+  return fn();
+}
+}  // namespace
+
 extern "C" {
 
 hexir_status_t hexir_shard_rows(uint64_t rows, uint32_t shards, uint32_t index,
@@ -1020,38 +1047,22 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
 hexir_status_t hexir_host_register(void *ptr, size_t bytes) {
   if (!ptr || !bytes)
     return HEXIR_ERROR_INVALID_ARGUMENT;
-  const Driver &d = driver();
-  if (!d.ok) {
-    set_last_error(d.error);
-    return HEXIR_ERROR_DEVICE;
-  }
-  std::string error;
-  DeviceState *dev = device_state(0, &error);
-  if (!dev) {
-    set_last_error(error);
-    return HEXIR_ERROR_DEVICE;
-  }
-  ContextGuard guard(dev->context);
-  const CUresult r = d.MemHostRegister(ptr, bytes, CU_MEMHOSTREGISTER_PORTABLE);
-  if (r != CUDA_SUCCESS)
-    return comm_fail(cuda_message("cuMemHostRegister", r));
-  return HEXIR_OK;
+  return with_some_context([&]() {
+    const CUresult r =
+        driver().MemHostRegister(ptr, bytes, CU_MEMHOSTREGISTER_PORTABLE);
+    return r == CUDA_SUCCESS ? HEXIR_OK
+                             : comm_fail(cuda_message("cuMemHostRegister", r));
+  });
 }
 
 hexir_status_t hexir_host_unregister(void *ptr) {
   if (!ptr)
     return HEXIR_ERROR_INVALID_ARGUMENT;
-  std::string error;
-  DeviceState *dev = device_state(0, &error);
-  if (!dev) {
-    set_last_error(error);
-    return HEXIR_ERROR_DEVICE;
-  }
-  ContextGuard guard(dev->context);
-  const CUresult r = driver().MemHostUnregister(ptr);
-  if (r != CUDA_SUCCESS)
-    return comm_fail(cuda_message("cuMemHostUnregister", r));
-  return HEXIR_OK;
+  return with_some_context([&]() {
+    const CUresult r = driver().MemHostUnregister(ptr);
+    return r == CUDA_SUCCESS ? HEXIR_OK
+                             : comm_fail(cuda_message("cuMemHostUnregister", r));
+  });
 }
 
 hexir_status_t hexir_comm_synchronize(hexir_comm_t *comm, void *stream) {

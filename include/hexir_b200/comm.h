@@ -160,7 +160,8 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
                                              uint32_t flags, void *stream);
 
 /* Page-lock (and unlock) an existing host range for fast copies to and from
- * every GPU of the process (cuMemHostRegister, portable). */
+ * every GPU of the process (cuMemHostRegister, portable), in the calling
+ * thread's current CUDA context, or GPU 0's where none is current. */
 hexir_status_t hexir_host_register(void *ptr, size_t bytes);
 hexir_status_t hexir_host_unregister(void *ptr);
 
