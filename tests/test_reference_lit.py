@@ -199,15 +199,8 @@ def test_rebuilt_lit_file_reads_back_the_same(tmp_path):
             {k: v for k, v in case.items() if k != "file"}, name
 
 
-@pytest.mark.parametrize("name", FILES)
-def test_reference_runtime_lit_file(tmp_path, name):
-    path = lit_path(tmp_path, name)
-    if path is None:
-        pytest.skip("needs the reference tree (its fixture directory)")
-    gpu = have_gpu()
-    missing = requires(path) - {"runtime", "compiler"} - ({"cuda"} if gpu else set())
-    if missing:
-        pytest.skip(f"needs {sorted(missing)} (lit would mark it UNSUPPORTED)")
+def run_lit_file(tmp_path, path, gpu):
+    """Every RUN line of one lit file; returns (ran, skipped) lines."""
     env = dict(os.environ,
                PATH=str(tools_dir(tmp_path)) + os.pathsep + os.environ["PATH"])
     ran, skipped = 0, []
@@ -223,9 +216,37 @@ def test_reference_runtime_lit_file(tmp_path, name):
         res = subprocess.run(["bash", "-o", "pipefail", "-c", cmd], env=env,
                              capture_output=True, text=True, timeout=300)
         assert res.returncode == 0, (
-            f"{name}: RUN: {line}\n--- stdout\n{res.stdout}\n--- stderr\n"
-            f"{res.stderr}")
+            f"{os.path.basename(path)}: RUN: {line}\n--- stdout\n{res.stdout}"
+            f"\n--- stderr\n{res.stderr}")
         ran += 1
+    return ran, skipped
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["hxb-cuda.mlir", "hxb-cpu-vs-gpu.mlir",
+                                  "hxb-errors.mlir"])
+def test_reference_cuda_lit_files_on_the_gpu(tmp_path, name):
+    """On a GPU machine (where the reference tree is absent, so the files
+    come from the fixture): every RUN line, the `--device=cuda` ones
+    included -- the CPU-vs-GPU diff, the GPU known answer, the misplaced
+    module refused on a CPU device, the CUDA HAL self-test."""
+    assert have_gpu(), "gpu-marked tests run where a GPU is expected"
+    path = lit_path(tmp_path, name)
+    assert path is not None
+    ran, skipped = run_lit_file(tmp_path, path, gpu=True)
+    assert ran == len(run_lines(path)) and not skipped
+
+
+@pytest.mark.parametrize("name", FILES)
+def test_reference_runtime_lit_file(tmp_path, name):
+    path = lit_path(tmp_path, name)
+    if path is None:
+        pytest.skip("needs the reference tree (its fixture directory)")
+    gpu = have_gpu()
+    missing = requires(path) - {"runtime", "compiler"} - ({"cuda"} if gpu else set())
+    if missing:
+        pytest.skip(f"needs {sorted(missing)} (lit would mark it UNSUPPORTED)")
+    ran, skipped = run_lit_file(tmp_path, path, gpu)
     assert ran > 0
     # Only the CUDA HAL self-test of hxb-errors.mlir needs a GPU outside the
     # files that require cuda.
