@@ -296,6 +296,110 @@ __device__ __forceinline__ void softmax_rows_bulk(
   }
 }
 
+// Rows longer than one block holds, split over a thread-block cluster of CL
+// CTAs: CTA r of the cluster holds columns [r seg, (r + 1) seg) of each row
+// (seg = cols / CL rounded up to even), in registers and, for the next row,
+// in its shared memory by bulk copy as in softmax_rows_bulk.  The row's
+// maximum and sum are each reduced in the CTA, published in one shared f64
+// of the CTA, and combined over the cluster in rank order through
+// distributed shared memory between two cluster barriers per row.  One slot
+// each is enough: a CTA writes its next maximum only after the second
+// barrier of the row, which every peer reaches only after reading the first
+// maximum, and its next sum only after the next row's first barrier, which
+// every peer reaches only after reading this sum.  Every CTA of a cluster
+// walks the same rows and executes the same barriers (a copy that times out
+// marks the error word and turns the CTA's remaining work off, never its
+// barriers); a last barrier keeps each CTA's shared memory alive until its
+// peers have read it.  The host runs it for even rows from a 16-byte
+// aligned x, so each segment starts 16-byte aligned.
+template <int THREADS, int PER, int CL>
+__device__ __forceinline__ void softmax_rows_cluster(
+    const hexir_activation_args_t &p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ double red[THREADS / 32];
+  __shared__ double part_max, part_sum;
+  __shared__ __align__(8) uint64_t bar;
+  double *buf = reinterpret_cast<double *>(smem_raw);
+  const uint32_t cols = p.cols;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t seg = ((cols + CL - 1) / CL + 1u) & ~1u;
+  const uint32_t c0 = min(cols, rank * seg);
+  const uint32_t len = min(cols, c0 + seg) - c0;
+  const uint32_t bytes = len * 8u;
+  const uint64_t clusters = gridDim.x / CL;
+  const uint64_t first = blockIdx.x / CL;  // the cluster's first row
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  bool live = true;  // false once a copy has run out of time
+  if (threadIdx.x == 0 && first < p.rows && bytes) {
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_load(buf, p.x + first * cols + c0, bytes, &bar);
+  }
+  uint32_t phase = 0;
+  for (uint64_t row = first; row < p.rows; row += clusters) {
+    if (bytes && live) {
+      const bool arrived = mbar_wait_bounded(&bar, phase, p.timeout_ns);
+      phase ^= 1u;
+      live = __syncthreads_and(arrived) != 0;
+    }
+    double v[PER];
+    double m = neg_inf();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      v[i] = j < len ? buf[j] : neg_inf();
+      m = v[i] > m ? v[i] : m;
+    }
+    m = block_reduce<THREADS>(m, red, MaxOp{});  // buf is read: free for the next row
+    const uint64_t next = row + clusters;
+    if (threadIdx.x == 0) {
+      if (live && bytes && next < p.rows) {
+        mbar_arrive_expect_tx(&bar, bytes);
+        bulk_load(buf, p.x + next * cols + c0, bytes, &bar);
+      }
+      part_max = m;
+    }
+    cluster_sync();
+    double rm = ld_cluster_f64(&part_max, 0);
+#pragma unroll
+    for (uint32_t r = 1; r < CL; ++r) {
+      const double x = ld_cluster_f64(&part_max, r);
+      rm = x > rm ? x : rm;
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t j = threadIdx.x + i * THREADS;
+      if (j < len) {
+        v[i] = exp(__dsub_rn(v[i], rm));
+        s = __dadd_rn(s, v[i]);
+      }
+    }
+    s = block_reduce<THREADS>(s, red, SumOp{});
+    if (threadIdx.x == 0)
+      part_sum = s;
+    cluster_sync();
+    double rs = ld_cluster_f64(&part_sum, 0);
+#pragma unroll
+    for (uint32_t r = 1; r < CL; ++r)
+      rs = __dadd_rn(rs, ld_cluster_f64(&part_sum, r));
+    rs = __drcp_rn(rs);
+    double *yr = p.out + row * cols + c0;
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const uint32_t j = threadIdx.x + i * THREADS;
+        if (j < len)
+          __stcs(yr + j, __dmul_rn(v[i], rs));
+      }
+    }
+  }
+  cluster_sync();
+}
+
 // Rows too long for registers: maximum, sum and output each read the row
 // (the second and third reads mostly from L2).
 template <int THREADS>
@@ -363,6 +467,23 @@ extern "C" __global__ void __launch_bounds__(512)
 extern "C" __global__ void __launch_bounds__(256, 2)
     hexir_softmax_bulk256_f64(const hexir_activation_args_t args) {
   softmax_rows_bulk<256, HEXIR_SOFTMAX_B256_COLS / 256>(args);
+}
+
+// Long even rows over clusters of 2, 4 and 8 CTAs, up to 8192 columns per
+// CTA (the host sets the cluster shape at launch).
+extern "C" __global__ void __launch_bounds__(256, 2)
+    hexir_softmax_cluster2_f64(const hexir_activation_args_t args) {
+  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 2>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(256, 2)
+    hexir_softmax_cluster4_f64(const hexir_activation_args_t args) {
+  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 4>(args);
+}
+
+extern "C" __global__ void __launch_bounds__(256, 2)
+    hexir_softmax_cluster8_f64(const hexir_activation_args_t args) {
+  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 8>(args);
 }
 
 // Short rows: the same persistent bulk-prefetch blocks with fewer elements

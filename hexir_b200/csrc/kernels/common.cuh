@@ -104,6 +104,39 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src,
       : "memory");
 }
 
+// Thread-block clusters.  This CTA's rank in its cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA of the cluster: writes before it (shared memory
+// included) are visible to reads after it in every CTA of the cluster.  The
+// hardware barrier has no timeout, so every CTA of a cluster must execute
+// the same sequence of these.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// An f64 in the shared memory of CTA `rank` of this cluster, at the place
+// `local` has in this CTA's (distributed shared memory).
+__device__ __forceinline__ double ld_cluster_f64(const double *local,
+                                                 uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(remote)
+               : "r"(smem_addr(local)), "r"(rank));
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];"
+               : "=d"(v)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(map))

@@ -95,6 +95,8 @@ void load() {
   // Optional: only used to make messages readable.
   d.GetErrorString =
       reinterpret_cast<decltype(d.GetErrorString)>(dlsym(lib, "cuGetErrorString"));
+  d.LaunchKernelEx =
+      reinterpret_cast<decltype(d.LaunchKernelEx)>(dlsym(lib, "cuLaunchKernelEx"));
   CUresult r = d.Init(0);
   if (r != CUDA_SUCCESS) {
     d.error = cuda_message("cuInit", r);

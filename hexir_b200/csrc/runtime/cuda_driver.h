@@ -85,6 +85,9 @@ struct Driver {
                                    CUtensorMapL2promotion,
                                    CUtensorMapFloatOOBfill) = nullptr;
   CUresult (*GetErrorString)(CUresult, const char **) = nullptr;
+  // Optional (launches with a cluster shape): null on drivers without it.
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **,
+                             void **) = nullptr;
 };
 
 // Loads libcuda once per process and calls cuInit(0).  Never null; check ok.

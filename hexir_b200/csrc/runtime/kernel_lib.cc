@@ -80,6 +80,41 @@ hexir_status_t launch(CUfunction fn, unsigned gx, unsigned gy, unsigned bx,
   return HEXIR_OK;
 }
 
+// A launch with a cluster shape of `cluster` CTAs along x.
+hexir_status_t launch_cluster(CUfunction fn, unsigned gx, unsigned cluster,
+                              unsigned bx, unsigned smem, CUstream stream,
+                              void **params, const char *what,
+                              std::string *error) {
+  if (fault_hit(FaultSite::Launch))
+    return fail(error, std::string(what) + ": injected fault (HEXIR_FAULT)");
+  const Driver &d = driver();
+  if (!d.LaunchKernelEx)
+    return fail(error, std::string(what) + ": the driver has no cuLaunchKernelEx");
+  CUlaunchAttribute attr;
+  std::memset(&attr, 0, sizeof(attr));
+  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+  attr.value.clusterDim.x = cluster;
+  attr.value.clusterDim.y = 1;
+  attr.value.clusterDim.z = 1;
+  CUlaunchConfig cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDimX = gx;
+  cfg.gridDimY = 1;
+  cfg.gridDimZ = 1;
+  cfg.blockDimX = bx;
+  cfg.blockDimY = 1;
+  cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = smem;
+  cfg.hStream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const CUresult r = d.LaunchKernelEx(&cfg, fn, params, nullptr);
+  if (r != CUDA_SUCCESS)
+    return fail(error, cuda_message(what, r));
+  count_launch();
+  return HEXIR_OK;
+}
+
 unsigned stream_grid(const DeviceState *dev, uint64_t pairs) {
   // Four 16-byte vectors per thread per pass, 256 threads per CTA; at most
   // 8 CTAs per SM, the rest by grid stride.
@@ -285,6 +320,23 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
        d.ModuleGetFunction(&lib->softmax_bulk_s4k, lib->module,
                            "hexir_softmax_bulk_s4k_f64") != CUDA_SUCCESS))
     lib->softmax_bulk_s2k = lib->softmax_bulk_s4k = nullptr;
+  // Optional: the cluster softmax for long rows, each CTA holding up to
+  // 8192 columns (64 KiB of shared memory).
+  {
+    const char *names[3] = {"hexir_softmax_cluster2_f64",
+                            "hexir_softmax_cluster4_f64",
+                            "hexir_softmax_cluster8_f64"};
+    bool all = lib->softmax_bulk256 != nullptr;
+    for (int i = 0; i < 3 && all; ++i)
+      all = d.ModuleGetFunction(&lib->softmax_cluster[i], lib->module,
+                                names[i]) == CUDA_SUCCESS &&
+            d.FuncSetAttribute(lib->softmax_cluster[i],
+                               CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                               HEXIR_SOFTMAX_B256_COLS * 8) == CUDA_SUCCESS;
+    if (!all)
+      for (CUfunction &f : lib->softmax_cluster)
+        f = nullptr;
+  }
   size_t word_bytes = 0;
   r = d.ModuleGetGlobal(&lib->error_word, &word_bytes, lib->module,
                         "hexir_device_error_word");
@@ -722,6 +774,24 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
                   static_cast<unsigned>(std::min<uint64_t>(rows, 3 * sms)), 1,
                   256, cols * 8u, stream, params,
                   "launch hexir_softmax_bulk_s4k_f64", error);
+  // Longer even rows: a cluster of 2, 4 or 8 CTAs per row, up to 8192
+  // columns each, two CTAs per SM.
+  const bool clustered = cols % 2 == 0 && cols > HEXIR_SOFTMAX_B256_COLS &&
+                         cols <= 8u * HEXIR_SOFTMAX_B256_COLS &&
+                         (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                         lib->softmax_cluster[0] && driver().LaunchKernelEx;
+  if (clustered) {
+    const unsigned cl = cols <= 2u * HEXIR_SOFTMAX_B256_COLS   ? 2u
+                        : cols <= 4u * HEXIR_SOFTMAX_B256_COLS ? 4u
+                                                               : 8u;
+    const uint32_t seg = ((cols + cl - 1) / cl + 1u) & ~1u;
+    const uint64_t clusters = std::max<uint64_t>(
+        1, std::min<uint64_t>(rows, 2 * sms / cl));
+    return launch_cluster(lib->softmax_cluster[cl == 2 ? 0 : cl == 4 ? 1 : 2],
+                          static_cast<unsigned>(clusters * cl), cl, 256,
+                          seg * 8u, stream, params,
+                          "launch hexir_softmax_cluster_f64", error);
+  }
   if (bulk && cols <= HEXIR_SOFTMAX_B256_COLS)
     return launch(lib->softmax_bulk256,
                   static_cast<unsigned>(std::min<uint64_t>(rows, 2 * sms)), 1,

@@ -39,6 +39,8 @@ struct KernelLib {
              softmax_b512 = nullptr, softmax_wide = nullptr,
              softmax_bulk256 = nullptr, softmax_bulk512 = nullptr,
              softmax_bulk_s2k = nullptr, softmax_bulk_s4k = nullptr;
+  // Long rows over thread-block clusters of 2, 4, 8 CTAs (all or none).
+  CUfunction softmax_cluster[3] = {};
   CUfunction dmma_probe = nullptr;
   // The reference's generated schedule, a measurement baseline only
   // (absent in images written before it existed).
