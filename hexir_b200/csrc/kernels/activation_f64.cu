@@ -469,22 +469,19 @@ extern "C" __global__ void __launch_bounds__(256, 2)
   softmax_rows_bulk<256, HEXIR_SOFTMAX_B256_COLS / 256>(args);
 }
 
-// Long even rows over clusters of 2, 4 and 8 CTAs, up to 8192 columns per
-// CTA (the host sets the cluster shape at launch).
-extern "C" __global__ void __launch_bounds__(256, 2)
-    hexir_softmax_cluster2_f64(const hexir_activation_args_t args) {
-  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 2>(args);
-}
-
-extern "C" __global__ void __launch_bounds__(256, 2)
-    hexir_softmax_cluster4_f64(const hexir_activation_args_t args) {
-  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 4>(args);
-}
-
-extern "C" __global__ void __launch_bounds__(256, 2)
-    hexir_softmax_cluster8_f64(const hexir_activation_args_t args) {
-  softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, 8>(args);
-}
+// Long even rows over clusters of 4-8 CTAs, up to 8192 columns per CTA (the
+// host sets the cluster shape at launch).
+#define HEXIR_SOFTMAX_CLUSTER_KERNEL(CL)                                   \
+  extern "C" __global__ void __launch_bounds__(256, 2)                     \
+      hexir_softmax_cluster##CL##_f64(const hexir_activation_args_t args) { \
+    softmax_rows_cluster<256, HEXIR_SOFTMAX_B256_COLS / 256, CL>(args);    \
+  }
+HEXIR_SOFTMAX_CLUSTER_KERNEL(4)
+HEXIR_SOFTMAX_CLUSTER_KERNEL(5)
+HEXIR_SOFTMAX_CLUSTER_KERNEL(6)
+HEXIR_SOFTMAX_CLUSTER_KERNEL(7)
+HEXIR_SOFTMAX_CLUSTER_KERNEL(8)
+#undef HEXIR_SOFTMAX_CLUSTER_KERNEL
 
 // Short rows: the same persistent bulk-prefetch blocks with fewer elements
 // per thread, so more blocks (and so more row copies in flight) fit an SM.

@@ -97,6 +97,9 @@ void load() {
       reinterpret_cast<decltype(d.GetErrorString)>(dlsym(lib, "cuGetErrorString"));
   d.LaunchKernelEx =
       reinterpret_cast<decltype(d.LaunchKernelEx)>(dlsym(lib, "cuLaunchKernelEx"));
+  d.OccupancyMaxActiveClusters =
+      reinterpret_cast<decltype(d.OccupancyMaxActiveClusters)>(
+          dlsym(lib, "cuOccupancyMaxActiveClusters"));
   CUresult r = d.Init(0);
   if (r != CUDA_SUCCESS) {
     d.error = cuda_message("cuInit", r);

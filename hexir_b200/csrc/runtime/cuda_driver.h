@@ -88,6 +88,8 @@ struct Driver {
   // Optional (launches with a cluster shape): null on drivers without it.
   CUresult (*LaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **,
                              void **) = nullptr;
+  CUresult (*OccupancyMaxActiveClusters)(int *, CUfunction,
+                                         const CUlaunchConfig *) = nullptr;
 };
 
 // Loads libcuda once per process and calls cuInit(0).  Never null; check ok.

@@ -80,6 +80,46 @@ hexir_status_t launch(CUfunction fn, unsigned gx, unsigned gy, unsigned bx,
   return HEXIR_OK;
 }
 
+// The launch configuration of `gx` CTAs in clusters of `cluster` along x.
+struct ClusterLaunch {
+  CUlaunchAttribute attr;
+  CUlaunchConfig cfg;
+  ClusterLaunch(unsigned gx, unsigned cluster, unsigned bx, unsigned smem,
+                CUstream stream) {
+    std::memset(&attr, 0, sizeof(attr));
+    attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr.value.clusterDim.x = cluster;
+    attr.value.clusterDim.y = 1;
+    attr.value.clusterDim.z = 1;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDimX = gx;
+    cfg.gridDimY = 1;
+    cfg.gridDimZ = 1;
+    cfg.blockDimX = bx;
+    cfg.blockDimY = 1;
+    cfg.blockDimZ = 1;
+    cfg.sharedMemBytes = smem;
+    cfg.hStream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+  }
+};
+
+// How many clusters of this shape can be resident at once: clusters are
+// placed inside a GPC, so fewer fit than SMs / cluster size suggests.  0 if
+// the driver cannot say.
+unsigned max_active_clusters(CUfunction fn, unsigned cluster, unsigned bx,
+                             unsigned smem) {
+  const Driver &d = driver();
+  if (!d.OccupancyMaxActiveClusters)
+    return 0;
+  ClusterLaunch l(cluster, cluster, bx, smem, nullptr);
+  int n = 0;
+  return d.OccupancyMaxActiveClusters(&n, fn, &l.cfg) == CUDA_SUCCESS && n > 0
+             ? static_cast<unsigned>(n)
+             : 0u;
+}
+
 // A launch with a cluster shape of `cluster` CTAs along x.
 hexir_status_t launch_cluster(CUfunction fn, unsigned gx, unsigned cluster,
                               unsigned bx, unsigned smem, CUstream stream,
@@ -90,25 +130,8 @@ hexir_status_t launch_cluster(CUfunction fn, unsigned gx, unsigned cluster,
   const Driver &d = driver();
   if (!d.LaunchKernelEx)
     return fail(error, std::string(what) + ": the driver has no cuLaunchKernelEx");
-  CUlaunchAttribute attr;
-  std::memset(&attr, 0, sizeof(attr));
-  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-  attr.value.clusterDim.x = cluster;
-  attr.value.clusterDim.y = 1;
-  attr.value.clusterDim.z = 1;
-  CUlaunchConfig cfg;
-  std::memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDimX = gx;
-  cfg.gridDimY = 1;
-  cfg.gridDimZ = 1;
-  cfg.blockDimX = bx;
-  cfg.blockDimY = 1;
-  cfg.blockDimZ = 1;
-  cfg.sharedMemBytes = smem;
-  cfg.hStream = stream;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  const CUresult r = d.LaunchKernelEx(&cfg, fn, params, nullptr);
+  ClusterLaunch l(gx, cluster, bx, smem, stream);
+  const CUresult r = d.LaunchKernelEx(&l.cfg, fn, params, nullptr);
   if (r != CUDA_SUCCESS)
     return fail(error, cuda_message(what, r));
   count_launch();
@@ -323,11 +346,12 @@ KernelLib *library_for_image(DeviceState *dev, const void *image, size_t size,
   // Optional: the cluster softmax for long rows, each CTA holding up to
   // 8192 columns (64 KiB of shared memory).
   {
-    const char *names[3] = {"hexir_softmax_cluster2_f64",
-                            "hexir_softmax_cluster4_f64",
-                            "hexir_softmax_cluster8_f64"};
+    const char *names[5] = {
+        "hexir_softmax_cluster4_f64", "hexir_softmax_cluster5_f64",
+        "hexir_softmax_cluster6_f64", "hexir_softmax_cluster7_f64",
+        "hexir_softmax_cluster8_f64"};
     bool all = lib->softmax_bulk256 != nullptr;
-    for (int i = 0; i < 3 && all; ++i)
+    for (int i = 0; i < 5 && all; ++i)
       all = d.ModuleGetFunction(&lib->softmax_cluster[i], lib->module,
                                 names[i]) == CUDA_SUCCESS &&
             d.FuncSetAttribute(lib->softmax_cluster[i],
@@ -774,20 +798,28 @@ hexir_status_t launch_activation(DeviceState *dev, KernelLib *lib, uint32_t op,
                   static_cast<unsigned>(std::min<uint64_t>(rows, 3 * sms)), 1,
                   256, cols * 8u, stream, params,
                   "launch hexir_softmax_bulk_s4k_f64", error);
-  // Longer even rows: a cluster of 2, 4 or 8 CTAs per row, up to 8192
-  // columns each, two CTAs per SM.
-  const bool clustered = cols % 2 == 0 && cols > HEXIR_SOFTMAX_B256_COLS &&
+  // Long even rows, 28674-65536 columns: a cluster of ceil(cols / 8192)
+  // CTAs per row (4-8), each holding a segment at least 7/8 full, two CTAs
+  // per SM.  Each row costs the cluster two barriers (~3.5 us with the
+  // reductions), so shorter rows, whose segments would be part empty, stay
+  // with the per-row blocks and the three-pass block.
+  const bool clustered = cols % 2 == 0 && cols > 3u * HEXIR_SOFTMAX_B256_COLS +
+                                                     HEXIR_SOFTMAX_B256_COLS / 2 &&
                          cols <= 8u * HEXIR_SOFTMAX_B256_COLS &&
                          (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                          lib->softmax_cluster[0] && driver().LaunchKernelEx;
   if (clustered) {
-    const unsigned cl = cols <= 2u * HEXIR_SOFTMAX_B256_COLS   ? 2u
-                        : cols <= 4u * HEXIR_SOFTMAX_B256_COLS ? 4u
-                                                               : 8u;
+    const unsigned cl = (cols + HEXIR_SOFTMAX_B256_COLS - 1) / HEXIR_SOFTMAX_B256_COLS;
     const uint32_t seg = ((cols + cl - 1) / cl + 1u) & ~1u;
-    const uint64_t clusters = std::max<uint64_t>(
-        1, std::min<uint64_t>(rows, 2 * sms / cl));
-    return launch_cluster(lib->softmax_cluster[cl == 2 ? 0 : cl == 4 ? 1 : 2],
+    CUfunction fn = lib->softmax_cluster[cl - 4];
+    // Persistent clusters, all resident at once (a cluster that waited for
+    // another to finish would add its whole share of rows to the time).
+    unsigned resident = max_active_clusters(fn, cl, 256, seg * 8u);
+    if (!resident)
+      resident = static_cast<unsigned>(2 * sms / cl);
+    const uint64_t clusters =
+        std::max<uint64_t>(1, std::min<uint64_t>(rows, resident));
+    return launch_cluster(fn,
                           static_cast<unsigned>(clusters * cl), cl, 256,
                           seg * 8u, stream, params,
                           "launch hexir_softmax_cluster_f64", error);

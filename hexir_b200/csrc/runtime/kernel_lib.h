@@ -39,8 +39,9 @@ struct KernelLib {
              softmax_b512 = nullptr, softmax_wide = nullptr,
              softmax_bulk256 = nullptr, softmax_bulk512 = nullptr,
              softmax_bulk_s2k = nullptr, softmax_bulk_s4k = nullptr;
-  // Long rows over thread-block clusters of 2, 4, 8 CTAs (all or none).
-  CUfunction softmax_cluster[3] = {};
+  // Long rows over thread-block clusters of 4-8 CTAs, by cluster size - 4
+  // (all or none).
+  CUfunction softmax_cluster[5] = {};
   CUfunction dmma_probe = nullptr;
   // The reference's generated schedule, a measurement baseline only
   // (absent in images written before it existed).

@@ -96,17 +96,18 @@ def test_elementwise_activation_over_the_whole_range(gpu, op):
     (64, 1026), (1000, 2048), (1200, 1026), (700, 2050), (450, 3000),
     (700, 4096), (40, 4097), (17, 8192), (700, 8192), (9, 8193),
     (9, 16384), (300, 12000), (5, 16385), (3, 40000),
-    # clusters of 2 / 4 / 8 CTAs per row, with more rows than clusters so
-    # every cluster walks several rows
-    (400, 8194), (400, 12000), (200, 16386), (200, 20000), (64, 32768),
-    (100, 32770), (100, 40000), (20, 65536)])
+    (400, 8194), (400, 12000), (200, 16386), (200, 20000),
+    # clusters of 4-8 CTAs per row (28674-65536 even columns), with more
+    # rows than resident clusters so every cluster walks several rows
+    (300, 24578), (300, 28674), (160, 32768), (100, 32770), (100, 40000), (60, 49152),
+    (50, 57000), (40, 65536)])
 def test_softmax_matches_oracle(gpu, rows, cols):
     """Every launch shape at and around its column limit: warp per row; the
     persistent bulk-prefetch blocks for even rows, short-row (<= 2048, <=
     4096 columns) and long (more rows than blocks, so each block walks
-    several); rows of 8194-65536 even columns split over thread-block
-    clusters of 2, 4 and 8 CTAs; the 256- and 512-thread blocks for odd
-    rows; the three-pass block beyond."""
+    several); rows of 28674-65536 even columns split over thread-block
+    clusters of 4-8 CTAs; the 256- and 512-thread blocks for odd rows; the
+    three-pass block for the rest."""
     x = np.random.default_rng(rows * cols).normal(0, 3, (rows, cols))
     got = run_gpu(gpu, "softmax", x)
     want = oracle.activation("softmax", x)
@@ -114,7 +115,7 @@ def test_softmax_matches_oracle(gpu, rows, cols):
     assert np.all(np.abs(got.sum(axis=1) - 1) <= (cols + 16) * 2.0 ** -52)
 
 
-@pytest.mark.parametrize("cols", [7, 1024, 5000, 16384, 20000, 40000])
+@pytest.mark.parametrize("cols", [7, 1024, 5000, 16384, 20000, 40000, 65536])
 def test_softmax_special_rows(gpu, cols):
     """A NaN or +inf anywhere in a row, or a row of -inf, makes that row NaN
     (x - max is NaN), like the oracle; -inf elsewhere gives exact zeros; a
