@@ -11,5 +11,6 @@ extern "C" __device__ unsigned int hexir_device_error_word = 0u;
 #include "elementwise_f64.cu"
 #include "activation_f64.cu"
 #include "linear_f64.cu"
+#include "linear_guarded_f64.cu"
 #include "probe_f64.cu"
 #include "baseline_f64.cu"

@@ -15,221 +15,13 @@
 //                             and 16x128x32 (3, two CTAs per SM) for tall,
 //                             medium and skinny row counts.
 //                             Needs k and n even and 16-byte aligned bases.
-//   hexir_linear_f64_guarded  any shape and alignment: bounds-checked loads,
-//                             64x64x16 tile, double-buffered shared memory.
-//   hexir_linear_f64_splitk_reduce
-//                             sums split-K partials in split order, then
-//                             applies the epilogue.
-//
-// Shared-memory layouts (both kernels):
-//   A tile [BM][BK] is held as BK/8 slabs of [BM rows][8 doubles] (64 B per
-//   row).  A thread's A fragment for one k8 step is one 16-byte load.
-//   B tile [BK][BN] is held as BN/16 slabs of [BK rows][16 doubles] (128 B
-//   per row) with the 16-byte chunk index XORed by (row & 7) -- the TMA
-//   128-byte swizzle -- so fragment loads hit 32 distinct banks.
-//   Within every k8 step the MMA's k slot s maps to physical k 2s (s < 4) and
-//   2(s-4)+1 (s >= 4), and within every 16-column block MMA tile j column nn
-//   maps to physical column 2nn + j.  Both permutations are applied to A and
-//   B alike, so the product is unchanged; they make every fragment a 16-byte
-//   load and every output row segment of a thread 4 contiguous doubles.
+//   hexir_linear_f64_tma_sk   the 128x128x32 pipeline as a persistent
+//   hexir_linear_f64_sk_fixup stream-K launch, and the kernel that sums the
+//                             tiles whose k range was split over CTAs.
+//   (hexir_linear_f64_guarded and hexir_linear_f64_splitk_reduce, which
+//   need no TMA, are in linear_guarded_f64.cu.)
 
-#include "common.cuh"
-
-namespace hexir {
-
-
-// Grouped raster: group_m row-tiles share each sweep over the column tiles,
-// so concurrently running CTAs reuse the same A and B panels from L2.
-__device__ __forceinline__ void tile_of(uint32_t linear, uint32_t tiles_m,
-                                        uint32_t tiles_n, uint32_t group_m,
-                                        uint32_t &tm, uint32_t &tn) {
-  const uint32_t per_group = group_m * tiles_n;
-  const uint32_t group = linear / per_group;
-  const uint32_t first_m = group * group_m;
-  const uint32_t rows = min(group_m, tiles_m - first_m);
-  const uint32_t in_group = linear - group * per_group;
-  tm = first_m + in_group % rows;
-  tn = in_group / rows;
-}
-
-// One k8 step of a warp tile of MI m16-tiles by NP 16-column blocks.
-//   a_slab   shared address of the [rows][8] A slab holding this k8 step
-//   a_row    first tile row of this warp
-//   b_slab   shared address of the warp's first [rows][16] B slab
-//   b_stride bytes between consecutive B slabs
-//   k_row    row of this k8 step inside the B slabs (a multiple of 8)
-template <int MI, int NP>
-__device__ __forceinline__ void dmma_k8_step(double (&acc)[MI][2 * NP][4],
-                                             uint32_t a_slab, uint32_t a_row,
-                                             uint32_t b_slab,
-                                             uint32_t b_stride, uint32_t k_row,
-                                             uint32_t g, uint32_t t) {
-  double2 alo[MI], ahi[MI];
-#pragma unroll
-  for (int mi = 0; mi < MI; ++mi) {
-    const uint32_t r = a_row + mi * 16 + g;
-    alo[mi] = lds128(a_slab + r * 64 + t * 16);
-    ahi[mi] = lds128(a_slab + (r + 8) * 64 + t * 16);
-  }
-  double2 bk0[NP], bk1[NP];
-  const uint32_t r0 = k_row + 2 * t, r1 = r0 + 1;
-#pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    const uint32_t base = b_slab + p * b_stride;
-    bk0[p] = lds128(base + r0 * 128 + ((g ^ (r0 & 7)) << 4));
-    bk1[p] = lds128(base + r1 * 128 + ((g ^ (r1 & 7)) << 4));
-  }
-#pragma unroll
-  for (int mi = 0; mi < MI; ++mi) {
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      dmma_16x8x8(acc[mi][2 * p], alo[mi].x, ahi[mi].x, alo[mi].y, ahi[mi].y,
-                  bk0[p].x, bk1[p].x);
-      dmma_16x8x8(acc[mi][2 * p + 1], alo[mi].x, ahi[mi].x, alo[mi].y,
-                  ahi[mi].y, bk0[p].y, bk1[p].y);
-    }
-  }
-}
-
-// Write a warp tile.  Row r of m16-tile mi holds, in this thread, the four
-// consecutive columns col..col+3 = (tile 2p).d0, (2p+1).d0, (2p).d1, (2p+1).d1;
-// row r+8 the same with d2, d3.
-template <int MI, int NP, bool VEC>
-__device__ __forceinline__ void store_warp_tile(
-    const double (&acc)[MI][2 * NP][4], double *__restrict__ c, uint32_t m,
-    uint32_t n, uint32_t row0, uint32_t col0, bool relu, uint32_t g,
-    uint32_t t, bool vec4 = false, const double *__restrict__ addend = nullptr,
-    bool stream = false) {
-#pragma unroll
-  for (int mi = 0; mi < MI; ++mi) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t row = row0 + mi * 16 + g + half * 8;
-      if (row >= m)
-        continue;
-      double *crow = c + (size_t)row * n;
-#pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        const uint32_t col = col0 + p * 16 + 4 * t;
-        double v[4] = {acc[mi][2 * p][2 * half], acc[mi][2 * p + 1][2 * half],
-                       acc[mi][2 * p][2 * half + 1],
-                       acc[mi][2 * p + 1][2 * half + 1]};
-        if (addend) {
-          // The fused add: the same rounding as adding the stored product.
-          const double *arow = addend + (size_t)row * n;
-          double b[4] = {0.0, 0.0, 0.0, 0.0};
-          if (VEC && vec4) {
-            if (col < n)
-              ldg256(arow + col, b);
-          } else if (VEC) {
-            if (col < n) {
-              const double2 x = *reinterpret_cast<const double2 *>(arow + col);
-              b[0] = x.x;
-              b[1] = x.y;
-            }
-            if (col + 2 < n) {
-              const double2 x = *reinterpret_cast<const double2 *>(arow + col + 2);
-              b[2] = x.x;
-              b[3] = x.y;
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (col + q < n)
-                b[q] = arow[col + q];
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            v[q] = __dadd_rn(v[q], b[q]);
-        }
-        if (relu) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            v[q] = relu_ref(v[q]);
-        }
-        if (VEC && vec4) {
-          // n % 4 == 0 and rows 32-byte aligned: quads never straddle n.
-          if (col < n) {
-            if (stream)
-              stg256_cs(crow + col, v[0], v[1], v[2], v[3]);
-            else
-              stg256(crow + col, v[0], v[1], v[2], v[3]);
-          }
-        } else if (VEC) {
-          // n is even and the base 16-byte aligned: pairs never straddle n.
-          double2 *q = reinterpret_cast<double2 *>(crow + col);
-          if (col < n) {
-            if (stream)
-              __stcs(q, make_double2(v[0], v[1]));
-            else
-              *q = make_double2(v[0], v[1]);
-          }
-          if (col + 2 < n) {
-            if (stream)
-              __stcs(q + 1, make_double2(v[2], v[3]));
-            else
-              q[1] = make_double2(v[2], v[3]);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (col + q < n)
-              crow[col + q] = v[q];
-        }
-      }
-    }
-  }
-}
-
-// Start a warp tile's sums from c_in: the inverse of store_warp_tile's
-// mapping (elements outside m x n stay 0 and are never stored).
-template <int MI, int NP, bool VEC>
-__device__ __forceinline__ void load_warp_tile(
-    double (&acc)[MI][2 * NP][4], const double *__restrict__ c_in, uint32_t m,
-    uint32_t n, uint32_t row0, uint32_t col0, uint32_t g, uint32_t t,
-    bool vec4 = false) {
-#pragma unroll
-  for (int mi = 0; mi < MI; ++mi) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t row = row0 + mi * 16 + g + half * 8;
-      if (row >= m)
-        continue;
-      const double *crow = c_in + (size_t)row * n;
-#pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        const uint32_t col = col0 + p * 16 + 4 * t;
-        double v[4] = {0.0, 0.0, 0.0, 0.0};
-        if (VEC && vec4) {
-          if (col < n)
-            ldg256(crow + col, v);
-        } else if (VEC) {
-          if (col < n) {
-            const double2 x = *reinterpret_cast<const double2 *>(crow + col);
-            v[0] = x.x;
-            v[1] = x.y;
-          }
-          if (col + 2 < n) {
-            const double2 x = *reinterpret_cast<const double2 *>(crow + col + 2);
-            v[2] = x.x;
-            v[3] = x.y;
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (col + q < n)
-              v[q] = crow[col + q];
-        }
-        acc[mi][2 * p][2 * half] = v[0];
-        acc[mi][2 * p + 1][2 * half] = v[1];
-        acc[mi][2 * p][2 * half + 1] = v[2];
-        acc[mi][2 * p + 1][2 * half + 1] = v[3];
-      }
-    }
-  }
-}
-
-}  // namespace hexir
+#include "linear_tiles.cuh"
 
 using namespace hexir;
 
@@ -673,139 +465,4 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 2)
                              const __grid_constant__ CUtensorMap map_b,
                              const hexir_linear_args_t args) {
   linear_tma_body<Tile16>(&map_a, &map_b, args);
-}
-
-// Guarded variant: every global load is bounds checked, so any m, n, k and
-// any 8-byte alignment works (odd k or n, 1x1x1, row shards at odd offsets).
-extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
-    hexir_linear_f64_guarded(const hexir_linear_args_t args) {
-  constexpr int BM = HEXIR_LINEAR_G_BM, BN = HEXIR_LINEAR_G_BN,
-                BK = HEXIR_LINEAR_G_BK;
-  constexpr int A_SLAB = BM * 8, B_SLAB = BK * 16;
-  constexpr int A_STAGE = BM * BK, B_STAGE = BK * BN;
-  constexpr int PER_THREAD_A = A_STAGE / HEXIR_LINEAR_G_THREADS;  // 8
-  constexpr int PER_THREAD_B = B_STAGE / HEXIR_LINEAR_G_THREADS;  // 8
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  double *sa = reinterpret_cast<double *>(smem_raw);
-  double *sb = sa + 2 * A_STAGE;
-
-  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t g = lane >> 2, t = lane & 3;
-  const uint32_t wm = warp >> 1, wn = warp & 1;  // warp tile 32 x 32
-
-  uint32_t tm, tn;
-  tile_of(blockIdx.x, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
-  const uint32_t split = blockIdx.y;
-  const uint32_t k_tiles = (args.k + BK - 1) / BK;
-  const uint32_t kt_begin = split * args.k_tiles_per_split;
-  const uint32_t kt_end = min(k_tiles, kt_begin + args.k_tiles_per_split);
-  const uint32_t m0 = tm * BM, n0 = tn * BN;
-  const uint32_t m = args.m, n = args.n, k = args.k;
-  const size_t lda = args.lda ? args.lda : k;
-  const double *__restrict__ a = args.a;
-  const double *__restrict__ b = args.b;
-
-  double ra[PER_THREAD_A], rb[PER_THREAD_B];
-  auto load_tile = [&](uint32_t kt) {
-    const uint32_t k0 = kt * BK;
-#pragma unroll
-    for (int i = 0; i < PER_THREAD_A; ++i) {
-      const uint32_t e = tid + i * HEXIR_LINEAR_G_THREADS;
-      const uint32_t row = e / BK, kc = e % BK;
-      const uint32_t gr = m0 + row, gk = k0 + kc;
-      ra[i] = (gr < m && gk < k) ? a[(size_t)gr * lda + gk] : 0.0;
-    }
-#pragma unroll
-    for (int i = 0; i < PER_THREAD_B; ++i) {
-      const uint32_t e = tid + i * HEXIR_LINEAR_G_THREADS;
-      const uint32_t kr = e / BN, col = e % BN;
-      const uint32_t gk = k0 + kr, gc = n0 + col;
-      rb[i] = (gk < k && gc < n) ? b[(size_t)gk * n + gc] : 0.0;
-    }
-  };
-  auto store_tile = [&](int buf) {
-    double *as = sa + buf * A_STAGE;
-    double *bs = sb + buf * B_STAGE;
-#pragma unroll
-    for (int i = 0; i < PER_THREAD_A; ++i) {
-      const uint32_t e = tid + i * HEXIR_LINEAR_G_THREADS;
-      const uint32_t row = e / BK, kc = e % BK;
-      as[(kc >> 3) * A_SLAB + row * 8 + (kc & 7)] = ra[i];
-    }
-#pragma unroll
-    for (int i = 0; i < PER_THREAD_B; ++i) {
-      const uint32_t e = tid + i * HEXIR_LINEAR_G_THREADS;
-      const uint32_t kr = e / BN, col = e % BN;
-      const uint32_t chunk = ((col & 15) >> 1) ^ (kr & 7);
-      bs[(col >> 4) * B_SLAB + kr * 16 + chunk * 2 + (col & 1)] = rb[i];
-    }
-  };
-
-  double acc[2][4][4];
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        acc[i][j][q] = 0.0;
-  if (args.c_in)
-    load_warp_tile<2, 2, false>(acc, args.c_in, m, n, m0 + wm * 32,
-                                n0 + wn * 32, g, t);
-
-  if (kt_begin < kt_end) {
-    load_tile(kt_begin);
-    store_tile(0);
-    __syncthreads();
-    const uint32_t sa_addr = smem_addr(sa), sb_addr = smem_addr(sb);
-    for (uint32_t kt = kt_begin; kt < kt_end; ++kt) {
-      const int buf = (kt - kt_begin) & 1;
-      const bool more = kt + 1 < kt_end;
-      if (more)
-        load_tile(kt + 1);
-      const uint32_t a_stage = sa_addr + buf * A_STAGE * 8;
-      const uint32_t b_stage = sb_addr + buf * B_STAGE * 8 + wn * 2 * B_SLAB * 8;
-#pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk)
-        dmma_k8_step<2, 2>(acc, a_stage + kk * A_SLAB * 8, wm * 32, b_stage,
-                           B_SLAB * 8, kk * 8, g, t);
-      if (more)
-        store_tile(buf ^ 1);
-      __syncthreads();
-    }
-  }
-
-  double *dst = args.c;
-  bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
-  const double *addend =
-      (args.epilogue & HEXIR_EPILOGUE_ADD) ? args.addend : nullptr;
-  if (args.split_k > 1) {
-    dst += (size_t)split * m * n;
-    relu = false;
-    addend = nullptr;
-  }
-  store_warp_tile<2, 2, false>(acc, dst, m, n, m0 + wm * 32, n0 + wn * 32,
-                               relu, g, t, false, addend);
-  if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
-    __threadfence_system();
-}
-
-// c[i] = epilogue(sum over s in 0..split-1 of partials[s][i]), summed in
-// split order so the result does not depend on scheduling; the epilogue adds
-// addend[i] (HEXIR_EPILOGUE_ADD), then applies the relu.
-extern "C" __global__ void __launch_bounds__(256)
-    hexir_linear_f64_splitk_reduce(const hexir_reduce_args_t args) {
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-       i < args.count; i += stride) {
-    double s = 0.0;
-    for (uint32_t p = 0; p < args.split; ++p)
-      s = __dadd_rn(s, args.partials[(size_t)p * args.count + i]);
-    if (args.epilogue & HEXIR_EPILOGUE_ADD)
-      s = __dadd_rn(s, args.addend[i]);
-    args.c[i] = relu ? relu_ref(s) : s;
-  }
-  if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)
-    __threadfence_system();
 }

@@ -27,17 +27,17 @@
 #include "hexir_b200/kernels.h"
 #include "kernel_lib.h"
 
-// The device code this path launches: its own copy of the linear kernels.
-// The error word below is this copy's own, and nothing reads it: only the
-// TMA kernels' bounded mbarrier waits ever set it, and this path launches
-// just the guarded kernel (double-buffered through __syncthreads) and the
-// split-K reduction, neither of which waits on anything.  A variant of this
-// path that launched a kernel with a bounded wait would have to read it
-// back (cudaMemcpyFromSymbol) to report a timeout.
+// The device code this path launches: its own copy of the guarded linear
+// kernel and the split-K reduction (not of the TMA kernels, which it never
+// launches).  Neither waits on anything but __syncthreads, so nothing sets
+// the error word below and nothing reads it; it is defined only because the
+// shared device helpers name one.  A variant of this path that launched a
+// kernel with a bounded wait would have to read it back
+// (cudaMemcpyFromSymbol) to report a timeout.
 extern "C" {
 __device__ unsigned int hexir_device_error_word = 0u;
 }
-#include "../kernels/linear_f64.cu"
+#include "../kernels/linear_guarded_f64.cu"
 
 // Split-K partial sums, HEXIR_NOALLOC_SCRATCH_BYTES of device memory on every
 // GPU where this library's device code is loaded, held until the process
