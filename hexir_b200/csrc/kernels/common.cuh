@@ -137,6 +137,22 @@ __device__ __forceinline__ double ld_cluster_f64(const double *local,
   return v;
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel of
+// the stream, when it was launched with programmatic stream serialization,
+// begin launching (its CTAs take SMs as this grid's CTAs retire); griddep_wait
+// in that kernel then blocks until this grid has completed and its memory
+// is visible.  For a kernel launched without the attribute both are no-ops
+// (stream order already holds).  Neither can wait for ever: the wait ends
+// when the prerequisite grid ends, and every wait inside these kernels is
+// bounded.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(map))

@@ -61,6 +61,9 @@ extern "C" {
  * with the streaming cache hint (evict first). */
 #define HEXIR_EPILOGUE_STREAM 0x10u
 
+/* CTAs per tile of the stream-K fix-up (grid.y). */
+#define HEXIR_SK_FIXUP_PARTS 16u
+
 /* Error bits a kernel ORs into the device error word. */
 #define HEXIR_KERR_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out of time */
 #define HEXIR_KERR_BAD_ARGS 0x2u      /* launch arguments failed a check */

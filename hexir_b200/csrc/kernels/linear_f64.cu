@@ -81,6 +81,10 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   const uint32_t kt_end = min(args.k_tiles, kt_begin + args.k_tiles_per_split);
   const int32_t nk = kt_end > kt_begin ? (int32_t)(kt_end - kt_begin) : 0;
   const uint32_t m0 = tm * BM, n0 = tn * BN;
+  // A split launch is followed by the reduction, which may start launching
+  // once every CTA of this grid has started (the last wave).
+  if (args.split_k > 1)
+    griddep_launch_dependents();
 
   if (issuer) {
     prefetch_tensormap(map_a);
@@ -261,6 +265,9 @@ __device__ __forceinline__ void linear_tma_sk_body(
   const bool issuer = threadIdx.x == 0;
   const SkSteps steps(args);
   const int32_t nk = (int32_t)steps.n_steps;
+  // The fix-up may start launching: the whole grid is resident (one CTA
+  // per SM), so its CTAs only take SMs this grid has left.
+  griddep_launch_dependents();
 
   if (issuer) {
     prefetch_tensormap(map_a);
@@ -410,13 +417,18 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_THREADS, 1)
   linear_tma_sk_body<Tile128>(&map_a, &map_b, args);
 }
 
-// Completes the stream-K tiles whose k units were split over CTAs: one CTA
-// per such tile sums the partial tiles in CTA order (the order of k), then
-// applies the epilogue (addend, relu).  Tiles owned by one CTA were stored by
-// it and are skipped.
+// Completes the stream-K tiles whose k units were split over CTAs: the
+// partial tiles are summed in CTA order (the order of k), then the epilogue
+// (addend, relu) applies.  Tiles owned by one CTA were stored by it and are
+// skipped.  Grid (tiles, HEXIR_SK_FIXUP_PARTS): each CTA takes every
+// PARTS-th group of four consecutive columns of its tile, so a thread has
+// one 256-bit load per partial in flight instead of walking the tile
+// element by element (one CTA per tile left each thread 64 dependent
+// trips to memory, longer than the whole stream-K loop at 1024^3).
 extern "C" __global__ void __launch_bounds__(256)
     hexir_linear_f64_sk_fixup(const hexir_linear_args_t args) {
   constexpr uint32_t BM = HEXIR_LINEAR_BM, BN = HEXIR_LINEAR_BN;
+  griddep_wait();  // the stream-K grid's partial tiles
   const uint32_t tile = args.sk_dp_tiles + blockIdx.x;
   const uint32_t k_tiles = args.k_tiles, U = args.sk_units;
   const uint32_t t0 = blockIdx.x * k_tiles;  // first unit of the tile
@@ -427,22 +439,54 @@ extern "C" __global__ void __launch_bounds__(256)
   tile_of(tile, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
   const bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
   const bool add = (args.epilogue & HEXIR_EPILOGUE_ADD) != 0;
-  for (uint32_t e = threadIdx.x; e < BM * BN; e += blockDim.x) {
+  const bool vec4 = (args.epilogue & HEXIR_EPILOGUE_VEC4) != 0;
+  const uint32_t stride = gridDim.y * blockDim.x * 4u;
+  for (uint32_t e = (blockIdx.y * blockDim.x + threadIdx.x) * 4u; e < BM * BN;
+       e += stride) {
     const uint32_t r = e / BN, col = e % BN;
     const uint32_t row = tm * BM + r, gcol = tn * BN + col;
     if (row >= args.m || gcol >= args.n)
       continue;
-    double s = 0.0;
+    double s[4] = {0.0, 0.0, 0.0, 0.0};
     for (uint32_t c = c0; c <= c1; ++c) {
       // The CTA's run starts in this tile: its first-tile slot.
       const uint32_t first = args.sk_dp_tiles + (c * U) / k_tiles;
       const uint32_t slot = 2 * c + (tile == first ? 0u : 1u);
-      s = __dadd_rn(s, args.sk_partials[(size_t)slot * BM * BN + e]);
+      // Slots are 32-byte aligned (the workspace base is) and e % 4 == 0.
+      double v[4];
+      ldg256(args.sk_partials + (size_t)slot * BM * BN + e, v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        s[q] = __dadd_rn(s[q], v[q]);
     }
     const size_t idx = (size_t)row * args.n + gcol;
-    if (add)
-      s = __dadd_rn(s, args.addend[idx]);
-    args.c[idx] = relu ? relu_ref(s) : s;
+    if (vec4) {
+      // Rows of c and the addend start 32-byte aligned and n % 4 == 0, so
+      // the four columns are in range together.
+      if (add) {
+        double a4[4];
+        ldg256(args.addend + idx, a4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          s[q] = __dadd_rn(s[q], a4[q]);
+      }
+      if (relu) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          s[q] = relu_ref(s[q]);
+      }
+      stg256(args.c + idx, s[0], s[1], s[2], s[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (gcol + q < args.n) {
+          double x = s[q];
+          if (add)
+            x = __dadd_rn(x, args.addend[idx + q]);
+          args.c[idx + q] = relu ? relu_ref(x) : x;
+        }
+      }
+    }
   }
   if (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE)
     __threadfence_system();

@@ -43,6 +43,8 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
   const uint32_t kt_end = min(k_tiles, kt_begin + args.k_tiles_per_split);
   const uint32_t m0 = tm * BM, n0 = tn * BN;
   const uint32_t m = args.m, n = args.n, k = args.k;
+  if (args.split_k > 1)
+    griddep_launch_dependents();  // the reduction may start launching
   const size_t lda = args.lda ? args.lda : k;
   const double *__restrict__ a = args.a;
   const double *__restrict__ b = args.b;
@@ -137,6 +139,7 @@ extern "C" __global__ void __launch_bounds__(HEXIR_LINEAR_G_THREADS)
 // addend[i] (HEXIR_EPILOGUE_ADD), then applies the relu.
 extern "C" __global__ void __launch_bounds__(256)
     hexir_linear_f64_splitk_reduce(const hexir_reduce_args_t args) {
+  griddep_wait();  // the split launch's partial sums
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   const bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;

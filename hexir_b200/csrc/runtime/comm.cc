@@ -550,7 +550,9 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   hexir_shard_rows(m, ranks, static_cast<uint32_t>(comm->rank), &begin, &rows);
 
   const bool root = comm->rank == 0;
-  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
+  // The relu, and no stream-K: a rank's rows run in gather pieces, and its
+  // block has the bits of one data-parallel or split-K launch.
+  const uint32_t mm_flags = (flags & HEXIR_MATMUL_RELU) | HEXIR_MATMUL_NO_STREAM_K;
   const uint32_t my_rows = static_cast<uint32_t>(rows);
   // The weight goes out in k pieces (one for short k or a single rank).  A
   // rank computes behind them -- one launch per piece, each continuing the
@@ -559,7 +561,7 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
   // whole weight has landed.
   uint32_t bounds[3] = {0, k, k};
   const uint32_t pieces = broadcast_pieces(k, ranks, bounds);
-  const MatmulPlan one = plan_matmul(dev, a_rows, w, c, my_rows, n, k, relu);
+  const MatmulPlan one = plan_matmul(dev, a_rows, w, c, my_rows, n, k, mm_flags);
   const bool chain = pieces > 1 && one.split_k == 1 && !one.stream_k();
 
   // 0. Where the rows go: the root describes its c (IPC handle + offset)
@@ -655,7 +657,7 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       if (!root)
         d.StreamWaitEvent(s, comm->w_done, 0);
       return launch_matmul(dev, lib, a_rows + cb * k, w, out, mm, n, k,
-                           relu | out_flags, s, &error);
+                           mm_flags | out_flags, s, &error);
     }
     hexir_status_t st = HEXIR_OK;
     for (uint32_t j = 1; j < pieces && st == HEXIR_OK; ++j) {
@@ -665,7 +667,7 @@ hexir_status_t hexir_sharded_linear_f64(hexir_comm_t *comm, const double *a_rows
       st = launch_matmul(dev, lib, a_rows + cb * k + bounds[j],
                          w + static_cast<size_t>(bounds[j]) * n,
                          last ? out : c + cb * n, mm, n, bounds[j + 1] - bounds[j],
-                         (last ? relu | out_flags : 0u) | HEXIR_MATMUL_SPLIT_K(1),
+                         (last ? mm_flags | out_flags : 0u) | HEXIR_MATMUL_SPLIT_K(1),
                          s, &error, k, c + cb * n);
     }
     return st;
@@ -788,7 +790,9 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
   CUstream gs = comm->gather_stream;
   const size_t row_a = static_cast<size_t>(k) * 8, row_c = static_cast<size_t>(n) * 8;
   const size_t w_size = static_cast<size_t>(k) * row_c;
-  const uint32_t relu = flags & HEXIR_MATMUL_RELU;
+  // The relu, and no stream-K: rows run in chunks, each with the bits of
+  // the same rows in one data-parallel or split-K launch.
+  const uint32_t mm_flags = (flags & HEXIR_MATMUL_RELU) | HEXIR_MATMUL_NO_STREAM_K;
 
   bool failed = false;
   auto note = [&](CUresult r, const char *what) {
@@ -874,9 +878,9 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
       dev, reinterpret_cast<const double *>(comm->a_dev),
       reinterpret_cast<const double *>(comm->w_dev),
       reinterpret_cast<const double *>(comm->c_dev), static_cast<uint32_t>(rows),
-      n, k, relu);
+      n, k, mm_flags);
   const bool chain = pieces > 1 && plan.split_k == 1 && !plan.stream_k() && rows;
-  const uint32_t chunk_flags = relu | HEXIR_MATMUL_SPLIT_K(plan.split_k);
+  const uint32_t chunk_flags = mm_flags | HEXIR_MATMUL_SPLIT_K(plan.split_k);
 
   // a's columns [c0, c1) of rows [r0, r0 + nr), a 2-D copy (row pitch k).
   auto upload_band = [&](uint64_t r0, uint64_t nr, uint32_t c0, uint32_t c1) {
@@ -994,7 +998,7 @@ hexir_status_t hexir_sharded_linear_host_f64(hexir_comm_t *comm,
           reinterpret_cast<const double *>(comm->a_dev + cb * row_a + static_cast<size_t>(kl) * 8),
           reinterpret_cast<const double *>(comm->w_dev + static_cast<size_t>(kl) * row_c),
           reinterpret_cast<double *>(comm->c_dev + cb * row_c),
-          static_cast<uint32_t>(cnt), n, k - kl, relu | HEXIR_MATMUL_SPLIT_K(1), on,
+          static_cast<uint32_t>(cnt), n, k - kl, mm_flags | HEXIR_MATMUL_SPLIT_K(1), on,
           &error, k, reinterpret_cast<const double *>(comm->c_dev + cb * row_c));
     } else {
       st = launch_matmul(

@@ -865,6 +865,20 @@ struct Vm {
     return *upload_a || *upload_w || *stream_out;
   }
 
+  // A matmul shape that want_pipeline could split into row chunks, whatever
+  // its operands' residency.  Every launch of such a dispatch, pipelined or
+  // not (constants kept on the GPU, operands already there), plans without
+  // stream-K, whose sums follow the whole tile set: so its bits do not
+  // depend on where its operands were.
+  static bool row_chunk_shape(const hexir_executable_entry_t &exe) {
+    if (exe.kind != HEXIR_KERNEL_MATMUL && exe.kind != HEXIR_KERNEL_MATMUL_RELU)
+      return false;
+    const uint64_t a = uint64_t{exe.m} * exe.k * 8, w = uint64_t{exe.k} * exe.n * 8,
+                   c = uint64_t{exe.m} * exe.n * 8;
+    return exe.m >= 1024 && (a >= kPipelineBytes || c >= kPipelineBytes ||
+                             (w >= kPipelineBytes && exe.k >= kPieceMinK));
+  }
+
   // Bounds of phase 1's k pieces over [0, k1): weight_stream_bounds.
   static std::vector<uint32_t> k_piece_bounds(uint32_t k1) {
     return weight_stream_bounds(k1);
@@ -892,40 +906,19 @@ struct Vm {
       return st;
     const uint32_t relu =
         exe.kind == HEXIR_KERNEL_MATMUL_RELU ? HEXIR_MATMUL_RELU : 0u;
+    // Row chunks and k pieces reproduce the one-shot launch's sums only
+    // for a data-parallel or split-K plan (row_chunk_shape).
     const MatmulPlan whole = plan_matmul(
         dev->state, reinterpret_cast<const double *>(a_dev),
         reinterpret_cast<const double *>(w_dev),
-        reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k, relu);
-    const bool pieces = upload_w && whole.split_k == 1 && !whole.stream_k();
+        reinterpret_cast<const double *>(c_dev), exe.m, exe.n, exe.k,
+        relu | HEXIR_MATMUL_NO_STREAM_K);
+    const bool pieces = upload_w && whole.split_k == 1;
     if (upload_w && !pieces) {
       // The one-shot launch splits k: upload w whole before the row chunks.
       if ((st = copy_range_to(ws, 0, ws.bytes, o, w_dev)) != HEXIR_OK)
         return st;
       ws.dev_valid.insert(o);
-    }
-    if (whole.stream_k()) {
-      // A stream-K plan's partial tiles follow the whole matrix's tiles:
-      // row chunks could not reproduce its sums, so the matmul runs as one
-      // launch after the uploads, and the capture copies after it.
-      if (upload_a) {
-        if ((st = copy_range_to(as, 0, as.bytes, o, a_dev)) != HEXIR_OK)
-          return st;
-        as.dev_valid.insert(o);
-      }
-      ContextGuard guard(dev->state->context);
-      Span *span = begin_span(dev);
-      std::string error;
-      st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(a_dev),
-                         reinterpret_cast<const double *>(w_dev),
-                         reinterpret_cast<double *>(c_dev), exe.m, exe.n, exe.k,
-                         relu, dev->stream, &error);
-      end_span(span);
-      if (st != HEXIR_OK) {
-        report(std::string("kernel '") + exe.name + "': " + error);
-        return st;
-      }
-      written_on_device(dst, o);
-      return HEXIR_OK;
     }
     CUstream cs = dev->copy_stream();
     if (!cs)
@@ -1336,7 +1329,9 @@ struct Vm {
     case HEXIR_KERNEL_MATMUL_ADD:
     case HEXIR_KERNEL_MATMUL_ADD_RELU:
       st = launch_matmul(dev->state, lib, a, b, c, exe.m, exe.n, exe.k,
-                         matmul_flags(exe.kind), dev->stream, &error, 0, nullptr,
+                         matmul_flags(exe.kind) |
+                             (row_chunk_shape(exe) ? HEXIR_MATMUL_NO_STREAM_K : 0u),
+                         dev->stream, &error, 0, nullptr,
                          has_addend(exe.kind)
                              ? reinterpret_cast<const double *>(in[2])
                              : nullptr);
@@ -1495,10 +1490,12 @@ struct Vm {
       case HEXIR_KERNEL_MATMUL_RELU:
       case HEXIR_KERNEL_MATMUL_ADD:
       case HEXIR_KERNEL_MATMUL_ADD_RELU:
+        // A shard is a row piece of one matmul: no stream-K, whose sums
+        // would follow this shard's tile set rather than the rows'.
         st = launch_matmul(dev->state, lib, reinterpret_cast<const double *>(x),
                            reinterpret_cast<const double *>(w[r]),
                            reinterpret_cast<double *>(out), m, exe.n, exe.k,
-                           matmul_flags(exe.kind) |
+                           matmul_flags(exe.kind) | HEXIR_MATMUL_NO_STREAM_K |
                                (r && direct[r] ? HEXIR_MATMUL_REMOTE_OUTPUT : 0u),
                            dev->stream, &error, 0, nullptr,
                            has_addend(exe.kind)

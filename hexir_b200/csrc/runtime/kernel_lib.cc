@@ -80,6 +80,42 @@ hexir_status_t launch(CUfunction fn, unsigned gx, unsigned gy, unsigned bx,
   return HEXIR_OK;
 }
 
+// A launch that depends on the kernel queued before it on `stream` only
+// through memory: with programmatic stream serialization its CTAs may be
+// placed while that kernel's last CTAs run, and the kernel itself waits
+// (griddepcontrol.wait) for that kernel's completion before reading.  Hides
+// the launch gap between a GEMM and its split-K reduction or stream-K
+// fix-up.  A plain launch where the driver has no cuLaunchKernelEx.
+hexir_status_t launch_after(CUfunction fn, unsigned gx, unsigned gy,
+                            unsigned bx, CUstream stream, void **params,
+                            const char *what, std::string *error) {
+  const Driver &d = driver();
+  if (!d.LaunchKernelEx)
+    return launch(fn, gx, gy, bx, 0, stream, params, what, error);
+  if (fault_hit(FaultSite::Launch))
+    return fail(error, std::string(what) + ": injected fault (HEXIR_FAULT)");
+  CUlaunchAttribute attr;
+  std::memset(&attr, 0, sizeof(attr));
+  attr.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr.value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDimX = gx;
+  cfg.gridDimY = gy;
+  cfg.gridDimZ = 1;
+  cfg.blockDimX = bx;
+  cfg.blockDimY = 1;
+  cfg.blockDimZ = 1;
+  cfg.hStream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const CUresult r = d.LaunchKernelEx(&cfg, fn, params, nullptr);
+  if (r != CUDA_SUCCESS)
+    return fail(error, cuda_message(what, r));
+  count_launch();
+  return HEXIR_OK;
+}
+
 // The launch configuration of `gx` CTAs in clusters of `cluster` along x.
 struct ClusterLaunch {
   CUlaunchAttribute attr;
@@ -494,19 +530,27 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   p.split_k = std::max<uint32_t>(1, ceil_div(std::max<uint32_t>(p.k_tiles, 1),
                                              p.k_tiles_per_split));
 
-  // Stream-K for the 128-row tiles, on request only: whole waves of tiles
-  // stay data-parallel except the last one or two, whose k-tile units are
-  // dealt out evenly over one CTA per SM (runs of >= 4 units).  Measured on
-  // B200 it loses to the data-parallel and split-k schedules at every shape
-  // tried (2048^3: 30.8 against 31.6 TFLOP/s; 8192^3: 34.9 against 35.2),
-  // so the planner never picks it by itself.
-  if ((flags & HEXIR_MATMUL_FORCE_STREAM_K) && p.variant == kTma128 && !c_in &&
-      ((flags >> 16) & 0xFFu) == 0 && !(flags & HEXIR_MATMUL_NO_STREAM_K) &&
-      sms > 0) {
+  // Stream-K for the 128-row tiles: whole waves of tiles stay
+  // data-parallel except the last one or two, whose k-tile units are dealt
+  // out evenly over one CTA per SM (runs of >= 4 units); a fix-up kernel
+  // sums the tiles split over CTAs.  (Keeping every whole wave
+  // data-parallel measured equal or slower: 512x8192x8192 34.9 against
+  // 35.3 TFLOP/s, 3072^3 34.4 against 34.6.)  Chosen by itself wherever the wave
+  // model above splits k (measured on B200 it beats the split-K schedule at
+  // every such shape tried: 1024^3 28.5 against 26.2 TFLOP/s, 2048^3 33.4
+  // against 31.4, 256x2048x8192 33.3 against 31.6, 512x8192x8192 35.3
+  // against 34.3), and on request (FORCE_STREAM_K) elsewhere, where it
+  // does not win (8192^3 34.9 against 35.2).  Never with an explicit split,
+  // continued sums (c_in) or NO_STREAM_K: callers that compute a matmul's
+  // rows in pieces pass that flag, since stream-K's partial sums follow the
+  // whole tile set and row pieces could not reproduce them.
+  const bool explicit_split = ((flags >> 16) & 0xFFu) != 0;
+  const bool want_sk = (flags & HEXIR_MATMUL_FORCE_STREAM_K) || p.split_k > 1;
+  if (want_sk && p.variant == kTma128 && !c_in && !explicit_split &&
+      !(flags & HEXIR_MATMUL_NO_STREAM_K) && sms > 0) {
     const uint64_t g = sms;
     const uint64_t dp_tiles = tiles >= 2 * g ? (tiles / g - 1) * g : 0;
-    const uint64_t sk_units_total = (tiles - dp_tiles) * p.k_tiles;
-    const uint64_t units = (sk_units_total + g - 1) / g;
+    const uint64_t units = ((tiles - dp_tiles) * p.k_tiles + g - 1) / g;
     if (units >= 4) {
       p.variant = kTma128Sk;
       p.split_k = 1;
@@ -679,8 +723,9 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
       const unsigned sk_tiles = p.tiles_m * p.tiles_n - p.sk_dp_tiles;
       void *fix_params[] = {&args};
       if (status == HEXIR_OK)
-        status = launch(lib->sk_fixup, sk_tiles, 1, 256, 0, stream, fix_params,
-                        "launch hexir_linear_f64_sk_fixup", error);
+        status = launch_after(lib->sk_fixup, sk_tiles, HEXIR_SK_FIXUP_PARTS, 256,
+                              stream, fix_params,
+                              "launch hexir_linear_f64_sk_fixup", error);
       d.EventRecord(dev->ws_ready, stream);
       return status;
     }
@@ -718,8 +763,8 @@ hexir_status_t launch_matmul(DeviceState *dev, KernelLib *lib, const double *a,
   const uint64_t want = (red.count + 255) / 256;
   const unsigned grid = static_cast<unsigned>(std::max<uint64_t>(
       1, std::min<uint64_t>(want, static_cast<uint64_t>(dev->sm_count) * 8)));
-  status = launch(lib->splitk_reduce, grid, 1, 256, 0, stream, params,
-                  "launch hexir_linear_f64_splitk_reduce", error);
+  status = launch_after(lib->splitk_reduce, grid, 1, 256, stream, params,
+                        "launch hexir_linear_f64_splitk_reduce", error);
   d.EventRecord(dev->ws_ready, stream);
   return status;
 }

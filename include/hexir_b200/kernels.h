@@ -44,9 +44,12 @@ extern "C" {
 #define HEXIR_MATMUL_REMOTE_OUTPUT 0x400u
 /* Stream-K schedule for 128-row tiles (the k units of the last waves' tiles
  * dealt out evenly over one CTA per SM, split tiles summed by a fix-up
- * kernel in CTA order): used only on request -- it measured slower than
- * the data-parallel and split-k schedules on B200 -- and only where no k
- * split is requested and no c_in is given.  NO_STREAM_K overrides. */
+ * kernel in CTA order).  The planner takes it by itself where its wave
+ * model would split k (too few tiles to fill the GPU's waves), and on
+ * FORCE_STREAM_K elsewhere; never where a k split is requested or c_in is
+ * given.  NO_STREAM_K rules it out: a caller that computes a matmul's rows
+ * in separate calls passes it, because stream-K's sums depend on the whole
+ * tile set, so row pieces would not have the bits of one call. */
 #define HEXIR_MATMUL_NO_STREAM_K 0x800u
 #define HEXIR_MATMUL_FORCE_STREAM_K 0x2000u
 /* tests: split the k range into S pieces (1..255; any S rules out stream-K);
@@ -70,7 +73,8 @@ hexir_status_t hexir_cuda_matmul_f64(int ordinal, const double *a,
  * the operands is still being copied or broadcast.  This call never splits
  * its k range (HEXIR_MATMUL_SPLIT_K(S) with S > 1 is refused), so the pieces
  * perform exactly the operations of one hexir_cuda_matmul_f64 call over all
- * of K whose plan has no k split (k0 a multiple of 32), and the result has
+ * of K whose plan neither splits k nor is stream-K (k0 a multiple of 32;
+ * hexir_cuda_matmul_plan reports the plan), and the result has
  * the same bits; HEXIR_MATMUL_RELU belongs on the last piece only. */
 hexir_status_t hexir_cuda_matmul_acc_f64(int ordinal, const double *a,
                                          uint32_t lda, const double *b,

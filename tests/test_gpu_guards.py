@@ -79,10 +79,11 @@ def test_fused_add_and_continued_sums_write_only_their_output(gpu, m, n, k):
     check(buf2, m * n)
 
 
-def test_stream_k_writes_only_its_output(gpu):
+@pytest.mark.parametrize("m,n,k", [(500, 2560, 2048), (300, 2050, 1536)])
+def test_stream_k_writes_only_its_output(gpu, m, n, k):
     """The stream-K launch and its fix-up (partial tiles in the workspace,
-    split tiles summed into c) on a ragged shape."""
-    m, n, k = 500, 2560, 2048
+    split tiles summed into c) on ragged shapes: a partial row tile, and a
+    partial column tile with n % 4 != 0 (the fix-up's scalar stores)."""
     flags = _ffi.MATMUL_FORCE_STREAM_K | _ffi.MATMUL_RELU
     assert hx.matmul_plan(m, n, k, flags)[0] == 5
     rng = np.random.default_rng(5)

@@ -322,15 +322,20 @@ def test_fused_matmul_add_is_matmul_then_add(gpu, m, n, k, flags):
     (640, 2048, 1024, 0, True),
     (128, 8192, 8192, _ffi.MATMUL_RELU, False),    # one row of tiles, long k
     (100, 8192, 2048, 0, False),                   # a partial row tile
+    (300, 2050, 1536, _ffi.MATMUL_RELU, True),     # n % 4 != 0: scalar fix-up
+    (1024, 1024, 1024, _ffi.MATMUL_RELU, False),
+    # 304 tiles: the first wave data-parallel, then every CTA's stream-K
+    # run (a data-parallel tile and a run in one CTA).
+    (2432, 2048, 1024, _ffi.MATMUL_RELU, True),
+    (4736, 512, 512, 0, False),                    # exactly one wave of tiles
 ])
 def test_stream_k_schedule(gpu, m, n, k, flags, add):
-    """The stream-K schedule (on request): a persistent launch plus fix-up,
-    within the bar of the oracle (rows sampled for the large shapes),
-    deterministic run to run, and within the bar of the planner's own
-    schedule."""
+    """The stream-K schedule: a persistent launch plus fix-up, within the bar
+    of the oracle (rows sampled for the large shapes), deterministic run to
+    run, and within the bar of the data-parallel / split-K schedule."""
     flags |= _ffi.MATMUL_FORCE_STREAM_K
     assert hx.matmul_plan(m, n, k, flags)[0] == 5
-    assert hx.matmul_plan(m, n, k, flags & ~_ffi.MATMUL_FORCE_STREAM_K)[0] == 1
+    assert hx.matmul_plan(m, n, k, flags | _ffi.MATMUL_NO_STREAM_K)[0] == 1
     rng = np.random.default_rng(m + n + k)
     a = rng.uniform(-1, 1, (m, k))
     b = rng.uniform(-1, 1, (k, n))
@@ -338,7 +343,7 @@ def test_stream_k_schedule(gpu, m, n, k, flags, add):
     ba, bb = gpu.upload(a), gpu.upload(b)
     bd = gpu.upload(d) if add else None
     outs = []
-    for extra in (0, 0, _ffi.MATMUL_NO_STREAM_K):  # forced, forced, planner
+    for extra in (0, 0, _ffi.MATMUL_NO_STREAM_K):  # twice, then without
         bc = gpu.buffer(m * n * 8)
         if add:
             hx.cuda_matmul_add(0, ba.ptr, bb.ptr, bd.ptr, bc.ptr, m, n, k,

@@ -76,7 +76,8 @@ def _rank(rank, world, port, m, n, k, result_path):
     lib.hexir_comm_release(comm)
     if rank == 0:
         from oracle import oracle
-        # Every rank's block as one launch on this GPU alone.
+        # Every rank's block as one launch on this GPU alone, planned as the
+        # sharded path plans (no stream-K: a rank's rows may run in pieces).
         single = np.empty((m, n))
         for r in range(world):
             rb, rr = hx.shard_rows(m, world, r)
@@ -85,7 +86,8 @@ def _rank(rank, world, port, m, n, k, result_path):
             xa = dev.upload(a[rb:rb + rr])
             xc = dev.buffer(rr * n * 8)
             hx.cuda_matmul(0, xa.ptr, bw.ptr, xc.ptr, rr, n, k,
-                           _ffi.MATMUL_RELU, dev.stream)
+                           _ffi.MATMUL_RELU | _ffi.MATMUL_NO_STREAM_K,
+                           dev.stream)
             hx.cuda_synchronize(0, dev.stream)
             single[rb:rb + rr] = xc.read((rr, n))
         bits = lambda x: x.view(np.uint64)
@@ -249,7 +251,8 @@ def _host_rank(rank, world, port, m, n, k, flags, result_path):
         for b, r, block, st in got:
             c[b:b + r] = block
             all_ok &= all(s == _ffi.OK for s in st)
-        # One launch per rank's block on this GPU alone: the bits to match.
+        # One launch per rank's block on this GPU alone, without stream-K
+        # (the rows run in chunks): the bits to match.
         single = np.empty((m, n))
         bw = dev.upload(w)
         for b, r, _, _ in got:
@@ -258,7 +261,8 @@ def _host_rank(rank, world, port, m, n, k, flags, result_path):
             xa = dev.upload(a[b:b + r])
             xc = dev.buffer(r * n * 8)
             hx.cuda_matmul(0, xa.ptr, bw.ptr, xc.ptr, r, n, k,
-                           flags & _ffi.MATMUL_RELU, dev.stream)
+                           (flags & _ffi.MATMUL_RELU) | _ffi.MATMUL_NO_STREAM_K,
+                           dev.stream)
             hx.cuda_synchronize(0, dev.stream)
             single[b:b + r] = xc.read((r, n))
         sample = np.unique(np.linspace(0, m - 1, min(m, 48)).astype(int))
