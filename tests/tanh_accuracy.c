@@ -1,0 +1,121 @@
+/* tanh_accuracy.c -- the arithmetic of the sm_100a tanh kernel
+ * (hexir_b200/csrc/kernels/activation_f64.cu, TanhOp), restated in C with
+ * fma() standing for the GPU's DFMA, checked against the C library's
+ * 64-bit-mantissa tanhl.  The reciprocal estimate is modelled by a
+ * reciprocal truncated to SEED_BITS bits (argv[1]); one Newton step and the
+ * quotient correction follow, as on the GPU.
+ *
+ * Prints: worst ulp error against tanhl, worst ulp difference from the
+ * double tanh, and the number of special values that differ from tanh's
+ * sign and saturation rules.  Test infrastructure for
+ * tests/test_tanh_accuracy.py. */
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+static double from_bits(uint64_t b) { double d; memcpy(&d, &b, 8); return d; }
+static uint64_t to_bits(double d) { uint64_t b; memcpy(&b, &d, 8); return b; }
+
+static int seed_bits = 20;
+
+static double rcp_estimate(double d) {
+  uint64_t b = to_bits(1.0 / d);
+  b &= ~((1ull << (52 - seed_bits)) - 1);
+  return from_bits(b);
+}
+
+static double kernel_tanh(double x) {
+  const double ax = fabs(x);
+  const double y = ax > 20.0 ? 20.0 : ax;
+  const double z = -2.0 * y;
+  const double shifter = 0x1.8p52;
+  const double t = fma(z, 0x1.71547652b82fep+0, shifter);
+  const double kd = t - shifter;
+  const int32_t k = (int32_t)(uint32_t)to_bits(t);
+  double r = fma(-kd, 0x1.62e42fefa39efp-1, z);
+  r = fma(-kd, 0x1.abc9e3b39803fp-56, r);
+  double q = 0x1.6124613a86d09p-33;
+  q = fma(q, r, 0x1.1eed8eff8d898p-29);
+  q = fma(q, r, 0x1.ae64567f544e4p-26);
+  q = fma(q, r, 0x1.27e4fb7789f5cp-22);
+  q = fma(q, r, 0x1.71de3a556c734p-19);
+  q = fma(q, r, 0x1.a01a01a01a01ap-16);
+  q = fma(q, r, 0x1.a01a01a01a01ap-13);
+  q = fma(q, r, 0x1.6c16c16c16c17p-10);
+  q = fma(q, r, 0x1.1111111111111p-7);
+  q = fma(q, r, 0x1.5555555555555p-5);
+  q = fma(q, r, 0x1.5555555555555p-3);
+  q = fma(q, r, 0.5);
+  const double p = fma(r * r, q, r);
+  const double s = from_bits((uint64_t)(uint32_t)(k + 1023) << 52);
+  const double u = fma(s, p, s - 1.0);
+  const double d = 2.0 + u;
+  const double n = -u;
+  double rc = rcp_estimate(d);
+  rc = fma(rc, fma(-d, rc, 1.0), rc);
+  const double q0 = n * rc;
+  return copysign(fma(rc, fma(-d, q0, n), q0), x);
+}
+
+/* |got - want| in units of the last place of the double nearest want. */
+static double ulp_error(double got, long double want) {
+  const double w = (double)want;
+  if (isnan(w))
+    return isnan(got) ? 0.0 : INFINITY;
+  double ulp = nextafter(fabs(w), INFINITY) - fabs(w);
+  if (!(ulp > 0))
+    ulp = 0x1p-1074;
+  return (double)(fabsl((long double)got - want) / ulp);
+}
+
+static uint64_t state = 0x2545F4914F6CDD1Dull;
+static uint64_t next(void) {
+  state ^= state << 13;
+  state ^= state >> 7;
+  state ^= state << 17;
+  return state;
+}
+static double uniform(void) { return (double)(next() >> 11) * 0x1p-53; }
+static double normal(void) {
+  double a = uniform(), b = uniform();
+  if (a < 1e-300)
+    a = 1e-300;
+  return sqrt(-2.0 * log(a)) * cos(6.283185307179586 * b);
+}
+
+int main(int argc, char **argv) {
+  if (argc > 1)
+    seed_bits = atoi(argv[1]);
+  const long per_kind = argc > 2 ? atol(argv[2]) : 200000;
+  double worst = 0.0, worst_libm = 0.0;
+  for (int kind = 0; kind < 5; ++kind)
+    for (long i = 0; i < per_kind; ++i) {
+      double x;
+      switch (kind) {
+      case 0: x = normal(); break;
+      case 1: x = (2.0 * uniform() - 1.0) * 25.0; break;
+      case 2: x = (2.0 * uniform() - 1.0) * 0.6; break;
+      case 3: x = ldexp(2.0 * uniform() - 1.0, -(int)(next() % 1070)); break;
+      default: x = (2.0 * uniform() - 1.0) * 0.3 + ((next() & 1) ? 0.17 : -0.17);
+      }
+      const double g = kernel_tanh(x);
+      const double e = ulp_error(g, tanhl((long double)x));
+      const double el = ulp_error(g, (long double)tanh(x));
+      if (e > worst)
+        worst = e;
+      if (el > worst_libm)
+        worst_libm = el;
+    }
+  const double specials[] = {0.0, -0.0, 0x1p-1074, -0x1p-1074, 20.0, -20.0,
+                             20.5, 700.0, -1e300, INFINITY, -INFINITY, NAN};
+  int bad = 0;
+  for (unsigned i = 0; i < sizeof specials / sizeof *specials; ++i) {
+    const double x = specials[i], g = kernel_tanh(x);
+    const int same = isnan(x) ? isnan(g) : to_bits(g) == to_bits(tanh(x));
+    bad += !same;
+  }
+  printf("%.4f %.4f %d\n", worst, worst_libm, bad);
+  return 0;
+}

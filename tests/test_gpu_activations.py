@@ -240,10 +240,11 @@ def test_softmax_misaligned_rows_take_the_register_blocks(gpu, rows, cols):
     assert_close("softmax", shifted, want)
 
 
-def test_tanh_expm1_form_is_within_4_ulp(gpu):
-    """tanh is evaluated as expm1(2x) / (expm1(2x) + 2), clamped to +-1
-    beyond |x| = 20: within 4 ulp of the oracle's C-library tanh over a
-    dense grid through the clamp, tiny magnitudes (where the relative
+def test_tanh_is_within_4_ulp(gpu):
+    """tanh is evaluated as -u / (2 + u) with u = expm1(-2|x|) computed in
+    the kernel (Cody-Waite reduction, Taylor polynomial, Newton-Raphson
+    quotient), |x| capped at 20: within 4 ulp of the oracle's C-library tanh
+    over a dense grid through the cap, tiny magnitudes (where the relative
     accuracy of expm1 is what keeps it), and the sign of zero."""
     grid = np.linspace(-25.0, 25.0, 1 << 18)
     tiny = np.geomspace(1e-300, 1e-2, 4096)

@@ -1,0 +1,43 @@
+"""The accuracy of the GPU tanh's arithmetic, on the host.
+
+tests/tanh_accuracy.c restates the kernel's evaluation (Cody-Waite
+reduction, Taylor polynomial of expm1, one Newton-Raphson step on a
+reciprocal estimate and a Markstein quotient correction) with C's fma()
+for the GPU's fused multiply-add, and compares it with the C library's
+64-bit-mantissa tanhl on 10^6 inputs: normal, uniform to +-25, near zero,
+tiny down to subnormals, and around the first reduction boundary.  The GPU
+test (test_gpu_activations.py::test_tanh_is_within_4_ulp) checks the kernel
+itself against the oracle.
+"""
+
+import os
+import shutil
+import subprocess
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module")
+def program(tmp_path_factory):
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    exe = str(tmp_path_factory.mktemp("tanh") / "tanh_accuracy")
+    subprocess.run([cc, "-O2", "-std=c11", "-ffp-contract=off", "-o", exe,
+                    os.path.join(HERE, "tanh_accuracy.c"), "-lm"], check=True)
+    return exe
+
+
+@pytest.mark.parametrize("seed_bits", [20, 23, 52])
+def test_tanh_arithmetic_is_within_3_ulp(program, seed_bits):
+    """Within 2.6 ulp of tanhl and 3 ulp of the double tanh, with the special
+    values (signed zeros, saturation, infinities, NaN) as tanh has them, for
+    any reciprocal estimate of 20 bits or more."""
+    out = subprocess.run([program, str(seed_bits), "200000"], check=True,
+                         capture_output=True, text=True).stdout.split()
+    worst, worst_libm, bad = float(out[0]), float(out[1]), int(out[2])
+    assert worst <= 2.6, worst
+    assert worst_libm <= 3.0, worst_libm
+    assert bad == 0
