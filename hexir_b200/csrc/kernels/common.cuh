@@ -79,6 +79,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar,
   }
 }
 
+// *p += v on a shared-memory word, returning the old value, with acquire and
+// release semantics at CTA scope: what this thread did before is visible to
+// a thread whose later add reads the result, and what threads did before
+// their earlier adds is visible to this thread after it.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_cta(uint32_t *p,
+                                                         uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "r"(smem_addr(p)), "r"(v)
+               : "memory");
+  return old;
+}
+
 // 2-D tiled TMA load into shared memory, completing on `bar`.  The caller
 // keeps x * 8 bytes a multiple of 16 (x is a multiple of 8 doubles here).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,

@@ -9,8 +9,9 @@
 // agree with the CPU to within f64 rounding, not bit for bit.
 //
 // Kernels:
-//   hexir_linear_f64_tma      TMA-fed mbarrier ring, 8 DMMA warps (thread 0
-//   hexir_linear_f64_tma_m64  also issues the TMA boxes), one CTA per SM;
+//   hexir_linear_f64_tma      TMA-fed mbarrier ring, 8 DMMA warps (the warp
+//   hexir_linear_f64_tma_m64  that releases a stage last refills it), one
+//                             CTA per SM;
 //   hexir_linear_f64_tma_m16  CTA tiles 128x128x32 (3 stages), 64x128x32 (4)
 //                             and 16x128x32 (3, two CTAs per SM) for tall,
 //                             medium and skinny row counts.
@@ -28,7 +29,11 @@ using namespace hexir;
 namespace hexir {
 
 // Tile configurations of the TMA pipeline.  All use 8 DMMA warps (256
-// threads, one CTA per SM); thread 0 also issues the TMA boxes.
+// threads, one CTA per SM); thread 0 issues the first STAGES k-tiles' TMA
+// boxes and the warp that releases a stage last issues its refill.  (A
+// ninth, producer-only warp does not fit: three warps on one SM
+// sub-partition cap a thread at 168 registers, and the 128-row tile needs
+// 194.)
 //   BM x BN x BK  CTA tile; STAGES smem ring depth
 //   WARPS_M x WARPS_N  warp grid; warp tile (BM/WARPS_M) x (BN/WARPS_N)
 template <int BM_, int BN_, int BK_, int STAGES_, int WARPS_M_>
@@ -69,7 +74,10 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   double *sa = reinterpret_cast<double *>(smem);
   double *sb = sa + STAGES * T::A_STAGE;
   uint64_t *full = reinterpret_cast<uint64_t *>(sb + STAGES * T::B_STAGE);
-  uint64_t *empty = full + STAGES;
+  // Per stage, how many warp releases it has seen (8 per use), and how many
+  // times the stages were armed in all.
+  uint32_t *released = reinterpret_cast<uint32_t *>(full + STAGES);
+  uint32_t *armed = released + STAGES;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool issuer = threadIdx.x == 0;
@@ -91,14 +99,17 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
     prefetch_tensormap(map_b);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], HEXIR_LINEAR_CONSUMER_WARPS);
+      released[s] = 0u;
     }
+    *armed = (uint32_t)min(nk, (int32_t)STAGES);
     fence_mbar_init();
   }
   __syncthreads();
 
-  // Thread 0 arms stage s for k-tile i and issues its TMA boxes: BK/8 A boxes
-  // of [BM][8] and BN/16 B boxes of [BK][16] (128-byte swizzled).
+  // Arm stage s for k-tile i and issue its TMA boxes: BK/8 A boxes of
+  // [BM][8] and BN/16 B boxes of [BK][16] (128-byte swizzled).  Thread 0
+  // issues the first STAGES k-tiles; after that the warp that releases a
+  // stage last refills it, so no warp waits for another to finish a k-tile.
   auto issue = [&](int32_t i) {
     const int s = i % STAGES;
     mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
@@ -113,10 +124,9 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
       tma_load_2d(bs + j * T::B_SLAB, map_b, (int32_t)(n0 + j * 16), k0,
                   &full[s]);
   };
-  int32_t issued = 0;
   if (issuer) {
-    for (; issued < nk && issued < STAGES; ++issued)
-      issue(issued);
+    for (int32_t i = 0; i < nk && i < STAGES; ++i)
+      issue(i);
   }
 
   const uint32_t g = lane >> 2, t = lane & 3;
@@ -151,33 +161,22 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
       dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
                            b_stage, T::B_SLAB * 8, kk * 8, g, t);
     __syncwarp();
-    if (lane == 0)
-      mbar_arrive(&empty[s]);
-    // Refill stage s with k-tile i + STAGES once all 8 warps released it.
-    if (issuer && issued < nk) {
-      if (!mbar_wait_bounded(&empty[s], use & 1u, args.timeout_ns)) {
-        ok = false;
-        break;
+    // Release stage s.  Every warp releases each use of it once, and no
+    // warp can release the next use before the refill lands, so the 8th
+    // release of a use is the last: that warp refills the stage with
+    // k-tile i + STAGES (its acquire orders the refill after every warp's
+    // reads of the stage).
+    if (lane == 0) {
+      const uint32_t before = atom_add_acq_rel_cta(&released[s], 1u);
+      if (before % HEXIR_LINEAR_CONSUMER_WARPS ==
+              HEXIR_LINEAR_CONSUMER_WARPS - 1 &&
+          i + STAGES < nk) {
+        issue(i + STAGES);
+        atomicAdd(armed, 1u);
       }
-      issue(issued++);
     }
-    // Reconverge warp 0 before the next iteration's warp-wide DMMAs.
     __syncwarp();
   }
-
-  if (issuer) {
-    // Nothing may still be writing this CTA's shared memory when it exits.
-    // Stage s was armed ceil((issued - s) / STAGES) times; wait for the phase
-    // of its last arm.  After a normal run these return at once.
-#pragma unroll
-    for (int s = 0; s < STAGES; ++s)
-      if (issued > s) {
-        const uint32_t uses = (uint32_t)(issued - s + STAGES - 1) / STAGES;
-        mbar_wait_bounded(&full[s], (uses - 1) & 1u, args.timeout_ns);
-      }
-  }
-  if (!ok)
-    return;
 
   double *dst = args.c;
   bool relu = (args.epilogue & HEXIR_EPILOGUE_RELU) != 0;
@@ -188,12 +187,28 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
     relu = false;
     addend = nullptr;
   }
-  store_warp_tile<MI, NP, true>(
-      acc, dst, args.m, args.n, m0 + wm * T::WTM, n0 + wn * T::WTN, relu, g, t,
-      vec4, addend,
-      args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_STREAM) != 0);
-  if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
-    __threadfence_system();
+  if (ok) {
+    store_warp_tile<MI, NP, true>(
+        acc, dst, args.m, args.n, m0 + wm * T::WTM, n0 + wn * T::WTN, relu, g,
+        t, vec4, addend,
+        args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_STREAM) != 0);
+    if (args.split_k == 1 && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
+      __threadfence_system();
+  }
+  // Nothing may still be writing this CTA's shared memory when it exits.
+  // Once every warp is past its loop no stage is armed again; wait for the
+  // phase of each stage's last arm (at once after a normal run, where every
+  // arm was waited for).
+  __syncthreads();
+  if (issuer) {
+    const int32_t issued = (int32_t)*(volatile uint32_t *)armed;
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s)
+      if (issued > s) {
+        const uint32_t uses = (uint32_t)(issued - s + STAGES - 1) / STAGES;
+        mbar_wait_bounded(&full[s], (uses - 1) & 1u, args.timeout_ns);
+      }
+  }
 }
 
 // The k-tile steps of one CTA of a stream-K launch, in the order it runs
@@ -259,7 +274,9 @@ __device__ __forceinline__ void linear_tma_sk_body(
   double *sa = reinterpret_cast<double *>(smem);
   double *sb = sa + STAGES * T::A_STAGE;
   uint64_t *full = reinterpret_cast<uint64_t *>(sb + STAGES * T::B_STAGE);
-  uint64_t *empty = full + STAGES;
+  // Stage releases and arms, as in linear_tma_body.
+  uint32_t *released = reinterpret_cast<uint32_t *>(full + STAGES);
+  uint32_t *armed = released + STAGES;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool issuer = threadIdx.x == 0;
@@ -274,40 +291,43 @@ __device__ __forceinline__ void linear_tma_sk_body(
     prefetch_tensormap(map_b);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], HEXIR_LINEAR_CONSUMER_WARPS);
+      released[s] = 0u;
     }
+    *armed = (uint32_t)min(nk, (int32_t)STAGES);
     fence_mbar_init();
   }
   __syncthreads();
 
-  // The producer's cursor and the row / column of its current tile.
-  SkSteps::Cursor prod = steps.begin();
-  uint32_t prod_tile = ~0u, ptm = 0, ptn = 0;
-  auto issue = [&](int32_t i) {
+  // Arm stage i % STAGES for the step at cursor `at` and issue its boxes.
+  // Thread 0 issues the first STAGES steps; after that the warp that
+  // releases a stage last refills it with the step STAGES ahead, which
+  // every warp tracks with its own cursor (`ahead`), with the row / column
+  // of that cursor's tile cached.
+  uint32_t at_tile = ~0u, atm = 0, atn = 0;
+  auto issue = [&](int32_t i, const SkSteps::Cursor &at) {
     const int s = i % STAGES;
-    if (prod.tile != prod_tile) {
-      prod_tile = prod.tile;
-      tile_of(prod_tile, args.tiles_m, args.tiles_n, args.group_m, ptm, ptn);
+    if (at.tile != at_tile) {
+      at_tile = at.tile;
+      tile_of(at_tile, args.tiles_m, args.tiles_n, args.group_m, atm, atn);
     }
-    const uint32_t tm = ptm, tn = ptn, kt = prod.kt;
-    steps.next(prod);
     mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
-    const int32_t k0 = (int32_t)(kt * BK);
+    const int32_t k0 = (int32_t)(at.kt * BK);
     double *as = sa + s * T::A_STAGE;
     double *bs = sb + s * T::B_STAGE;
 #pragma unroll
     for (int j = 0; j < BK / 8; ++j)
-      tma_load_2d(as + j * T::A_SLAB, map_a, k0 + j * 8, (int32_t)(tm * BM),
+      tma_load_2d(as + j * T::A_SLAB, map_a, k0 + j * 8, (int32_t)(atm * BM),
                   &full[s]);
 #pragma unroll
     for (int j = 0; j < BN / 16; ++j)
-      tma_load_2d(bs + j * T::B_SLAB, map_b, (int32_t)(tn * BN + j * 16), k0,
+      tma_load_2d(bs + j * T::B_SLAB, map_b, (int32_t)(atn * BN + j * 16), k0,
                   &full[s]);
   };
-  int32_t issued = 0;
-  if (issuer) {
-    for (; issued < nk && issued < STAGES; ++issued)
-      issue(issued);
+  SkSteps::Cursor ahead = steps.begin();
+  for (int32_t j = 0; j < nk && j < STAGES; ++j) {
+    if (issuer)
+      issue(j, ahead);
+    steps.next(ahead);
   }
 
   const uint32_t g = lane >> 2, t = lane & 3;
@@ -349,15 +369,18 @@ __device__ __forceinline__ void linear_tma_sk_body(
         dmma_k8_step<MI, NP>(acc, a_stage + kk * T::A_SLAB * 8, wm * T::WTM,
                              b_stage, T::B_SLAB * 8, kk * 8, g, t);
       __syncwarp();
-      if (lane == 0)
-        mbar_arrive(&empty[s]);
-      if (issuer && issued < nk) {
-        if (!mbar_wait_bounded(&empty[s], use & 1u, args.timeout_ns)) {
-          ok = false;
-          break;
+      // Release stage s; the last of its 8 releases refills it with the
+      // step STAGES ahead (see linear_tma_body).
+      if (lane == 0) {
+        const uint32_t before = atom_add_acq_rel_cta(&released[s], 1u);
+        if (before % HEXIR_LINEAR_CONSUMER_WARPS ==
+                HEXIR_LINEAR_CONSUMER_WARPS - 1 &&
+            i + STAGES < nk) {
+          issue(i + STAGES, ahead);
+          atomicAdd(armed, 1u);
         }
-        issue(issued++);
       }
+      steps.next(ahead);
       __syncwarp();
     }
     if (!ok)
@@ -386,7 +409,13 @@ __device__ __forceinline__ void linear_tma_sk_body(
     }
   }
 
+  if (ok && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
+    __threadfence_system();
+  // Nothing may still be writing this CTA's shared memory when it exits
+  // (see linear_tma_body).
+  __syncthreads();
   if (issuer) {
+    const int32_t issued = (int32_t)*(volatile uint32_t *)armed;
 #pragma unroll
     for (int s = 0; s < STAGES; ++s)
       if (issued > s) {
@@ -394,8 +423,6 @@ __device__ __forceinline__ void linear_tma_sk_body(
         mbar_wait_bounded(&full[s], (uses - 1) & 1u, args.timeout_ns);
       }
   }
-  if (ok && (args.epilogue & HEXIR_EPILOGUE_SYSTEM_FENCE))
-    __threadfence_system();
 }
 
 }  // namespace hexir
