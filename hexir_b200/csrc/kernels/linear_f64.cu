@@ -149,7 +149,10 @@ __device__ __forceinline__ void linear_tma_body(const CUtensorMap *map_a,
   for (int32_t i = 0; i < nk; ++i) {
     const int s = i % STAGES;
     const uint32_t use = (uint32_t)i / STAGES;
-    if (!mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns)) {
+    // The warp leaves together if any lane's wait ran out: the DMMAs below
+    // are warp-wide.
+    if (!__all_sync(0xffffffffu,
+                    mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns))) {
       ok = false;
       break;
     }
@@ -357,7 +360,8 @@ __device__ __forceinline__ void linear_tma_sk_body(
     for (int32_t j = 0; j < seg_len; ++j, ++i) {
       const int s = i % STAGES;
       const uint32_t use = (uint32_t)i / STAGES;
-      if (!mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns)) {
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(&full[s], use & 1u, args.timeout_ns))) {
         ok = false;
         break;
       }
