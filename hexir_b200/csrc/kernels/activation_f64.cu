@@ -46,14 +46,98 @@ __device__ __forceinline__ double neg_inf() {
   return __longlong_as_double(static_cast<long long>(0xfff0000000000000ull));
 }
 
+// e^z for z <= 0, built from its parts (no call, no branch):
+//  - z = k ln2 + r, |r| <= ln2 / 2: k by adding and subtracting 1.5 * 2^52
+//    (round to nearest), r by Cody and Waite's two-part ln 2 (the first fma
+//    is exact);
+//  - expm1(r) by its Taylor series to r^13 / 13! (truncation below 2^-56
+//    relative for |r| <= ln2 / 2), Horner in fma.
+// neg_exp_parts returns p = expm1(r) and k, for z in [-746, 0] or NaN.
+// Measured on B200 against CUDA's functions in the same kernels: in place of
+// expm1 it wins (tanh, elu), and so it does beside the divide-free quotient
+// in mish; sigmoid, swish and softmax stay faster with CUDA's exp (and
+// sigmoid and swish with the IEEE divide: with the quotient below CUDA's exp
+// spilled registers there).  The order of the differences was 5-15 %.
+__device__ __forceinline__ double neg_exp_parts(double z, int &k) {
+  const double shifter = 0x1.8p52;
+  const double t = __fma_rn(z, 0x1.71547652b82fep+0, shifter);  // z / ln2
+  const double kd = __dsub_rn(t, shifter);
+  k = __double2loint(t);
+  double r = __fma_rn(-kd, 0x1.62e42fefa39efp-1, z);
+  r = __fma_rn(-kd, 0x1.abc9e3b39803fp-56, r);
+  double q = 0x1.6124613a86d09p-33;  // 1 / 13!
+  q = __fma_rn(q, r, 0x1.1eed8eff8d898p-29);
+  q = __fma_rn(q, r, 0x1.ae64567f544e4p-26);
+  q = __fma_rn(q, r, 0x1.27e4fb7789f5cp-22);
+  q = __fma_rn(q, r, 0x1.71de3a556c734p-19);
+  q = __fma_rn(q, r, 0x1.a01a01a01a01ap-16);
+  q = __fma_rn(q, r, 0x1.a01a01a01a01ap-13);
+  q = __fma_rn(q, r, 0x1.6c16c16c16c17p-10);
+  q = __fma_rn(q, r, 0x1.1111111111111p-7);
+  q = __fma_rn(q, r, 0x1.5555555555555p-5);
+  q = __fma_rn(q, r, 0x1.5555555555555p-3);
+  q = __fma_rn(q, r, 0.5);                                      // 1 / 2!
+  return __fma_rn(__dmul_rn(r, r), q, r);
+}
+
+// 2^k for k in [-1022, 1023], in the exponent bits.
+__device__ __forceinline__ double pow2i(int k) {
+  return __hiloint2double((k + 1023) << 20, 0);
+}
+
+// e^z for z <= 0 (below -746 it is 0; NaN passes): 2^k (1 + p), scaled in
+// two halves of k so that results in the subnormal range round once.
+__device__ __forceinline__ double exp_neg(double z) {
+  int k;
+  const double p = neg_exp_parts(z < -746.0 ? -746.0 : z, k);
+  const int k1 = k >> 1;
+  return __dmul_rn(__dmul_rn(__dadd_rn(1.0, p), pow2i(k1)), pow2i(k - k1));
+}
+
+// expm1(z) for z in [-40, 0] or NaN: 2^k p + (2^k - 1) in one fma.
+__device__ __forceinline__ double expm1_neg_core(double z) {
+  int k;
+  const double p = neg_exp_parts(z, k);
+  const double s = pow2i(k);
+  return __fma_rn(s, p, __dsub_rn(s, 1.0));
+}
+
+// expm1(z) for any z <= 0 (below -40 it rounds to -1; NaN passes).
+__device__ __forceinline__ double expm1_neg(double z) {
+  return expm1_neg_core(z < -40.0 ? -40.0 : z);
+}
+
+__device__ __forceinline__ double rcp_estimate(double d) {
+  double r;
+  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(d));
+  return r;
+}
+
+// n / d for a normal d > 0 and a finite n, without the IEEE divide: one
+// Newton-Raphson step on the hardware reciprocal estimate, then one
+// Markstein correction of the quotient.  The error after both is about the
+// estimate's to the fourth power, so any estimate of 20 bits or more gives
+// the quotient of the exact reciprocal (on B200 the results equal those of
+// two Newton steps on 2^28 inputs): within an ulp, not always the correctly
+// rounded one.  A zero quotient comes out +0.
+__device__ __forceinline__ double quotient(double n, double d) {
+  double rc = rcp_estimate(d);
+  rc = __fma_rn(rc, __fma_rn(-d, rc, 1.0), rc);
+  const double q0 = __dmul_rn(n, rc);
+  return __fma_rn(rc, __fma_rn(-d, q0, n), q0);
+}
+
 struct LeakyReluOp {
   __device__ __forceinline__ double operator()(double x, double) const {
     return x > 0.0 ? x : __dmul_rn(HEXIR_LEAKY_RELU_ALPHA, x);
   }
 };
+// elu(x) = x for x > 0, alpha expm1(x) below (alpha 1); +-0 and NaN pass
+// through (expm1(+-0) = +-0).
 struct EluOp {
   __device__ __forceinline__ double operator()(double x, double) const {
-    return x > 0.0 ? x : __dmul_rn(HEXIR_ELU_ALPHA, expm1(x));
+    static_assert(HEXIR_ELU_ALPHA == 1.0, "expm1 below zero is scaled by 1");
+    return x < 0.0 ? expm1_neg(x) : x;
   }
 };
 struct SigmoidOp {
@@ -62,64 +146,20 @@ struct SigmoidOp {
   }
 };
 // tanh(x) = sign(x) * -u / (2 + u) with u = expm1(-2|x|) in [-1, 0]
-// (tanh|x| = (1 - e^{-2|x|}) / (1 + e^{-2|x|})), evaluated without a call
-// or a branch so that every lane runs the same ~30 FP64 instructions:
-//  - |x| is capped at 20 (beyond 19.1 tanh rounds to 1); NaN passes;
-//  - z = -2|x| = k ln2 + r, |r| <= ln2 / 2: k by adding and subtracting
-//    1.5 * 2^52 (round to nearest), r by Cody and Waite's two-part ln 2
-//    (the first fma is exact);
-//  - expm1(r) by its Taylor series to r^13 / 13! (truncation below 2^-56
-//    relative for |r| <= ln2 / 2), Horner in fma;
-//  - u = 2^k expm1(r) + (2^k - 1) in one fma (2^k built in the exponent
-//    bits);
-//  - the quotient by one Newton-Raphson step on the hardware reciprocal
-//    estimate and one Markstein correction of the quotient: the error after
-//    both is about the estimate's to the fourth power, so any estimate of
-//    20 bits or more gives the quotient of the exact reciprocal (on B200 the
-//    results equal those of two Newton steps on 2^28 inputs).
+// (tanh|x| = (1 - e^{-2|x|}) / (1 + e^{-2|x|})), |x| capped at 20 (beyond
+// 19.1 tanh rounds to 1; NaN passes), by expm1_neg and quotient above: no
+// call and no branch, so every lane runs the same ~30 FP64 instructions.
 // Within 3 ulp of the C library's tanh and 2.6 ulp of a 64-bit reference
 // on 2 * 10^7 sampled inputs (normal, uniform to +-25, tiny, subnormal, the
 // k boundaries); +-0 keeps its sign.  Measured 0.87 of copy bandwidth on
 // B200, against 0.72 for expm1 and an IEEE divide: the kernel is bound by
 // FP64 instruction issue, so each instruction saved shows.
-__device__ __forceinline__ double rcp_estimate(double d) {
-  double r;
-  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(d));
-  return r;
-}
 struct TanhOp {
   __device__ __forceinline__ double operator()(double x, double) const {
     const double ax = fabs(x);
     const double y = ax > 20.0 ? 20.0 : ax;
-    const double z = __dmul_rn(-2.0, y);
-    const double shifter = 0x1.8p52;
-    const double t = __fma_rn(z, 0x1.71547652b82fep+0, shifter);  // z / ln2
-    const double kd = __dsub_rn(t, shifter);
-    const int k = __double2loint(t);
-    double r = __fma_rn(-kd, 0x1.62e42fefa39efp-1, z);
-    r = __fma_rn(-kd, 0x1.abc9e3b39803fp-56, r);
-    double q = 0x1.6124613a86d09p-33;  // 1 / 13!
-    q = __fma_rn(q, r, 0x1.1eed8eff8d898p-29);
-    q = __fma_rn(q, r, 0x1.ae64567f544e4p-26);
-    q = __fma_rn(q, r, 0x1.27e4fb7789f5cp-22);
-    q = __fma_rn(q, r, 0x1.71de3a556c734p-19);
-    q = __fma_rn(q, r, 0x1.a01a01a01a01ap-16);
-    q = __fma_rn(q, r, 0x1.a01a01a01a01ap-13);
-    q = __fma_rn(q, r, 0x1.6c16c16c16c17p-10);
-    q = __fma_rn(q, r, 0x1.1111111111111p-7);
-    q = __fma_rn(q, r, 0x1.5555555555555p-5);
-    q = __fma_rn(q, r, 0x1.5555555555555p-3);
-    q = __fma_rn(q, r, 0.5);                                      // 1 / 2!
-    const double p = __fma_rn(__dmul_rn(r, r), q, r);             // expm1(r)
-    const double s = __hiloint2double((k + 1023) << 20, 0);       // 2^k
-    const double u = __fma_rn(s, p, __dsub_rn(s, 1.0));
-    const double d = __dadd_rn(2.0, u);                           // [1, 2]
-    const double n = -u;
-    double rc = rcp_estimate(d);
-    rc = __fma_rn(rc, __fma_rn(-d, rc, 1.0), rc);
-    const double q0 = __dmul_rn(n, rc);
-    const double v = __fma_rn(rc, __fma_rn(-d, q0, n), q0);
-    return copysign(v, x);
+    const double u = expm1_neg_core(__dmul_rn(-2.0, y));  // -2y >= -40
+    return copysign(quotient(-u, __dadd_rn(2.0, u)), x);  // d in [1, 2]
   }
 };
 struct GeluOp {
@@ -136,12 +176,12 @@ struct SwishOp {
 struct MishOp {
   __device__ __forceinline__ double operator()(double x, double) const {
     const bool neg = x <= 0.0;
-    const double u = exp(neg ? x : -x);
+    const double u = exp_neg(-fabs(x));
     const double num = neg ? __dmul_rn(u, __dadd_rn(u, 2.0))
                            : __dadd_rn(1.0, __dmul_rn(2.0, u));
     const double den =
         __dadd_rn(num, neg ? 2.0 : __dmul_rn(__dmul_rn(2.0, u), u));
-    return __dmul_rn(x, __ddiv_rn(num, den));
+    return __dmul_rn(x, quotient(num, den));  // den in [1, 5]
   }
 };
 
