@@ -1,5 +1,6 @@
-/* tanh_accuracy.c -- the arithmetic of the sm_100a tanh kernel
- * (hexir_b200/csrc/kernels/activation_f64.cu, TanhOp), restated in C with
+/* tanh_accuracy.c -- the arithmetic of the sm_100a tanh kernel and of the
+ * exp / expm1 core it shares with elu and mish
+ * (hexir_b200/csrc/kernels/activation_f64.cu), restated in C with
  * fma() standing for the GPU's DFMA, checked against the C library's
  * 64-bit-mantissa tanhl.  The reciprocal estimate is modelled by a
  * reciprocal truncated to SEED_BITS bits (argv[1]); one Newton step and the
@@ -24,6 +25,45 @@ static double rcp_estimate(double d) {
   uint64_t b = to_bits(1.0 / d);
   b &= ~((1ull << (52 - seed_bits)) - 1);
   return from_bits(b);
+}
+
+/* exp_neg and expm1_neg of activation_f64.cu (the core of kernel_tanh):
+ * e^z and expm1(z) for z <= 0. */
+static double neg_exp_parts(double z, int32_t *k) {
+  const double shifter = 0x1.8p52;
+  const double t = fma(z, 0x1.71547652b82fep+0, shifter);
+  const double kd = t - shifter;
+  *k = (int32_t)(uint32_t)to_bits(t);
+  double r = fma(-kd, 0x1.62e42fefa39efp-1, z);
+  r = fma(-kd, 0x1.abc9e3b39803fp-56, r);
+  double q = 0x1.6124613a86d09p-33;
+  q = fma(q, r, 0x1.1eed8eff8d898p-29);
+  q = fma(q, r, 0x1.ae64567f544e4p-26);
+  q = fma(q, r, 0x1.27e4fb7789f5cp-22);
+  q = fma(q, r, 0x1.71de3a556c734p-19);
+  q = fma(q, r, 0x1.a01a01a01a01ap-16);
+  q = fma(q, r, 0x1.a01a01a01a01ap-13);
+  q = fma(q, r, 0x1.6c16c16c16c17p-10);
+  q = fma(q, r, 0x1.1111111111111p-7);
+  q = fma(q, r, 0x1.5555555555555p-5);
+  q = fma(q, r, 0x1.5555555555555p-3);
+  q = fma(q, r, 0.5);
+  return fma(r * r, q, r);
+}
+static double pow2i(int32_t k) {
+  return from_bits((uint64_t)(uint32_t)(k + 1023) << 52);
+}
+static double exp_neg(double z) {
+  int32_t k;
+  const double p = neg_exp_parts(z < -746.0 ? -746.0 : z, &k);
+  const int32_t k1 = k >> 1;
+  return ((1.0 + p) * pow2i(k1)) * pow2i(k - k1);
+}
+static double expm1_neg(double z) {
+  int32_t k;
+  const double p = neg_exp_parts(z < -40.0 ? -40.0 : z, &k);
+  const double s = pow2i(k);
+  return fma(s, p, s - 1.0);
 }
 
 static double kernel_tanh(double x) {
@@ -85,7 +125,33 @@ static double normal(void) {
   return sqrt(-2.0 * log(a)) * cos(6.283185307179586 * b);
 }
 
+/* argv[1] == "exp": worst ulp errors of exp_neg against expl and of
+ * expm1_neg against expm1l over z in [-750, 0]. */
+static int exp_main(long n) {
+  double worst_exp = 0.0, worst_expm1 = 0.0;
+  for (int kind = 0; kind < 4; ++kind)
+    for (long i = 0; i < n; ++i) {
+      double z;
+      switch (kind) {
+      case 0: z = -750.0 * uniform(); break;               /* to underflow */
+      case 1: z = -(708.0 + 38.0 * uniform()); break;      /* subnormal results */
+      case 2: z = -45.0 * uniform(); break;
+      default: z = -ldexp(uniform(), -(int)(next() % 1070)); /* tiny */
+      }
+      const double e = ulp_error(exp_neg(z), expl((long double)z));
+      const double m = ulp_error(expm1_neg(z), expm1l((long double)z));
+      if (e > worst_exp)
+        worst_exp = e;
+      if (m > worst_expm1)
+        worst_expm1 = m;
+    }
+  printf("%.4f %.4f\n", worst_exp, worst_expm1);
+  return 0;
+}
+
 int main(int argc, char **argv) {
+  if (argc > 1 && strcmp(argv[1], "exp") == 0)
+    return exp_main(argc > 2 ? atol(argv[2]) : 200000);
   if (argc > 1)
     seed_bits = atoi(argv[1]);
   const long per_kind = argc > 2 ? atol(argv[2]) : 200000;

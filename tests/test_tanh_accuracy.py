@@ -1,4 +1,5 @@
-"""The accuracy of the GPU tanh's arithmetic, on the host.
+"""The accuracy of the GPU tanh's arithmetic, and of the exp / expm1 core it
+shares with elu and mish, on the host.
 
 tests/tanh_accuracy.c restates the kernel's evaluation (Cody-Waite
 reduction, Taylor polynomial of expm1, one Newton-Raphson step on a
@@ -41,3 +42,15 @@ def test_tanh_arithmetic_is_within_3_ulp(program, seed_bits):
     assert worst <= 2.6, worst
     assert worst_libm <= 3.0, worst_libm
     assert bad == 0
+
+
+def test_exp_core_is_within_1_2_ulp(program):
+    """exp_neg (mish's e^-|x|, scaled in two halves of k so that subnormal
+    results round once) within 1 ulp of expl over [-750, 0], underflow and
+    the subnormal range included; expm1_neg (elu below zero, clamped at -40)
+    within 1.2 ulp of expm1l."""
+    out = subprocess.run([program, "exp", "200000"], check=True,
+                         capture_output=True, text=True).stdout.split()
+    worst_exp, worst_expm1 = float(out[0]), float(out[1])
+    assert worst_exp <= 1.0, worst_exp
+    assert worst_expm1 <= 1.2, worst_expm1
