@@ -535,15 +535,16 @@ MatmulPlan plan_matmul(const DeviceState *dev, const double *a, const double *b,
   // out evenly over one CTA per SM (runs of >= 4 units); a fix-up kernel
   // sums the tiles split over CTAs.  (Keeping every whole wave
   // data-parallel measured equal or slower: 512x8192x8192 34.9 against
-  // 35.3 TFLOP/s, 3072^3 34.4 against 34.6.)  Chosen by itself wherever the wave
-  // model above splits k (measured on B200 it beats the split-K schedule at
-  // every such shape tried: 1024^3 28.5 against 26.2 TFLOP/s, 2048^3 33.4
-  // against 31.4, 256x2048x8192 33.3 against 31.6, 512x8192x8192 35.3
-  // against 34.3), and on request (FORCE_STREAM_K) elsewhere, where it
-  // does not win (8192^3 34.9 against 35.2).  Never with an explicit split,
-  // continued sums (c_in) or NO_STREAM_K: callers that compute a matmul's
-  // rows in pieces pass that flag, since stream-K's partial sums follow the
-  // whole tile set and row pieces could not reproduce them.
+  // 35.3 TFLOP/s, 3072^3 34.4 against 34.6.)  Chosen by itself wherever
+  // the wave model above splits k: measured on B200 it beats the split-K
+  // schedule at every such shape tried (1024^3 29.8 against 26.2 TFLOP/s,
+  // 2048^3 33.1 against 31.5, 256x2048x8192 33.6 against 31.9,
+  // 512x8192x8192 35.6 against 34.3).  On request (FORCE_STREAM_K)
+  // elsewhere, where it does not win (8192^3 34.9 against 35.2).  Never with
+  // an explicit split, continued sums (c_in) or NO_STREAM_K: callers that
+  // compute a matmul's rows in pieces pass that flag, since stream-K's
+  // partial sums follow the whole tile set and row pieces could not
+  // reproduce them.
   const bool explicit_split = ((flags >> 16) & 0xFFu) != 0;
   const bool want_sk = (flags & HEXIR_MATMUL_FORCE_STREAM_K) || p.split_k > 1;
   if (want_sk && p.variant == kTma128 && !c_in && !explicit_split &&
