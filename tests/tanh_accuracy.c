@@ -1,5 +1,5 @@
-/* tanh_accuracy.c -- the arithmetic of the sm_100a tanh kernel and of the
- * exp / expm1 core it shares with elu and mish
+/* tanh_accuracy.c -- the arithmetic of the sm_100a tanh and gelu kernels
+ * and of the exp / expm1 core they share with elu and mish
  * (hexir_b200/csrc/kernels/activation_f64.cu), restated in C with
  * fma() standing for the GPU's DFMA, checked against the C library's
  * 64-bit-mantissa tanhl.  The reciprocal estimate is modelled by a
@@ -64,6 +64,27 @@ static double expm1_neg(double z) {
   const double p = neg_exp_parts(z < -40.0 ? -40.0 : z, &k);
   const double s = pow2i(k);
   return fma(s, p, s - 1.0);
+}
+
+/* GeluOp of activation_f64.cu with its table. */
+static const double gelu_table[228][10] = {
+#include "../hexir_b200/csrc/kernels/gelu_table.inc"
+};
+static double kernel_gelu(double x) {
+  const double u0 = fabs(x) * 0.70710678118654752440;
+  const double u = u0 > 28.5 ? 28.5 : u0;
+  int j = isnan(u) ? 0 : (int)(u * 8.0);
+  j = j < 0 ? 0 : (j > 227 ? 227 : j);
+  const double t = fma(u, 16.0, -(double)(2 * j + 1));
+  const double *c = gelu_table[j];
+  double p = fma(c[9], t, c[8]);
+  for (int k = 7; k >= 0; --k)
+    p = fma(p, t, c[k]);
+  const double uu = u * u, lo = fma(u, u, -uu);
+  double e = exp_neg(-uu);
+  e = fma(-lo, e, e);
+  const double q = p * e;
+  return x * (x < 0.0 ? q : 1.0 - q);
 }
 
 static double kernel_tanh(double x) {
@@ -149,7 +170,54 @@ static int exp_main(long n) {
   return 0;
 }
 
+/* argv[1] == "gelu": worst ulp errors of kernel_gelu against the formula
+ * as written, (x / 2) erfc(-RN(x RN(1 / sqrt 2))), evaluated in long
+ * double, and against the same formula in double with the C library's
+ * erfc (the oracle's evaluation), results within 2^-1000 of the reference
+ * counting as exact; then the special values that differ from the double
+ * formula's. */
+static int gelu_main(long n) {
+  double worst = 0.0, worst_libm = 0.0;
+  for (int kind = 0; kind < 5; ++kind)
+    for (long i = 0; i < n; ++i) {
+      double x;
+      switch (kind) {
+      case 0: x = normal(); break;
+      case 1: x = (2.0 * uniform() - 1.0) * 45.0; break;
+      case 2: x = -40.0 * uniform(); break;
+      case 3: x = ldexp(2.0 * uniform() - 1.0, -(int)(next() % 1070)); break;
+      default: x = (2.0 * uniform() - 1.0) * 3.0;
+      }
+      const double g = kernel_gelu(x);
+      const double arg = -x * 0.70710678118654752440;
+      const long double exact = 0.5L * (long double)x * erfcl((long double)arg);
+      const double libm = (0.5 * x) * erfc(arg);
+      /* Below 2^-1000 only the absolute error counts, as in the GPU tests:
+       * near the subnormals e^{-u^2} carries fewer bits. */
+      const double e = fabsl((long double)g - exact) <= 0x1p-1000L
+                           ? 0.0 : ulp_error(g, exact);
+      const double el = fabs(g - libm) <= 0x1p-1000
+                            ? 0.0 : ulp_error(g, (long double)libm);
+      if (e > worst)
+        worst = e;
+      if (el > worst_libm)
+        worst_libm = el;
+    }
+  const double specials[] = {0.0, -0.0, 0x1p-1074, -0x1p-1074, 40.0, -40.0,
+                             1e300, -1e300, INFINITY, -INFINITY, NAN};
+  int bad = 0;
+  for (unsigned i = 0; i < sizeof specials / sizeof *specials; ++i) {
+    const double x = specials[i], g = kernel_gelu(x);
+    const double want = (0.5 * x) * erfc(-x * 0.70710678118654752440);
+    bad += !(isnan(want) ? isnan(g) : to_bits(g) == to_bits(want));
+  }
+  printf("%.4f %.4f %d\n", worst, worst_libm, bad);
+  return 0;
+}
+
 int main(int argc, char **argv) {
+  if (argc > 1 && strcmp(argv[1], "gelu") == 0)
+    return gelu_main(argc > 2 ? atol(argv[2]) : 200000);
   if (argc > 1 && strcmp(argv[1], "exp") == 0)
     return exp_main(argc > 2 ? atol(argv[2]) : 200000);
   if (argc > 1)

@@ -54,3 +54,31 @@ def test_exp_core_is_within_1_2_ulp(program):
     worst_exp, worst_expm1 = float(out[0]), float(out[1])
     assert worst_exp <= 1.0, worst_exp
     assert worst_expm1 <= 1.2, worst_expm1
+
+
+def test_gelu_arithmetic_is_within_4_ulp(program):
+    """The table-driven gelu (a degree-9 polynomial per interval for
+    erfc(u) e^{u^2} / 2, times e^{-u^2} from the exp core) within 4 ulp of
+    the formula as written evaluated in long double, 5 ulp of its double
+    evaluation with the C library's erfc (the oracle's), and with the
+    oracle's special values (signed zeros, saturation, infinities, NaN)."""
+    out = subprocess.run([program, "gelu", "200000"], check=True,
+                         capture_output=True, text=True).stdout.split()
+    worst, worst_libm, bad = float(out[0]), float(out[1]), int(out[2])
+    assert worst <= 4.0, worst
+    assert worst_libm <= 5.0, worst_libm
+    assert bad == 0
+
+
+def test_gelu_table_is_its_generators_output(tmp_path):
+    """gelu_table.inc is exactly what gelu_table_gen.c writes."""
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    kernels = os.path.join(HERE, "..", "hexir_b200", "csrc", "kernels")
+    exe = str(tmp_path / "gelu_table_gen")
+    subprocess.run([cc, "-O2", "-o", exe,
+                    os.path.join(kernels, "gelu_table_gen.c"), "-lm"], check=True)
+    out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+    with open(os.path.join(kernels, "gelu_table.inc")) as f:
+        assert f.read() == out
