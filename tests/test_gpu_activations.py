@@ -10,7 +10,8 @@ bit.  Tolerances, per element (oracle.ulp_error_ok):
   leaky_relu            bit-exact (a compare and one multiply)
   elu, sigmoid, tanh,   16 ulp of the oracle's value (2^-1000 absolute floor
   swish, mish           for results that underflow)
-  gelu                  32 ulp (erfc is the least accurate of the functions)
+  gelu                  8 ulp (its table-driven erfc is within 5 of the
+                        oracle's C-library form on the host)
   softmax               (cols + 16) ulp: the row sum is taken in a different
                         order (a tree over the row instead of left to right)
 
@@ -26,7 +27,7 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-ULPS = {"leaky_relu": 0, "elu": 16, "sigmoid": 16, "tanh": 16, "gelu": 32,
+ULPS = {"leaky_relu": 0, "elu": 16, "sigmoid": 16, "tanh": 16, "gelu": 8,
         "swish": 16, "mish": 16}
 ELEMENTWISE = sorted(ULPS)
 
